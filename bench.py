@@ -1,0 +1,543 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE layer (qwen-go moeMLP.forward, model/moe.go:41-99).
+
+Default workload = BASELINE config 3: the Qwen3-30B-A3B-shaped layer
+(H=2048, E=128, top-8, I=768, int8 group-32 experts with fp16 scales, f32
+router) in prefill over 4096 tokens whose routing follows a Zipf(1.1) skew.
+One step = one full MoE-layer forward over the batch.  Inputs are synthetic
+(seeded counter-based generator); weights are random-init of that
+architecture.  The weights (641.7 MB) exceed the 126 MB L2, so no flush is
+needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  --impl reference times the CPU restatement
+of the reference's Go MoE forward (token-parallel over all host cores).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(REPO, "qwen-go_b200"), os.path.join(REPO, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CONFIGS = {
+    # name: shapes, bits, tokens, seed, zipf skew
+    "c1": dict(H=1024, E=16, k=4, I=512, Is=1024, bits=8, T=32, seed=1, zipf=False,
+               desc="c1 int8 decode MoE layer (H=1024, E=16, top-4, I=512, shared 1024)"),
+    "c2": dict(H=2048, E=128, k=8, I=768, Is=0, bits=4, T=64, seed=2, zipf=False,
+               desc="c2 int4 decode MoE layer (Qwen3-30B-A3B-shaped)"),
+    "c3": dict(H=2048, E=128, k=8, I=768, Is=0, bits=8, T=4096, seed=3, zipf=True,
+               desc="c3 int8 prefill MoE layer (Qwen3-30B-A3B-shaped), Zipf(1.1) routing"),
+}
+L2_BYTES = 126 * 2**20
+MU = 1.0  # activation mean for the Zipf construction
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def weight_bytes(cfg):
+    """Bytes of one expert's gate_up + down weights (codes + fp16 scales)."""
+    H, I, bits = cfg["H"], cfg["I"], cfg["bits"]
+    n = 3 * H * I
+    if bits == 32:
+        return n * 4
+    return n * bits // 8 + (n // 32) * 2
+
+
+def layer_flops(cfg, T):
+    H, E, k, I, Is = cfg["H"], cfg["E"], cfg["k"], cfg["I"], cfg["Is"]
+    return 2 * T * k * 3 * H * I + 2 * T * E * H + (2 * T * 3 * H * Is if Is else 0)
+
+
+# --------------------------------------------------------------------------
+# Zipf routing construction (weights-side bias, the reference math unchanged)
+# --------------------------------------------------------------------------
+
+
+def zipf_target(T, k, E, s=1.1):
+    f = np.arange(1, E + 1, dtype=np.float64) ** (-s)
+    total = T * k
+    cap = float(T)
+    tgt = np.zeros(E)
+    free = np.ones(E, bool)
+    rem = float(total)
+    for _ in range(E):
+        share = f * free
+        t = rem * share / share.sum()
+        over = (t > cap) & free
+        if not over.any():
+            tgt[free] = t[free]
+            break
+        tgt[over] = cap
+        free &= ~over
+        rem = total - tgt[~free].sum()
+    return tgt
+
+
+def calibrate_zipf(router, x, k):
+    """Picks c so that adding b_e = -1.1 ln(e+1) c / (mu H) to router row e
+    makes the TOPK selection histogram closest (L1, sorted) to Zipf(1.1)."""
+    E, H = router.shape
+    T = x.shape[0]
+    base = x.astype(np.float64) @ router.astype(np.float64).T           # [T, E]
+    xs = x.astype(np.float64).sum(axis=1, keepdims=True)                 # [T, 1]
+    tgt = np.sort(zipf_target(T, k, E))[::-1]
+    best = (None, math.inf, None)
+    for c in np.arange(0.0, 4.01, 0.1):
+        b = -1.1 * np.log(np.arange(E) + 1.0) * c
+        logits = base + xs * (b / (MU * H))[None, :]
+        sel = np.argpartition(-logits, k - 1, axis=1)[:, :k]
+        hist = np.bincount(sel.ravel(), minlength=E)
+        d = np.abs(np.sort(hist)[::-1] - tgt).sum()
+        if d < best[1]:
+            best = (float(round(c, 2)), d, hist)
+    return best[0], best[2]
+
+
+def zipf_bias_rows(E, H, c):
+    b = -1.1 * np.log(np.arange(E) + 1.0) * c
+    return (b / (MU * H)).astype(np.float32)
+
+
+# --------------------------------------------------------------------------
+# Layer construction
+# --------------------------------------------------------------------------
+
+
+def build_gpu_layer(cfg, device, experts=None):
+    """Generates the layer on the GPU with the library's generator/quantiser.
+    Returns (MoeMLP, host copies for the CPU baseline, routing info)."""
+    import torch
+    import qgmoe
+
+    H, E, k, I, Is, bits, seed = (cfg[n] for n in ("H", "E", "k", "I", "Is", "bits", "seed"))
+    dev = torch.device("cuda", device)
+
+    def g(stream, shape, std=0.02):
+        t = torch.empty(shape, dtype=torch.float32, device=dev)
+        return qgmoe.randn_device(t, seed, stream, std)
+
+    router = g(0, (E, H))
+    info = {}
+    x = g(100, (cfg["T"], H), 1.0)
+    if cfg["zipf"]:
+        x += MU
+        xs = x[:1024].cpu().numpy()
+        c, hist = calibrate_zipf(router.cpu().numpy(), xs, k)
+        router += torch.from_numpy(zipf_bias_rows(E, H, c)).to(dev)[:, None]
+        info["zipf_c"] = c
+    args = dict(router=router)
+    host = {"router": router.cpu().numpy()}
+    mats = {"gate_up": (1, (E * 2 * I, H)), "down": (2, (E * H, I))}
+    if Is:
+        args["shared_gate"] = g(3, (H,))
+        host["shared_gate"] = args["shared_gate"].cpu().numpy()
+        mats.update(shared_gate=(4, (Is, H)), shared_up=(5, (Is, H)), shared_down=(6, (H, Is)))
+    for name, (stream, shape) in mats.items():
+        w = g(stream, shape)
+        if bits == 32:
+            key = {"gate_up": "gate_up", "down": "down"}.get(name, name + "_proj")
+            args[key] = w
+            host[name] = w.cpu().numpy()
+        else:
+            q, _s32, s16 = qgmoe.quantize_device(w, bits)
+            args[name + "_q"] = q
+            args[name + "_scale"] = s16
+            host[name + "_q"] = q.cpu().numpy()
+            host[name + "_s"] = s16.cpu().numpy().view(np.float16).astype(np.float32)
+        del w
+    torch.cuda.synchronize(dev)
+    layer = qgmoe.MoeMLP(n_embed=H, n_experts=E, top_k=k, n_moe_mlp=I, n_shared_mlp=Is, bits=bits,
+                         router_mode=qgmoe.ROUTER_TOPK, device=device, **args)
+    del args
+    torch.cuda.empty_cache()
+    return layer, x, host, info
+
+
+def oracle_weights(cfg, host):
+    import qg_oracle as O
+    H, E, k, I, Is, bits = (cfg[n] for n in ("H", "E", "k", "I", "Is", "bits"))
+    m = O.MoeWeights(H=H, E=E, k=k, I=I, Is=Is, bits=bits, router=host["router"],
+                     shared_gate=host.get("shared_gate"))
+    if bits == 32:
+        m.gate_up = host["gate_up"].reshape(E, 2 * I, H)
+        m.down = host["down"].reshape(E, H, I)
+        if Is:
+            m.sh_gate, m.sh_up, m.sh_down = (host["shared_gate"], host["shared_up"],
+                                             host["shared_down"])
+    else:
+        for name, key in (("gate_up", "gate_up"), ("down", "down"), ("shared_gate", "sh_gate"),
+                          ("shared_up", "sh_up"), ("shared_down", "sh_down")):
+            if name + "_q" in host:
+                m.q[key] = host[name + "_q"]
+                m.s[key] = host[name + "_s"]
+    return m
+
+
+def oracle_layer_cpu(cfg, threads):
+    """The same layer generated entirely on the CPU by the oracle's generator
+    and quantiser (used by the reference arm, which runs no GPU code)."""
+    import qg_oracle as O
+    from concurrent.futures import ThreadPoolExecutor
+    H, E, k, I, Is, bits, seed = (cfg[n] for n in ("H", "E", "k", "I", "Is", "bits", "seed"))
+
+    def gen(stream, shape, std=0.02):
+        n = int(np.prod(shape))
+        out = np.empty(n, np.float32)
+        chunk = (n + threads - 1) // threads
+
+        def part(i):
+            lo, hi = i * chunk, min(n, (i + 1) * chunk)
+            if lo < hi:
+                out[lo:hi] = O.randn(seed, stream, (hi - lo,), std, offset=lo)
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(part, range(threads)))
+        return out.reshape(shape)
+
+    host = {"router": gen(0, (E, H))}
+    x = gen(100, (cfg["T"], H), 1.0)
+    if cfg["zipf"]:
+        x += MU
+        c, _ = calibrate_zipf(host["router"], x[:1024], k)
+        host["router"] += zipf_bias_rows(E, H, c)[:, None]
+    mats = {"gate_up": (1, (E * 2 * I, H)), "down": (2, (E * H, I))}
+    if Is:
+        host["shared_gate"] = gen(3, (H,))
+        mats.update(shared_gate=(4, (Is, H)), shared_up=(5, (Is, H)), shared_down=(6, (H, Is)))
+    for name, (stream, shape) in mats.items():
+        w = gen(stream, shape)
+        if bits == 32:
+            host[name] = w
+        else:
+            q, s = O.quantize(w, bits)
+            host[name + "_q"] = q
+            host[name + "_s"] = O.f16_round(s)
+    return oracle_weights(cfg, host), x
+
+
+# --------------------------------------------------------------------------
+# Clock sampling
+# --------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# Arms
+# --------------------------------------------------------------------------
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline_ours(cfg, host, x_host, budget_s=12.0):
+    """The oracle (C restatement of moe.go, -O2, no FMA contraction), one
+    thread, as decodeLayers calls mlp.forward: token by token."""
+    import qg_oracle as O
+    m = oracle_weights(cfg, host)
+    t0 = time.perf_counter()
+    O.moe_forward(m, x_host[:1])
+    t1 = max(time.perf_counter() - t0, 1e-4)
+    n = int(max(1, min(cfg["T"], budget_s / t1)))
+    t0 = time.perf_counter()
+    O.moe_forward(m, x_host[1:1 + n] if n + 1 <= cfg["T"] else x_host[:n])
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{n} of the {cfg['T']} tokens, same weights, serial per token "
+                      f"(oracle/qg_oracle.c, 1 thread; the Go reference's MoE is serial, "
+                      f"model/model.go:507-514)"}
+
+
+def run_reference(args, cfg):
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return
+    import qg_oracle as O
+    threads = os.cpu_count() or 1
+    m, x = oracle_layer_cpu(cfg, threads)
+    # size one step to a bounded token sample (a few seconds on all cores)
+    t0 = time.perf_counter()
+    O.moe_forward_mt(m, x[:threads], threads)
+    per_tok = max((time.perf_counter() - t0) / threads, 1e-6)  # wall per token per core
+    budget = float(os.environ.get("QG_REF_STEP_S", "6"))
+    n = int(max(threads, min(cfg["T"], budget * threads / max(per_tok * threads, 1e-6))))
+    n = min(n, cfg["T"])
+    for _ in range(args.warmup):
+        O.moe_forward_mt(m, x[:n], threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_forward_mt(m, x[:n], threads)
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    val = n * args.steps / tot
+    line = {
+        "impl": "reference", "metric": "MoE-layer tokens/s", "value": val, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "none", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_json(cfg, world),
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} of {cfg['T']} tokens per step, token-parallel over "
+                                   f"{threads} threads (the Go reference runs the MoE serially "
+                                   f"per token; this restatement spreads tokens over cores)"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_json(cfg, world):
+    wb = weight_bytes(cfg)
+    return {"workload": cfg["desc"], "H": cfg["H"], "E": cfg["E"], "top_k": cfg["k"],
+            "I": cfg["I"], "shared_I": cfg["Is"], "bits": cfg["bits"],
+            "scale": "fp16 group-32", "tokens": cfg["T"], "router": "topk f32",
+            "l2": ("no flush: weights %.1f MB > 126 MB L2" % (cfg["E"] * wb / 1e6)
+                   if cfg["E"] * wb > L2_BYTES else "L2 flushed between steps"),
+            "parallelism": "single GPU" if world == 1 else f"ep{world}"}
+
+
+def run_ours(args, cfg):
+    import torch
+    import qgmoe
+
+    world, rank, local = dist_setup(args.gpus)
+    dev = local
+    torch.cuda.set_device(dev)
+    if world > 1:
+        raise SystemExit("expert-parallel path not built yet")
+    layer, x, host, info = build_gpu_layer(cfg, dev)
+    T, H, k = cfg["T"], cfg["H"], cfg["k"]
+    out = torch.empty_like(x)
+    sel = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    flush = None
+    if cfg["E"] * weight_bytes(cfg) <= L2_BYTES:
+        flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=x.device)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        if flush is not None:
+            flush.zero_()
+        layer.forward_device(x, out, sel_idx=sel, stream=stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    layer.sync(stream)
+    hist = np.bincount(sel.cpu().numpy().ravel(), minlength=cfg["E"])
+    distinct = int((hist > 0).sum())
+
+    # ---- timed region (device events, max over ranks) ----
+    layer.set_timing(True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    stage_ms, nf = layer.read_timing()
+    layer.set_timing(False)
+    layer.sync(stream)
+    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    forward_ms = sum(stage_ms.values()) / max(nf, 1)
+    ms_per_step = total_ms / args.steps
+    value = T * world * args.steps / (total_ms / 1e3)
+
+    # ---- roofline of the dominant kernel ----
+    peaks, peak_src = load_peaks()
+    stages = {kname: v / max(nf, 1) for kname, v in stage_ms.items()}
+    dom = max(stages, key=stages.get)
+    dom_ms = stages[dom]
+    prefill = cfg["T"] >= 512
+    if prefill:
+        Iw = 2 * cfg["I"] if dom == "gate_up" else cfg["I"]
+        flops = 2.0 * T * k * Iw * H if dom in ("gate_up", "down") else 2.0 * T * cfg["E"] * H
+        achieved = flops / (dom_ms / 1e3) / 1e12
+        peak = peaks["bf16_tflops"]
+        roof = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peak_src} bf16 dense (MEASURED_PEAKS.json bf16_tflops)",
+                "algorithmic_per_launch": f"{flops / 1e9:.1f} GFLOP", "traffic": None}
+    else:
+        frac_w = (2 / 3) if dom == "gate_up" else (1 / 3)
+        bytes_ = distinct * weight_bytes(cfg) * frac_w + T * H * 4 * 2
+        achieved = bytes_ / (dom_ms / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"{peak_src} HBM copy",
+                "algorithmic_per_launch": f"{bytes_ / 1e6:.2f} MB", "traffic": None}
+
+    # ---- end to end through the public host API (pinned buffers) ----
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    L = qgmoe.lib()
+    for _ in range(2):
+        rc = L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
+        assert rc == 0, qgmoe.last_error()
+    e2e_steps = max(1, min(args.steps, 20))
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        if flush is not None:
+            flush.zero_()
+            torch.cuda.synchronize(dev)
+        L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = {"value": T * world * e2e_steps / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+           "api": "qgmoe_forward (host pointers, blocking)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_ours(cfg, host, x.cpu().numpy())
+
+    if rank == 0:
+        cfgj = config_json(cfg, world)
+        cfgj.update(info)
+        cfgj["expert_load_top8"] = sorted(hist.tolist(), reverse=True)[:8]
+        cfgj["expert_load_min"] = int(hist.min())
+        cfgj["distinct_experts"] = distinct
+        line = {
+            "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak" if world > 1 else "none",
+            "vs_baseline": None, "dtype": "f32 activations, int%d weights" % cfg["bits"]
+            if cfg["bits"] != 32 else "f32", "data": "synthetic", "config": cfgj,
+            "stage_ms": stages, "forward_ms_device": forward_ms,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": layer.last_launch_count() * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.tokens:
+        cfg["T"] = args.tokens
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

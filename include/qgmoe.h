@@ -1,0 +1,176 @@
+/*
+ * qgmoe.h -- C ABI of the B200 (sm_100a) Mixture-of-Experts layer and
+ * group-32 QuantLinear matmuls for qwen-go.
+ *
+ * Plain C: pointers, sizes and integer status codes only.  Every entry point
+ * returns 0 (QGMOE_OK) or a negative QGMOE_ERR_* code; none aborts or exits.
+ * qgmoe_strerror() and qgmoe_last_error() give the text.
+ *
+ * Seams of the reference this library replaces (jackkey143084/qwen-go):
+ *   mixer.forward(x []float32) []float32        model/model.go:373-375, called
+ *                                               per token at model/model.go:512
+ *   moeMLP{...} / moeMLP.forward                model/moe.go:10-25, 41-99
+ *   quantLinear{...} / .forward / .dequantize   model/moe.go:126-162
+ *   quantizeInt8 / quantizeInt4                 model/moe.go:165-217, 233-239
+ *   proj(x, T, l, q, out) over a quantLinear     model/model.go:196-205
+ *
+ * Threading: a handle is not re-entrant; callers serialise calls on one
+ * handle (the Go shim holds a mutex).  Each call sets its CUDA device first,
+ * so the calling OS thread may change between calls (cgo).
+ */
+#ifndef QGMOE_H
+#define QGMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+#define QGMOE_OK 0
+#define QGMOE_ERR_INVALID_ARG (-1) /* bad shape, null pointer, unsupported combo */
+#define QGMOE_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define QGMOE_ERR_NCCL (-3)        /* reserved for the expert-parallel path */
+#define QGMOE_ERR_TIMEOUT (-4)     /* a bounded device wait ran out */
+#define QGMOE_ERR_DEVICE_FLAG (-5) /* a kernel's bounds check fired (see last_error) */
+#define QGMOE_ERR_UNSUPPORTED (-6) /* valid request this build does not implement */
+#define QGMOE_ERR_NO_DEVICE (-7)   /* no CUDA device / not an sm_100 device */
+
+/* ---- enums ------------------------------------------------------------ */
+/* Router selection.  TOPK: the documented semantics (softmax then the k
+ * largest probabilities, descending, ties to the lower expert index) -- the
+ * insertion sort of model/moe.go:49-53 run over all experts.  PREFIX: the
+ * literal loop bound of model/moe.go:49 (`i < m.topK`), which orders only
+ * experts 0..k-1. */
+#define QGMOE_ROUTER_TOPK 0
+#define QGMOE_ROUTER_PREFIX 1
+
+/* dtype of the host/device scale arrays handed to create(); the library
+ * always stores fp16 scales on the device (RNE rounding from f32). */
+#define QGMOE_SCALE_F16 0 /* uint16_t IEEE half bits */
+#define QGMOE_SCALE_F32 1 /* float, as quantizeInt8/Int4 emit (moe.go:164) */
+
+/* ---- MoE layer -------------------------------------------------------- */
+typedef struct qgmoe qgmoe_t;
+
+/* Weights of one moeMLP (model/moe.go:10-25).  Layouts are the reference's:
+ * rows are (out, in), row-major.  bits selects the expert + shared-expert
+ * weight format: 32 = float32 (gateUpW/downW), 8 or 4 = quantLinear codes
+ * (int8 [O, I] bytes, or int4 packed [O, I/2] with element 2c in the high
+ * nibble of byte c, both stored +8 ... see quantizeInt4) plus group-32
+ * scales [O, I/32].  The router (gate) and sharedGate stay float32.
+ * All pointers are either host pointers (weights_on_device = 0) or device
+ * pointers on `device` (1); create() copies them, the caller keeps
+ * ownership of its buffers. */
+typedef struct qgmoe_desc {
+    int32_t n_embed;      /* H   moeMLP.nEmbed */
+    int32_t n_experts;    /* E   moeMLP.nExperts */
+    int32_t top_k;        /* k   moeMLP.topK (1..32, <= E) */
+    int32_t n_moe_mlp;    /* I   moeMLP.nMoeMlp */
+    int32_t n_shared_mlp; /* Is  shared expert width, 0 = none */
+    int32_t bits;         /* 32, 8 or 4 */
+    int32_t router_mode;  /* QGMOE_ROUTER_* */
+    int32_t scale_dtype;  /* QGMOE_SCALE_* for the *_scale arrays */
+    int32_t weights_on_device;
+    int32_t device;       /* CUDA ordinal that owns the handle */
+    const float *router;        /* [E, H]   mlp.gate.weight */
+    const float *shared_gate;   /* [H]      mlp.shared_expert_gate.weight (Is > 0) */
+    /* bits == 32 */
+    const float *gate_up;       /* [E, 2I, H] mlp.experts.gate_up_proj (gate rows 0..I-1) */
+    const float *down;          /* [E, H, I]  mlp.experts.down_proj */
+    const float *shared_gate_proj; /* [Is, H] */
+    const float *shared_up_proj;   /* [Is, H] */
+    const float *shared_down_proj; /* [H, Is] */
+    /* bits == 8 / 4: codes and scales, same tensors quantised row-wise */
+    const uint8_t *gate_up_q;
+    const void *gate_up_scale;
+    const uint8_t *down_q;
+    const void *down_scale;
+    const uint8_t *shared_gate_q;
+    const void *shared_gate_scale;
+    const uint8_t *shared_up_q;
+    const void *shared_up_scale;
+    const uint8_t *shared_down_q;
+    const void *shared_down_scale;
+} qgmoe_desc;
+
+/* Uploads the weights (device copies owned by the handle). */
+int qgmoe_create(const qgmoe_desc *desc, qgmoe_t **out);
+int qgmoe_destroy(qgmoe_t *h);
+
+/* moeMLP.forward over T independent tokens (T = 1 is mixer.forward; T > 1
+ * is the batched form decodeLayers hands over).  HOST pointers; blocking.
+ * x [T, H] f32 -> out [T, H] f32.  sel_idx [T, k] int32 and sel_w [T, k]
+ * f32 (the selected experts in routing order and their renormalised
+ * weights, model/moe.go:53-63) are optional (NULL to skip). */
+int qgmoe_forward(qgmoe_t *h, const float *x, int32_t T, float *out, int32_t *sel_idx,
+                  float *sel_w);
+
+/* Same on DEVICE pointers, enqueued on `stream` (a cudaStream_t; NULL = the
+ * handle's own stream).  Returns after enqueueing; device-side bounds flags
+ * are reported by qgmoe_sync(). */
+int qgmoe_forward_device(qgmoe_t *h, const float *x, int32_t T, float *out, int32_t *sel_idx,
+                         float *sel_w, void *stream);
+
+/* Waits for `stream` (NULL = the handle's stream) and reports any
+ * device-side bounds flag raised since the last check. */
+int qgmoe_sync(qgmoe_t *h, void *stream);
+
+/* Number of kernel launches the last forward enqueued (instrumentation). */
+int qgmoe_last_launch_count(const qgmoe_t *h);
+
+/* Per-stage device timing (instrumentation for benchmarks): when enabled,
+ * every forward records CUDA events on its stream between consecutive
+ * stages, without host syncs.  read_timing waits for those forwards, writes
+ * up to n per-stage durations in milliseconds SUMMED over the forwards since
+ * the previous read to ms, their count to *n_forwards, and returns the stage
+ * count (or a negative status); stage_name gives stage i's name ("route",
+ * "gate_up", ...). */
+int qgmoe_set_timing(qgmoe_t *h, int32_t enable);
+int qgmoe_read_timing(qgmoe_t *h, float *ms, int32_t n, int32_t *n_forwards);
+const char *qgmoe_stage_name(const qgmoe_t *h, int32_t i);
+
+/* ---- QuantLinear -------------------------------------------------------- */
+typedef struct qgql qgql_t;
+
+/* quantLinear{bits, outFeatures, inFeatures, qweight, scale}
+ * (model/moe.go:126-132).  bits 8 or 4, or 32 for a plain f32 linear
+ * (then q holds float32 rows and scale is ignored).  in_features % 32 == 0. */
+int qgql_create(int32_t bits, int32_t out_features, int32_t in_features, const void *q,
+                const void *scale, int32_t scale_dtype, int32_t weights_on_device,
+                int32_t device, qgql_t **out);
+int qgql_destroy(qgql_t *h);
+
+/* proj(x, T, nil, q, out) / quantLinear.forward: y[T, out] = x[T, in] W^T
+ * with the dequantisation fused into the weight load.  HOST pointers. */
+int qgql_forward(qgql_t *h, const float *x, int32_t T, float *y);
+/* Same on DEVICE pointers, enqueued on `stream` (NULL = handle stream). */
+int qgql_forward_device(qgql_t *h, const float *x, int32_t T, float *y, void *stream);
+/* quantLinear.dequantize (model/moe.go:134-157) into w_dev [out, in] f32. */
+int qgql_dequantize_device(qgql_t *h, float *w_dev, void *stream);
+
+/* quantizeInt8 / quantizeInt4 (model/moe.go:165-217) on the GPU, bit-exact:
+ * w_dev [out, in] f32 -> q_dev (int8 [out,in] or int4 [out,in/2] bytes),
+ * scale_f32_dev [out, in/32] (optional) and scale_f16_dev (optional, RNE). */
+int qgql_quantize_device(int32_t bits, int32_t out_features, int32_t in_features,
+                         const float *w_dev, uint8_t *q_dev, float *scale_f32_dev,
+                         uint16_t *scale_f16_dev, void *stream);
+
+/* ---- utilities -------------------------------------------------------------- */
+/* Fills dev[0..n) with stdv * N(0,1) from the counter-based generator
+ * (splitmix64 + Box-Muller) keyed by (seed, stream), values offset..offset+n. */
+int qg_randn_device(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
+                    float *dev, void *cuda_stream);
+
+const char *qgmoe_strerror(int status);
+/* Detail of the last failure on this thread (e.g. the CUDA error string). */
+const char *qgmoe_last_error(void);
+/* 1 when built for and running on an sm_100 device, else 0. */
+int qgmoe_device_ok(int32_t device);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QGMOE_H */

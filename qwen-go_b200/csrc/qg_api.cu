@@ -1,0 +1,632 @@
+// C ABI (include/qgmoe.h): handle lifetime, weight upload, forward calls.
+//
+// The handle mirrors moeMLP (model/moe.go:10-25): router + stacked expert
+// gate_up/down + optional gated shared expert, in f32 or quantLinear format.
+// It owns every device buffer.  Forward is route/dispatch -> grouped
+// gate_up+SwiGLU -> grouped down -> combine, four launches on one stream.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "qg_common.cuh"
+
+namespace qg {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int num_sms(int device) {
+    static int cache[64] = {0};
+    if (device >= 0 && device < 64 && cache[device]) return cache[device];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) n = 148;
+    if (device >= 0 && device < 64) cache[device] = n;
+    return n;
+}
+
+// Device allocation list owned by a handle.
+struct Allocs {
+    std::vector<void *> ptrs;
+    int alloc(void **p, size_t bytes) {
+        *p = nullptr;
+        if (bytes == 0) return QGMOE_OK;
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e != cudaSuccess)
+            return set_error(QGMOE_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+        ptrs.push_back(*p);
+        return QGMOE_OK;
+    }
+    void free_all() {
+        for (void *p : ptrs) cudaFree(p);
+        ptrs.clear();
+    }
+};
+
+static int check_device(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
+        return set_error(QGMOE_ERR_NO_DEVICE, "no CUDA device visible");
+    if (device < 0 || device >= n)
+        return set_error(QGMOE_ERR_INVALID_ARG, "device %d out of range (%d devices)", device, n);
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    if (major != 10)
+        return set_error(QGMOE_ERR_NO_DEVICE,
+                         "device %d is sm_%d.x; this library is built for sm_100a only", device,
+                         major);
+    QG_CUDA(cudaSetDevice(device));
+    return QGMOE_OK;
+}
+
+// Copies `bytes` from a host or device source into a fresh device buffer.
+static int upload(Allocs &al, const void *src, size_t bytes, bool src_dev, void **dst,
+                  cudaStream_t s) {
+    int rc = al.alloc(dst, bytes);
+    if (rc) return rc;
+    if (bytes == 0) return QGMOE_OK;
+    QG_CUDA(cudaMemcpyAsync(*dst, src, bytes, src_dev ? cudaMemcpyDeviceToDevice
+                                                       : cudaMemcpyHostToDevice, s));
+    return QGMOE_OK;
+}
+
+// Builds one WeightSet from `parts` stacked row blocks (the shared expert's
+// gate and up projections become one [2Is, H] gate_up set).
+struct Part {
+    const float *w32;
+    const uint8_t *q;
+    const void *scale;
+    int rows;
+};
+
+static int build_set(Allocs &al, int bits, int K, int rows_per_group, int groups,
+                     const Part *parts, int nparts, int scale_dtype, bool src_dev, WeightSet *ws,
+                     cudaStream_t s) {
+    ws->bits = bits;
+    ws->rows = rows_per_group;
+    ws->K = K;
+    ws->w32 = nullptr;
+    ws->q = nullptr;
+    ws->s = nullptr;
+    int64_t total_rows = 0;
+    for (int i = 0; i < nparts; i++) total_rows += parts[i].rows;
+    if (total_rows != (int64_t)rows_per_group * groups)
+        return set_error(QGMOE_ERR_INVALID_ARG, "internal: row count mismatch");
+    const size_t row_bytes = bits == 32 ? (size_t)K * 4 : (bits == 8 ? (size_t)K : (size_t)K / 2);
+    const cudaMemcpyKind kind = src_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    uint8_t *w = nullptr;
+    int rc = al.alloc(reinterpret_cast<void **>(&w), row_bytes * total_rows);
+    if (rc) return rc;
+    size_t off = 0;
+    for (int i = 0; i < nparts; i++) {
+        const void *src = bits == 32 ? static_cast<const void *>(parts[i].w32) : parts[i].q;
+        if (!src) return set_error(QGMOE_ERR_INVALID_ARG, "missing weight tensor");
+        QG_CUDA(cudaMemcpyAsync(w + off, src, row_bytes * parts[i].rows, kind, s));
+        off += row_bytes * parts[i].rows;
+    }
+    if (bits == 32) {
+        ws->w32 = reinterpret_cast<const float *>(w);
+        return QGMOE_OK;
+    }
+    ws->q = w;
+    __half *sc = nullptr;
+    rc = al.alloc(reinterpret_cast<void **>(&sc), sizeof(__half) * total_rows * (K / QG_GROUP));
+    if (rc) return rc;
+    int64_t soff = 0;
+    for (int i = 0; i < nparts; i++) {
+        if (!parts[i].scale) return set_error(QGMOE_ERR_INVALID_ARG, "missing scale tensor");
+        const int64_t n = (int64_t)parts[i].rows * (K / QG_GROUP);
+        if (scale_dtype == QGMOE_SCALE_F16) {
+            QG_CUDA(cudaMemcpyAsync(sc + soff, parts[i].scale, sizeof(__half) * n, kind, s));
+        } else {
+            float *tmp = nullptr;
+            QG_CUDA(cudaMalloc(&tmp, sizeof(float) * n));
+            cudaError_t e = cudaMemcpyAsync(tmp, parts[i].scale, sizeof(float) * n, kind, s);
+            if (e == cudaSuccess) rc = launch_f32_to_f16(tmp, sc + soff, n, s);
+            cudaStreamSynchronize(s);
+            cudaFree(tmp);
+            if (e != cudaSuccess)
+                return set_error(QGMOE_ERR_CUDA, "scale upload: %s", cudaGetErrorString(e));
+            if (rc) return rc;
+        }
+        soff += n;
+    }
+    ws->s = sc;
+    return QGMOE_OK;
+}
+
+}  // namespace qg
+
+using namespace qg;
+
+struct qgmoe {
+    int device = 0;
+    int H = 0, E = 0, k = 0, I = 0, Is = 0, bits = 0, mode = 0, has_shared = 0;
+    cudaStream_t stream = nullptr;
+    Allocs weights;
+    Allocs work;
+    float *router = nullptr;
+    float *shared_gate = nullptr;
+    WeightSet gu{}, dn{}, sgu{}, sdn{};
+    // workspace (capacity cap_T tokens)
+    int cap_T = 0;
+    RouteState st{};
+    float *h = nullptr;  // [slots, hmax]
+    float *d = nullptr;  // [slots, H]
+    float *x_dev = nullptr, *out_dev = nullptr;
+    int *err_dev = nullptr;
+    int hmax = 0;
+    int last_launches = 0;
+    // stage timing (qgmoe_set_timing): one event set per timed forward since
+    // the last read, so a whole timed loop runs without host syncs.
+    static constexpr int kMaxStages = 8;
+    bool timing = false;
+    std::vector<std::vector<cudaEvent_t>> ev_sets;
+    int ev_used = 0, ev_cur = -1;
+    const char *stage_names[kMaxStages] = {};
+    int n_stages = 0;
+    void begin_timed() {
+        ev_cur = -1;
+        if (!timing) return;
+        if (ev_used == (int)ev_sets.size()) {
+            std::vector<cudaEvent_t> set(kMaxStages + 1, nullptr);
+            for (auto &e : set)
+                if (cudaEventCreate(&e) != cudaSuccess) return;
+            ev_sets.push_back(set);
+        }
+        ev_cur = ev_used++;
+    }
+    void mark(int i, const char *name_after, cudaStream_t s) {
+        if (ev_cur < 0 || i > kMaxStages) return;
+        cudaEventRecord(ev_sets[ev_cur][i], s);
+        if (i > 0) stage_names[i - 1] = name_after;
+        n_stages = i;
+    }
+};
+
+static int ensure_capacity(qgmoe *m, int T) {
+    if (T <= m->cap_T) return QGMOE_OK;
+    cudaStreamSynchronize(m->stream);
+    m->work.free_all();
+    int cap = m->cap_T ? m->cap_T : 1;
+    while (cap < T) cap *= 2;
+    const size_t pairs = (size_t)cap * m->k;
+    const size_t slots = pairs + (m->has_shared ? cap : 0);
+    Allocs &w = m->work;
+    RouteState &st = m->st;
+    int rc = 0;
+#define QG_A(ptr, bytes) \
+    if ((rc = w.alloc(reinterpret_cast<void **>(&(ptr)), (bytes)))) return rc
+    QG_A(st.topk_idx, sizeof(int32_t) * pairs);
+    QG_A(st.topk_w, sizeof(float) * pairs);
+    QG_A(st.shared_w, sizeof(float) * cap);
+    QG_A(st.counts, sizeof(int32_t) * m->E);
+    QG_A(st.done_ctr, sizeof(int32_t));
+    QG_A(st.pair_slot, sizeof(int32_t) * pairs);
+    QG_A(st.slot_token, sizeof(int32_t) * slots);
+    QG_A(st.act_group, sizeof(int32_t) * (m->E + 1));
+    QG_A(st.act_begin, sizeof(int32_t) * (m->E + 1));
+    QG_A(st.act_n, sizeof(int32_t) * (m->E + 1));
+    QG_A(st.n_act, sizeof(int32_t));
+    QG_A(m->h, sizeof(float) * slots * m->hmax);
+    QG_A(m->d, sizeof(float) * slots * m->H);
+    QG_A(m->x_dev, sizeof(float) * (size_t)cap * m->H);
+    QG_A(m->out_dev, sizeof(float) * (size_t)cap * m->H);
+    QG_A(m->err_dev, sizeof(int));
+#undef QG_A
+    QG_CUDA(cudaMemsetAsync(st.counts, 0, sizeof(int32_t) * m->E, m->stream));
+    QG_CUDA(cudaMemsetAsync(st.done_ctr, 0, sizeof(int32_t), m->stream));
+    QG_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream));
+    QG_CUDA(cudaStreamSynchronize(m->stream));
+    m->cap_T = cap;
+    return QGMOE_OK;
+}
+
+static int read_flag(qgmoe *m, cudaStream_t s) {
+    int flag = 0;
+    QG_CUDA(cudaMemcpyAsync(&flag, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
+    QG_CUDA(cudaStreamSynchronize(s));
+    if (flag) {
+        cudaMemsetAsync(m->err_dev, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
+        return set_error(QGMOE_ERR_DEVICE_FLAG, "device bounds flag 0x%x (1=expert id, 2=slot, 4=group)",
+                         flag);
+    }
+    return QGMOE_OK;
+}
+
+static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    m->begin_timed();
+    m->mark(0, nullptr, s);
+    int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
+                          m->has_shared, m->st, m->err_dev, s);
+    if (rc) return rc;
+    m->mark(1, "route", s);
+    ExpertArgs a{};
+    a.n_experts = m->E;
+    a.has_shared = m->has_shared;
+    a.act_group = m->st.act_group;
+    a.act_begin = m->st.act_begin;
+    a.act_n = m->st.act_n;
+    a.n_act = m->st.n_act;
+    a.slot_token = m->st.slot_token;
+    a.err = m->err_dev;
+    int groups = (T * m->k < m->E ? T * m->k : m->E) + m->has_shared;
+    // gate_up + SwiGLU: x -> h
+    a.routed = m->gu;
+    a.shared = m->sgu;
+    a.in = x;
+    a.in_stride = m->H;
+    a.out = m->h;
+    a.out_stride = m->hmax;
+    if ((rc = launch_expert(true, a, groups, s))) return rc;
+    m->mark(2, "gate_up", s);
+    // down: h -> d
+    a.routed = m->dn;
+    a.shared = m->sdn;
+    a.in = m->h;
+    a.in_stride = m->hmax;
+    a.out = m->d;
+    a.out_stride = m->H;
+    if ((rc = launch_expert(false, a, groups, s))) return rc;
+    m->mark(3, "down", s);
+    if ((rc = launch_combine(m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, m->st.shared_w,
+                             m->has_shared, out, s)))
+        return rc;
+    m->mark(4, "combine", s);
+    m->last_launches = 4;
+    return QGMOE_OK;
+}
+
+extern "C" {
+
+int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
+    if (!d || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null desc/out");
+    *out = nullptr;
+    const int H = d->n_embed, E = d->n_experts, k = d->top_k, I = d->n_moe_mlp,
+              Is = d->n_shared_mlp, bits = d->bits;
+    if (H <= 0 || H % QG_GROUP || E <= 0 || E > QG_MAX_EXPERTS || k <= 0 || k > QG_MAX_TOPK ||
+        k > E || I <= 0 || I % QG_GROUP || Is < 0 || Is % QG_GROUP)
+        return set_error(QGMOE_ERR_INVALID_ARG,
+                         "bad shape H=%d E=%d k=%d I=%d Is=%d (H, I, Is multiples of 32; "
+                         "1<=k<=min(E,32); E<=1024)",
+                         H, E, k, I, Is);
+    if (bits != 32 && bits != 8 && bits != 4)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 8 or 4 (got %d)", bits);
+    if (d->router_mode != QGMOE_ROUTER_TOPK && d->router_mode != QGMOE_ROUTER_PREFIX)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad router_mode %d", d->router_mode);
+    if (d->scale_dtype != QGMOE_SCALE_F16 && d->scale_dtype != QGMOE_SCALE_F32)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad scale_dtype %d", d->scale_dtype);
+    if (!d->router || (Is > 0 && !d->shared_gate))
+        return set_error(QGMOE_ERR_INVALID_ARG, "router / shared_gate pointer missing");
+    int rc = check_device(d->device);
+    if (rc) return rc;
+
+    qgmoe *m = new qgmoe();
+    m->device = d->device;
+    m->H = H;
+    m->E = E;
+    m->k = k;
+    m->I = I;
+    m->Is = Is;
+    m->bits = bits;
+    m->mode = d->router_mode;
+    m->has_shared = Is > 0;
+    m->hmax = I > Is ? I : Is;
+    const bool dev = d->weights_on_device != 0;
+    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete m;
+        return set_error(QGMOE_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+    }
+    cudaStream_t s = m->stream;
+    do {
+        if ((rc = upload(m->weights, d->router, sizeof(float) * E * H, dev,
+                         reinterpret_cast<void **>(&m->router), s)))
+            break;
+        if (m->has_shared &&
+            (rc = upload(m->weights, d->shared_gate, sizeof(float) * H, dev,
+                         reinterpret_cast<void **>(&m->shared_gate), s)))
+            break;
+        Part pgu{d->gate_up, d->gate_up_q, d->gate_up_scale, E * 2 * I};
+        if ((rc = build_set(m->weights, bits, H, 2 * I, E, &pgu, 1, d->scale_dtype, dev, &m->gu, s)))
+            break;
+        Part pdn{d->down, d->down_q, d->down_scale, E * H};
+        if ((rc = build_set(m->weights, bits, I, H, E, &pdn, 1, d->scale_dtype, dev, &m->dn, s)))
+            break;
+        if (m->has_shared) {
+            Part psg[2] = {{d->shared_gate_proj, d->shared_gate_q, d->shared_gate_scale, Is},
+                           {d->shared_up_proj, d->shared_up_q, d->shared_up_scale, Is}};
+            if ((rc = build_set(m->weights, bits, H, 2 * Is, 1, psg, 2, d->scale_dtype, dev,
+                                &m->sgu, s)))
+                break;
+            Part psd{d->shared_down_proj, d->shared_down_q, d->shared_down_scale, H};
+            if ((rc = build_set(m->weights, bits, Is, H, 1, &psd, 1, d->scale_dtype, dev, &m->sdn,
+                                s)))
+                break;
+        }
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) {
+            rc = set_error(QGMOE_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
+            break;
+        }
+        if ((rc = ensure_capacity(m, 1))) break;
+    } while (0);
+    if (rc) {
+        qgmoe_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return QGMOE_OK;
+}
+
+int qgmoe_destroy(qgmoe_t *m) {
+    if (!m) return QGMOE_OK;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    m->work.free_all();
+    m->weights.free_all();
+    for (auto &set : m->ev_sets)
+        for (auto e : set)
+            if (e) cudaEventDestroy(e);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return QGMOE_OK;
+}
+
+int qgmoe_forward_device(qgmoe_t *m, const float *x, int32_t T, float *out, int32_t *sel_idx,
+                         float *sel_w, void *stream) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (T < 0) return set_error(QGMOE_ERR_INVALID_ARG, "T < 0");
+    if (T == 0) return QGMOE_OK;
+    if (!x || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null x/out");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = ensure_capacity(m, T);
+    if (rc) return rc;
+    if ((rc = enqueue_forward(m, x, T, out, s))) return rc;
+    if (sel_idx)
+        QG_CUDA(cudaMemcpyAsync(sel_idx, m->st.topk_idx, sizeof(int32_t) * T * m->k,
+                                cudaMemcpyDeviceToDevice, s));
+    if (sel_w)
+        QG_CUDA(cudaMemcpyAsync(sel_w, m->st.topk_w, sizeof(float) * T * m->k,
+                                cudaMemcpyDeviceToDevice, s));
+    return QGMOE_OK;
+}
+
+int qgmoe_forward(qgmoe_t *m, const float *x, int32_t T, float *out, int32_t *sel_idx,
+                  float *sel_w) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (T < 0) return set_error(QGMOE_ERR_INVALID_ARG, "T < 0");
+    if (T == 0) return QGMOE_OK;
+    if (!x || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null x/out");
+    QG_CUDA(cudaSetDevice(m->device));
+    int rc = ensure_capacity(m, T);
+    if (rc) return rc;
+    cudaStream_t s = m->stream;
+    QG_CUDA(cudaMemcpyAsync(m->x_dev, x, sizeof(float) * T * m->H, cudaMemcpyHostToDevice, s));
+    if ((rc = enqueue_forward(m, m->x_dev, T, m->out_dev, s))) return rc;
+    QG_CUDA(cudaMemcpyAsync(out, m->out_dev, sizeof(float) * T * m->H, cudaMemcpyDeviceToHost, s));
+    if (sel_idx)
+        QG_CUDA(cudaMemcpyAsync(sel_idx, m->st.topk_idx, sizeof(int32_t) * T * m->k,
+                                cudaMemcpyDeviceToHost, s));
+    if (sel_w)
+        QG_CUDA(cudaMemcpyAsync(sel_w, m->st.topk_w, sizeof(float) * T * m->k,
+                                cudaMemcpyDeviceToHost, s));
+    return read_flag(m, s);
+}
+
+int qgmoe_sync(qgmoe_t *m, void *stream) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    QG_CUDA(cudaStreamSynchronize(s));
+    return read_flag(m, s);
+}
+
+int qgmoe_last_launch_count(const qgmoe_t *m) { return m ? m->last_launches : 0; }
+
+int qgmoe_set_timing(qgmoe_t *m, int32_t enable) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    QG_CUDA(cudaSetDevice(m->device));
+    m->timing = enable != 0;
+    m->ev_used = 0;
+    m->n_stages = 0;
+    return QGMOE_OK;
+}
+
+int qgmoe_read_timing(qgmoe_t *m, float *ms, int32_t n, int32_t *n_forwards) {
+    if (!m || (n > 0 && !ms)) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/out");
+    if (n_forwards) *n_forwards = m->ev_used;
+    for (int i = 0; i < n; i++) ms[i] = 0.f;
+    if (!m->timing || m->ev_used == 0) return 0;
+    QG_CUDA(cudaSetDevice(m->device));
+    for (int j = 0; j < m->ev_used; j++) {
+        auto &set = m->ev_sets[j];
+        QG_CUDA(cudaEventSynchronize(set[m->n_stages]));
+        for (int i = 0; i < m->n_stages && i < n; i++) {
+            float t = 0.f;
+            QG_CUDA(cudaEventElapsedTime(&t, set[i], set[i + 1]));
+            ms[i] += t;
+        }
+    }
+    m->ev_used = 0;
+    return m->n_stages;
+}
+
+const char *qgmoe_stage_name(const qgmoe_t *m, int32_t i) {
+    if (!m || i < 0 || i >= m->n_stages || !m->stage_names[i]) return "";
+    return m->stage_names[i];
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// QuantLinear
+// ---------------------------------------------------------------------------
+struct qgql {
+    int device = 0;
+    int bits = 0, O = 0, I = 0;
+    cudaStream_t stream = nullptr;
+    Allocs weights;
+    WeightSet ws{};
+    int *err_dev = nullptr;
+    float *x_dev = nullptr, *y_dev = nullptr;
+    int cap_T = 0;
+    Allocs work;
+};
+
+extern "C" {
+
+int qgql_create(int32_t bits, int32_t O, int32_t I, const void *q, const void *scale,
+                int32_t scale_dtype, int32_t on_device, int32_t device, qgql_t **out) {
+    if (!out) return set_error(QGMOE_ERR_INVALID_ARG, "null out");
+    *out = nullptr;
+    if (bits != 32 && bits != 8 && bits != 4)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 8 or 4 (got %d)", bits);
+    if (O <= 0 || I <= 0 || I % QG_GROUP)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad shape out=%d in=%d (in %% 32 == 0)", O, I);
+    if (!q || (bits != 32 && !scale)) return set_error(QGMOE_ERR_INVALID_ARG, "null weights");
+    if (scale_dtype != QGMOE_SCALE_F16 && scale_dtype != QGMOE_SCALE_F32)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad scale_dtype %d", scale_dtype);
+    int rc = check_device(device);
+    if (rc) return rc;
+    qgql *h = new qgql();
+    h->device = device;
+    h->bits = bits;
+    h->O = O;
+    h->I = I;
+    cudaError_t e = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete h;
+        return set_error(QGMOE_ERR_CUDA, "stream: %s", cudaGetErrorString(e));
+    }
+    Part p{bits == 32 ? static_cast<const float *>(q) : nullptr,
+           bits == 32 ? nullptr : static_cast<const uint8_t *>(q), scale, O};
+    rc = build_set(h->weights, bits, I, O, 1, &p, 1, scale_dtype, on_device != 0, &h->ws, h->stream);
+    if (!rc) rc = h->weights.alloc(reinterpret_cast<void **>(&h->err_dev), sizeof(int));
+    if (!rc && cudaMemsetAsync(h->err_dev, 0, sizeof(int), h->stream) != cudaSuccess)
+        rc = set_error(QGMOE_ERR_CUDA, "memset");
+    if (!rc && cudaStreamSynchronize(h->stream) != cudaSuccess)
+        rc = set_error(QGMOE_ERR_CUDA, "weight upload failed");
+    if (rc) {
+        qgql_destroy(h);
+        return rc;
+    }
+    *out = h;
+    return QGMOE_OK;
+}
+
+int qgql_destroy(qgql_t *h) {
+    if (!h) return QGMOE_OK;
+    cudaSetDevice(h->device);
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    h->work.free_all();
+    h->weights.free_all();
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+    return QGMOE_OK;
+}
+
+int qgql_forward_device(qgql_t *h, const float *x, int32_t T, float *y, void *stream) {
+    if (!h) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (T < 0) return set_error(QGMOE_ERR_INVALID_ARG, "T < 0");
+    if (T == 0) return QGMOE_OK;
+    if (!x || !y) return set_error(QGMOE_ERR_INVALID_ARG, "null x/y");
+    QG_CUDA(cudaSetDevice(h->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    ExpertArgs a{};
+    a.routed = h->ws;
+    a.shared = h->ws;
+    a.n_experts = 0;
+    a.has_shared = 1;
+    a.single_n = T;
+    a.in = x;
+    a.in_stride = h->I;
+    a.out = y;
+    a.out_stride = h->O;
+    a.err = h->err_dev;
+    return launch_expert(false, a, 1, s);
+}
+
+int qgql_forward(qgql_t *h, const float *x, int32_t T, float *y) {
+    if (!h) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (T < 0) return set_error(QGMOE_ERR_INVALID_ARG, "T < 0");
+    if (T == 0) return QGMOE_OK;
+    if (!x || !y) return set_error(QGMOE_ERR_INVALID_ARG, "null x/y");
+    QG_CUDA(cudaSetDevice(h->device));
+    if (T > h->cap_T) {
+        cudaStreamSynchronize(h->stream);
+        h->work.free_all();
+        int rc = h->work.alloc(reinterpret_cast<void **>(&h->x_dev), sizeof(float) * T * h->I);
+        if (!rc) rc = h->work.alloc(reinterpret_cast<void **>(&h->y_dev), sizeof(float) * T * h->O);
+        if (rc) {
+            h->cap_T = 0;
+            return rc;
+        }
+        h->cap_T = T;
+    }
+    cudaStream_t s = h->stream;
+    QG_CUDA(cudaMemcpyAsync(h->x_dev, x, sizeof(float) * T * h->I, cudaMemcpyHostToDevice, s));
+    int rc = qgql_forward_device(h, h->x_dev, T, h->y_dev, s);
+    if (rc) return rc;
+    QG_CUDA(cudaMemcpyAsync(y, h->y_dev, sizeof(float) * T * h->O, cudaMemcpyDeviceToHost, s));
+    QG_CUDA(cudaStreamSynchronize(s));
+    return QGMOE_OK;
+}
+
+int qgql_dequantize_device(qgql_t *h, float *w, void *stream) {
+    if (!h || !w) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/out");
+    QG_CUDA(cudaSetDevice(h->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    return launch_dequantize(h->bits, h->O, h->I, h->ws.q, h->ws.s, h->ws.w32, w, s);
+}
+
+int qgql_quantize_device(int32_t bits, int32_t O, int32_t I, const float *w, uint8_t *q,
+                         float *s32, uint16_t *s16, void *stream) {
+    if (bits != 8 && bits != 4) return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 8 or 4");
+    if (O <= 0 || I <= 0 || I % QG_GROUP || !w || !q)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad quantize arguments");
+    return launch_quantize(bits, O, I, w, q, s32, reinterpret_cast<__half *>(s16),
+                           static_cast<cudaStream_t>(stream));
+}
+
+int qg_randn_device(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
+                    float *dev, void *cuda_stream) {
+    if (n < 0 || (n > 0 && !dev)) return set_error(QGMOE_ERR_INVALID_ARG, "bad randn arguments");
+    return launch_randn(seed, stream, offset, n, stdv, dev, static_cast<cudaStream_t>(cuda_stream));
+}
+
+const char *qgmoe_strerror(int status) {
+    switch (status) {
+        case QGMOE_OK: return "ok";
+        case QGMOE_ERR_INVALID_ARG: return "invalid argument";
+        case QGMOE_ERR_CUDA: return "CUDA error";
+        case QGMOE_ERR_NCCL: return "NCCL error";
+        case QGMOE_ERR_TIMEOUT: return "device wait timed out";
+        case QGMOE_ERR_DEVICE_FLAG: return "device bounds check fired";
+        case QGMOE_ERR_UNSUPPORTED: return "unsupported";
+        case QGMOE_ERR_NO_DEVICE: return "no usable sm_100 device";
+    }
+    return "unknown status";
+}
+
+const char *qgmoe_last_error(void) { return g_err; }
+
+int qgmoe_device_ok(int32_t device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return 0;
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    return major == 10;
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Shared definitions for the qgmoe CUDA library (sm_100a only).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/qgmoe.h"
+
+#define QG_GROUP 32        // quantGroup, model/moe.go:124
+#define QG_MAX_TOPK 32     // router keeps the k winners in one warp
+#define QG_MAX_EXPERTS 1024
+#define QG_ROUTE_THREADS 256
+
+namespace qg {
+
+// Records a failure detail for qgmoe_last_error() and returns `code`.
+int set_error(int code, const char *fmt, ...);
+
+#define QG_CUDA(call)                                                                 \
+    do {                                                                              \
+        cudaError_t e_ = (call);                                                      \
+        if (e_ != cudaSuccess)                                                        \
+            return ::qg::set_error(QGMOE_ERR_CUDA, "%s:%d %s: %s", __FILE__, __LINE__, \
+                                   #call, cudaGetErrorString(e_));                    \
+    } while (0)
+
+// Device-side error word bits (an int in device memory, read back by the host).
+enum : int {
+    QG_FLAG_BAD_EXPERT = 1,   // router produced an expert id out of [0, E)
+    QG_FLAG_BAD_SLOT = 2,     // dispatch slot out of range
+    QG_FLAG_BAD_GROUP = 4,    // expert kernel saw an active group out of range
+};
+
+// One stacked weight family (e.g. all experts' gate_up) in device memory.
+// bits 32: w32 [G*rows, K]; bits 8: q [G*rows, K] int8; bits 4: q [G*rows, K/2].
+// Scales: [G*rows, K/32] fp16.
+struct WeightSet {
+    int bits;
+    int rows;  // output rows per group (expert)
+    int K;     // input features
+    const float *w32;
+    const uint8_t *q;
+    const __half *s;
+};
+
+// Per-call routing state produced by the router/dispatch kernel.
+struct RouteState {
+    int32_t *topk_idx;   // [T*k]
+    float *topk_w;       // [T*k]
+    float *shared_w;     // [T]   sigmoid(sharedGate . x)
+    int32_t *counts;     // [E]   zero between calls
+    int32_t *done_ctr;   // [1]   zero between calls
+    int32_t *pair_slot;  // [T*k] slot of pair (t, r)
+    int32_t *slot_token; // [T*k + T] token of each slot (shared slots appended)
+    int32_t *act_group;  // [E+1] active groups, ascending expert id, shared last
+    int32_t *act_begin;  // [E+1] first slot of the group
+    int32_t *act_n;      // [E+1] tokens in the group
+    int32_t *n_act;      // [1]
+};
+
+// Arguments of the grouped expert kernels.
+struct ExpertArgs {
+    WeightSet routed;     // gate_up (GATEUP) or down (DOWN) of the routed experts
+    WeightSet shared;     // same for the shared expert (group id == n_experts)
+    int n_experts;
+    int has_shared;
+    // Active-group list from the dispatch kernel.  When n_act is null the
+    // kernel runs one group: the `shared` weight set over single_n rows
+    // starting at slot 0 (the plain QuantLinear forward).
+    const int32_t *act_group, *act_begin, *act_n, *n_act;
+    int single_n;
+    const int32_t *slot_token;  // GATEUP: input row of a slot; DOWN: unused
+    const float *in;            // GATEUP: x [T, H]; DOWN: h [slots, in_stride]
+    int in_stride;
+    float *out;                 // GATEUP: h [slots, out_stride]; DOWN: d [slots, out_stride]
+    int out_stride;
+    int *err;
+};
+
+// Launch helpers implemented in the .cu files.
+int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
+                 const float *shared_gate, int has_shared, RouteState st, int *err,
+                 cudaStream_t s);
+int launch_expert(bool gateup, const ExpertArgs &a, int max_items, cudaStream_t s);
+int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
+                   const float *topk_w, const float *shared_w, int has_shared, float *out,
+                   cudaStream_t s);
+int launch_quantize(int bits, int O, int I, const float *w, uint8_t *q, float *s32,
+                    __half *s16, cudaStream_t s);
+int launch_dequantize(int bits, int O, int I, const uint8_t *q, const __half *scale,
+                      const float *w32, float *w, cudaStream_t s);
+int launch_f32_to_f16(const float *in, __half *out, int64_t n, cudaStream_t s);
+int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
+                 float *out, cudaStream_t s);
+int num_sms(int device);
+
+}  // namespace qg

@@ -1,0 +1,77 @@
+"""CPU tests of the C-ABI boundary: the library builds for sm_100a, loads,
+exports every function include/qgmoe.h declares, and rejects bad arguments
+before touching a device.  No compute runs here."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+import qgmoe
+from qgmoe.build import LIB, build
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(REPO, "include", "qgmoe.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(qg\w+)\s*\(", src)))
+
+
+def test_library_builds_and_loads():
+    path = build()
+    assert path == LIB and os.path.exists(LIB)
+    assert qgmoe.lib() is not None
+
+
+def test_exports_every_declared_symbol():
+    names = header_functions()
+    assert len(names) >= 16
+    L = C.CDLL(LIB)
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(qgmoe.SIGNATURES), set(names) ^ set(qgmoe.SIGNATURES)
+
+
+def test_status_strings():
+    assert qgmoe.status_text(0) == "ok"
+    assert "invalid" in qgmoe.status_text(-1)
+    assert qgmoe.status_text(12345) == "unknown status"
+
+
+def test_create_rejects_bad_shapes_without_device():
+    d = qgmoe._Desc()
+    h = C.c_void_p()
+    d.n_embed, d.n_experts, d.top_k, d.n_moe_mlp, d.bits = 30, 4, 2, 32, 32  # H % 32 != 0
+    assert qgmoe.lib().qgmoe_create(C.byref(d), C.byref(h)) == -1
+    assert "bad shape" in qgmoe.last_error()
+    d.n_embed, d.top_k = 64, 5  # k > E
+    assert qgmoe.lib().qgmoe_create(C.byref(d), C.byref(h)) == -1
+    d.top_k, d.bits = 2, 6
+    assert qgmoe.lib().qgmoe_create(C.byref(d), C.byref(h)) == -1
+    assert "bits" in qgmoe.last_error()
+    assert qgmoe.lib().qgmoe_create(None, C.byref(h)) == -1
+
+
+def test_quantlinear_rejects_bad_arguments_without_device():
+    h = C.c_void_p()
+    assert qgmoe.lib().qgql_create(5, 4, 64, None, None, 0, 0, 0, C.byref(h)) == -1
+    assert qgmoe.lib().qgql_create(8, 4, 48, None, None, 0, 0, 0, C.byref(h)) == -1
+    assert qgmoe.lib().qgql_quantize_device(3, 4, 64, None, None, None, None, None) == -1
+
+
+def test_null_handles_are_errors_not_crashes():
+    L = qgmoe.lib()
+    assert L.qgmoe_forward(None, None, 1, None, None, None) == -1
+    assert L.qgmoe_destroy(None) == 0
+    assert L.qgql_forward(None, None, 1, None) == -1
+    assert L.qgmoe_last_launch_count(None) == 0
+
+
+@pytest.mark.skipif(os.environ.get("CUDA_VISIBLE_DEVICES", None) == "", reason="n/a")
+def test_device_ok_is_false_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    assert qgmoe.lib().qgmoe_device_ok(0) == 0

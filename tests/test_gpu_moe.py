@@ -1,0 +1,143 @@
+"""GPU parity of the MoE layer (moeMLP.forward, model/moe.go:41-99) against
+the oracle on identical seeded weights and inputs.
+
+Bar: selected experts and their order match the oracle except for near-ties
+(probabilities within 1e-5 relative, listed by check_routing); outputs within
+|gpu - ref| <= tol + tol*|ref|, tol = 1e-3 (2e-3 for int4)."""
+import numpy as np
+import pytest
+
+import qg_oracle as O
+import qgmoe
+from moe_cases import (CONFIGS, check_outputs, check_routing, device_case, host_case,
+                       make_gpu_moe)
+
+pytestmark = pytest.mark.gpu
+
+
+def run_both(m, x, mode, gpu=None):
+    gpu = gpu or make_gpu_moe(m, mode)
+    out_g, idx_g, w_g = gpu.forward_batch(x, return_routing=True)
+    out_o, idx_o, w_o, _sg, probs = O.moe_forward(m, x, mode, want_probs=True)
+    flipped = check_routing(idx_g, w_g, idx_o, w_o, probs)
+    check_outputs(out_g, out_o, m.bits, skip_tokens=flipped)
+    return out_g, flipped
+
+
+@pytest.mark.parametrize("bits", [32, 8, 4])
+@pytest.mark.parametrize("mode", [O.ROUTER_TOPK, O.ROUTER_PREFIX])
+@pytest.mark.parametrize("Is", [0, 96])
+@pytest.mark.parametrize("T", [1, 3, 17])
+def test_small_layers(bits, mode, Is, T):
+    m = host_case(H=256, E=8, k=3, I=64, Is=Is, bits=bits, seed=31 + T)
+    x = O.randn(31, 100 + T, (T, 256))
+    run_both(m, x, mode)
+
+
+@pytest.mark.parametrize("T", [64])
+def test_config0_fp32(T):
+    c = CONFIGS["c0"]
+    m, dev = device_case(**c)
+    x = O.randn(c["seed"], 100, (T, c["H"]))
+    run_both(m, x, O.ROUTER_TOPK, make_gpu_moe(m, O.ROUTER_TOPK, dev))
+
+
+@pytest.mark.parametrize("mode", [O.ROUTER_TOPK, O.ROUTER_PREFIX])
+def test_config1_int8_decode(mode):
+    c = CONFIGS["c1"]
+    m, dev = device_case(**c)
+    gpu = make_gpu_moe(m, mode, dev)
+    for T in (1, 8, 32):
+        x = O.randn(c["seed"], 100 + T, (T, c["H"]))
+        run_both(m, x, mode, gpu)
+
+
+def test_config2_int4_decode():
+    c = CONFIGS["c2"]
+    m, dev = device_case(**c)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK, dev)
+    for T in (1, 16, 64):
+        x = O.randn(c["seed"], 100 + T, (T, c["H"]))
+        run_both(m, x, O.ROUTER_TOPK, gpu)
+
+
+# ---- properties and edge cases ------------------------------------------
+
+
+def test_batch_invariance_and_permutation():
+    m = host_case(H=128, E=8, k=2, I=64, Is=64, bits=8, seed=40)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(40, 1, (9, 128))
+    full = gpu.forward_batch(x)
+    for t in range(9):
+        assert np.array_equal(gpu.forward(x[t]), full[t])
+    perm = np.random.default_rng(0).permutation(9)
+    assert np.array_equal(gpu.forward_batch(x[perm]), full[perm])
+
+
+def test_ties_pick_lowest_index():
+    m = host_case(H=64, E=8, k=3, I=32, Is=0, bits=32, seed=41)
+    m.router[:] = 0  # all logits equal
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(41, 1, (4, 64))
+    out, idx, w = gpu.forward_batch(x, return_routing=True)
+    assert np.all(idx == [0, 1, 2])
+    ref, *_ = O.moe_forward(m, x)
+    check_outputs(out, ref, 32)
+
+
+@pytest.mark.parametrize("E,k", [(1, 1), (8, 8), (8, 1), (64, 32)])
+def test_extreme_topk(E, k):
+    m = host_case(H=64, E=E, k=k, I=32, Is=32, bits=8, seed=42 + E + k)
+    x = O.randn(42, 1, (5, 64))
+    run_both(m, x, O.ROUTER_TOPK)
+
+
+def test_one_expert_takes_every_token():
+    m = host_case(H=64, E=8, k=1, I=32, Is=0, bits=4, seed=43)
+    m.router[:] = 0
+    m.router[5] = 1.0  # x ~ N(0,1) -> expert 5 wins unless sum(x) < 0 ... force it
+    x = np.abs(O.randn(43, 1, (40, 64))) + 0.1
+    _, flipped = run_both(m, x, O.ROUTER_TOPK)
+    assert not flipped
+
+
+def test_large_activations_stay_finite():
+    m = host_case(H=128, E=8, k=2, I=64, Is=64, bits=8, seed=44)
+    x = O.randn(44, 1, (3, 128), std=30.0)
+    out, _ = run_both(m, x, O.ROUTER_TOPK)
+    assert np.all(np.isfinite(out))
+
+
+def test_T0_is_noop_and_bad_args():
+    m = host_case(H=64, E=4, k=2, I=32, Is=0, bits=32, seed=45)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    assert qgmoe.lib().qgmoe_forward(gpu.h, None, 0, None, None, None) == 0
+    assert qgmoe.lib().qgmoe_forward(gpu.h, None, 2, None, None, None) == -1
+    assert qgmoe.lib().qgmoe_forward(gpu.h, None, -1, None, None, None) == -1
+
+
+def test_device_entry_point_matches_host_entry_point():
+    import torch
+    m = host_case(H=128, E=8, k=2, I=64, Is=64, bits=8, seed=46)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(46, 1, (6, 128))
+    ref = gpu.forward_batch(x)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty_like(xd)
+    idx = torch.empty((6, 2), dtype=torch.int32, device="cuda")
+    s = torch.cuda.Stream()
+    gpu.forward_device(xd, out, sel_idx=idx, stream=s)
+    gpu.sync(s)
+    assert np.array_equal(out.cpu().numpy(), ref)
+    assert gpu.last_launch_count() >= 4
+
+
+def test_workspace_growth_keeps_results():
+    m = host_case(H=64, E=8, k=2, I=32, Is=32, bits=4, seed=47)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(47, 1, (100, 64))
+    small = gpu.forward_batch(x[:3])
+    big = gpu.forward_batch(x)
+    assert np.array_equal(big[:3], small)
+    assert np.array_equal(gpu.forward_batch(x[:3]), small)
