@@ -121,6 +121,16 @@ int qgmoe_sync(qgmoe_t *h, void *stream);
 /* Number of kernel launches the last forward enqueued (instrumentation). */
 int qgmoe_last_launch_count(const qgmoe_t *h);
 
+/* Expert-product path.  AUTO picks the tcgen05 tensor-core grouped GEMM for
+ * large token batches (T*k >= 2048) when the layer allows it (int8/int4
+ * experts, no shared expert, H and I multiples of 128) and the CUDA-core
+ * streaming GEMV otherwise.  CUDA_CORE / TENSOR force one path (TENSOR
+ * returns QGMOE_ERR_UNSUPPORTED when the layer does not allow it). */
+#define QGMOE_PATH_AUTO 0
+#define QGMOE_PATH_CUDA_CORE 1
+#define QGMOE_PATH_TENSOR 2
+int qgmoe_set_path(qgmoe_t *h, int32_t mode);
+
 /* Per-stage device timing (instrumentation for benchmarks): when enabled,
  * every forward records CUDA events on its stream between consecutive
  * stages, without host syncs.  read_timing waits for those forwards, writes

@@ -4,6 +4,8 @@
 // gate_up/down + optional gated shared expert, in f32 or quantLinear format.
 // It owns every device buffer.  Forward is route/dispatch -> grouped
 // gate_up+SwiGLU -> grouped down -> combine, four launches on one stream.
+#include <cuda.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -165,6 +167,14 @@ struct qgmoe {
     int *err_dev = nullptr;
     int hmax = 0;
     int last_launches = 0;
+    // tensor-core path (qg_umma.cu): UMMA-tiled weight copies, fp16
+    // activation buffers and their TMA descriptors
+    bool tensor_ok = false;
+    int path_mode = QGMOE_PATH_AUTO;
+    uint8_t *gu_pq = nullptr, *dn_pq = nullptr;
+    __half2 *gu_ps = nullptr, *dn_ps = nullptr;
+    __half *xp16 = nullptr, *h16 = nullptr;
+    CUtensorMap tmap_x{}, tmap_h{};
     // stage timing (qgmoe_set_timing): one event set per timed forward since
     // the last read, so a whole timed loop runs without host syncs.
     static constexpr int kMaxStages = 8;
@@ -216,6 +226,11 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(st.act_begin, sizeof(int32_t) * (m->E + 1));
     QG_A(st.act_n, sizeof(int32_t) * (m->E + 1));
     QG_A(st.n_act, sizeof(int32_t));
+    QG_A(st.tile_prefix, sizeof(int32_t) * (m->E + 2));
+    if (m->tensor_ok) {
+        QG_A(m->xp16, sizeof(__half) * pairs * m->H);
+        QG_A(m->h16, sizeof(__half) * pairs * m->I);
+    }
     QG_A(m->h, sizeof(float) * slots * m->hmax);
     QG_A(m->d, sizeof(float) * slots * m->H);
     QG_A(m->x_dev, sizeof(float) * (size_t)cap * m->H);
@@ -226,7 +241,93 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_CUDA(cudaMemsetAsync(st.done_ctr, 0, sizeof(int32_t), m->stream));
     QG_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream));
     QG_CUDA(cudaStreamSynchronize(m->stream));
+    if (m->tensor_ok) {
+        if ((rc = encode_act_map(&m->tmap_x, m->xp16, (int)pairs, m->H))) return rc;
+        if ((rc = encode_act_map(&m->tmap_h, m->h16, (int)pairs, m->I))) return rc;
+    }
     m->cap_T = cap;
+    return QGMOE_OK;
+}
+
+// Tensor-core path: int8/int4 weights, no shared expert, H and I multiples
+// of 128 (128-row weight tiles, 64-wide K blocks).
+static int build_tensor_weights(qgmoe *m) {
+    const int E = m->E, H = m->H, I = m->I, bits = m->bits;
+    if (!((bits == 8 || bits == 4) && !m->has_shared && H % 128 == 0 && I % 128 == 0))
+        return QGMOE_OK;
+    Allocs &al = m->weights;
+    int rc;
+    const size_t gu_bytes = (size_t)E * 2 * I * H * bits / 8;
+    const size_t dn_bytes = (size_t)E * H * I * bits / 8;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&m->gu_pq), gu_bytes))) return rc;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&m->dn_pq), dn_bytes))) return rc;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&m->gu_ps),
+                       sizeof(__half2) * (size_t)E * 2 * I * (H / 64))))
+        return rc;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&m->dn_ps),
+                       sizeof(__half2) * (size_t)E * H * (I / 64))))
+        return rc;
+    if ((rc = launch_repack(m->gu.q, m->gu.s, bits, E, 2 * I, H, I / 128, 2, I, m->gu_pq,
+                            m->gu_ps, m->stream)))
+        return rc;
+    if ((rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 1, 0, m->dn_pq, m->dn_ps,
+                            m->stream)))
+        return rc;
+    QG_CUDA(cudaStreamSynchronize(m->stream));
+    m->tensor_ok = true;
+    return QGMOE_OK;
+}
+
+static bool use_tensor(const qgmoe *m, int T) {
+    if (!m->tensor_ok || m->path_mode == QGMOE_PATH_CUDA_CORE) return false;
+    if (m->path_mode == QGMOE_PATH_TENSOR) return true;
+    return T * m->k >= 2048;
+}
+
+static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    m->begin_timed();
+    m->mark(0, nullptr, s);
+    int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
+                          m->has_shared, m->st, m->err_dev, s);
+    if (rc) return rc;
+    m->mark(1, "route", s);
+    const int pairs = T * m->k;
+    if ((rc = launch_gather_f16(x, m->st.slot_token, pairs, m->H, m->xp16, s))) return rc;
+    m->mark(2, "gather", s);
+    const int tiles = (pairs + 127) / 128 + (pairs < m->E ? pairs : m->E);
+    UmmaLaunch l{};
+    l.act_group = m->st.act_group;
+    l.act_begin = m->st.act_begin;
+    l.act_n = m->st.act_n;
+    l.n_act = m->st.n_act;
+    l.tile_prefix = m->st.tile_prefix;
+    l.err = m->err_dev;
+    // gate_up + SwiGLU -> h16
+    l.wq = m->gu_pq;
+    l.ws = m->gu_ps;
+    l.RT = m->I / 128;
+    l.KB = m->H / 64;
+    l.h_out = m->h16;
+    l.h_stride = m->I;
+    l.grid = tiles * l.RT;
+    if ((rc = launch_umma(m->bits, 2, &m->tmap_x, l, s))) return rc;
+    m->mark(3, "gate_up", s);
+    // down -> d
+    l.wq = m->dn_pq;
+    l.ws = m->dn_ps;
+    l.RT = m->H / 128;
+    l.KB = m->I / 64;
+    l.h_out = nullptr;
+    l.d_out = m->d;
+    l.d_stride = m->H;
+    l.grid = tiles * l.RT;
+    if ((rc = launch_umma(m->bits, 1, &m->tmap_h, l, s))) return rc;
+    m->mark(4, "down", s);
+    if ((rc = launch_combine(m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, m->st.shared_w,
+                             m->has_shared, out, s)))
+        return rc;
+    m->mark(5, "combine", s);
+    m->last_launches = 5;
     return QGMOE_OK;
 }
 
@@ -244,6 +345,7 @@ static int read_flag(qgmoe *m, cudaStream_t s) {
 }
 
 static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    if (use_tensor(m, T)) return enqueue_forward_tensor(m, x, T, out, s);
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
@@ -358,6 +460,7 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             rc = set_error(QGMOE_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
             break;
         }
+        if ((rc = build_tensor_weights(m))) break;
         if ((rc = ensure_capacity(m, 1))) break;
     } while (0);
     if (rc) {
@@ -433,6 +536,18 @@ int qgmoe_sync(qgmoe_t *m, void *stream) {
 }
 
 int qgmoe_last_launch_count(const qgmoe_t *m) { return m ? m->last_launches : 0; }
+
+int qgmoe_set_path(qgmoe_t *m, int32_t mode) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (mode != QGMOE_PATH_AUTO && mode != QGMOE_PATH_CUDA_CORE && mode != QGMOE_PATH_TENSOR)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad path mode %d", mode);
+    if (mode == QGMOE_PATH_TENSOR && !m->tensor_ok)
+        return set_error(QGMOE_ERR_UNSUPPORTED,
+                         "tensor-core path needs int8/int4 experts, no shared expert, "
+                         "H and I multiples of 128");
+    m->path_mode = mode;
+    return QGMOE_OK;
+}
 
 int qgmoe_set_timing(qgmoe_t *m, int32_t enable) {
     if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");

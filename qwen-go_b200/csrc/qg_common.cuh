@@ -29,6 +29,7 @@ enum : int {
     QG_FLAG_BAD_EXPERT = 1,   // router produced an expert id out of [0, E)
     QG_FLAG_BAD_SLOT = 2,     // dispatch slot out of range
     QG_FLAG_BAD_GROUP = 4,    // expert kernel saw an active group out of range
+    QG_FLAG_TIMEOUT = 8,      // a bounded mbarrier wait in the tensor-core kernel ran out
 };
 
 // One stacked weight family (e.g. all experts' gate_up) in device memory.
@@ -56,6 +57,21 @@ struct RouteState {
     int32_t *act_begin;  // [E+1] first slot of the group
     int32_t *act_n;      // [E+1] tokens in the group
     int32_t *n_act;      // [1]
+    int32_t *tile_prefix;  // [E+2] 128-token tiles before each routed group, total last
+};
+
+// One launch of the tensor-core grouped GEMM (qg_umma.cu).
+struct UmmaLaunch {
+    const uint8_t *wq;          // packed codes
+    const __half2 *ws;          // packed scales
+    int RT, KB;                 // row tiles per expert, 64-wide K blocks
+    const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
+    __half *h_out;              // GEMM1: h [slots, h_stride] fp16
+    int h_stride;
+    float *d_out;               // GEMM2: d [slots, d_stride] f32
+    int d_stride;
+    int *err;
+    int grid;                   // upper bound of work units
 };
 
 // Arguments of the grouped expert kernels.
@@ -93,5 +109,11 @@ int launch_f32_to_f16(const float *in, __half *out, int64_t n, cudaStream_t s);
 int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
                  float *out, cudaStream_t s);
 int num_sms(int device);
+int encode_act_map(void *map_out, const __half *ptr, int rows, int cols);
+int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
+                  int RT, int P, int up_offset, uint8_t *qo, __half2 *so, cudaStream_t s);
+int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
+                      cudaStream_t s);
+int launch_umma(int bits, int P, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
 
 }  // namespace qg

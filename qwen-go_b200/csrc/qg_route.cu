@@ -195,6 +195,14 @@ k_route(const float *__restrict__ x, int T, int H, int E, int k, int mode,
             }
         int total_act = __shfl_sync(0xffffffffu, nzi, 31);
         if (lane == 0) {
+            // 128-token tiles per routed group, for the tensor-core kernels
+            int tiles = 0, ai = 0;
+            for (int e = 0; e < E; e++)
+                if (cnt[e] > 0) {
+                    st.tile_prefix[ai++] = tiles;
+                    tiles += (cnt[e] + 127) / 128;
+                }
+            st.tile_prefix[ai] = tiles;
             if (has_shared) {
                 st.act_group[total_act] = E;
                 st.act_begin[total_act] = T * k;

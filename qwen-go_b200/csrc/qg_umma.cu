@@ -1,0 +1,497 @@
+// Grouped expert GEMMs on the 5th-generation tensor cores (kernels K3'/K4',
+// prefill-sized token counts).
+//
+// Swap-AB formulation per (expert e, 128-row weight tile, <=128-token tile):
+//   D[rows, tokens] = W[rows, K] * X[tokens, K]^T      (tcgen05.mma kind::f16)
+// A = expert weights, dequantised from int8/int4 group-32 codes with fp16
+//     scales (model/moe.go:134-157) by four converter warps straight into the
+//     128B-swizzled UMMA layout in shared memory;
+// B = the expert's token rows in fp16, brought in by TMA (SWIZZLE_128B box);
+// D = fp32 accumulators in TMEM, read back by the converter warps after the
+//     K loop (tcgen05.ld) for the epilogue.
+//
+// GEMM1 (P = 2): the gate rows [r, r+128) and the matching up rows
+// [I + r, I + r + 128) (model/moe.go:70-71) accumulate side by side in TMEM,
+// so the epilogue computes h = silu(gate) * up (model/moe.go:72-76) without
+// a round trip, and writes h in fp16 for GEMM2.
+// GEMM2 (P = 1): D = W_down * h^T (model/moe.go:77-81), written as f32 d
+// rows for the rank-ordered combine.
+//
+// Pipeline (per CTA): STAGES shared-memory stages of (A tiles, B tile); the
+// TMA warp and the converter warps fill a stage and signal fullB/fullA; one
+// elected thread issues the UMMAs and tcgen05.commit frees the stage.  Every
+// mbarrier wait is bounded (clock64 budget); on timeout the CTA raises
+// QG_FLAG_TIMEOUT, drains its own TMA loads and UMMAs, frees TMEM and exits.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "qg_common.cuh"
+#include "qg_sm100.cuh"
+
+namespace qg {
+using namespace sm100;
+
+constexpr int UM_THREADS = 192;  // warps 0-3: dequant + epilogue, 4: TMA, 5: MMA
+constexpr int UM_M = 128;        // weight rows per tile
+constexpr int UM_N = 128;        // max tokens per tile
+constexpr int UM_BK = 64;        // K elements per stage (one 128-byte fp16 row)
+constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+template <int BITS>
+struct UmTile {
+    static constexpr int BYTES = UM_M * UM_BK * BITS / 8;  // codes of one (row tile, k block)
+};
+
+template <int P>
+struct UmCfg {
+    static constexpr int STAGES = P == 2 ? 4 : 6;
+    static constexpr int A_BYTES = UM_M * UM_BK * 2;
+    static constexpr int B_BYTES = UM_N * UM_BK * 2;
+    static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = P == 2 ? 256 : 128;
+    static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2) + 16;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+};
+
+// int8 x4 -> two fp16x2 (q * s), exact codes then one correctly rounded product.
+__device__ __forceinline__ void cvt_i8x4(uint32_t w, __half2 s2, uint32_t &o0, uint32_t &o1) {
+    const uint32_t u = w ^ 0x80808080u;
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+    uint32_t p0 = __byte_perm(u, 0x64646464u, 0x4140);
+    uint32_t p1 = __byte_perm(u, 0x64646464u, 0x4342);
+    __half2 h0 = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p0), bias), s2);
+    __half2 h1 = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p1), bias), s2);
+    o0 = *reinterpret_cast<uint32_t *>(&h0);
+    o1 = *reinterpret_cast<uint32_t *>(&h1);
+}
+
+// int4 word in the repacked nibble order (element 2j in bits [4j, 4j+4),
+// element 2j+1 in bits [16+4j, 20+4j)) -> four fp16x2 ((code - 8) * s).
+__device__ __forceinline__ void cvt_i4x8(uint32_t w, __half2 s2, uint32_t (&o)[4]) {
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+        __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), bias), s2);
+        o[j] = *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+struct UmmaArgs {
+    const uint8_t *wq;    // packed codes [E][RT][KB][P][tile]
+    const __half2 *ws;    // packed scales [E][RT][KB][P][128] (2 groups per row)
+    int RT, KB;
+    const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
+    __half *h_out;        // GEMM1 output [slots, h_stride]
+    int h_stride;
+    float *d_out;         // GEMM2 output [slots, d_stride]
+    int d_stride;
+    int *err;
+};
+
+template <int BITS, int P>
+__global__ void __launch_bounds__(UM_THREADS, 1)
+k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
+    using Cfg = UmCfg<P>;
+    constexpr int S = Cfg::STAGES;
+    constexpr int TB = UmTile<BITS>::BYTES;
+    constexpr int U4_TILE = TB / 16;
+    constexpr int PER_THREAD = P * U4_TILE / 128;
+    extern __shared__ uint8_t smem_raw[];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- work unit: (active expert, token tile, row tile) -----------------
+    const int n_act = *a.n_act;
+    const int total_tiles = a.tile_prefix[n_act];
+    const int unit = blockIdx.x;
+    if (unit >= total_tiles * a.RT) return;
+    const int ti = unit / a.RT, rt = unit - ti * a.RT;
+    int lo = 0, hi = n_act - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.tile_prefix[mid] <= ti) lo = mid; else hi = mid - 1;
+    }
+    const int e = a.act_group[lo];
+    const int tt = ti - a.tile_prefix[lo];
+    const int slot0 = a.act_begin[lo] + tt * UM_N;
+    const int nval = min(UM_N, a.act_n[lo] - tt * UM_N);
+    const int N = (nval + 15) & ~15;
+
+    uint8_t *base = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(base + S * Cfg::STAGE_BYTES);
+    uint64_t *fullB = fullA + S;
+    uint64_t *empty = fullB + S;
+    uint64_t *accb = empty + S;
+    uint64_t *drain = accb + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&fullA[s], 4);
+            mbar_init(&fullB[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accb, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&]() {
+        if (!*abort_flag) {
+            *abort_flag = 1;
+            atomicOr(a.err, QG_FLAG_TIMEOUT);
+        }
+    };
+    const size_t tile_base = (size_t)(e * a.RT + rt) * a.KB;
+
+    if (warp < 4) {
+        // ================= converters ================================
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.wq + tile_base * P * TB);
+        const __half2 *scs = a.ws + tile_base * P * UM_M;
+        uint4 cur[PER_THREAD], nxt[PER_THREAD];
+        __half2 cs[PER_THREAD], ns[PER_THREAD];
+        auto load = [&](int kb, uint4 (&q)[PER_THREAD], __half2 (&sc)[PER_THREAD]) {
+#pragma unroll
+            for (int j = 0; j < PER_THREAD; j++) {
+                const int i = tid + 128 * j;
+                const int p = i / U4_TILE, ii = i - p * U4_TILE;
+                const int row = BITS == 8 ? (ii >> 2) : (ii >> 1);
+                q[j] = __ldg(src + (size_t)kb * P * U4_TILE + i);
+                sc[j] = __ldg(scs + ((size_t)kb * P + p) * UM_M + row);
+            }
+        };
+        load(0, cur, cs);
+        bool ok = true;
+        for (int kb = 0; kb < a.KB && ok; kb++) {
+            const int s = kb % S;
+            if (kb + 1 < a.KB) load(kb + 1, nxt, ns);
+            if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
+                fail();
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < PER_THREAD; j++) {
+                const int i = tid + 128 * j;
+                const int p = i / U4_TILE, ii = i - p * U4_TILE;
+                const uint32_t A = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
+                if constexpr (BITS == 8) {
+                    const int row = ii >> 2, c = ii & 3;
+                    const __half2 s2 = (c < 2) ? __low2half2(cs[j]) : __high2half2(cs[j]);
+                    uint32_t o[8];
+                    cvt_i8x4(cur[j].x, s2, o[0], o[1]);
+                    cvt_i8x4(cur[j].y, s2, o[2], o[3]);
+                    cvt_i8x4(cur[j].z, s2, o[4], o[5]);
+                    cvt_i8x4(cur[j].w, s2, o[6], o[7]);
+                    const uint32_t rowa = A + row * 128;
+                    const int x7 = row & 7;
+                    st_shared_v4(rowa + (((2 * c) ^ x7) << 4), o[0], o[1], o[2], o[3]);
+                    st_shared_v4(rowa + (((2 * c + 1) ^ x7) << 4), o[4], o[5], o[6], o[7]);
+                } else {
+                    const int row = ii >> 1, hh = ii & 1;
+                    const __half2 s2 = hh ? __high2half2(cs[j]) : __low2half2(cs[j]);
+                    uint32_t o[16];
+                    cvt_i4x8(cur[j].x, s2, *reinterpret_cast<uint32_t(*)[4]>(o));
+                    cvt_i4x8(cur[j].y, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 4));
+                    cvt_i4x8(cur[j].z, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 8));
+                    cvt_i4x8(cur[j].w, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 12));
+                    const uint32_t rowa = A + row * 128;
+                    const int x7 = row & 7;
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        st_shared_v4(rowa + (((4 * hh + q) ^ x7) << 4), o[4 * q], o[4 * q + 1],
+                                     o[4 * q + 2], o[4 * q + 3]);
+                }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fullA[s]);
+#pragma unroll
+            for (int j = 0; j < PER_THREAD; j++) {
+                cur[j] = nxt[j];
+                cs[j] = ns[j];
+            }
+        }
+
+        // ================= epilogue ================================
+        if (ok && mbar_wait(accb, 0, abort_flag, UM_WAIT_CYCLES)) {
+            tc_fence_after();
+            const int r = warp * 32 + lane;
+            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+            for (int c0 = 0; c0 < N; c0 += 32) {
+                float g[32];
+                tmem_ld32(lane_addr + c0, g);
+                if constexpr (P == 2) {
+                    float u[32];
+                    tmem_ld32(lane_addr + 128 + c0, u);
+                    __half *dst = a.h_out + (size_t)slot0 * a.h_stride + rt * UM_M + r;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int t = c0 + j;
+                        if (t < nval) {
+                            const float gv = g[j];
+                            const float hv = gv / (1.f + expf(-gv)) * u[j];
+                            dst[(size_t)t * a.h_stride] = __float2half_rn(hv);
+                        }
+                    }
+                } else {
+                    float *dst = a.d_out + (size_t)slot0 * a.d_stride + rt * UM_M + r;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int t = c0 + j;
+                        if (t < nval) dst[(size_t)t * a.d_stride] = g[j];
+                    }
+                }
+            }
+        } else {
+            fail();
+        }
+    } else if (warp == 4) {
+        // ================= TMA producer (activation tiles) ================
+        if (lane == 0) {
+            prefetch_tmap(&tmap_b);
+            int issued = -1;
+            for (int kb = 0; kb < a.KB; kb++) {
+                const int s = kb % S;
+                if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
+                    fail();
+                    break;
+                }
+                mbar_arrive_expect_tx(&fullB[s], Cfg::B_BYTES);
+                tma_load_2d(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES, &tmap_b, kb * UM_BK,
+                            slot0, &fullB[s]);
+                issued = kb;
+            }
+            if (*abort_flag && issued >= 0) {
+                // let our own last copy land before the CTA's smem goes away
+                volatile int never = 0;
+                mbar_wait(&fullB[issued % S], (issued / S) & 1, &never, UM_WAIT_CYCLES);
+            }
+        }
+    } else {
+        // ================= MMA issuer ================================
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(UM_M, N);
+            bool ok = true;
+            for (int kb = 0; kb < a.KB; kb++) {
+                const int s = kb % S;
+                const uint32_t par = (kb / S) & 1;
+                if (!mbar_wait(&fullB[s], par, abort_flag, UM_WAIT_CYCLES) ||
+                    !mbar_wait(&fullA[s], par, abort_flag, UM_WAIT_CYCLES)) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t bsm = smem_u32(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES);
+#pragma unroll
+                for (int p = 0; p < P; p++) {
+                    const uint32_t asm_ = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
+#pragma unroll
+                    for (int k16 = 0; k16 < UM_BK / 16; k16++)
+                        umma_f16(tmem + p * 128, desc_k_sw128(asm_ + k16 * 32),
+                                 desc_k_sw128(bsm + k16 * 32), idesc, (kb | k16) != 0);
+                }
+                umma_commit(&empty[s]);
+            }
+            if (ok) {
+                umma_commit(accb);
+            } else {
+                // drain our own UMMAs before TMEM is released
+                umma_commit(drain);
+                volatile int never = 0;
+                mbar_wait(drain, 0, &never, UM_WAIT_CYCLES);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+// ---- activation gather: xp[s, :] = fp16(x[slot_token[s], :]) -------------
+__global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restrict__ slot_token,
+                             int nslots, int H, __half *__restrict__ xp) {
+    const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int s = wg; s < nslots; s += nw) {
+        const float *src = x + (size_t)slot_token[s] * H;
+        __half *dst = xp + (size_t)s * H;
+        for (int k = lane * 8; k < H; k += 256) {
+            const float4 v0 = *reinterpret_cast<const float4 *>(src + k);
+            const float4 v1 = *reinterpret_cast<const float4 *>(src + k + 4);
+            __half2 h[4] = {__floats2half2_rn(v0.x, v0.y), __floats2half2_rn(v0.z, v0.w),
+                            __floats2half2_rn(v1.x, v1.y), __floats2half2_rn(v1.z, v1.w)};
+            *reinterpret_cast<uint4 *>(dst + k) = *reinterpret_cast<uint4 *>(h);
+        }
+    }
+}
+
+// ---- weight repack into UMMA tiles --------------------------------------
+// One thread per (e, rt, kb, p, row).  Source rows: p = 0 -> rt*128 + row,
+// p = 1 -> up_offset + rt*128 + row (the up half of gate_up).  int4 words
+// are reordered so element 2j sits in bits [4j, 4j+4) and element 2j+1 in
+// bits [16+4j, 20+4j): one shift+mask per fp16 pair in the converter.
+__global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict__ sc, int bits,
+                         int E, int rows_per_e, int K, int RT, int P, int up_offset,
+                         uint8_t *__restrict__ qo, __half2 *__restrict__ so) {
+    const int KB = K / UM_BK;
+    const int64_t n = (int64_t)E * RT * KB * P * UM_M;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int row = (int)(i % UM_M);
+    int64_t rest = i / UM_M;
+    const int p = (int)(rest % P);
+    rest /= P;
+    const int kb = (int)(rest % KB);
+    rest /= KB;
+    const int rt = (int)(rest % RT);
+    const int e = (int)(rest / RT);
+    const int64_t srow = (int64_t)e * rows_per_e + (p ? up_offset : 0) + rt * UM_M + row;
+    const int row_bytes = bits == 8 ? K : K / 2;
+    const int blk_bytes = bits == 8 ? UM_BK : UM_BK / 2;
+    const uint8_t *s = q + srow * row_bytes + (int64_t)kb * blk_bytes;
+    const int64_t tile = (((int64_t)e * RT + rt) * KB + kb) * P + p;
+    uint8_t *d = qo + tile * (UM_M * blk_bytes) + (int64_t)row * blk_bytes;
+    if (bits == 8) {
+        for (int b = 0; b < blk_bytes; b += 16)
+            *reinterpret_cast<uint4 *>(d + b) = *reinterpret_cast<const uint4 *>(s + b);
+    } else {
+        for (int w = 0; w < blk_bytes / 4; w++) {
+            uint32_t src = *reinterpret_cast<const uint32_t *>(s + 4 * w);
+            uint32_t out = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t byte = (src >> (8 * j)) & 0xFFu;
+                out |= (byte >> 4) << (4 * j);          // element 2j
+                out |= (byte & 0xFu) << (16 + 4 * j);   // element 2j+1
+            }
+            *reinterpret_cast<uint32_t *>(d + 4 * w) = out;
+        }
+    }
+    const __half *ss = sc + srow * (K / QG_GROUP) + kb * 2;
+    so[tile * UM_M + row] = __halves2half2(ss[0], ss[1]);
+}
+
+// ---- host side --------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 row-major [rows, cols] tensor, box 64 cols x 128 rows, 128B swizzle.
+int encode_act_map(void *map_out, const __half *ptr, int rows, int cols) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(QGMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16)
+        return set_error(QGMOE_ERR_INVALID_ARG, "activation buffer not 16-byte aligned");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {UM_BK, UM_N};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<__half *>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(QGMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QGMOE_OK;
+}
+
+int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
+                  int RT, int P, int up_offset, uint8_t *qo, __half2 *so, cudaStream_t s) {
+    const int64_t n = (int64_t)E * RT * (K / UM_BK) * P * UM_M;
+    if (n == 0) return QGMOE_OK;
+    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, sc, bits, E, rows_per_e, K, RT, P,
+                                                          up_offset, qo, so);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
+int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
+                      cudaStream_t s) {
+    if (nslots <= 0) return QGMOE_OK;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int blocks = (nslots + 7) / 8;
+    const int cap = num_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    k_gather_f16<<<blocks, 256, 0, s>>>(x, slot_token, nslots, H, xp);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
+template <int BITS, int P>
+static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStream_t s) {
+    using Cfg = UmCfg<P>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool done[64] = {false};
+    if (dev < 64 && !done[dev]) {
+        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cfg::SMEM));
+        done[dev] = true;
+    }
+    k_umma<BITS, P><<<grid, UM_THREADS, Cfg::SMEM, s>>>(
+        *reinterpret_cast<const CUtensorMap *>(tmap), a);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
+int launch_umma(int bits, int P, const void *tmap, const UmmaLaunch &l, cudaStream_t s) {
+    UmmaArgs a{};
+    a.wq = l.wq;
+    a.ws = l.ws;
+    a.RT = l.RT;
+    a.KB = l.KB;
+    a.act_group = l.act_group;
+    a.act_begin = l.act_begin;
+    a.act_n = l.act_n;
+    a.n_act = l.n_act;
+    a.tile_prefix = l.tile_prefix;
+    a.h_out = l.h_out;
+    a.h_stride = l.h_stride;
+    a.d_out = l.d_out;
+    a.d_stride = l.d_stride;
+    a.err = l.err;
+    if (l.grid <= 0) return QGMOE_OK;
+    if (bits == 8 && P == 2) return launch_umma_t<8, 2>(tmap, a, l.grid, s);
+    if (bits == 8 && P == 1) return launch_umma_t<8, 1>(tmap, a, l.grid, s);
+    if (bits == 4 && P == 2) return launch_umma_t<4, 2>(tmap, a, l.grid, s);
+    if (bits == 4 && P == 1) return launch_umma_t<4, 1>(tmap, a, l.grid, s);
+    return set_error(QGMOE_ERR_UNSUPPORTED, "tensor path needs int8/int4 weights");
+}
+
+}  // namespace qg

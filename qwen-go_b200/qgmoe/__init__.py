@@ -28,6 +28,9 @@ ROUTER_TOPK = 0
 ROUTER_PREFIX = 1
 SCALE_F16 = 0
 SCALE_F32 = 1
+PATH_AUTO = 0
+PATH_CUDA_CORE = 1
+PATH_TENSOR = 2
 
 _vp = C.c_void_p
 
@@ -63,6 +66,7 @@ SIGNATURES = {
     "qgmoe_forward_device": ([_vp, _vp, C.c_int32, _vp, _vp, _vp, _vp], C.c_int),
     "qgmoe_sync": ([_vp, _vp], C.c_int),
     "qgmoe_last_launch_count": ([_vp], C.c_int),
+    "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_timing": ([_vp, C.c_int32], C.c_int),
     "qgmoe_read_timing": ([_vp, C.POINTER(C.c_float), C.c_int32, C.POINTER(C.c_int32)], C.c_int),
     "qgmoe_stage_name": ([_vp, C.c_int32], C.c_char_p),
@@ -218,6 +222,10 @@ class MoeMLP:
 
     def last_launch_count(self) -> int:
         return lib().qgmoe_last_launch_count(self.h)
+
+    def set_path(self, mode: int):
+        """PATH_AUTO, PATH_CUDA_CORE or PATH_TENSOR (see include/qgmoe.h)."""
+        _check(lib().qgmoe_set_path(self.h, mode), "qgmoe_set_path")
 
     def set_timing(self, enable: bool = True):
         _check(lib().qgmoe_set_timing(self.h, int(enable)), "qgmoe_set_timing")
