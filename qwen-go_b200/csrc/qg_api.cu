@@ -227,6 +227,17 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(st.act_n, sizeof(int32_t) * (m->E + 1));
     QG_A(st.n_act, sizeof(int32_t));
     QG_A(st.tile_prefix, sizeof(int32_t) * (m->E + 2));
+    {
+        const int Ep = m->E + m->has_shared;
+        size_t rows = 0;  // max over T' <= cap of splits(T') * T'
+        for (int t = 1; t <= cap; t++) {
+            const size_t r = (size_t)route_splits(t, m->H, Ep, num_sms(m->device)) * t;
+            if (r > rows) rows = r;
+        }
+        QG_A(st.logits, sizeof(float) * rows * Ep);
+        QG_A(st.hist, sizeof(int32_t) * (size_t)((cap + 31) / 32) * m->E);
+        QG_A(st.expert_off, sizeof(int32_t) * m->E);
+    }
     if (m->tensor_ok) {
         QG_A(m->xp16, sizeof(__half) * pairs * m->H);
         QG_A(m->h16, sizeof(__half) * pairs * m->I);
@@ -288,12 +299,10 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, m->err_dev, s);
+                          m->has_shared, m->st, m->xp16, m->err_dev, s);
     if (rc) return rc;
     m->mark(1, "route", s);
     const int pairs = T * m->k;
-    if ((rc = launch_gather_f16(x, m->st.slot_token, pairs, m->H, m->xp16, s))) return rc;
-    m->mark(2, "gather", s);
     const int tiles = (pairs + 127) / 128 + (pairs < m->E ? pairs : m->E);
     UmmaLaunch l{};
     l.act_group = m->st.act_group;
@@ -311,7 +320,7 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     l.h_stride = m->I;
     l.grid = tiles * l.RT;
     if ((rc = launch_umma(m->bits, 2, &m->tmap_x, l, s))) return rc;
-    m->mark(3, "gate_up", s);
+    m->mark(2, "gate_up", s);
     // down -> d
     l.wq = m->dn_pq;
     l.ws = m->dn_ps;
@@ -322,12 +331,12 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     l.d_stride = m->H;
     l.grid = tiles * l.RT;
     if ((rc = launch_umma(m->bits, 1, &m->tmap_h, l, s))) return rc;
-    m->mark(4, "down", s);
+    m->mark(3, "down", s);
     if ((rc = launch_combine(m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, m->st.shared_w,
                              m->has_shared, out, s)))
         return rc;
-    m->mark(5, "combine", s);
-    m->last_launches = 5;
+    m->mark(4, "combine", s);
+    m->last_launches = 6;  // logits, top-k, scatter+gather, gate_up, down, combine
     return QGMOE_OK;
 }
 
@@ -349,7 +358,7 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, m->err_dev, s);
+                          m->has_shared, m->st, nullptr, m->err_dev, s);
     if (rc) return rc;
     m->mark(1, "route", s);
     ExpertArgs a{};
@@ -384,7 +393,7 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
                              m->has_shared, out, s)))
         return rc;
     m->mark(4, "combine", s);
-    m->last_launches = 4;
+    m->last_launches = 6;  // logits, top-k, scatter, gate_up, down, combine
     return QGMOE_OK;
 }
 

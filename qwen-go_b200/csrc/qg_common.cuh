@@ -58,6 +58,9 @@ struct RouteState {
     int32_t *act_n;      // [E+1] tokens in the group
     int32_t *n_act;      // [1]
     int32_t *tile_prefix;  // [E+2] 128-token tiles before each routed group, total last
+    float *logits;         // [splits][T][E+1] split-K partial router logits
+    int32_t *hist;         // [ceil(T/32)][E] expert histogram of each top-k CTA
+    int32_t *expert_off;   // [E] first slot of each expert
 };
 
 // One launch of the tensor-core grouped GEMM (qg_umma.cu).
@@ -94,9 +97,12 @@ struct ExpertArgs {
 };
 
 // Launch helpers implemented in the .cu files.
+// Router + dispatch: 3 launches.  xp (optional) receives the fp16 activation
+// row of every slot for the tensor-core path.
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
-                 const float *shared_gate, int has_shared, RouteState st, int *err,
+                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
                  cudaStream_t s);
+int route_splits(int T, int H, int Ep, int sms);
 int launch_expert(bool gateup, const ExpertArgs &a, int max_items, cudaStream_t s);
 int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
                    const float *topk_w, const float *shared_w, int has_shared, float *out,

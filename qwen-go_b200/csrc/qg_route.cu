@@ -1,21 +1,32 @@
-// Router + dispatch (kernels K1 and K2).
+// Router + dispatch (kernels K1 and K2), three launches for any token count.
 //
-// One CTA per token computes the router logits (proj(x,1,&m.gate,...),
-// model/moe.go:42), the softmax (model/tensors.go:106-121: max-subtract, exp
-// evaluated in float64 and rounded to float32, divide by the sum), the top-k
-// selection (model/moe.go:44-52, PREFIX or TOPK mode), the renormalised
-// weights w = p / (wSum + 1e-9) (model/moe.go:53-63) and the shared-expert
-// gate sigmoid(sharedGate . x) (model/moe.go:87-93).  The last CTA to finish
-// (atomic ticket) builds the per-expert token lists in one pass: exclusive
-// scan of the expert histogram, a stable scatter of the (token, rank) pairs
-// into expert-sorted slots, and the compact list of active experts.  It
-// re-zeroes the histogram and the ticket so the next call (or a CUDA-graph
-// replay) starts clean.
-#include <cstdio>
-
+// 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...), model/moe.go:42)
+//    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 32 tokens x 128
+//    router rows x one K slice, writes its partial sums.  The shared-expert
+//    gate vector rides along as router row E (model/moe.go:87-93).  Split-K
+//    keeps decode-sized batches (T = 1..64) spread over the SMs while the
+//    1 MiB router matrix is read about once.
+// 2. k_topk: one warp per token adds the partials in a fixed order, then
+//    softmax (model/tensors.go:106-121: max-subtract, exp in float64 rounded
+//    to float32, divide by the sum), top-k (model/moe.go:44-52, TOPK or the
+//    literal PREFIX bound), w = p / (wSum + 1e-9) (model/moe.go:53-63) and
+//    sigmoid of the shared gate.  Each CTA writes its expert histogram; the
+//    last CTA (atomic ticket) scans the totals into expert offsets, the list
+//    of active experts and the 128-token tile prefix, and re-zeroes the
+//    counters and the ticket so the next call (or a graph replay) starts clean.
+// 3. k_scatter: each CTA ranks its own (token, rank) pairs per expert in pair
+//    order (warp match + per-warp counts) and adds the histograms of the CTAs
+//    before it, so slots are expert-sorted and deterministic without a serial
+//    pass.  With `xp` set it also writes the slot's fp16 activation row for
+//    the tensor-core path.
 #include "qg_common.cuh"
 
 namespace qg {
+
+constexpr int LG_TOK = 32;   // tokens per logits tile
+constexpr int LG_ROWS = 128; // router rows per logits tile
+constexpr int LG_KC = 32;    // K chunk staged in shared memory
+constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA (8 warps x 4)
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -23,8 +34,8 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// Picks the better of two (prob, index) candidates: larger prob, then lower
-// index -- the order a stable descending insertion sort produces.
+// Larger prob, then lower index: the order a stable descending insertion
+// sort produces.
 __device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
     if (v2 > v || (v2 == v && i2 < i)) {
         v = v2;
@@ -32,170 +43,215 @@ __device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
     }
 }
 
-__global__ void __launch_bounds__(QG_ROUTE_THREADS)
-k_route(const float *__restrict__ x, int T, int H, int E, int k, int mode,
-        const float *__restrict__ router, const float *__restrict__ shared_gate,
-        int has_shared, RouteState st, int *err) {
-    extern __shared__ float smem[];
-    float *xs = smem;              // [H]
-    float *p = smem + H;           // [E + 1] logits -> probabilities
-    __shared__ int s_idx[QG_MAX_TOPK];
-    __shared__ int s_last;
+int route_splits(int T, int H, int Ep, int sms) {
+    const int tt = (T + LG_TOK - 1) / LG_TOK;
+    const int te = (Ep + LG_ROWS - 1) / LG_ROWS;
+    int s = (2 * sms) / (tt * te);
+    const int smax = H / LG_KC < 32 ? H / LG_KC : 32;
+    if (s > smax) s = smax;
+    if (s < 1) s = 1;
+    return s;
+}
 
-    const int t = blockIdx.x;
+// ---- 1. logits ------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *__restrict__ router,
+         const float *__restrict__ shared_gate, int ksplit, float *__restrict__ part) {
+    __shared__ __align__(16) float xs[LG_KC][LG_TOK + 4];
+    __shared__ __align__(16) float ws[LG_KC][LG_ROWS + 4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int nwarps = QG_ROUTE_THREADS / 32;
-
-    const float4 *xg = reinterpret_cast<const float4 *>(x + (size_t)t * H);
-    for (int i = tid; i < H / 4; i += QG_ROUTE_THREADS)
-        reinterpret_cast<float4 *>(xs)[i] = xg[i];
-    __syncthreads();
-
-    // logits: one warp per router row; the shared gate vector is row E.
-    const int nrows = E + (has_shared ? 1 : 0);
-    for (int e = warp; e < nrows; e += nwarps) {
-        const float4 *wr = reinterpret_cast<const float4 *>(e < E ? router + (size_t)e * H
-                                                                  : shared_gate);
-        float acc = 0.f;
-        for (int i = lane; i < H / 4; i += 32) {
-            float4 w = __ldg(wr + i);
-            float4 xv = reinterpret_cast<const float4 *>(xs)[i];
-            acc = fmaf(xv.x, w.x, acc);
-            acc = fmaf(xv.y, w.y, acc);
-            acc = fmaf(xv.z, w.z, acc);
-            acc = fmaf(xv.w, w.w, acc);
+    const int t0 = blockIdx.x * LG_TOK, r0 = blockIdx.y * LG_ROWS, s = blockIdx.z;
+    const int kc = ((H / LG_KC + ksplit - 1) / ksplit) * LG_KC;
+    const int k0 = s * kc, k1 = min(H, k0 + kc);
+    float acc[4][4] = {};
+    for (int kb = k0; kb < k1; kb += LG_KC) {
+        {   // x chunk: 32 tokens x 32 k, float4 along k, stored transposed
+            const int tok = tid >> 3, k4 = (tid & 7) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + tok < T) v = *reinterpret_cast<const float4 *>(x + (size_t)(t0 + tok) * H + kb + k4);
+            xs[k4][tok] = v.x;
+            xs[k4 + 1][tok] = v.y;
+            xs[k4 + 2][tok] = v.z;
+            xs[k4 + 3][tok] = v.w;
         }
-        acc = warp_sum(acc);
-        if (lane == 0) p[e] = acc;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {  // router chunk: 128 rows x 32 k
+            const int row = (tid >> 3) + 32 * j, k4 = (tid & 7) * 4;
+            const int r = r0 + row;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r < Ep) {
+                const float *src = r < E ? router + (size_t)r * H : shared_gate;
+                v = __ldg(reinterpret_cast<const float4 *>(src + kb + k4));
+            }
+            ws[k4][row] = v.x;
+            ws[k4 + 1][row] = v.y;
+            ws[k4 + 2][row] = v.z;
+            ws[k4 + 3][row] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < LG_KC; kk++) {
+            const float4 a = *reinterpret_cast<const float4 *>(&xs[kk][4 * warp]);
+            const float4 b = *reinterpret_cast<const float4 *>(&ws[kk][4 * lane]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
     }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int t = t0 + 4 * warp + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int r = r0 + 4 * lane + j;
+            if (r < Ep) part[((size_t)s * T + t) * Ep + r] = acc[i][j];
+        }
+    }
+}
+
+// ---- 2. softmax + top-k + histograms --------------------------------------------
+__global__ void __launch_bounds__(256)
+k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, int mode,
+       int has_shared, RouteState st, int *err) {
+    extern __shared__ float smem[];  // [8 warps][Ep] probabilities, then scan scratch
+    __shared__ int s_idx[8][QG_MAX_TOPK];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float *p = smem + warp * Ep;
+    int *hist_s = reinterpret_cast<int *>(smem + 8 * Ep);  // [E]
+    for (int e = tid; e < E; e += 256) hist_s[e] = 0;
     __syncthreads();
 
-    if (warp == 0) {
-        // softmax over E (tensors.go:106-121)
+    for (int i = 0; i < TK_TOK / 8; i++) {
+        const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / 8) + i;
+        if (t >= T) break;
+        for (int e = lane; e < Ep; e += 32) {
+            float v = 0.f;
+            for (int s = 0; s < ksplit; s++) v += part[((size_t)s * T + t) * Ep + e];
+            p[e] = v;
+        }
+        __syncwarp();
         float mx = -INFINITY;
         for (int e = lane; e < E; e += 32) mx = fmaxf(mx, p[e]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.f;
         for (int e = lane; e < E; e += 32) {
-            float v = (float)exp((double)(p[e] - mx));
+            const float v = (float)exp((double)(p[e] - mx));
             p[e] = v;
             sum += v;
         }
         sum = warp_sum(sum);
         for (int e = lane; e < E; e += 32) p[e] = p[e] / sum;
         __syncwarp();
-
+        int *sel = s_idx[warp];
         if (mode == QGMOE_ROUTER_TOPK) {
-            // k rounds of warp arg-max; winners are knocked out by index.
             for (int r = 0; r < k; r++) {
                 float bv = -1.f;
                 int bi = 0x7fffffff;
                 for (int e = lane; e < E; e += 32) {
                     bool used = false;
-                    for (int q = 0; q < r; q++) used |= (s_idx[q] == e);
+                    for (int q = 0; q < r; q++) used |= (sel[q] == e);
                     if (!used) better(bv, bi, p[e], e);
                 }
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
-                    float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-                    int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+                    const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
                     better(bv, bi, v2, i2);
                 }
-                if (lane == 0) s_idx[r] = bi;
+                if (lane == 0) sel[r] = bi;
                 __syncwarp();
             }
         } else {
             // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1.
             if (lane == 0) {
-                for (int i = 0; i < k; i++) s_idx[i] = i;
-                for (int i = 1; i < k && i < E; i++)
-                    for (int j = i; j > 0 && p[s_idx[j]] > p[s_idx[j - 1]]; j--) {
-                        int tmp = s_idx[j];
-                        s_idx[j] = s_idx[j - 1];
-                        s_idx[j - 1] = tmp;
+                for (int q = 0; q < k; q++) sel[q] = q;
+                for (int a = 1; a < k && a < E; a++)
+                    for (int b = a; b > 0 && p[sel[b]] > p[sel[b - 1]]; b--) {
+                        const int tmp = sel[b];
+                        sel[b] = sel[b - 1];
+                        sel[b - 1] = tmp;
                     }
             }
             __syncwarp();
         }
         if (lane == 0) {
             float wsum = 0.f;
-            for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, p[s_idx[r]]);
+            for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, p[sel[r]]);
             const float den = __fadd_rn(wsum, 1e-9f);
             for (int r = 0; r < k; r++) {
-                int e = s_idx[r];
+                const int e = sel[r];
                 st.topk_idx[(size_t)t * k + r] = e;
                 st.topk_w[(size_t)t * k + r] = __fdiv_rn(p[e], den);
             }
-            if (has_shared) {
-                float g = p[E];  // raw logit row E was not touched by softmax
-                st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)g));
-            }
+            if (has_shared) st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)p[E]));
         }
         __syncwarp();
         if (lane < k) {
-            int e = s_idx[lane];
+            const int e = sel[lane];
             if (e >= 0 && e < E)
-                atomicAdd(&st.counts[e], 1);
+                atomicAdd(&hist_s[e], 1);
             else
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
         }
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += 256) {
+        const int c = hist_s[e];
+        st.hist[(size_t)blockIdx.x * E + e] = c;
+        if (c) atomicAdd(&st.counts[e], c);
     }
 
-    // ---- last CTA: dispatch --------------------------------------------
+    // ---- last CTA: expert offsets, active list, tile prefix ------------------
     __threadfence();
     __syncthreads();
     if (tid == 0) s_last = (atomicAdd(st.done_ctr, 1) == (int)gridDim.x - 1);
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-
-    // Reuse dynamic smem: cnt[E], off[E], cur[E], wcnt[nwarps][E].
-    int *cnt = reinterpret_cast<int *>(smem);
-    int *cur = cnt + E;
-    int *wcnt = cur + E;
-    for (int e = tid; e < E; e += QG_ROUTE_THREADS) {
+    int *cnt = hist_s;
+    for (int e = tid; e < E; e += 256) {
         cnt[e] = __ldcg(st.counts + e);
-        st.counts[e] = 0;  // ready for the next call
+        st.counts[e] = 0;
     }
     __syncthreads();
     if (warp == 0) {
-        // exclusive scan (serial per lane chunk, then warp scan of totals)
         const int per = (E + 31) / 32;
-        int lo = lane * per, hi = min(E, lo + per);
-        int run = 0;
-        for (int e = lo; e < hi; e++) run += cnt[e];
-        int incl = run;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        int base = incl - run;
+        const int lo = lane * per, hi = min(E, lo + per);
+        int run = 0, nz = 0;
         for (int e = lo; e < hi; e++) {
-            cur[e] = base;
-            base += cnt[e];
+            run += cnt[e];
+            nz += cnt[e] > 0;
         }
-        // compact list of active experts, ascending id
-        int nz = 0;
-        for (int e = lo; e < hi; e++) nz += cnt[e] > 0;
-        int nzi = nz;
+        int incl = run, nzi = nz;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            int v = __shfl_up_sync(0xffffffffu, nzi, o);
-            if (lane >= o) nzi += v;
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            const int w = __shfl_up_sync(0xffffffffu, nzi, o);
+            if (lane >= o) {
+                incl += v;
+                nzi += w;
+            }
         }
-        int a = nzi - nz;
-        for (int e = lo; e < hi; e++)
+        int base = incl - run, a = nzi - nz;
+        for (int e = lo; e < hi; e++) {
+            st.expert_off[e] = base;
             if (cnt[e] > 0) {
                 st.act_group[a] = e;
-                st.act_begin[a] = cur[e];
+                st.act_begin[a] = base;
                 st.act_n[a] = cnt[e];
                 a++;
             }
+            base += cnt[e];
+        }
         int total_act = __shfl_sync(0xffffffffu, nzi, 31);
         if (lane == 0) {
-            // 128-token tiles per routed group, for the tensor-core kernels
             int tiles = 0, ai = 0;
             for (int e = 0; e < E; e++)
                 if (cnt[e] > 0) {
@@ -213,31 +269,45 @@ k_route(const float *__restrict__ x, int T, int H, int E, int k, int mode,
             *st.done_ctr = 0;
         }
     }
-    __syncthreads();
+}
 
-    // stable scatter of pairs (t, r) in pair order
-    const int npairs = T * k;
-    const unsigned lt_mask = (1u << lane) - 1u;
-    for (int base = 0; base < npairs; base += QG_ROUTE_THREADS) {
-        for (int i = tid; i < nwarps * E; i += QG_ROUTE_THREADS) wcnt[i] = 0;
+// ---- 3. scatter (+ fp16 gather) ---------------------------------------------------
+__global__ void __launch_bounds__(256)
+k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_shared, RouteState st,
+          __half *__restrict__ xp, int *err) {
+    extern __shared__ int sm[];
+    int *cur = sm;            // [E] next slot per expert for this CTA
+    int *wcnt = sm + E;       // [8][E]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = blockIdx.x;
+    for (int e = tid; e < E; e += 256) {
+        int base = st.expert_off[e];
+        for (int cc = 0; cc < c; cc++) base += st.hist[(size_t)cc * E + e];
+        cur[e] = base;
+    }
+    const int p0 = c * TK_TOK * k;
+    const int p1 = min(T * k, p0 + TK_TOK * k);
+    const unsigned lt = (1u << lane) - 1u;
+    for (int base = p0; base < p1; base += 256) {
+        for (int i = tid; i < 8 * E; i += 256) wcnt[i] = 0;
         __syncthreads();
         const int pi = base + tid;
         int e = -1;
-        if (pi < npairs) {
-            e = __ldcg(st.topk_idx + pi);
+        if (pi < p1) {
+            e = st.topk_idx[pi];
             if (e < 0 || e >= E) {
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
                 e = -1;
             }
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);
-        const int rank = __popc(peers & lt_mask);
+        const int rank = __popc(peers & lt);
         if (e >= 0 && rank == 0) wcnt[warp * E + e] = __popc(peers);
         __syncthreads();
         if (e >= 0) {
             int slot = cur[e] + rank;
             for (int w = 0; w < warp; w++) slot += wcnt[w * E + e];
-            if (slot < 0 || slot >= npairs) {
+            if (slot < 0 || slot >= T * k) {
                 atomicOr(err, QG_FLAG_BAD_SLOT);
             } else {
                 st.pair_slot[pi] = slot;
@@ -245,32 +315,55 @@ k_route(const float *__restrict__ x, int T, int H, int E, int k, int mode,
             }
         }
         __syncthreads();
-        for (int ee = tid; ee < E; ee += QG_ROUTE_THREADS) {
+        for (int ee = tid; ee < E; ee += 256) {
             int add = 0;
-            for (int w = 0; w < nwarps; w++) add += wcnt[w * E + ee];
+            for (int w = 0; w < 8; w++) add += wcnt[w * E + ee];
             cur[ee] += add;
         }
         __syncthreads();
     }
     if (has_shared)
-        for (int i = tid; i < T; i += QG_ROUTE_THREADS) st.slot_token[npairs + i] = i;
+        for (int t = c * TK_TOK + tid; t < min(T, (c + 1) * TK_TOK); t += 256)
+            st.slot_token[T * k + t] = t;
+    if (!xp) return;
+    // fp16 activation rows for the tensor-core path: one warp per pair
+    for (int pi = p0 + warp; pi < p1; pi += 8) {
+        const int slot = st.pair_slot[pi];
+        if (slot < 0 || slot >= T * k) continue;
+        const float *src = x + (size_t)(pi / k) * H;
+        __half *dst = xp + (size_t)slot * H;
+        for (int kk = lane * 8; kk < H; kk += 256) {
+            const float4 v0 = *reinterpret_cast<const float4 *>(src + kk);
+            const float4 v1 = *reinterpret_cast<const float4 *>(src + kk + 4);
+            __half2 h[4] = {__floats2half2_rn(v0.x, v0.y), __floats2half2_rn(v0.z, v0.w),
+                            __floats2half2_rn(v1.x, v1.y), __floats2half2_rn(v1.z, v1.w)};
+            *reinterpret_cast<uint4 *>(dst + kk) = *reinterpret_cast<uint4 *>(h);
+        }
+    }
 }
 
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
-                 const float *shared_gate, int has_shared, RouteState st, int *err,
+                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
                  cudaStream_t s) {
-    const int nwarps = QG_ROUTE_THREADS / 32;
-    size_t route_bytes = sizeof(float) * ((size_t)H + E + 1);
-    size_t disp_bytes = sizeof(int) * ((size_t)2 * E + (size_t)nwarps * E);
-    size_t smem = route_bytes > disp_bytes ? route_bytes : disp_bytes;
-    static bool attr_set = false;
-    if (!attr_set) {
-        QG_CUDA(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024));
-        attr_set = true;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int Ep = E + (has_shared ? 1 : 0);
+    const int ks = route_splits(T, H, Ep, num_sms(dev));
+    dim3 g1((T + LG_TOK - 1) / LG_TOK, (Ep + LG_ROWS - 1) / LG_ROWS, ks);
+    k_logits<<<g1, 256, 0, s>>>(x, T, H, E, Ep, router, shared_gate, ks, st.logits);
+    QG_CUDA(cudaGetLastError());
+    const int nc = (T + TK_TOK - 1) / TK_TOK;
+    const size_t sm2 = sizeof(float) * (size_t)8 * Ep + sizeof(int) * (size_t)E;
+    const size_t sm3 = sizeof(int) * (size_t)9 * E;
+    static bool attr[64] = {false};
+    if (dev < 64 && !attr[dev]) {
+        QG_CUDA(cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        QG_CUDA(cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        attr[dev] = true;
     }
-    k_route<<<T, QG_ROUTE_THREADS, smem, s>>>(x, T, H, E, k, mode, router, shared_gate,
-                                              has_shared, st, err);
+    k_topk<<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    QG_CUDA(cudaGetLastError());
+    k_scatter<<<nc, 256, sm3, s>>>(x, T, H, E, k, has_shared, st, xp, err);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
