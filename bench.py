@@ -422,6 +422,9 @@ def run_ours(args, cfg):
     if world > 1:
         raise SystemExit("expert-parallel path not built yet")
     layer, x, host, info = build_gpu_layer(cfg, dev)
+    layer.set_path({"auto": qgmoe.PATH_AUTO, "cuda_core": qgmoe.PATH_CUDA_CORE,
+                    "tensor": qgmoe.PATH_TENSOR}[args.path])
+    info["path"] = args.path
     T, H, k = cfg["T"], cfg["H"], cfg["k"]
     out = torch.empty_like(x)
     sel = torch.empty((T, k), dtype=torch.int32, device=x.device)
@@ -545,6 +548,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c3", choices=sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--path", default="auto", choices=["auto", "cuda_core", "tensor"],
+                    help="expert-product path (qgmoe_set_path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])

@@ -64,31 +64,40 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
     const int kc = ((H / LG_KC + ksplit - 1) / ksplit) * LG_KC;
     const int k0 = s * kc, k1 = min(H, k0 + kc);
     float acc[4][4] = {};
-    for (int kb = k0; kb < k1; kb += LG_KC) {
-        {   // x chunk: 32 tokens x 32 k, float4 along k, stored transposed
-            const int tok = tid >> 3, k4 = (tid & 7) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + tok < T) v = *reinterpret_cast<const float4 *>(x + (size_t)(t0 + tok) * H + kb + k4);
-            xs[k4][tok] = v.x;
-            xs[k4 + 1][tok] = v.y;
-            xs[k4 + 2][tok] = v.z;
-            xs[k4 + 3][tok] = v.w;
-        }
+    // Each thread stages one float4 of x and four float4 of the router per
+    // chunk; the next chunk is fetched into registers while this one computes.
+    const int tok = tid >> 3, k4 = (tid & 7) * 4;
+    const float *xrow = (t0 + tok < T) ? x + (size_t)(t0 + tok) * H : nullptr;
+    const float *wrow[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {  // router chunk: 128 rows x 32 k
-            const int row = (tid >> 3) + 32 * j, k4 = (tid & 7) * 4;
-            const int r = r0 + row;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < Ep) {
-                const float *src = r < E ? router + (size_t)r * H : shared_gate;
-                v = __ldg(reinterpret_cast<const float4 *>(src + kb + k4));
-            }
-            ws[k4][row] = v.x;
-            ws[k4 + 1][row] = v.y;
-            ws[k4 + 2][row] = v.z;
-            ws[k4 + 3][row] = v.w;
+    for (int j = 0; j < 4; j++) {
+        const int r = r0 + tok + 32 * j;
+        wrow[j] = r < Ep ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
+    }
+    auto fetch = [&](int kb, float4 &xv, float4 (&wv)[4]) {
+        xv = xrow ? *reinterpret_cast<const float4 *>(xrow + kb + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            wv[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + k4))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    float4 xn, wn[4];
+    if (k0 < k1) fetch(k0, xn, wn);
+    for (int kb = k0; kb < k1; kb += LG_KC) {
+        xs[k4][tok] = xn.x;
+        xs[k4 + 1][tok] = xn.y;
+        xs[k4 + 2][tok] = xn.z;
+        xs[k4 + 3][tok] = xn.w;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int row = tok + 32 * j;
+            ws[k4][row] = wn[j].x;
+            ws[k4 + 1][row] = wn[j].y;
+            ws[k4 + 2][row] = wn[j].z;
+            ws[k4 + 3][row] = wn[j].w;
         }
         __syncthreads();
+        if (kb + LG_KC < k1) fetch(kb + LG_KC, xn, wn);
 #pragma unroll 8
         for (int kk = 0; kk < LG_KC; kk++) {
             const float4 a = *reinterpret_cast<const float4 *>(&xs[kk][4 * warp]);
@@ -114,90 +123,119 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
 }
 
 // ---- 2. softmax + top-k + histograms --------------------------------------------
+// A warp holds one token's probabilities in registers: lane l owns experts
+// l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
+template <int NJ>
 __global__ void __launch_bounds__(256)
 k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, int mode,
        int has_shared, RouteState st, int *err) {
-    extern __shared__ float smem[];  // [8 warps][Ep] probabilities, then scan scratch
+    extern __shared__ int hist_s[];  // [E]
     __shared__ int s_idx[8][QG_MAX_TOPK];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float *p = smem + warp * Ep;
-    int *hist_s = reinterpret_cast<int *>(smem + 8 * Ep);  // [E]
     for (int e = tid; e < E; e += 256) hist_s[e] = 0;
     __syncthreads();
 
     for (int i = 0; i < TK_TOK / 8; i++) {
         const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / 8) + i;
         if (t >= T) break;
-        for (int e = lane; e < Ep; e += 32) {
-            float v = 0.f;
-            for (int s = 0; s < ksplit; s++) v += part[((size_t)s * T + t) * Ep + e];
-            p[e] = v;
+        float v[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int e = lane + 32 * j;
+            float acc = 0.f;
+            if (e < E)
+                for (int s = 0; s < ksplit; s++) acc += part[((size_t)s * T + t) * Ep + e];
+            v[j] = e < E ? acc : -INFINITY;
         }
-        __syncwarp();
-        float mx = -INFINITY;
-        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, p[e]);
+        float mx = v[0];
+#pragma unroll
+        for (int j = 1; j < NJ; j++) mx = fmaxf(mx, v[j]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.f;
-        for (int e = lane; e < E; e += 32) {
-            const float v = (float)exp((double)(p[e] - mx));
-            p[e] = v;
-            sum += v;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            if (lane + 32 * j < E) {
+                v[j] = (float)exp((double)(v[j] - mx));
+                sum += v[j];
+            } else {
+                v[j] = -1.f;  // never selected
+            }
         }
         sum = warp_sum(sum);
-        for (int e = lane; e < E; e += 32) p[e] = p[e] / sum;
-        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < NJ; j++)
+            if (lane + 32 * j < E) v[j] = v[j] / sum;
         int *sel = s_idx[warp];
+        float selp = 0.f;  // lane r < k: probability of the rank-r expert
         if (mode == QGMOE_ROUTER_TOPK) {
+            unsigned used = 0;
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if (lane + 32 * j >= E) used |= 1u << j;  // padding lanes never win
             for (int r = 0; r < k; r++) {
-                float bv = -1.f;
+                float bv = -2.f;
                 int bi = 0x7fffffff;
-                for (int e = lane; e < E; e += 32) {
-                    bool used = false;
-                    for (int q = 0; q < r; q++) used |= (sel[q] == e);
-                    if (!used) better(bv, bi, p[e], e);
-                }
+#pragma unroll
+                for (int j = 0; j < NJ; j++)
+                    if (!((used >> j) & 1u)) better(bv, bi, v[j], lane + 32 * j);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
                     const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
                     better(bv, bi, v2, i2);
                 }
+                if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+                if (lane == r) selp = bv;
                 if (lane == 0) sel[r] = bi;
-                __syncwarp();
             }
         } else {
-            // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1.
+            // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1
+            // (k <= 32, so expert q < k is v[0] of lane q).
+            const float pq = v[0];
+            float pk[QG_MAX_TOPK];
+            int ik[QG_MAX_TOPK];
+            for (int q = 0; q < k; q++) {
+                pk[q] = __shfl_sync(0xffffffffu, pq, q);
+                ik[q] = q;
+            }
             if (lane == 0) {
-                for (int q = 0; q < k; q++) sel[q] = q;
-                for (int a = 1; a < k && a < E; a++)
-                    for (int b = a; b > 0 && p[sel[b]] > p[sel[b - 1]]; b--) {
-                        const int tmp = sel[b];
-                        sel[b] = sel[b - 1];
-                        sel[b - 1] = tmp;
+                for (int a2 = 1; a2 < k && a2 < E; a2++)
+                    for (int b2 = a2; b2 > 0 && pk[b2] > pk[b2 - 1]; b2--) {
+                        const float tp = pk[b2];
+                        pk[b2] = pk[b2 - 1];
+                        pk[b2 - 1] = tp;
+                        const int ti = ik[b2];
+                        ik[b2] = ik[b2 - 1];
+                        ik[b2 - 1] = ti;
                     }
+                for (int q = 0; q < k; q++) sel[q] = ik[q];
             }
             __syncwarp();
-        }
-        if (lane == 0) {
-            float wsum = 0.f;
-            for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, p[sel[r]]);
-            const float den = __fadd_rn(wsum, 1e-9f);
-            for (int r = 0; r < k; r++) {
-                const int e = sel[r];
-                st.topk_idx[(size_t)t * k + r] = e;
-                st.topk_w[(size_t)t * k + r] = __fdiv_rn(p[e], den);
-            }
-            if (has_shared) st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)p[E]));
+            // probability of rank `lane`: the owner of expert sel[lane] is lane sel[lane]
+            const int myexp = lane < k ? sel[lane] : 0;
+            const float got = __shfl_sync(0xffffffffu, pq, myexp);
+            if (lane < k) selp = got;
         }
         __syncwarp();
+        // wSum over ranks in rank order, then w = p / (wSum + 1e-9)
+        float wsum = 0.f;
+        for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, selp, r));
+        const float den = __fadd_rn(wsum, 1e-9f);
         if (lane < k) {
             const int e = sel[lane];
+            st.topk_idx[(size_t)t * k + lane] = e;
+            st.topk_w[(size_t)t * k + lane] = __fdiv_rn(selp, den);
             if (e >= 0 && e < E)
                 atomicAdd(&hist_s[e], 1);
             else
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
+        }
+        if (has_shared && lane == 0) {
+            float g = 0.f;
+            for (int s = 0; s < ksplit; s++) g += part[((size_t)s * T + t) * Ep + E];
+            st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)g));
         }
         __syncwarp();
     }
@@ -278,12 +316,38 @@ k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_share
     extern __shared__ int sm[];
     int *cur = sm;            // [E] next slot per expert for this CTA
     int *wcnt = sm + E;       // [8][E]
+    __shared__ int partial[256];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int c = blockIdx.x;
-    for (int e = tid; e < E; e += 256) {
-        int base = st.expert_off[e];
-        for (int cc = 0; cc < c; cc++) base += st.hist[(size_t)cc * E + e];
-        cur[e] = base;
+    // Slots of this CTA's pairs start after the earlier CTAs' pairs of the
+    // same expert: sum histogram rows 0..c-1, split over nparts threads per
+    // expert with independent accumulators so the loads overlap.
+    const int nparts = E >= 256 ? 1 : 256 / E;
+    for (int e0 = 0; e0 < E; e0 += 256) {
+        const int idx = tid, e = e0 + idx % (E >= 256 ? 256 : E), part = idx / (E >= 256 ? 256 : E);
+        int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+        if (e < E && part < nparts) {
+            const int per = (c + nparts - 1) / nparts;
+            const int lo = part * per, hi = min(c, lo + per);
+            int cc = lo;
+            for (; cc + 4 <= hi; cc += 4) {
+                acc0 += st.hist[(size_t)cc * E + e];
+                acc1 += st.hist[(size_t)(cc + 1) * E + e];
+                acc2 += st.hist[(size_t)(cc + 2) * E + e];
+                acc3 += st.hist[(size_t)(cc + 3) * E + e];
+            }
+            for (; cc < hi; cc++) acc0 += st.hist[(size_t)cc * E + e];
+        }
+        partial[tid] = acc0 + acc1 + acc2 + acc3;
+        __syncthreads();
+        if (tid < (E - e0 < 256 ? E - e0 : 256) && e0 + tid < E) {
+            const int ee = e0 + tid;
+            const int stride = E >= 256 ? 256 : E;
+            int base = st.expert_off[ee];
+            for (int pp = 0; pp < nparts; pp++) base += partial[pp * stride + tid];
+            cur[ee] = base;
+        }
+        __syncthreads();
     }
     const int p0 = c * TK_TOK * k;
     const int p1 = min(T * k, p0 + TK_TOK * k);
@@ -353,15 +417,26 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     k_logits<<<g1, 256, 0, s>>>(x, T, H, E, Ep, router, shared_gate, ks, st.logits);
     QG_CUDA(cudaGetLastError());
     const int nc = (T + TK_TOK - 1) / TK_TOK;
-    const size_t sm2 = sizeof(float) * (size_t)8 * Ep + sizeof(int) * (size_t)E;
+    const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)9 * E;
     static bool attr[64] = {false};
     if (dev < 64 && !attr[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
         QG_CUDA(cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
         attr[dev] = true;
     }
-    k_topk<<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    const int nj = (E + 31) / 32;
+    if (nj <= 1)
+        k_topk<1><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    else if (nj <= 2)
+        k_topk<2><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    else if (nj <= 4)
+        k_topk<4><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    else if (nj <= 8)
+        k_topk<8><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    else if (nj <= 16)
+        k_topk<16><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+    else
+        k_topk<32><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     QG_CUDA(cudaGetLastError());
     k_scatter<<<nc, 256, sm3, s>>>(x, T, H, E, k, has_shared, st, xp, err);
     QG_CUDA(cudaGetLastError());

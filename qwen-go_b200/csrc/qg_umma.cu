@@ -32,7 +32,7 @@
 namespace qg {
 using namespace sm100;
 
-constexpr int UM_THREADS = 192;  // warps 0-3: dequant + epilogue, 4: TMA, 5: MMA
+constexpr int UM_THREADS = 224;  // warps 0-3 dequant+epilogue, 4 code TMA, 5 MMA, 6 act TMA
 constexpr int UM_M = 128;        // weight rows per tile
 constexpr int UM_N = 128;        // max tokens per tile
 constexpr int UM_BK = 64;        // K elements per stage (one 128-byte fp16 row)
@@ -43,15 +43,22 @@ struct UmTile {
     static constexpr int BYTES = UM_M * UM_BK * BITS / 8;  // codes of one (row tile, k block)
 };
 
-template <int P>
+// Shared memory: S stages of (P fp16 A tiles + B tile) consumed by the MMA,
+// and R stages of raw codes + scales brought in by bulk TMA copies for the
+// converters (the deep ring hides the DRAM latency of the weight stream).
+template <int BITS, int P>
 struct UmCfg {
-    static constexpr int STAGES = P == 2 ? 4 : 6;
+    static constexpr int STAGES = P == 2 ? 3 : 4;
+    static constexpr int RAW_STAGES = P == 2 ? (BITS == 8 ? 4 : 6) : (BITS == 8 ? 6 : 8);
     static constexpr int A_BYTES = UM_M * UM_BK * 2;
     static constexpr int B_BYTES = UM_N * UM_BK * 2;
     static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
+    static constexpr int RAW_CODE = P * UmTile<BITS>::BYTES;
+    static constexpr int RAW_BYTES = RAW_CODE + P * UM_M * 4;
     static constexpr int TMEM_COLS = P == 2 ? 256 : 128;
-    static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2) + 16;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+    static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 2) + 16;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + BAR_BYTES + 1024;
+    static_assert(SMEM <= 232448, "shared memory budget");
 };
 
 // int8 x4 -> two fp16x2 (q * s), exact codes then one correctly rounded product.
@@ -100,8 +107,9 @@ struct UmmaArgs {
 template <int BITS, int P>
 __global__ void __launch_bounds__(UM_THREADS, 1)
 k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
-    using Cfg = UmCfg<P>;
+    using Cfg = UmCfg<BITS, P>;
     constexpr int S = Cfg::STAGES;
+    constexpr int R = Cfg::RAW_STAGES;
     constexpr int TB = UmTile<BITS>::BYTES;
     constexpr int U4_TILE = TB / 16;
     constexpr int PER_THREAD = P * U4_TILE / 128;
@@ -128,10 +136,13 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(base + S * Cfg::STAGE_BYTES);
+    uint8_t *raw = base + S * Cfg::STAGE_BYTES;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
-    uint64_t *accb = empty + S;
+    uint64_t *rawFull = empty + S;
+    uint64_t *rawEmpty = rawFull + R;
+    uint64_t *accb = rawEmpty + R;
     uint64_t *drain = accb + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -141,6 +152,10 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             mbar_init(&fullA[s], 4);
             mbar_init(&fullB[s], 1);
             mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < R; r++) {
+            mbar_init(&rawFull[r], 1);
+            mbar_init(&rawEmpty[r], 4);
         }
         mbar_init(accb, 1);
         mbar_init(drain, 1);
@@ -165,78 +180,66 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const size_t tile_base = (size_t)(e * a.RT + rt) * a.KB;
 
     if (warp < 4) {
-        // ================= converters ================================
-        const uint4 *src = reinterpret_cast<const uint4 *>(a.wq + tile_base * P * TB);
-        const __half2 *scs = a.ws + tile_base * P * UM_M;
-        uint4 cur[PER_THREAD], nxt[PER_THREAD];
-        __half2 cs[PER_THREAD], ns[PER_THREAD];
-        auto load = [&](int kb, uint4 (&q)[PER_THREAD], __half2 (&sc)[PER_THREAD]) {
-#pragma unroll
-            for (int j = 0; j < PER_THREAD; j++) {
-                const int i = tid + 128 * j;
-                const int p = i / U4_TILE, ii = i - p * U4_TILE;
-                const int row = BITS == 8 ? (ii >> 2) : (ii >> 1);
-                q[j] = __ldg(src + (size_t)kb * P * U4_TILE + i);
-                sc[j] = __ldg(scs + ((size_t)kb * P + p) * UM_M + row);
-            }
-        };
-        load(0, cur, cs);
+        // ================= converters: raw ring -> fp16 swizzled A ==========
         bool ok = true;
-        for (int kb = 0; kb < a.KB && ok; kb++) {
-            const int s = kb % S;
-            if (kb + 1 < a.KB) load(kb + 1, nxt, ns);
-            if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
+        for (int kb = 0; kb < a.KB; kb++) {
+            const int r = kb % R, s = kb % S;
+            if (!mbar_wait(&rawFull[r], (kb / R) & 1, abort_flag, UM_WAIT_CYCLES) ||
+                !mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
                 fail();
                 ok = false;
                 break;
             }
+            const uint8_t *rs = raw + r * Cfg::RAW_BYTES;
+            const __half2 *scs = reinterpret_cast<const __half2 *>(rs + Cfg::RAW_CODE);
 #pragma unroll
             for (int j = 0; j < PER_THREAD; j++) {
                 const int i = tid + 128 * j;
                 const int p = i / U4_TILE, ii = i - p * U4_TILE;
+                const uint4 q = *reinterpret_cast<const uint4 *>(rs + (size_t)i * 16);
                 const uint32_t A = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
                 if constexpr (BITS == 8) {
                     const int row = ii >> 2, c = ii & 3;
-                    const __half2 s2 = (c < 2) ? __low2half2(cs[j]) : __high2half2(cs[j]);
+                    const __half2 sc = scs[p * UM_M + row];
+                    const __half2 s2 = (c < 2) ? __low2half2(sc) : __high2half2(sc);
                     uint32_t o[8];
-                    cvt_i8x4(cur[j].x, s2, o[0], o[1]);
-                    cvt_i8x4(cur[j].y, s2, o[2], o[3]);
-                    cvt_i8x4(cur[j].z, s2, o[4], o[5]);
-                    cvt_i8x4(cur[j].w, s2, o[6], o[7]);
+                    cvt_i8x4(q.x, s2, o[0], o[1]);
+                    cvt_i8x4(q.y, s2, o[2], o[3]);
+                    cvt_i8x4(q.z, s2, o[4], o[5]);
+                    cvt_i8x4(q.w, s2, o[6], o[7]);
                     const uint32_t rowa = A + row * 128;
                     const int x7 = row & 7;
                     st_shared_v4(rowa + (((2 * c) ^ x7) << 4), o[0], o[1], o[2], o[3]);
                     st_shared_v4(rowa + (((2 * c + 1) ^ x7) << 4), o[4], o[5], o[6], o[7]);
                 } else {
                     const int row = ii >> 1, hh = ii & 1;
-                    const __half2 s2 = hh ? __high2half2(cs[j]) : __low2half2(cs[j]);
+                    const __half2 sc = scs[p * UM_M + row];
+                    const __half2 s2 = hh ? __high2half2(sc) : __low2half2(sc);
                     uint32_t o[16];
-                    cvt_i4x8(cur[j].x, s2, *reinterpret_cast<uint32_t(*)[4]>(o));
-                    cvt_i4x8(cur[j].y, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 4));
-                    cvt_i4x8(cur[j].z, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 8));
-                    cvt_i4x8(cur[j].w, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 12));
+                    cvt_i4x8(q.x, s2, *reinterpret_cast<uint32_t(*)[4]>(o));
+                    cvt_i4x8(q.y, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 4));
+                    cvt_i4x8(q.z, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 8));
+                    cvt_i4x8(q.w, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 12));
                     const uint32_t rowa = A + row * 128;
                     const int x7 = row & 7;
 #pragma unroll
-                    for (int q = 0; q < 4; q++)
-                        st_shared_v4(rowa + (((4 * hh + q) ^ x7) << 4), o[4 * q], o[4 * q + 1],
-                                     o[4 * q + 2], o[4 * q + 3]);
+                    for (int qq = 0; qq < 4; qq++)
+                        st_shared_v4(rowa + (((4 * hh + qq) ^ x7) << 4), o[4 * qq], o[4 * qq + 1],
+                                     o[4 * qq + 2], o[4 * qq + 3]);
                 }
             }
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&fullA[s]);
-#pragma unroll
-            for (int j = 0; j < PER_THREAD; j++) {
-                cur[j] = nxt[j];
-                cs[j] = ns[j];
+            if (lane == 0) {
+                mbar_arrive(&fullA[s]);
+                mbar_arrive(&rawEmpty[r]);
             }
         }
 
         // ================= epilogue ================================
         if (ok && mbar_wait(accb, 0, abort_flag, UM_WAIT_CYCLES)) {
             tc_fence_after();
-            const int r = warp * 32 + lane;
+            const int rr = warp * 32 + lane;
             const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
             for (int c0 = 0; c0 < N; c0 += 32) {
                 float g[32];
@@ -244,7 +247,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 if constexpr (P == 2) {
                     float u[32];
                     tmem_ld32(lane_addr + 128 + c0, u);
-                    __half *dst = a.h_out + (size_t)slot0 * a.h_stride + rt * UM_M + r;
+                    __half *dst = a.h_out + (size_t)slot0 * a.h_stride + rt * UM_M + rr;
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int t = c0 + j;
@@ -255,7 +258,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                         }
                     }
                 } else {
-                    float *dst = a.d_out + (size_t)slot0 * a.d_stride + rt * UM_M + r;
+                    float *dst = a.d_out + (size_t)slot0 * a.d_stride + rt * UM_M + rr;
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int t = c0 + j;
@@ -267,7 +270,31 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             fail();
         }
     } else if (warp == 4) {
-        // ================= TMA producer (activation tiles) ================
+        // ================= code/scale producer (bulk TMA) ================
+        if (lane == 0) {
+            const uint8_t *codes = a.wq + tile_base * P * TB;
+            const __half2 *scales = a.ws + tile_base * P * UM_M;
+            int issued = -1;
+            for (int kb = 0; kb < a.KB; kb++) {
+                const int r = kb % R;
+                if (!mbar_wait(&rawEmpty[r], ((kb / R) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
+                    fail();
+                    break;
+                }
+                uint8_t *dst = raw + r * Cfg::RAW_BYTES;
+                mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
+                bulk_load(dst, codes + (size_t)kb * P * TB, Cfg::RAW_CODE, &rawFull[r]);
+                bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * P * UM_M, P * UM_M * 4,
+                          &rawFull[r]);
+                issued = kb;
+            }
+            if (*abort_flag && issued >= 0) {
+                volatile int never = 0;
+                mbar_wait(&rawFull[issued % R], (issued / R) & 1, &never, UM_WAIT_CYCLES);
+            }
+        }
+    } else if (warp == 6) {
+        // ================= activation producer (tiled TMA) ================
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
             int issued = -1;
@@ -283,13 +310,12 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 issued = kb;
             }
             if (*abort_flag && issued >= 0) {
-                // let our own last copy land before the CTA's smem goes away
                 volatile int never = 0;
                 mbar_wait(&fullB[issued % S], (issued / S) & 1, &never, UM_WAIT_CYCLES);
             }
         }
     } else {
-        // ================= MMA issuer ================================
+        // ================= MMA issuer (warp 5) ================================
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(UM_M, N);
             bool ok = true;
@@ -317,7 +343,6 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             if (ok) {
                 umma_commit(accb);
             } else {
-                // drain our own UMMAs before TMEM is released
                 umma_commit(drain);
                 volatile int never = 0;
                 mbar_wait(drain, 0, &never, UM_WAIT_CYCLES);
@@ -455,7 +480,7 @@ int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int
 
 template <int BITS, int P>
 static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStream_t s) {
-    using Cfg = UmCfg<P>;
+    using Cfg = UmCfg<BITS, P>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool done[64] = {false};
