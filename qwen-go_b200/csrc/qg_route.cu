@@ -1,5 +1,6 @@
-// Router + dispatch (kernels K1 and K2), three launches for any token count.
+// Router + dispatch (kernels K1 and K2).
 //
+// Launches: k_logits, k_topk, k_scatter (+ k_gather_f16 for the tensor path).
 // 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...), model/moe.go:42)
 //    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 32 tokens x 128
 //    router rows x one K slice, writes its partial sums.  The shared-expert
@@ -17,8 +18,8 @@
 // 3. k_scatter: each CTA ranks its own (token, rank) pairs per expert in pair
 //    order (warp match + per-warp counts) and adds the histograms of the CTAs
 //    before it, so slots are expert-sorted and deterministic without a serial
-//    pass.  With `xp` set it also writes the slot's fp16 activation row for
-//    the tensor-core path.
+//    pass.  For the tensor-core path k_gather_f16 then writes each slot's fp16
+//    activation row.
 #include "qg_common.cuh"
 
 namespace qg {
@@ -26,7 +27,9 @@ namespace qg {
 constexpr int LG_TOK = 32;   // tokens per logits tile
 constexpr int LG_ROWS = 128; // router rows per logits tile
 constexpr int LG_KC = 32;    // K chunk staged in shared memory
-constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA (8 warps x 4)
+constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA
+constexpr int RT_THREADS = 1024;  // top-k and scatter CTAs: one warp per token
+constexpr int RT_WARPS = RT_THREADS / 32;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -126,18 +129,18 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
 // A warp holds one token's probabilities in registers: lane l owns experts
 // l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
 template <int NJ>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(RT_THREADS)
 k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, int mode,
        int has_shared, RouteState st, int *err) {
     extern __shared__ int hist_s[];  // [E]
-    __shared__ int s_idx[8][QG_MAX_TOPK];
+    __shared__ int s_idx[RT_WARPS][QG_MAX_TOPK];
     __shared__ int s_last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e < E; e += 256) hist_s[e] = 0;
+    for (int e = tid; e < E; e += RT_THREADS) hist_s[e] = 0;
     __syncthreads();
 
-    for (int i = 0; i < TK_TOK / 8; i++) {
-        const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / 8) + i;
+    for (int i = 0; i < TK_TOK / RT_WARPS; i++) {
+        const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / RT_WARPS) + i;
         if (t >= T) break;
         float v[NJ];
 #pragma unroll
@@ -240,7 +243,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
         __syncwarp();
     }
     __syncthreads();
-    for (int e = tid; e < E; e += 256) {
+    for (int e = tid; e < E; e += RT_THREADS) {
         const int c = hist_s[e];
         st.hist[(size_t)blockIdx.x * E + e] = c;
         if (c) atomicAdd(&st.counts[e], c);
@@ -254,7 +257,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
     if (!s_last) return;
     __threadfence();
     int *cnt = hist_s;
-    for (int e = tid; e < E; e += 256) {
+    for (int e = tid; e < E; e += RT_THREADS) {
         cnt[e] = __ldcg(st.counts + e);
         st.counts[e] = 0;
     }
@@ -310,21 +313,21 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
 }
 
 // ---- 3. scatter (+ fp16 gather) ---------------------------------------------------
-__global__ void __launch_bounds__(256)
-k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_shared, RouteState st,
-          __half *__restrict__ xp, int *err) {
+__global__ void __launch_bounds__(RT_THREADS)
+k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
     extern __shared__ int sm[];
     int *cur = sm;            // [E] next slot per expert for this CTA
-    int *wcnt = sm + E;       // [8][E]
-    __shared__ int partial[256];
+    int *wcnt = sm + E;       // [RT_WARPS][E]
+    __shared__ int partial[RT_THREADS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int c = blockIdx.x;
     // Slots of this CTA's pairs start after the earlier CTAs' pairs of the
     // same expert: sum histogram rows 0..c-1, split over nparts threads per
     // expert with independent accumulators so the loads overlap.
-    const int nparts = E >= 256 ? 1 : 256 / E;
-    for (int e0 = 0; e0 < E; e0 += 256) {
-        const int idx = tid, e = e0 + idx % (E >= 256 ? 256 : E), part = idx / (E >= 256 ? 256 : E);
+    const int nparts = E >= RT_THREADS ? 1 : RT_THREADS / E;
+    for (int e0 = 0; e0 < E; e0 += RT_THREADS) {
+        const int stride = E >= RT_THREADS ? RT_THREADS : E;
+        const int e = e0 + tid % stride, part = tid / stride;
         int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
         if (e < E && part < nparts) {
             const int per = (c + nparts - 1) / nparts;
@@ -340,9 +343,8 @@ k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_share
         }
         partial[tid] = acc0 + acc1 + acc2 + acc3;
         __syncthreads();
-        if (tid < (E - e0 < 256 ? E - e0 : 256) && e0 + tid < E) {
+        if (tid < stride && e0 + tid < E) {
             const int ee = e0 + tid;
-            const int stride = E >= 256 ? 256 : E;
             int base = st.expert_off[ee];
             for (int pp = 0; pp < nparts; pp++) base += partial[pp * stride + tid];
             cur[ee] = base;
@@ -352,8 +354,8 @@ k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_share
     const int p0 = c * TK_TOK * k;
     const int p1 = min(T * k, p0 + TK_TOK * k);
     const unsigned lt = (1u << lane) - 1u;
-    for (int base = p0; base < p1; base += 256) {
-        for (int i = tid; i < 8 * E; i += 256) wcnt[i] = 0;
+    for (int base = p0; base < p1; base += RT_THREADS) {
+        for (int i = tid; i < RT_WARPS * E; i += RT_THREADS) wcnt[i] = 0;
         __syncthreads();
         const int pi = base + tid;
         int e = -1;
@@ -379,31 +381,16 @@ k_scatter(const float *__restrict__ x, int T, int H, int E, int k, int has_share
             }
         }
         __syncthreads();
-        for (int ee = tid; ee < E; ee += 256) {
+        for (int ee = tid; ee < E; ee += RT_THREADS) {
             int add = 0;
-            for (int w = 0; w < 8; w++) add += wcnt[w * E + ee];
+            for (int w = 0; w < RT_WARPS; w++) add += wcnt[w * E + ee];
             cur[ee] += add;
         }
         __syncthreads();
     }
     if (has_shared)
-        for (int t = c * TK_TOK + tid; t < min(T, (c + 1) * TK_TOK); t += 256)
+        for (int t = c * TK_TOK + tid; t < min(T, (c + 1) * TK_TOK); t += RT_THREADS)
             st.slot_token[T * k + t] = t;
-    if (!xp) return;
-    // fp16 activation rows for the tensor-core path: one warp per pair
-    for (int pi = p0 + warp; pi < p1; pi += 8) {
-        const int slot = st.pair_slot[pi];
-        if (slot < 0 || slot >= T * k) continue;
-        const float *src = x + (size_t)(pi / k) * H;
-        __half *dst = xp + (size_t)slot * H;
-        for (int kk = lane * 8; kk < H; kk += 256) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(src + kk);
-            const float4 v1 = *reinterpret_cast<const float4 *>(src + kk + 4);
-            __half2 h[4] = {__floats2half2_rn(v0.x, v0.y), __floats2half2_rn(v0.z, v0.w),
-                            __floats2half2_rn(v1.x, v1.y), __floats2half2_rn(v1.z, v1.w)};
-            *reinterpret_cast<uint4 *>(dst + kk) = *reinterpret_cast<uint4 *>(h);
-        }
-    }
 }
 
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
@@ -418,28 +405,29 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     QG_CUDA(cudaGetLastError());
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
-    const size_t sm3 = sizeof(int) * (size_t)9 * E;
+    const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
     static bool attr[64] = {false};
     if (dev < 64 && !attr[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        QG_CUDA(cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
         attr[dev] = true;
     }
     const int nj = (E + 31) / 32;
     if (nj <= 1)
-        k_topk<1><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<1><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 2)
-        k_topk<2><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<2><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 4)
-        k_topk<4><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<4><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 8)
-        k_topk<8><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<8><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 16)
-        k_topk<16><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<16><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     else
-        k_topk<32><<<nc, 256, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<32><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
     QG_CUDA(cudaGetLastError());
-    k_scatter<<<nc, 256, sm3, s>>>(x, T, H, E, k, has_shared, st, xp, err);
+    k_scatter<<<nc, RT_THREADS, sm3, s>>>(T, E, k, has_shared, st, err);
     QG_CUDA(cudaGetLastError());
+    if (xp) return launch_gather_f16(x, st.slot_token, T * k, H, xp, s);
     return QGMOE_OK;
 }
 

@@ -32,7 +32,9 @@
 namespace qg {
 using namespace sm100;
 
-constexpr int UM_THREADS = 224;  // warps 0-3 dequant+epilogue, 4 code TMA, 5 MMA, 6 act TMA
+constexpr int UM_THREADS = 352;  // warps 0-7 dequant (0-3 also epilogue), 8 code TMA, 9 MMA, 10 act TMA
+constexpr int UM_CONV = 256;     // converter threads
+constexpr int UM_CONV_WARPS = UM_CONV / 32;
 constexpr int UM_M = 128;        // weight rows per tile
 constexpr int UM_N = 128;        // max tokens per tile
 constexpr int UM_BK = 64;        // K elements per stage (one 128-byte fp16 row)
@@ -61,9 +63,9 @@ struct UmCfg {
     static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-// int8 x4 -> two fp16x2 (q * s), exact codes then one correctly rounded product.
-__device__ __forceinline__ void cvt_i8x4(uint32_t w, __half2 s2, uint32_t &o0, uint32_t &o1) {
-    const uint32_t u = w ^ 0x80808080u;
+// int8 x4 stored biased (q + 128, repacked at create time) -> two fp16x2
+// (q * s): exact codes, then one correctly rounded product.
+__device__ __forceinline__ void cvt_i8x4(uint32_t u, __half2 s2, uint32_t &o0, uint32_t &o1) {
     const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
     uint32_t p0 = __byte_perm(u, 0x64646464u, 0x4140);
     uint32_t p1 = __byte_perm(u, 0x64646464u, 0x4342);
@@ -75,14 +77,11 @@ __device__ __forceinline__ void cvt_i8x4(uint32_t w, __half2 s2, uint32_t &o0, u
 
 // int4 word in the repacked nibble order (element 2j in bits [4j, 4j+4),
 // element 2j+1 in bits [16+4j, 20+4j)) -> four fp16x2 ((code - 8) * s).
-__device__ __forceinline__ void cvt_i4x8(uint32_t w, __half2 s2, uint32_t (&o)[4]) {
+__device__ __forceinline__ uint32_t cvt_i4_pair(uint32_t w, int j, __half2 s2) {
     const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-        __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), bias), s2);
-        o[j] = *reinterpret_cast<uint32_t *>(&h);
-    }
+    uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+    __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), bias), s2);
+    return *reinterpret_cast<uint32_t *>(&h);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -112,7 +111,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     constexpr int R = Cfg::RAW_STAGES;
     constexpr int TB = UmTile<BITS>::BYTES;
     constexpr int U4_TILE = TB / 16;
-    constexpr int PER_THREAD = P * U4_TILE / 128;
+    constexpr int PER_THREAD = P * U4_TILE / UM_CONV;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -149,20 +148,20 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&fullA[s], 4);
+            mbar_init(&fullA[s], UM_CONV_WARPS);
             mbar_init(&fullB[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < R; r++) {
             mbar_init(&rawFull[r], 1);
-            mbar_init(&rawEmpty[r], 4);
+            mbar_init(&rawEmpty[r], UM_CONV_WARPS);
         }
         mbar_init(accb, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
@@ -179,7 +178,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     };
     const size_t tile_base = (size_t)(e * a.RT + rt) * a.KB;
 
-    if (warp < 4) {
+    if (warp < UM_CONV_WARPS) {
         // ================= converters: raw ring -> fp16 swizzled A ==========
         bool ok = true;
         for (int kb = 0; kb < a.KB; kb++) {
@@ -194,7 +193,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             const __half2 *scs = reinterpret_cast<const __half2 *>(rs + Cfg::RAW_CODE);
 #pragma unroll
             for (int j = 0; j < PER_THREAD; j++) {
-                const int i = tid + 128 * j;
+                const int i = tid + UM_CONV * j;
                 const int p = i / U4_TILE, ii = i - p * U4_TILE;
                 const uint4 q = *reinterpret_cast<const uint4 *>(rs + (size_t)i * 16);
                 const uint32_t A = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
@@ -215,17 +214,14 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                     const int row = ii >> 1, hh = ii & 1;
                     const __half2 sc = scs[p * UM_M + row];
                     const __half2 s2 = hh ? __high2half2(sc) : __low2half2(sc);
-                    uint32_t o[16];
-                    cvt_i4x8(q.x, s2, *reinterpret_cast<uint32_t(*)[4]>(o));
-                    cvt_i4x8(q.y, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 4));
-                    cvt_i4x8(q.z, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 8));
-                    cvt_i4x8(q.w, s2, *reinterpret_cast<uint32_t(*)[4]>(o + 12));
                     const uint32_t rowa = A + row * 128;
                     const int x7 = row & 7;
+                    const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                     for (int qq = 0; qq < 4; qq++)
-                        st_shared_v4(rowa + (((4 * hh + qq) ^ x7) << 4), o[4 * qq], o[4 * qq + 1],
-                                     o[4 * qq + 2], o[4 * qq + 3]);
+                        st_shared_v4(rowa + (((4 * hh + qq) ^ x7) << 4), cvt_i4_pair(wv[qq], 0, s2),
+                                     cvt_i4_pair(wv[qq], 1, s2), cvt_i4_pair(wv[qq], 2, s2),
+                                     cvt_i4_pair(wv[qq], 3, s2));
                 }
             }
             fence_proxy_async_smem();
@@ -236,8 +232,10 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             }
         }
 
-        // ================= epilogue ================================
-        if (ok && mbar_wait(accb, 0, abort_flag, UM_WAIT_CYCLES)) {
+        // ================= epilogue (warps 0-3 own TMEM lanes 0-127) =======
+        if (warp >= 4) {
+            // converter-only warps
+        } else if (ok && mbar_wait(accb, 0, abort_flag, UM_WAIT_CYCLES)) {
             tc_fence_after();
             const int rr = warp * 32 + lane;
             const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
@@ -269,7 +267,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         } else {
             fail();
         }
-    } else if (warp == 4) {
+    } else if (warp == 8) {
         // ================= code/scale producer (bulk TMA) ================
         if (lane == 0) {
             const uint8_t *codes = a.wq + tile_base * P * TB;
@@ -293,7 +291,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 mbar_wait(&rawFull[issued % R], (issued / R) & 1, &never, UM_WAIT_CYCLES);
             }
         }
-    } else if (warp == 6) {
+    } else if (warp == 10) {
         // ================= activation producer (tiled TMA) ================
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
@@ -315,7 +313,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             }
         }
     } else {
-        // ================= MMA issuer (warp 5) ================================
+        // ================= MMA issuer (warp 9) ================================
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(UM_M, N);
             bool ok = true;
@@ -352,7 +350,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
@@ -404,8 +402,15 @@ __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict
     const int64_t tile = (((int64_t)e * RT + rt) * KB + kb) * P + p;
     uint8_t *d = qo + tile * (UM_M * blk_bytes) + (int64_t)row * blk_bytes;
     if (bits == 8) {
-        for (int b = 0; b < blk_bytes; b += 16)
-            *reinterpret_cast<uint4 *>(d + b) = *reinterpret_cast<const uint4 *>(s + b);
+        // stored biased (q + 128): the converter splices bytes under 0x64
+        for (int b = 0; b < blk_bytes; b += 16) {
+            uint4 v = *reinterpret_cast<const uint4 *>(s + b);
+            v.x ^= 0x80808080u;
+            v.y ^= 0x80808080u;
+            v.z ^= 0x80808080u;
+            v.w ^= 0x80808080u;
+            *reinterpret_cast<uint4 *>(d + b) = v;
+        }
     } else {
         for (int w = 0; w < blk_bytes / 4; w++) {
             uint32_t src = *reinterpret_cast<const uint32_t *>(s + 4 * w);
