@@ -12,6 +12,28 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---- explicit shared-memory accesses (32-bit shared addresses) ---------------
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ int ld_volatile_shared(uint32_t addr) {
+    int v;
+    asm volatile("ld.volatile.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_volatile_shared(uint32_t addr, int v) {
+    asm volatile("st.volatile.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // ---- mbarrier ----------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -39,13 +61,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: returns false after ~`budget` clock cycles (or when *abort
-// is set by another role), so a lost arrival can never hang the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort, long long budget) {
+// Bounded wait: returns false after ~`budget` clock cycles (or when the
+// shared abort word at `abort_addr` is set by another role), so a lost
+// arrival can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t abort_addr,
+                                          long long budget) {
+    if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (*abort) return false;
+        if (abort_addr && ld_volatile_shared(abort_addr)) return false;
         if (clock64() - t0 > budget) return false;
     }
     return true;

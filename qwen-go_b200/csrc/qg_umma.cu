@@ -1,14 +1,17 @@
 // Grouped expert GEMMs on the 5th-generation tensor cores (kernels K3'/K4',
-// prefill-sized token counts).
+// prefill-sized token counts; also used for decode batches when forced).
 //
-// Swap-AB formulation per (expert e, 128-row weight tile, <=128-token tile):
+// Swap-AB formulation per work unit (expert e, 128-row weight tile, <=128
+// token tile):
 //   D[rows, tokens] = W[rows, K] * X[tokens, K]^T      (tcgen05.mma kind::f16)
 // A = expert weights, dequantised from int8/int4 group-32 codes with fp16
-//     scales (model/moe.go:134-157) by four converter warps straight into the
-//     128B-swizzled UMMA layout in shared memory;
-// B = the expert's token rows in fp16, brought in by TMA (SWIZZLE_128B box);
-// D = fp32 accumulators in TMEM, read back by the converter warps after the
-//     K loop (tcgen05.ld) for the epilogue.
+//     scales (model/moe.go:134-157) by eight converter warps straight into
+//     the 128B-swizzled UMMA layout in shared memory; the raw codes and
+//     scales arrive through a deep ring of bulk TMA copies;
+// B = the expert's token rows in fp16, brought in by tiled TMA (SWIZZLE_128B);
+// D = fp32 accumulators in TMEM, double-buffered: a dedicated epilogue
+//     warpgroup drains one buffer (tcgen05.ld) while the next unit
+//     accumulates into the other.
 //
 // GEMM1 (P = 2): the gate rows [r, r+128) and the matching up rows
 // [I + r, I + r + 128) (model/moe.go:70-71) accumulate side by side in TMEM,
@@ -17,11 +20,12 @@
 // GEMM2 (P = 1): D = W_down * h^T (model/moe.go:77-81), written as f32 d
 // rows for the rank-ordered combine.
 //
-// Pipeline (per CTA): STAGES shared-memory stages of (A tiles, B tile); the
-// TMA warp and the converter warps fill a stage and signal fullB/fullA; one
-// elected thread issues the UMMAs and tcgen05.commit frees the stage.  Every
-// mbarrier wait is bounded (clock64 budget); on timeout the CTA raises
-// QG_FLAG_TIMEOUT, drains its own TMA loads and UMMAs, frees TMEM and exits.
+// The kernel is persistent (one CTA per SM, static stride over work units)
+// and warp-specialised: converters, epilogue, code producer, MMA issuer and
+// activation producer each run their own loop over the same unit sequence,
+// coupled only by mbarriers.  Every mbarrier wait is bounded (clock64 budget);
+// on timeout the CTA raises QG_FLAG_TIMEOUT, drains its own TMA loads and
+// UMMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
 #include <cstdio>
@@ -32,9 +36,14 @@
 namespace qg {
 using namespace sm100;
 
-constexpr int UM_THREADS = 352;  // warps 0-7 dequant (0-3 also epilogue), 8 code TMA, 9 MMA, 10 act TMA
-constexpr int UM_CONV = 256;     // converter threads
-constexpr int UM_CONV_WARPS = UM_CONV / 32;
+// Warp roles of the persistent CTA (one per SM).
+constexpr int UM_CONV_WARPS = 8;   // warps 0-7: dequantise codes into swizzled fp16 A tiles
+constexpr int UM_EPI_WARP0 = 8;    // warps 8-11: epilogue (TMEM lanes 0-127, one warp each)
+constexpr int UM_CODE_WARP = 12;   // bulk TMA of raw codes + scales
+constexpr int UM_MMA_WARP = 13;    // TMEM alloc + UMMA issue
+constexpr int UM_ACT_WARP = 14;    // tiled TMA of the activation (B) tiles
+constexpr int UM_THREADS = 15 * 32;
+constexpr int UM_CONV = UM_CONV_WARPS * 32;
 constexpr int UM_M = 128;        // weight rows per tile
 constexpr int UM_N = 128;        // max tokens per tile
 constexpr int UM_BK = 64;        // K elements per stage (one 128-byte fp16 row)
@@ -48,6 +57,8 @@ struct UmTile {
 // Shared memory: S stages of (P fp16 A tiles + B tile) consumed by the MMA,
 // and R stages of raw codes + scales brought in by bulk TMA copies for the
 // converters (the deep ring hides the DRAM latency of the weight stream).
+// TMEM: two accumulator buffers (P x 128 columns each) so the epilogue of
+// one tile overlaps the next tile's K loop.
 template <int BITS, int P>
 struct UmCfg {
     static constexpr int STAGES = P == 2 ? 3 : 4;
@@ -57,8 +68,9 @@ struct UmCfg {
     static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
     static constexpr int RAW_CODE = P * UmTile<BITS>::BYTES;
     static constexpr int RAW_BYTES = RAW_CODE + P * UM_M * 4;
-    static constexpr int TMEM_COLS = P == 2 ? 256 : 128;
-    static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 2) + 16;
+    static constexpr int ACC_COLS = P * 128;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 5) + 16;
     static constexpr int SMEM = STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -76,7 +88,7 @@ __device__ __forceinline__ void cvt_i8x4(uint32_t u, __half2 s2, uint32_t &o0, u
 }
 
 // int4 word in the repacked nibble order (element 2j in bits [4j, 4j+4),
-// element 2j+1 in bits [16+4j, 20+4j)) -> four fp16x2 ((code - 8) * s).
+// element 2j+1 in bits [16+4j, 20+4j)) -> fp16x2 ((code - 8) * s) of pair j.
 __device__ __forceinline__ uint32_t cvt_i4_pair(uint32_t w, int j, __half2 s2) {
     const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
     uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
@@ -91,6 +103,20 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
 struct UmmaArgs {
     const uint8_t *wq;    // packed codes [E][RT][KB][P][tile]
     const __half2 *ws;    // packed scales [E][RT][KB][P][128] (2 groups per row)
@@ -102,6 +128,27 @@ struct UmmaArgs {
     int d_stride;
     int *err;
 };
+
+// Decodes work unit u = (token tile, row tile) of the routed groups.
+struct Unit {
+    int e, rt, slot0, nval, N;
+};
+__device__ __forceinline__ Unit decode_unit(const UmmaArgs &a, int n_act, int u) {
+    Unit w;
+    const int ti = u / a.RT;
+    w.rt = u - ti * a.RT;
+    int lo = 0, hi = n_act - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.tile_prefix[mid] <= ti) lo = mid; else hi = mid - 1;
+    }
+    w.e = a.act_group[lo];
+    const int tt = ti - a.tile_prefix[lo];
+    w.slot0 = a.act_begin[lo] + tt * UM_N;
+    w.nval = min(UM_N, a.act_n[lo] - tt * UM_N);
+    w.N = (w.nval + 15) & ~15;
+    return w;
+}
 
 template <int BITS, int P>
 __global__ void __launch_bounds__(UM_THREADS, 1)
@@ -115,36 +162,25 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    // ---- work unit: (active expert, token tile, row tile) -----------------
     const int n_act = *a.n_act;
-    const int total_tiles = a.tile_prefix[n_act];
-    const int unit = blockIdx.x;
-    if (unit >= total_tiles * a.RT) return;
-    const int ti = unit / a.RT, rt = unit - ti * a.RT;
-    int lo = 0, hi = n_act - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (a.tile_prefix[mid] <= ti) lo = mid; else hi = mid - 1;
-    }
-    const int e = a.act_group[lo];
-    const int tt = ti - a.tile_prefix[lo];
-    const int slot0 = a.act_begin[lo] + tt * UM_N;
-    const int nval = min(UM_N, a.act_n[lo] - tt * UM_N);
-    const int N = (nval + 15) & ~15;
+    const int n_units = a.tile_prefix[n_act] * a.RT;
+    if ((int)blockIdx.x >= n_units) return;
 
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t base_u32 = smem_u32(base);
     uint8_t *raw = base + S * Cfg::STAGE_BYTES;
+    const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_BYTES;
     uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
     uint64_t *rawFull = empty + S;
     uint64_t *rawEmpty = rawFull + R;
-    uint64_t *accb = rawEmpty + R;
-    uint64_t *drain = accb + 1;
+    uint64_t *accFull = rawEmpty + R;   // [2]
+    uint64_t *accEmpty = accFull + 2;   // [2]
+    uint64_t *drain = accEmpty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const uint32_t abort_addr = smem_u32(tmem_slot + 1);
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
@@ -156,12 +192,15 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             mbar_init(&rawFull[r], 1);
             mbar_init(&rawEmpty[r], UM_CONV_WARPS);
         }
-        mbar_init(accb, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accFull[b], 1);
+            mbar_init(&accEmpty[b], 4);
+        }
         mbar_init(drain, 1);
-        *abort_flag = 0;
+        st_volatile_shared(abort_addr, 0);
         fence_mbar_init();
     }
-    if (warp == 9) {
+    if (warp == UM_MMA_WARP) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
@@ -171,186 +210,220 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const uint32_t tmem = *tmem_slot;
 
     auto fail = [&]() {
-        if (!*abort_flag) {
-            *abort_flag = 1;
+        if (!ld_volatile_shared(abort_addr)) {
+            st_volatile_shared(abort_addr, 1);
             atomicOr(a.err, QG_FLAG_TIMEOUT);
         }
     };
-    const size_t tile_base = (size_t)(e * a.RT + rt) * a.KB;
 
     if (warp < UM_CONV_WARPS) {
-        // ================= converters: raw ring -> fp16 swizzled A ==========
+        // ============ converters: raw ring -> fp16 swizzled A tiles ==========
+        int g = 0;  // running k-block counter across this CTA's tiles
         bool ok = true;
-        for (int kb = 0; kb < a.KB; kb++) {
-            const int r = kb % R, s = kb % S;
-            if (!mbar_wait(&rawFull[r], (kb / R) & 1, abort_flag, UM_WAIT_CYCLES) ||
-                !mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
-                fail();
-                ok = false;
-                break;
-            }
-            const uint8_t *rs = raw + r * Cfg::RAW_BYTES;
-            const __half2 *scs = reinterpret_cast<const __half2 *>(rs + Cfg::RAW_CODE);
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            for (int kb = 0; kb < a.KB; kb++, g++) {
+                const int r = g % R, s = g % S;
+                if (!mbar_wait(&rawFull[r], (g / R) & 1, abort_addr, UM_WAIT_CYCLES) ||
+                    !mbar_wait(&empty[s], ((g / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                const uint32_t rs = raw_u32 + r * Cfg::RAW_BYTES;
+                const uint32_t A0 = base_u32 + s * Cfg::STAGE_BYTES;
 #pragma unroll
-            for (int j = 0; j < PER_THREAD; j++) {
-                const int i = tid + UM_CONV * j;
-                const int p = i / U4_TILE, ii = i - p * U4_TILE;
-                const uint4 q = *reinterpret_cast<const uint4 *>(rs + (size_t)i * 16);
-                const uint32_t A = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
-                if constexpr (BITS == 8) {
-                    const int row = ii >> 2, c = ii & 3;
-                    const __half2 sc = scs[p * UM_M + row];
-                    const __half2 s2 = (c < 2) ? __low2half2(sc) : __high2half2(sc);
-                    uint32_t o[8];
-                    cvt_i8x4(q.x, s2, o[0], o[1]);
-                    cvt_i8x4(q.y, s2, o[2], o[3]);
-                    cvt_i8x4(q.z, s2, o[4], o[5]);
-                    cvt_i8x4(q.w, s2, o[6], o[7]);
-                    const uint32_t rowa = A + row * 128;
-                    const int x7 = row & 7;
-                    st_shared_v4(rowa + (((2 * c) ^ x7) << 4), o[0], o[1], o[2], o[3]);
-                    st_shared_v4(rowa + (((2 * c + 1) ^ x7) << 4), o[4], o[5], o[6], o[7]);
-                } else {
-                    const int row = ii >> 1, hh = ii & 1;
-                    const __half2 sc = scs[p * UM_M + row];
-                    const __half2 s2 = hh ? __high2half2(sc) : __low2half2(sc);
-                    const uint32_t rowa = A + row * 128;
-                    const int x7 = row & 7;
-                    const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                    for (int qq = 0; qq < 4; qq++)
-                        st_shared_v4(rowa + (((4 * hh + qq) ^ x7) << 4), cvt_i4_pair(wv[qq], 0, s2),
-                                     cvt_i4_pair(wv[qq], 1, s2), cvt_i4_pair(wv[qq], 2, s2),
-                                     cvt_i4_pair(wv[qq], 3, s2));
+                for (int j = 0; j < PER_THREAD; j++) {
+                    const int i = tid + UM_CONV * j;
+                    const int p = i / U4_TILE, ii = i - p * U4_TILE;
+                    const uint4 q = ld_shared_v4(rs + i * 16);
+                    const uint32_t A = A0 + p * Cfg::A_BYTES;
+                    if constexpr (BITS == 8) {
+                        const int row = ii >> 2, c = ii & 3;
+                        uint32_t scw = ld_shared_u32(rs + Cfg::RAW_CODE + (p * UM_M + row) * 4);
+                        const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
+                        const __half2 s2 = (c < 2) ? __low2half2(sc) : __high2half2(sc);
+                        uint32_t o[8];
+                        cvt_i8x4(q.x, s2, o[0], o[1]);
+                        cvt_i8x4(q.y, s2, o[2], o[3]);
+                        cvt_i8x4(q.z, s2, o[4], o[5]);
+                        cvt_i8x4(q.w, s2, o[6], o[7]);
+                        const uint32_t rowa = A + row * 128;
+                        const int x7 = row & 7;
+                        st_shared_v4(rowa + (((2 * c) ^ x7) << 4), o[0], o[1], o[2], o[3]);
+                        st_shared_v4(rowa + (((2 * c + 1) ^ x7) << 4), o[4], o[5], o[6], o[7]);
+                    } else {
+                        const int row = ii >> 1, hh = ii & 1;
+                        uint32_t scw = ld_shared_u32(rs + Cfg::RAW_CODE + (p * UM_M + row) * 4);
+                        const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
+                        const __half2 s2 = hh ? __high2half2(sc) : __low2half2(sc);
+                        const uint32_t rowa = A + row * 128;
+                        const int x7 = row & 7;
+                        st_shared_v4(rowa + (((4 * hh + 0) ^ x7) << 4), cvt_i4_pair(q.x, 0, s2),
+                                     cvt_i4_pair(q.x, 1, s2), cvt_i4_pair(q.x, 2, s2),
+                                     cvt_i4_pair(q.x, 3, s2));
+                        st_shared_v4(rowa + (((4 * hh + 1) ^ x7) << 4), cvt_i4_pair(q.y, 0, s2),
+                                     cvt_i4_pair(q.y, 1, s2), cvt_i4_pair(q.y, 2, s2),
+                                     cvt_i4_pair(q.y, 3, s2));
+                        st_shared_v4(rowa + (((4 * hh + 2) ^ x7) << 4), cvt_i4_pair(q.z, 0, s2),
+                                     cvt_i4_pair(q.z, 1, s2), cvt_i4_pair(q.z, 2, s2),
+                                     cvt_i4_pair(q.z, 3, s2));
+                        st_shared_v4(rowa + (((4 * hh + 3) ^ x7) << 4), cvt_i4_pair(q.w, 0, s2),
+                                     cvt_i4_pair(q.w, 1, s2), cvt_i4_pair(q.w, 2, s2),
+                                     cvt_i4_pair(q.w, 3, s2));
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&fullA[s]);
+                    mbar_arrive(&rawEmpty[r]);
                 }
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&fullA[s]);
-                mbar_arrive(&rawEmpty[r]);
-            }
         }
-
-        // ================= epilogue (warps 0-3 own TMEM lanes 0-127) =======
-        if (warp >= 4) {
-            // converter-only warps
-        } else if (ok && mbar_wait(accb, 0, abort_flag, UM_WAIT_CYCLES)) {
+    } else if (warp < UM_EPI_WARP0 + 4) {
+        // ============ epilogue: TMEM -> SwiGLU / store ============================
+        const int ew = warp - UM_EPI_WARP0;  // TMEM lane quarter
+        const int rr = ew * 32 + lane;
+        int lt = 0;
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, lt++) {
+            const int buf = lt & 1;
+            if (!mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES)) {
+                fail();
+                break;
+            }
             tc_fence_after();
-            const int rr = warp * 32 + lane;
-            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-            for (int c0 = 0; c0 < N; c0 += 32) {
-                float g[32];
-                tmem_ld32(lane_addr + c0, g);
+            const Unit w = decode_unit(a, n_act, u);
+            const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
+            for (int c0 = 0; c0 < w.N; c0 += 16) {
+                float gv[16];
+                tmem_ld16(lane_addr + c0, gv);
                 if constexpr (P == 2) {
-                    float u[32];
-                    tmem_ld32(lane_addr + 128 + c0, u);
-                    __half *dst = a.h_out + (size_t)slot0 * a.h_stride + rt * UM_M + rr;
+                    float uv[16];
+                    tmem_ld16(lane_addr + 128 + c0, uv);
+                    __half *dst = a.h_out + (size_t)w.slot0 * a.h_stride + w.rt * UM_M + rr;
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
+                    for (int j = 0; j < 16; j++) {
                         const int t = c0 + j;
-                        if (t < nval) {
-                            const float gv = g[j];
-                            const float hv = gv / (1.f + expf(-gv)) * u[j];
-                            dst[(size_t)t * a.h_stride] = __float2half_rn(hv);
+                        if (t < w.nval) {
+                            const float x = gv[j];
+                            dst[(size_t)t * a.h_stride] = __float2half_rn(x / (1.f + expf(-x)) * uv[j]);
                         }
                     }
                 } else {
-                    float *dst = a.d_out + (size_t)slot0 * a.d_stride + rt * UM_M + rr;
+                    float *dst = a.d_out + (size_t)w.slot0 * a.d_stride + w.rt * UM_M + rr;
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
+                    for (int j = 0; j < 16; j++) {
                         const int t = c0 + j;
-                        if (t < nval) dst[(size_t)t * a.d_stride] = g[j];
+                        if (t < w.nval) dst[(size_t)t * a.d_stride] = gv[j];
                     }
                 }
             }
-        } else {
-            fail();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accEmpty[buf]);
         }
-    } else if (warp == 8) {
-        // ================= code/scale producer (bulk TMA) ================
+    } else if (warp == UM_CODE_WARP) {
+        // ============ code/scale producer (bulk TMA) ==============================
         if (lane == 0) {
-            const uint8_t *codes = a.wq + tile_base * P * TB;
-            const __half2 *scales = a.ws + tile_base * P * UM_M;
-            int issued = -1;
-            for (int kb = 0; kb < a.KB; kb++) {
-                const int r = kb % R;
-                if (!mbar_wait(&rawEmpty[r], ((kb / R) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
-                    fail();
-                    break;
+            int g = 0, last = -1;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const Unit w = decode_unit(a, n_act, u);
+                const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
+                const uint8_t *codes = a.wq + tb * P * TB;
+                const __half2 *scales = a.ws + tb * P * UM_M;
+                for (int kb = 0; kb < a.KB; kb++, g++) {
+                    const int r = g % R;
+                    if (!mbar_wait(&rawEmpty[r], ((g / R) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *dst = raw + r * Cfg::RAW_BYTES;
+                    mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
+                    bulk_load(dst, codes + (size_t)kb * P * TB, Cfg::RAW_CODE, &rawFull[r]);
+                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * P * UM_M, P * UM_M * 4,
+                              &rawFull[r]);
+                    last = g;
                 }
-                uint8_t *dst = raw + r * Cfg::RAW_BYTES;
-                mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
-                bulk_load(dst, codes + (size_t)kb * P * TB, Cfg::RAW_CODE, &rawFull[r]);
-                bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * P * UM_M, P * UM_M * 4,
-                          &rawFull[r]);
-                issued = kb;
             }
-            if (*abort_flag && issued >= 0) {
-                volatile int never = 0;
-                mbar_wait(&rawFull[issued % R], (issued / R) & 1, &never, UM_WAIT_CYCLES);
-            }
+            if (!ok && last >= 0)  // let our own last copy land before smem goes away
+                mbar_wait(&rawFull[last % R], (last / R) & 1, 0, UM_WAIT_CYCLES);
         }
-    } else if (warp == 10) {
-        // ================= activation producer (tiled TMA) ================
+    } else if (warp == UM_ACT_WARP) {
+        // ============ activation producer (tiled TMA) =============================
         if (lane == 0) {
             prefetch_tmap(&tmap_b);
-            int issued = -1;
-            for (int kb = 0; kb < a.KB; kb++) {
-                const int s = kb % S;
-                if (!mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, abort_flag, UM_WAIT_CYCLES)) {
-                    fail();
-                    break;
+            int g = 0, last = -1;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const Unit w = decode_unit(a, n_act, u);
+                for (int kb = 0; kb < a.KB; kb++, g++) {
+                    const int s = g % S;
+                    if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&fullB[s], Cfg::B_BYTES);
+                    tma_load_2d(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES, &tmap_b,
+                                kb * UM_BK, w.slot0, &fullB[s]);
+                    last = g;
                 }
-                mbar_arrive_expect_tx(&fullB[s], Cfg::B_BYTES);
-                tma_load_2d(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES, &tmap_b, kb * UM_BK,
-                            slot0, &fullB[s]);
-                issued = kb;
             }
-            if (*abort_flag && issued >= 0) {
-                volatile int never = 0;
-                mbar_wait(&fullB[issued % S], (issued / S) & 1, &never, UM_WAIT_CYCLES);
-            }
+            if (!ok && last >= 0)
+                mbar_wait(&fullB[last % S], (last / S) & 1, 0, UM_WAIT_CYCLES);
         }
     } else {
-        // ================= MMA issuer (warp 9) ================================
+        // ============ MMA issuer =====================================================
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(UM_M, N);
+            int g = 0, lt = 0;
             bool ok = true;
-            for (int kb = 0; kb < a.KB; kb++) {
-                const int s = kb % S;
-                const uint32_t par = (kb / S) & 1;
-                if (!mbar_wait(&fullB[s], par, abort_flag, UM_WAIT_CYCLES) ||
-                    !mbar_wait(&fullA[s], par, abort_flag, UM_WAIT_CYCLES)) {
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, lt++) {
+                const Unit w = decode_unit(a, n_act, u);
+                const uint32_t idesc = idesc_f16_f32(UM_M, w.N);
+                const int buf = lt & 1;
+                if (!mbar_wait(&accEmpty[buf], ((lt >> 1) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
                     fail();
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t bsm = smem_u32(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES);
+                const uint32_t acc = tmem + buf * Cfg::ACC_COLS;
+                for (int kb = 0; kb < a.KB; kb++, g++) {
+                    const int s = g % S;
+                    const uint32_t par = (g / S) & 1;
+                    if (!mbar_wait(&fullB[s], par, abort_addr, UM_WAIT_CYCLES) ||
+                        !mbar_wait(&fullA[s], par, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st0 = base_u32 + s * Cfg::STAGE_BYTES;
+                    const uint32_t bsm = st0 + P * Cfg::A_BYTES;
 #pragma unroll
-                for (int p = 0; p < P; p++) {
-                    const uint32_t asm_ = smem_u32(base + s * Cfg::STAGE_BYTES + p * Cfg::A_BYTES);
+                    for (int p = 0; p < P; p++) {
+                        const uint32_t asm_ = st0 + p * Cfg::A_BYTES;
 #pragma unroll
-                    for (int k16 = 0; k16 < UM_BK / 16; k16++)
-                        umma_f16(tmem + p * 128, desc_k_sw128(asm_ + k16 * 32),
-                                 desc_k_sw128(bsm + k16 * 32), idesc, (kb | k16) != 0);
+                        for (int k16 = 0; k16 < UM_BK / 16; k16++)
+                            umma_f16(acc + p * 128, desc_k_sw128(asm_ + k16 * 32),
+                                     desc_k_sw128(bsm + k16 * 32), idesc, (kb | k16) != 0);
+                    }
+                    umma_commit(&empty[s]);
                 }
-                umma_commit(&empty[s]);
+                if (ok) umma_commit(&accFull[buf]);
             }
-            if (ok) {
-                umma_commit(accb);
-            } else {
-                umma_commit(drain);
-                volatile int never = 0;
-                mbar_wait(drain, 0, &never, UM_WAIT_CYCLES);
+            if (!ok) {
+                umma_commit(drain);  // our own UMMAs finish before TMEM is released
+                mbar_wait(drain, 0, 0, UM_WAIT_CYCLES);
             }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == UM_MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
@@ -494,7 +567,9 @@ static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStre
                                      Cfg::SMEM));
         done[dev] = true;
     }
-    k_umma<BITS, P><<<grid, UM_THREADS, Cfg::SMEM, s>>>(
+    int g = num_sms(dev);
+    if (grid < g) g = grid;
+    k_umma<BITS, P><<<g, UM_THREADS, Cfg::SMEM, s>>>(
         *reinterpret_cast<const CUtensorMap *>(tmap), a);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
