@@ -173,7 +173,7 @@ struct qgmoe {
     int path_mode = QGMOE_PATH_AUTO;
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr;
     __half2 *gu_ps = nullptr, *dn_ps = nullptr;
-    __half *xp16 = nullptr, *h16 = nullptr;
+    __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
     CUtensorMap tmap_x{}, tmap_h{};
     // stage timing (qgmoe_set_timing): one event set per timed forward since
     // the last read, so a whole timed loop runs without host syncs.
@@ -241,6 +241,7 @@ static int ensure_capacity(qgmoe *m, int T) {
     if (m->tensor_ok) {
         QG_A(m->xp16, sizeof(__half) * pairs * m->H);
         QG_A(m->h16, sizeof(__half) * pairs * m->I);
+        QG_A(m->d16, sizeof(__half) * pairs * m->H);
     }
     QG_A(m->h, sizeof(float) * slots * m->hmax);
     QG_A(m->d, sizeof(float) * slots * m->H);
@@ -278,10 +279,11 @@ static int build_tensor_weights(qgmoe *m) {
     if ((rc = al.alloc(reinterpret_cast<void **>(&m->dn_ps),
                        sizeof(__half2) * (size_t)E * H * (I / 64))))
         return rc;
-    if ((rc = launch_repack(m->gu.q, m->gu.s, bits, E, 2 * I, H, I / 128, 2, I, m->gu_pq,
+    // gate_up tiles: 64 gate rows + the matching 64 up rows; down: 128 rows
+    if ((rc = launch_repack(m->gu.q, m->gu.s, bits, E, 2 * I, H, I / 64, 1, I, m->gu_pq,
                             m->gu_ps, m->stream)))
         return rc;
-    if ((rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 1, 0, m->dn_pq, m->dn_ps,
+    if ((rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 0, 0, m->dn_pq, m->dn_ps,
                             m->stream)))
         return rc;
     QG_CUDA(cudaStreamSynchronize(m->stream));
@@ -303,7 +305,8 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     if (rc) return rc;
     m->mark(1, "route", s);
     const int pairs = T * m->k;
-    const int tiles = (pairs + 127) / 128 + (pairs < m->E ? pairs : m->E);
+    const int tiles =
+        (pairs + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS + (pairs < m->E ? pairs : m->E);
     UmmaLaunch l{};
     l.act_group = m->st.act_group;
     l.act_begin = m->st.act_begin;
@@ -314,26 +317,25 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     // gate_up + SwiGLU -> h16
     l.wq = m->gu_pq;
     l.ws = m->gu_ps;
-    l.RT = m->I / 128;
+    l.RT = m->I / 64;
     l.KB = m->H / 64;
-    l.h_out = m->h16;
-    l.h_stride = m->I;
+    l.out = m->h16;
+    l.out_stride = m->I;
     l.grid = tiles * l.RT;
-    if ((rc = launch_umma(m->bits, 2, &m->tmap_x, l, s))) return rc;
+    if ((rc = launch_umma(m->bits, true, &m->tmap_x, l, s))) return rc;
     m->mark(2, "gate_up", s);
-    // down -> d
+    // down -> d16
     l.wq = m->dn_pq;
     l.ws = m->dn_ps;
     l.RT = m->H / 128;
     l.KB = m->I / 64;
-    l.h_out = nullptr;
-    l.d_out = m->d;
-    l.d_stride = m->H;
+    l.out = m->d16;
+    l.out_stride = m->H;
     l.grid = tiles * l.RT;
-    if ((rc = launch_umma(m->bits, 1, &m->tmap_h, l, s))) return rc;
+    if ((rc = launch_umma(m->bits, false, &m->tmap_h, l, s))) return rc;
     m->mark(3, "down", s);
-    if ((rc = launch_combine(m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, m->st.shared_w,
-                             m->has_shared, out, s)))
+    if ((rc = launch_combine_f16(m->d16, m->H, T, m->k, m->st.pair_slot, m->st.topk_w,
+                                 m->st.shared_w, m->has_shared, out, s)))
         return rc;
     m->mark(4, "combine", s);
     m->last_launches = 6;  // logits, top-k, scatter+gather, gate_up, down, combine

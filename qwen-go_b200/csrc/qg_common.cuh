@@ -57,7 +57,7 @@ struct RouteState {
     int32_t *act_begin;  // [E+1] first slot of the group
     int32_t *act_n;      // [E+1] tokens in the group
     int32_t *n_act;      // [1]
-    int32_t *tile_prefix;  // [E+2] 128-token tiles before each routed group, total last
+    int32_t *tile_prefix;  // [E+2] QG_TILE_TOKENS-token tiles before each routed group, total last
     float *logits;         // [splits][T][E+1] split-K partial router logits
     int32_t *hist;         // [ceil(T/32)][E] expert histogram of each top-k CTA
     int32_t *expert_off;   // [E] first slot of each expert
@@ -69,13 +69,12 @@ struct UmmaLaunch {
     const __half2 *ws;          // packed scales
     int RT, KB;                 // row tiles per expert, 64-wide K blocks
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
-    __half *h_out;              // GEMM1: h [slots, h_stride] fp16
-    int h_stride;
-    float *d_out;               // GEMM2: d [slots, d_stride] f32
-    int d_stride;
+    __half *out;                // GEMM1: h [slots, I]; GEMM2: d [slots, H] (fp16)
+    int out_stride;
     int *err;
     int grid;                   // upper bound of work units
 };
+constexpr int QG_TILE_TOKENS = 256;  // token rows per tensor-core work unit
 
 // Arguments of the grouped expert kernels.
 struct ExpertArgs {
@@ -97,13 +96,17 @@ struct ExpertArgs {
 };
 
 // Launch helpers implemented in the .cu files.
-// Router + dispatch: 3 launches.  xp (optional) receives the fp16 activation
-// row of every slot for the tensor-core path.
+// Router + dispatch: logits, top-k, scatter; with xp set, a 4th launch writes
+// every slot's fp16 activation row for the tensor-core path.
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
                  const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
                  cudaStream_t s);
 int route_splits(int T, int H, int Ep, int sms);
 int launch_expert(bool gateup, const ExpertArgs &a, int max_items, cudaStream_t s);
+// d rows are f32 (CUDA-core path) or fp16 (tensor-core path).
+int launch_combine_f16(const __half *d, int H, int T, int k, const int32_t *pair_slot,
+                       const float *topk_w, const float *shared_w, int has_shared, float *out,
+                       cudaStream_t s);
 int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
                    const float *topk_w, const float *shared_w, int has_shared, float *out,
                    cudaStream_t s);
@@ -117,9 +120,10 @@ int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, flo
 int num_sms(int device);
 int encode_act_map(void *map_out, const __half *ptr, int rows, int cols);
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
-                  int RT, int P, int up_offset, uint8_t *qo, __half2 *so, cudaStream_t s);
+                  int RT, int interleave, int up_offset, uint8_t *qo, __half2 *so,
+                  cudaStream_t s);
 int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
                       cudaStream_t s);
-int launch_umma(int bits, int P, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
+int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
 
 }  // namespace qg

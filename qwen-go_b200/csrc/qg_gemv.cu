@@ -271,8 +271,18 @@ int launch_expert(bool gateup, const ExpertArgs &a, int max_items_groups, cudaSt
 
 // out[t, j] = sum_r w[t,r] * d[slot(t,r), j]  (+ sg[t] * d[T*k + t, j]),
 // accumulated from zero in rank order with separately rounded products, as
-// `out[j] += w * d[j]` in model/moe.go:82-85 and :94-96.
-__global__ void k_combine(const float *__restrict__ d, int H, int T, int k,
+// `out[j] += w * d[j]` in model/moe.go:82-85 and :94-96.  d rows are f32
+// (CUDA-core path) or fp16 (tensor-core path).
+__device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 load4(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename D>
+__global__ void k_combine(const D *__restrict__ d, int H, int T, int k,
                           const int32_t *__restrict__ pair_slot,
                           const float *__restrict__ topk_w, const float *__restrict__ shared_w,
                           int has_shared, float *__restrict__ out) {
@@ -283,7 +293,7 @@ __global__ void k_combine(const float *__restrict__ d, int H, int T, int k,
     for (int r = 0; r < k; r++) {
         const int slot = pair_slot[(size_t)t * k + r];
         const float w = topk_w[(size_t)t * k + r];
-        const float4 v = reinterpret_cast<const float4 *>(d + (size_t)slot * H)[j4];
+        const float4 v = load4(d + (size_t)slot * H + 4 * j4);
         acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
         acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
         acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
@@ -291,7 +301,7 @@ __global__ void k_combine(const float *__restrict__ d, int H, int T, int k,
     }
     if (has_shared) {
         const float w = shared_w[t];
-        const float4 v = reinterpret_cast<const float4 *>(d + (size_t)(T * k + t) * H)[j4];
+        const float4 v = load4(d + (size_t)(T * k + t) * H + 4 * j4);
         acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
         acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
         acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
@@ -300,14 +310,28 @@ __global__ void k_combine(const float *__restrict__ d, int H, int T, int k,
     reinterpret_cast<float4 *>(out + (size_t)t * H)[j4] = acc;
 }
 
+template <typename D>
+static int launch_combine_t(const D *d, int H, int T, int k, const int32_t *pair_slot,
+                            const float *topk_w, const float *shared_w, int has_shared, float *out,
+                            cudaStream_t s) {
+    const int threads = 128;
+    dim3 grid((H / 4 + threads - 1) / threads, T);
+    k_combine<D><<<grid, threads, 0, s>>>(d, H, T, k, pair_slot, topk_w, shared_w, has_shared,
+                                          out);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
 int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
                    const float *topk_w, const float *shared_w, int has_shared, float *out,
                    cudaStream_t s) {
-    const int threads = 128;
-    dim3 grid((H / 4 + threads - 1) / threads, T);
-    k_combine<<<grid, threads, 0, s>>>(d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out);
-    QG_CUDA(cudaGetLastError());
-    return QGMOE_OK;
+    return launch_combine_t(d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
+}
+
+int launch_combine_f16(const __half *d, int H, int T, int k, const int32_t *pair_slot,
+                       const float *topk_w, const float *shared_w, int has_shared, float *out,
+                       cudaStream_t s) {
+    return launch_combine_t(d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
 }
 
 }  // namespace qg

@@ -13,7 +13,7 @@
 //    literal PREFIX bound), w = p / (wSum + 1e-9) (model/moe.go:53-63) and
 //    sigmoid of the shared gate.  Each CTA writes its expert histogram; the
 //    last CTA (atomic ticket) scans the totals into expert offsets, the list
-//    of active experts and the 128-token tile prefix, and re-zeroes the
+//    of active experts and the tensor-core tile prefix, and re-zeroes the
 //    counters and the ticket so the next call (or a graph replay) starts clean.
 // 3. k_scatter: each CTA ranks its own (token, rank) pairs per expert in pair
 //    order (warp match + per-warp counts) and adds the histograms of the CTAs
@@ -297,7 +297,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
             for (int e = 0; e < E; e++)
                 if (cnt[e] > 0) {
                     st.tile_prefix[ai++] = tiles;
-                    tiles += (cnt[e] + 127) / 128;
+                    tiles += (cnt[e] + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS;
                 }
             st.tile_prefix[ai] = tiles;
             if (has_shared) {

@@ -1,7 +1,7 @@
 // Grouped expert GEMMs on the 5th-generation tensor cores (kernels K3'/K4',
 // prefill-sized token counts; also used for decode batches when forced).
 //
-// Swap-AB formulation per work unit (expert e, 128-row weight tile, <=128
+// Swap-AB formulation per work unit (expert e, 128-row weight tile, <=256
 // token tile):
 //   D[rows, tokens] = W[rows, K] * X[tokens, K]^T      (tcgen05.mma kind::f16)
 // A = expert weights, dequantised from int8/int4 group-32 codes with fp16
@@ -9,15 +9,16 @@
 //     the 128B-swizzled UMMA layout in shared memory; the raw codes and
 //     scales arrive through a deep ring of bulk TMA copies;
 // B = the expert's token rows in fp16, brought in by tiled TMA (SWIZZLE_128B);
-// D = fp32 accumulators in TMEM, double-buffered: a dedicated epilogue
-//     warpgroup drains one buffer (tcgen05.ld) while the next unit
-//     accumulates into the other.
+// D = fp32 accumulators in TMEM, double-buffered (2 x 256 columns): a
+//     dedicated epilogue warpgroup drains one buffer (tcgen05.ld) while the
+//     next unit accumulates into the other.
 //
-// GEMM1 (P = 2): the gate rows [r, r+128) and the matching up rows
-// [I + r, I + r + 128) (model/moe.go:70-71) accumulate side by side in TMEM,
-// so the epilogue computes h = silu(gate) * up (model/moe.go:72-76) without
-// a round trip, and writes h in fp16 for GEMM2.
-// GEMM2 (P = 1): D = W_down * h^T (model/moe.go:77-81), written as f32 d
+// GEMM1 (SWIGLU): a weight tile holds 64 gate rows [r, r+64) in TMEM lanes
+// 0-63 and the matching up rows [I + r, I + r + 64) (model/moe.go:70-71) in
+// lanes 64-127, so one 128-row dequantised tile feeds a 256-token MMA and the
+// epilogue pairs gate and up through a small shared-memory exchange to write
+// h = silu(gate) * up (model/moe.go:72-76) in fp16 for GEMM2.
+// GEMM2 (STORE): D = W_down * h^T (model/moe.go:77-81), written as fp16 d
 // rows for the rank-ordered combine.
 //
 // The kernel is persistent (one CTA per SM, static stride over work units)
@@ -44,35 +45,29 @@ constexpr int UM_MMA_WARP = 13;    // TMEM alloc + UMMA issue
 constexpr int UM_ACT_WARP = 14;    // tiled TMA of the activation (B) tiles
 constexpr int UM_THREADS = 15 * 32;
 constexpr int UM_CONV = UM_CONV_WARPS * 32;
-constexpr int UM_M = 128;        // weight rows per tile
-constexpr int UM_N = 128;        // max tokens per tile
-constexpr int UM_BK = 64;        // K elements per stage (one 128-byte fp16 row)
+constexpr int UM_M = 128;          // weight rows per tile (= TMEM lanes)
+constexpr int UM_N = 256;          // max tokens per tile (= TMEM columns per buffer)
+constexpr int UM_BK = 64;          // K elements per stage (one 128-byte fp16 row)
+constexpr int UM_XS = 17;          // epilogue exchange row stride (floats)
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 template <int BITS>
-struct UmTile {
-    static constexpr int BYTES = UM_M * UM_BK * BITS / 8;  // codes of one (row tile, k block)
-};
-
-// Shared memory: S stages of (P fp16 A tiles + B tile) consumed by the MMA,
-// and R stages of raw codes + scales brought in by bulk TMA copies for the
-// converters (the deep ring hides the DRAM latency of the weight stream).
-// TMEM: two accumulator buffers (P x 128 columns each) so the epilogue of
-// one tile overlaps the next tile's K loop.
-template <int BITS, int P>
 struct UmCfg {
-    static constexpr int STAGES = P == 2 ? 3 : 4;
-    static constexpr int RAW_STAGES = P == 2 ? (BITS == 8 ? 4 : 6) : (BITS == 8 ? 6 : 8);
-    static constexpr int A_BYTES = UM_M * UM_BK * 2;
-    static constexpr int B_BYTES = UM_N * UM_BK * 2;
-    static constexpr int STAGE_BYTES = P * A_BYTES + B_BYTES;
-    static constexpr int RAW_CODE = P * UmTile<BITS>::BYTES;
-    static constexpr int RAW_BYTES = RAW_CODE + P * UM_M * 4;
-    static constexpr int ACC_COLS = P * 128;
+    static constexpr int STAGES = 3;
+    static constexpr int RAW_STAGES = BITS == 8 ? 6 : 8;
+    static constexpr int A_BYTES = UM_M * UM_BK * 2;            // 16 KB fp16
+    static constexpr int B_BYTES = UM_N * UM_BK * 2;            // 32 KB fp16
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int RAW_CODE = UM_M * UM_BK * BITS / 8;    // codes of one k block
+    static constexpr int RAW_BYTES = RAW_CODE + UM_M * 4;       // + 2 fp16 scales per row
+    static constexpr int ACC_COLS = UM_N;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    static constexpr int XCH_BYTES = 64 * UM_XS * 4;
     static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 5) + 16;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + BAR_BYTES + 1024;
+    static constexpr int SMEM =
+        STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + XCH_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(STAGE_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
 };
 
 // int8 x4 stored biased (q + 128, repacked at create time) -> two fp16x2
@@ -117,15 +112,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// Named barrier for the 4 epilogue warps only.
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Same barrier, returning the OR of every participant's predicate, so the
+// four warps take one uniform decision.
+__device__ __forceinline__ bool epi_bar_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, 1, 128, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)p)
+        : "memory");
+    return r != 0;
+}
+
 struct UmmaArgs {
-    const uint8_t *wq;    // packed codes [E][RT][KB][P][tile]
-    const __half2 *ws;    // packed scales [E][RT][KB][P][128] (2 groups per row)
+    const uint8_t *wq;    // packed codes [E][RT][KB][128 rows][64 or 32 B]
+    const __half2 *ws;    // packed scales [E][RT][KB][128] (the row's 2 groups)
     int RT, KB;
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
-    __half *h_out;        // GEMM1 output [slots, h_stride]
-    int h_stride;
-    float *d_out;         // GEMM2 output [slots, d_stride]
-    int d_stride;
+    __half *out;          // SWIGLU: h [slots, out_stride]; STORE: d [slots, out_stride]
+    int out_stride;
     int *err;
 };
 
@@ -150,15 +160,15 @@ __device__ __forceinline__ Unit decode_unit(const UmmaArgs &a, int n_act, int u)
     return w;
 }
 
-template <int BITS, int P>
+template <int BITS, bool SWIGLU>
 __global__ void __launch_bounds__(UM_THREADS, 1)
 k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
-    using Cfg = UmCfg<BITS, P>;
+    using Cfg = UmCfg<BITS>;
     constexpr int S = Cfg::STAGES;
     constexpr int R = Cfg::RAW_STAGES;
-    constexpr int TB = UmTile<BITS>::BYTES;
-    constexpr int U4_TILE = TB / 16;
-    constexpr int PER_THREAD = P * U4_TILE / UM_CONV;
+    constexpr int U4_TILE = Cfg::RAW_CODE / 16;
+    constexpr int PER_THREAD = U4_TILE / UM_CONV;
+    constexpr int CHUNKS = BITS == 8 ? 2 : 4;  // 16-byte fp16 chunks written per uint4 of codes
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -171,7 +181,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const uint32_t base_u32 = smem_u32(base);
     uint8_t *raw = base + S * Cfg::STAGE_BYTES;
     const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_BYTES;
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES);
+    float *xch = reinterpret_cast<float *>(raw + R * Cfg::RAW_BYTES);
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
     uint64_t *rawFull = empty + S;
@@ -218,7 +229,24 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     if (warp < UM_CONV_WARPS) {
         // ============ converters: raw ring -> fp16 swizzled A tiles ==========
-        int g = 0;  // running k-block counter across this CTA's tiles
+        // Each thread always converts the same rows/chunks of a k block, so
+        // its shared-memory offsets are fixed.
+        uint32_t code_off[PER_THREAD], scale_off[PER_THREAD], st_off[PER_THREAD][CHUNKS];
+        bool hi_half[PER_THREAD];
+#pragma unroll
+        for (int j = 0; j < PER_THREAD; j++) {
+            const int i = tid + UM_CONV * j;
+            const int row = BITS == 8 ? (i >> 2) : (i >> 1);
+            const int sub = BITS == 8 ? (i & 3) : (i & 1);  // 16-code chunk / 32-code half
+            code_off[j] = i * 16;
+            scale_off[j] = Cfg::RAW_CODE + row * 4;
+            hi_half[j] = BITS == 8 ? (sub >= 2) : (sub == 1);
+            const int x7 = row & 7;
+#pragma unroll
+            for (int q = 0; q < CHUNKS; q++)
+                st_off[j][q] = row * 128 + (((CHUNKS * sub + q) ^ x7) << 4);
+        }
+        int g = 0;  // running k-block counter across this CTA's units
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             for (int kb = 0; kb < a.KB; kb++, g++) {
@@ -230,44 +258,32 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                     break;
                 }
                 const uint32_t rs = raw_u32 + r * Cfg::RAW_BYTES;
-                const uint32_t A0 = base_u32 + s * Cfg::STAGE_BYTES;
+                const uint32_t A = base_u32 + s * Cfg::STAGE_BYTES;
 #pragma unroll
                 for (int j = 0; j < PER_THREAD; j++) {
-                    const int i = tid + UM_CONV * j;
-                    const int p = i / U4_TILE, ii = i - p * U4_TILE;
-                    const uint4 q = ld_shared_v4(rs + i * 16);
-                    const uint32_t A = A0 + p * Cfg::A_BYTES;
+                    const uint4 q = ld_shared_v4(rs + code_off[j]);
+                    uint32_t scw = ld_shared_u32(rs + scale_off[j]);
+                    const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
+                    const __half2 s2 = hi_half[j] ? __high2half2(sc) : __low2half2(sc);
                     if constexpr (BITS == 8) {
-                        const int row = ii >> 2, c = ii & 3;
-                        uint32_t scw = ld_shared_u32(rs + Cfg::RAW_CODE + (p * UM_M + row) * 4);
-                        const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
-                        const __half2 s2 = (c < 2) ? __low2half2(sc) : __high2half2(sc);
                         uint32_t o[8];
                         cvt_i8x4(q.x, s2, o[0], o[1]);
                         cvt_i8x4(q.y, s2, o[2], o[3]);
                         cvt_i8x4(q.z, s2, o[4], o[5]);
                         cvt_i8x4(q.w, s2, o[6], o[7]);
-                        const uint32_t rowa = A + row * 128;
-                        const int x7 = row & 7;
-                        st_shared_v4(rowa + (((2 * c) ^ x7) << 4), o[0], o[1], o[2], o[3]);
-                        st_shared_v4(rowa + (((2 * c + 1) ^ x7) << 4), o[4], o[5], o[6], o[7]);
+                        st_shared_v4(A + st_off[j][0], o[0], o[1], o[2], o[3]);
+                        st_shared_v4(A + st_off[j][1], o[4], o[5], o[6], o[7]);
                     } else {
-                        const int row = ii >> 1, hh = ii & 1;
-                        uint32_t scw = ld_shared_u32(rs + Cfg::RAW_CODE + (p * UM_M + row) * 4);
-                        const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
-                        const __half2 s2 = hh ? __high2half2(sc) : __low2half2(sc);
-                        const uint32_t rowa = A + row * 128;
-                        const int x7 = row & 7;
-                        st_shared_v4(rowa + (((4 * hh + 0) ^ x7) << 4), cvt_i4_pair(q.x, 0, s2),
+                        st_shared_v4(A + st_off[j][0], cvt_i4_pair(q.x, 0, s2),
                                      cvt_i4_pair(q.x, 1, s2), cvt_i4_pair(q.x, 2, s2),
                                      cvt_i4_pair(q.x, 3, s2));
-                        st_shared_v4(rowa + (((4 * hh + 1) ^ x7) << 4), cvt_i4_pair(q.y, 0, s2),
+                        st_shared_v4(A + st_off[j][1], cvt_i4_pair(q.y, 0, s2),
                                      cvt_i4_pair(q.y, 1, s2), cvt_i4_pair(q.y, 2, s2),
                                      cvt_i4_pair(q.y, 3, s2));
-                        st_shared_v4(rowa + (((4 * hh + 2) ^ x7) << 4), cvt_i4_pair(q.z, 0, s2),
+                        st_shared_v4(A + st_off[j][2], cvt_i4_pair(q.z, 0, s2),
                                      cvt_i4_pair(q.z, 1, s2), cvt_i4_pair(q.z, 2, s2),
                                      cvt_i4_pair(q.z, 3, s2));
-                        st_shared_v4(rowa + (((4 * hh + 3) ^ x7) << 4), cvt_i4_pair(q.w, 0, s2),
+                        st_shared_v4(A + st_off[j][3], cvt_i4_pair(q.w, 0, s2),
                                      cvt_i4_pair(q.w, 1, s2), cvt_i4_pair(q.w, 2, s2),
                                      cvt_i4_pair(q.w, 3, s2));
                     }
@@ -283,11 +299,15 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     } else if (warp < UM_EPI_WARP0 + 4) {
         // ============ epilogue: TMEM -> SwiGLU / store ============================
         const int ew = warp - UM_EPI_WARP0;  // TMEM lane quarter
-        const int rr = ew * 32 + lane;
+        const int L = ew * 32 + lane;        // TMEM lane = tile row
         int lt = 0;
         for (int u = blockIdx.x; u < n_units; u += gridDim.x, lt++) {
             const int buf = lt & 1;
-            if (!mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES)) {
+            bool bad = !mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES);
+            // SWIGLU: the four warps meet at named barriers below, so they
+            // must agree on stopping; the OR-barrier makes that decision uniform.
+            if (SWIGLU) bad = epi_bar_or(bad || ld_volatile_shared(abort_addr));
+            if (bad) {
                 fail();
                 break;
             }
@@ -295,26 +315,33 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             const Unit w = decode_unit(a, n_act, u);
             const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
             for (int c0 = 0; c0 < w.N; c0 += 16) {
-                float gv[16];
-                tmem_ld16(lane_addr + c0, gv);
-                if constexpr (P == 2) {
-                    float uv[16];
-                    tmem_ld16(lane_addr + 128 + c0, uv);
-                    __half *dst = a.h_out + (size_t)w.slot0 * a.h_stride + w.rt * UM_M + rr;
+                float v[16];
+                tmem_ld16(lane_addr + c0, v);
+                if constexpr (SWIGLU) {
+                    if (ew >= 2) {
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int t = c0 + j;
-                        if (t < w.nval) {
-                            const float x = gv[j];
-                            dst[(size_t)t * a.h_stride] = __float2half_rn(x / (1.f + expf(-x)) * uv[j]);
+                        for (int j = 0; j < 16; j++) xch[(L - 64) * UM_XS + j] = v[j];
+                    }
+                    epi_bar();
+                    if (ew < 2) {
+                        __half *dst = a.out + (size_t)w.slot0 * a.out_stride + w.rt * 64 + L;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) {
+                            const int t = c0 + j;
+                            if (t < w.nval) {
+                                const float gte = v[j], up = xch[L * UM_XS + j];
+                                dst[(size_t)t * a.out_stride] =
+                                    __float2half_rn(gte / (1.f + expf(-gte)) * up);
+                            }
                         }
                     }
+                    epi_bar();
                 } else {
-                    float *dst = a.d_out + (size_t)w.slot0 * a.d_stride + w.rt * UM_M + rr;
+                    __half *dst = a.out + (size_t)w.slot0 * a.out_stride + w.rt * UM_M + L;
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int t = c0 + j;
-                        if (t < w.nval) dst[(size_t)t * a.d_stride] = gv[j];
+                        if (t < w.nval) dst[(size_t)t * a.out_stride] = __float2half_rn(v[j]);
                     }
                 }
             }
@@ -330,8 +357,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const Unit w = decode_unit(a, n_act, u);
                 const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
-                const uint8_t *codes = a.wq + tb * P * TB;
-                const __half2 *scales = a.ws + tb * P * UM_M;
+                const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
+                const __half2 *scales = a.ws + tb * UM_M;
                 for (int kb = 0; kb < a.KB; kb++, g++) {
                     const int r = g % R;
                     if (!mbar_wait(&rawEmpty[r], ((g / R) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -341,8 +368,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                     }
                     uint8_t *dst = raw + r * Cfg::RAW_BYTES;
                     mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
-                    bulk_load(dst, codes + (size_t)kb * P * TB, Cfg::RAW_CODE, &rawFull[r]);
-                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * P * UM_M, P * UM_M * 4,
+                    bulk_load(dst, codes + (size_t)kb * Cfg::RAW_CODE, Cfg::RAW_CODE, &rawFull[r]);
+                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * UM_M, UM_M * 4,
                               &rawFull[r]);
                     last = g;
                 }
@@ -366,8 +393,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                         break;
                     }
                     mbar_arrive_expect_tx(&fullB[s], Cfg::B_BYTES);
-                    tma_load_2d(base + s * Cfg::STAGE_BYTES + P * Cfg::A_BYTES, &tmap_b,
-                                kb * UM_BK, w.slot0, &fullB[s]);
+                    tma_load_2d(base + s * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmap_b, kb * UM_BK,
+                                w.slot0, &fullB[s]);
                     last = g;
                 }
             }
@@ -400,16 +427,12 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st0 = base_u32 + s * Cfg::STAGE_BYTES;
-                    const uint32_t bsm = st0 + P * Cfg::A_BYTES;
+                    const uint32_t asm_ = base_u32 + s * Cfg::STAGE_BYTES;
+                    const uint32_t bsm = asm_ + Cfg::A_BYTES;
 #pragma unroll
-                    for (int p = 0; p < P; p++) {
-                        const uint32_t asm_ = st0 + p * Cfg::A_BYTES;
-#pragma unroll
-                        for (int k16 = 0; k16 < UM_BK / 16; k16++)
-                            umma_f16(acc + p * 128, desc_k_sw128(asm_ + k16 * 32),
-                                     desc_k_sw128(bsm + k16 * 32), idesc, (kb | k16) != 0);
-                    }
+                    for (int k16 = 0; k16 < UM_BK / 16; k16++)
+                        umma_f16(acc, desc_k_sw128(asm_ + k16 * 32), desc_k_sw128(bsm + k16 * 32),
+                                 idesc, (kb | k16) != 0);
                     umma_commit(&empty[s]);
                 }
                 if (ok) umma_commit(&accFull[buf]);
@@ -449,33 +472,37 @@ __global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restr
 }
 
 // ---- weight repack into UMMA tiles --------------------------------------
-// One thread per (e, rt, kb, p, row).  Source rows: p = 0 -> rt*128 + row,
-// p = 1 -> up_offset + rt*128 + row (the up half of gate_up).  int4 words
-// are reordered so element 2j sits in bits [4j, 4j+4) and element 2j+1 in
-// bits [16+4j, 20+4j): one shift+mask per fp16 pair in the converter.
+// One thread per (e, rt, kb, row).  Tile row `row` comes from source row
+//   interleave (SWIGLU): row < 64 -> rt*64 + row (gate),
+//                        row >= 64 -> up_offset + rt*64 + row - 64 (up);
+//   plain (STORE):       rt*128 + row.
+// int8 codes are stored biased (q + 128) for the converter's byte splice;
+// int4 words are reordered so element 2j sits in bits [4j, 4j+4) and element
+// 2j+1 in bits [16+4j, 20+4j): one shift+mask per fp16 pair.
 __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict__ sc, int bits,
-                         int E, int rows_per_e, int K, int RT, int P, int up_offset,
+                         int E, int rows_per_e, int K, int RT, int interleave, int up_offset,
                          uint8_t *__restrict__ qo, __half2 *__restrict__ so) {
     const int KB = K / UM_BK;
-    const int64_t n = (int64_t)E * RT * KB * P * UM_M;
+    const int64_t n = (int64_t)E * RT * KB * UM_M;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int row = (int)(i % UM_M);
     int64_t rest = i / UM_M;
-    const int p = (int)(rest % P);
-    rest /= P;
     const int kb = (int)(rest % KB);
     rest /= KB;
     const int rt = (int)(rest % RT);
     const int e = (int)(rest / RT);
-    const int64_t srow = (int64_t)e * rows_per_e + (p ? up_offset : 0) + rt * UM_M + row;
+    int64_t srow;
+    if (interleave)
+        srow = (int64_t)e * rows_per_e + (row < 64 ? rt * 64 + row : up_offset + rt * 64 + row - 64);
+    else
+        srow = (int64_t)e * rows_per_e + rt * UM_M + row;
     const int row_bytes = bits == 8 ? K : K / 2;
     const int blk_bytes = bits == 8 ? UM_BK : UM_BK / 2;
     const uint8_t *s = q + srow * row_bytes + (int64_t)kb * blk_bytes;
-    const int64_t tile = (((int64_t)e * RT + rt) * KB + kb) * P + p;
+    const int64_t tile = ((int64_t)e * RT + rt) * KB + kb;
     uint8_t *d = qo + tile * (UM_M * blk_bytes) + (int64_t)row * blk_bytes;
     if (bits == 8) {
-        // stored biased (q + 128): the converter splices bytes under 0x64
         for (int b = 0; b < blk_bytes; b += 16) {
             uint4 v = *reinterpret_cast<const uint4 *>(s + b);
             v.x ^= 0x80808080u;
@@ -515,7 +542,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D fp16 row-major [rows, cols] tensor, box 64 cols x 128 rows, 128B swizzle.
+// 2-D fp16 row-major [rows, cols] tensor, box 64 cols x 256 rows, 128B swizzle.
 int encode_act_map(void *map_out, const __half *ptr, int rows, int cols) {
     auto fn = encode_fn();
     if (!fn) return set_error(QGMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -534,11 +561,12 @@ int encode_act_map(void *map_out, const __half *ptr, int rows, int cols) {
 }
 
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
-                  int RT, int P, int up_offset, uint8_t *qo, __half2 *so, cudaStream_t s) {
-    const int64_t n = (int64_t)E * RT * (K / UM_BK) * P * UM_M;
+                  int RT, int interleave, int up_offset, uint8_t *qo, __half2 *so,
+                  cudaStream_t s) {
+    const int64_t n = (int64_t)E * RT * (K / UM_BK) * UM_M;
     if (n == 0) return QGMOE_OK;
-    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, sc, bits, E, rows_per_e, K, RT, P,
-                                                          up_offset, qo, so);
+    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, sc, bits, E, rows_per_e, K, RT,
+                                                          interleave, up_offset, qo, so);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
@@ -556,26 +584,26 @@ int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int
     return QGMOE_OK;
 }
 
-template <int BITS, int P>
+template <int BITS, bool SWIGLU>
 static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStream_t s) {
-    using Cfg = UmCfg<BITS, P>;
+    using Cfg = UmCfg<BITS>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool done[64] = {false};
     if (dev < 64 && !done[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     Cfg::SMEM));
+        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, SWIGLU>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
         done[dev] = true;
     }
     int g = num_sms(dev);
     if (grid < g) g = grid;
-    k_umma<BITS, P><<<g, UM_THREADS, Cfg::SMEM, s>>>(
+    k_umma<BITS, SWIGLU><<<g, UM_THREADS, Cfg::SMEM, s>>>(
         *reinterpret_cast<const CUtensorMap *>(tmap), a);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
 
-int launch_umma(int bits, int P, const void *tmap, const UmmaLaunch &l, cudaStream_t s) {
+int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s) {
     UmmaArgs a{};
     a.wq = l.wq;
     a.ws = l.ws;
@@ -586,16 +614,14 @@ int launch_umma(int bits, int P, const void *tmap, const UmmaLaunch &l, cudaStre
     a.act_n = l.act_n;
     a.n_act = l.n_act;
     a.tile_prefix = l.tile_prefix;
-    a.h_out = l.h_out;
-    a.h_stride = l.h_stride;
-    a.d_out = l.d_out;
-    a.d_stride = l.d_stride;
+    a.out = l.out;
+    a.out_stride = l.out_stride;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
-    if (bits == 8 && P == 2) return launch_umma_t<8, 2>(tmap, a, l.grid, s);
-    if (bits == 8 && P == 1) return launch_umma_t<8, 1>(tmap, a, l.grid, s);
-    if (bits == 4 && P == 2) return launch_umma_t<4, 2>(tmap, a, l.grid, s);
-    if (bits == 4 && P == 1) return launch_umma_t<4, 1>(tmap, a, l.grid, s);
+    if (bits == 8 && swiglu) return launch_umma_t<8, true>(tmap, a, l.grid, s);
+    if (bits == 8 && !swiglu) return launch_umma_t<8, false>(tmap, a, l.grid, s);
+    if (bits == 4 && swiglu) return launch_umma_t<4, true>(tmap, a, l.grid, s);
+    if (bits == 4 && !swiglu) return launch_umma_t<4, false>(tmap, a, l.grid, s);
     return set_error(QGMOE_ERR_UNSUPPORTED, "tensor path needs int8/int4 weights");
 }
 
