@@ -48,7 +48,8 @@ constexpr int UM_CONV = UM_CONV_WARPS * 32;
 constexpr int UM_M = 128;          // weight rows per tile (= TMEM lanes)
 constexpr int UM_N = 256;          // max tokens per tile (= TMEM columns per buffer)
 constexpr int UM_BK = 64;          // K elements per stage (one 128-byte fp16 row)
-constexpr int UM_XS = 17;          // epilogue exchange row stride (floats)
+constexpr int UM_XS = UM_M + 4;    // epilogue staging row stride (floats, 16 B aligned)
+constexpr int UM_EC = 16;          // token columns per epilogue chunk
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 template <int BITS>
@@ -62,7 +63,7 @@ struct UmCfg {
     static constexpr int RAW_BYTES = RAW_CODE + UM_M * 4;       // + 2 fp16 scales per row
     static constexpr int ACC_COLS = UM_N;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
-    static constexpr int XCH_BYTES = 64 * UM_XS * 4;
+    static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
     static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 5) + 16;
     static constexpr int SMEM =
         STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + XCH_BYTES + BAR_BYTES + 1024;
@@ -181,7 +182,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const uint32_t base_u32 = smem_u32(base);
     uint8_t *raw = base + S * Cfg::STAGE_BYTES;
     const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_BYTES;
-    float *xch = reinterpret_cast<float *>(raw + R * Cfg::RAW_BYTES);
+    const uint32_t xch_u32 = raw_u32 + R * Cfg::RAW_BYTES;  // [UM_EC tokens][UM_XS] f32
     uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
@@ -298,15 +299,23 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         }
     } else if (warp < UM_EPI_WARP0 + 4) {
         // ============ epilogue: TMEM -> SwiGLU / store ============================
+        // Per chunk of 16 token columns: every thread copies its TMEM lane
+        // (tile row) into a [token][row] staging buffer; then each thread
+        // takes one token and 8 (SwiGLU) or 16 (store) consecutive rows and
+        // writes them as 16-byte vectors, so each token row of h / d goes out
+        // in coalesced 128-256 byte runs.
         const int ew = warp - UM_EPI_WARP0;  // TMEM lane quarter
         const int L = ew * 32 + lane;        // TMEM lane = tile row
+        const int et = tid - UM_EPI_WARP0 * 32;  // 0..127
+        const int ej = et >> 3;                  // token column within the chunk
+        const int er = (et & 7) * (SWIGLU ? 8 : 16);  // first row handled
         int lt = 0;
         for (int u = blockIdx.x; u < n_units; u += gridDim.x, lt++) {
             const int buf = lt & 1;
             bool bad = !mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES);
-            // SWIGLU: the four warps meet at named barriers below, so they
-            // must agree on stopping; the OR-barrier makes that decision uniform.
-            if (SWIGLU) bad = epi_bar_or(bad || ld_volatile_shared(abort_addr));
+            // the four warps meet at named barriers below, so they must agree
+            // on stopping; the OR-barrier makes that decision uniform
+            bad = epi_bar_or(bad || ld_volatile_shared(abort_addr));
             if (bad) {
                 fail();
                 break;
@@ -314,36 +323,46 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             tc_fence_after();
             const Unit w = decode_unit(a, n_act, u);
             const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
-            for (int c0 = 0; c0 < w.N; c0 += 16) {
+            for (int c0 = 0; c0 < w.N; c0 += UM_EC) {
                 float v[16];
                 tmem_ld16(lane_addr + c0, v);
-                if constexpr (SWIGLU) {
-                    if (ew >= 2) {
 #pragma unroll
-                        for (int j = 0; j < 16; j++) xch[(L - 64) * UM_XS + j] = v[j];
-                    }
-                    epi_bar();
-                    if (ew < 2) {
-                        __half *dst = a.out + (size_t)w.slot0 * a.out_stride + w.rt * 64 + L;
+                for (int j = 0; j < UM_EC; j++) st_shared_f32(xch_u32 + (j * UM_XS + L) * 4, v[j]);
+                epi_bar();
+                const int t = c0 + ej;
+                if (t < w.nval) {
+                    const uint32_t rowp = xch_u32 + (ej * UM_XS + er) * 4;
+                    if constexpr (SWIGLU) {
+                        const float4 g0 = ld_shared_f4(rowp), g1 = ld_shared_f4(rowp + 16);
+                        const float4 u0 = ld_shared_f4(rowp + 256), u1 = ld_shared_f4(rowp + 272);
+                        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+                        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                        uint32_t o[4];
 #pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const int t = c0 + j;
-                            if (t < w.nval) {
-                                const float gte = v[j], up = xch[L * UM_XS + j];
-                                dst[(size_t)t * a.out_stride] =
-                                    __float2half_rn(gte / (1.f + expf(-gte)) * up);
-                            }
+                        for (int q = 0; q < 4; q++) {
+                            const float h0 = __fdividef(gv[2 * q], 1.f + __expf(-gv[2 * q])) * uv[2 * q];
+                            const float h1 =
+                                __fdividef(gv[2 * q + 1], 1.f + __expf(-gv[2 * q + 1])) * uv[2 * q + 1];
+                            __half2 hh = __floats2half2_rn(h0, h1);
+                            o[q] = *reinterpret_cast<uint32_t *>(&hh);
                         }
-                    }
-                    epi_bar();
-                } else {
-                    __half *dst = a.out + (size_t)w.slot0 * a.out_stride + w.rt * UM_M + L;
+                        __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * 64 + er;
+                        *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        uint32_t o[8];
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int t = c0 + j;
-                        if (t < w.nval) dst[(size_t)t * a.out_stride] = __float2half_rn(v[j]);
+                        for (int q = 0; q < 4; q++) {
+                            const float4 f = ld_shared_f4(rowp + 16 * q);
+                            __half2 a2 = __floats2half2_rn(f.x, f.y), b2 = __floats2half2_rn(f.z, f.w);
+                            o[2 * q] = *reinterpret_cast<uint32_t *>(&a2);
+                            o[2 * q + 1] = *reinterpret_cast<uint32_t *>(&b2);
+                        }
+                        __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * UM_M + er;
+                        reinterpret_cast<uint4 *>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                        reinterpret_cast<uint4 *>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
                     }
                 }
+                epi_bar();
             }
             tc_fence_before();
             __syncwarp();
