@@ -142,6 +142,27 @@ int qgmoe_set_timing(qgmoe_t *h, int32_t enable);
 int qgmoe_read_timing(qgmoe_t *h, float *ms, int32_t n, int32_t *n_forwards);
 const char *qgmoe_stage_name(const qgmoe_t *h, int32_t i);
 
+/* ---- allocation-free router ---------------------------------------------
+ * No counterpart in the reference: qwen-go runs on the CPU with Go's heap.
+ * For callers that cannot call cudaMalloc -- a host runtime that owns every
+ * device allocation itself, a stream-capture region in which allocation is
+ * not permitted, or a serving loop whose memory budget is fixed at start-up
+ * -- this runs the router step (logits, softmax, top-k and renormalised
+ * weights, the same kernels qgmoe_forward uses) with all of its scratch in
+ * one static device array of QGMOE_ROUTE_STATIC_SCRATCH bytes, which every
+ * GPU that loads this library holds until the process exits.  x [T, H] f32,
+ * router [E, H] f32 and the outputs sel_idx / sel_w [T, k] are DEVICE
+ * pointers on the calling thread's current device; the work is enqueued on
+ * `stream` (a cudaStream_t, NULL = legacy default stream) and the call
+ * returns.  A size whose scratch would not fit the array is rejected with
+ * QGMOE_ERR_INVALID_ARG.  The first call on a device resolves the array's
+ * device address; make that first call before any stream capture.  All
+ * calls on a device share the array: calls that overlap on the GPU race, so
+ * order them on one stream. */
+#define QGMOE_ROUTE_STATIC_SCRATCH (8 << 20)
+int qgmoe_route_static(const float *x, const float *router, int32_t T, int32_t H, int32_t E,
+                       int32_t k, int32_t mode, int32_t *sel_idx, float *sel_w, void *stream);
+
 /* ---- QuantLinear -------------------------------------------------------- */
 typedef struct qgql qgql_t;
 

@@ -79,6 +79,8 @@ SIGNATURES = {
     "qgql_quantize_device": ([C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "qg_randn_device": ([C.c_uint64, C.c_uint64, C.c_uint64, C.c_int64, C.c_float, _vp, _vp],
                         C.c_int),
+    "qgmoe_route_static": ([_vp, _vp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                            _vp, _vp, _vp], C.c_int),
     "qgmoe_strerror": ([C.c_int], C.c_char_p),
     "qgmoe_last_error": ([], C.c_char_p),
     "qgmoe_device_ok": ([C.c_int32], C.c_int),
