@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 MoE layer (qwen-go moeMLP.forward, model/moe.go:41-99).
 
-Default workload = BASELINE config 3: the Qwen3-30B-A3B-shaped layer
+Default workload = config 3 of the benchmark plan: the Qwen3-30B-A3B-shaped layer
 (H=2048, E=128, top-8, I=768, int8 group-32 experts with fp16 scales, f32
 router) in prefill over 4096 tokens whose routing follows a Zipf(1.1) skew.
 One step = one full MoE-layer forward over the batch.  Inputs are synthetic
@@ -128,18 +128,21 @@ def zipf_bias_rows(E, H, c):
 # --------------------------------------------------------------------------
 
 
-def build_gpu_layer(cfg, device, experts=None):
+def build_gpu_layer(cfg, device, ep_world=1, ep_rank=0, keep_host=True):
     """Generates the layer on the GPU with the library's generator/quantiser.
-    Returns (MoeMLP, host copies for the CPU baseline, routing info)."""
+    With ep_world > 1 only the experts this rank owns (e % W == rank) are
+    generated, from the same counter-based streams at their offsets, so every
+    rank holds exactly the slice of the single-GPU layer.
+    Returns (MoeMLP, x [T, H] for all tokens, host copies, routing info)."""
     import torch
     import qgmoe
 
     H, E, k, I, Is, bits, seed = (cfg[n] for n in ("H", "E", "k", "I", "Is", "bits", "seed"))
     dev = torch.device("cuda", device)
 
-    def g(stream, shape, std=0.02):
+    def g(stream, shape, std=0.02, offset=0):
         t = torch.empty(shape, dtype=torch.float32, device=dev)
-        return qgmoe.randn_device(t, seed, stream, std)
+        return qgmoe.randn_device(t, seed, stream, std, offset=offset)
 
     router = g(0, (E, H))
     info = {}
@@ -152,28 +155,41 @@ def build_gpu_layer(cfg, device, experts=None):
         router += torch.from_numpy(zipf_bias_rows(E, H, c)).to(dev)[:, None]
         info["zipf_c"] = c
     args = dict(router=router)
-    host = {"router": router.cpu().numpy()}
-    mats = {"gate_up": (1, (E * 2 * I, H)), "down": (2, (E * H, I))}
+    host = {"router": router.cpu().numpy()} if keep_host else {}
+    mine = list(range(ep_rank, E, ep_world))  # local expert order
+
+    def expert_stack(stream, rows_per_e, cols):
+        if ep_world == 1:
+            return g(stream, (E * rows_per_e, cols))
+        return torch.cat([g(stream, (rows_per_e, cols), offset=e * rows_per_e * cols)
+                          for e in mine])
+
+    mats = {"gate_up": lambda: expert_stack(1, 2 * I, H), "down": lambda: expert_stack(2, H, I)}
     if Is:
         args["shared_gate"] = g(3, (H,))
-        host["shared_gate"] = args["shared_gate"].cpu().numpy()
-        mats.update(shared_gate=(4, (Is, H)), shared_up=(5, (Is, H)), shared_down=(6, (H, Is)))
-    for name, (stream, shape) in mats.items():
-        w = g(stream, shape)
+        if keep_host:
+            host["shared_gate"] = args["shared_gate"].cpu().numpy()
+        mats.update(shared_gate=lambda: g(4, (Is, H)), shared_up=lambda: g(5, (Is, H)),
+                    shared_down=lambda: g(6, (H, Is)))
+    for name, make in mats.items():
+        w = make()
         if bits == 32:
             key = {"gate_up": "gate_up", "down": "down"}.get(name, name + "_proj")
             args[key] = w
-            host[name] = w.cpu().numpy()
+            if keep_host:
+                host[name] = w.cpu().numpy()
         else:
             q, _s32, s16 = qgmoe.quantize_device(w, bits)
             args[name + "_q"] = q
             args[name + "_scale"] = s16
-            host[name + "_q"] = q.cpu().numpy()
-            host[name + "_s"] = s16.cpu().numpy().view(np.float16).astype(np.float32)
+            if keep_host:
+                host[name + "_q"] = q.cpu().numpy()
+                host[name + "_s"] = s16.cpu().numpy().view(np.float16).astype(np.float32)
         del w
     torch.cuda.synchronize(dev)
     layer = qgmoe.MoeMLP(n_embed=H, n_experts=E, top_k=k, n_moe_mlp=I, n_shared_mlp=Is, bits=bits,
-                         router_mode=qgmoe.ROUTER_TOPK, device=device, **args)
+                         router_mode=qgmoe.ROUTER_TOPK, device=device, ep_world=ep_world,
+                         ep_rank=ep_rank, **args)
     del args
     torch.cuda.empty_cache()
     return layer, x, host, info
@@ -390,7 +406,7 @@ def run_reference(args, cfg):
         "impl": "reference", "metric": "MoE-layer tokens/s", "value": val, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
-        "scaling": "weak" if world > 1 else "none", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": config_json(cfg, world),
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{n} of {cfg['T']} tokens per step, token-parallel over "
@@ -420,7 +436,7 @@ def run_ours(args, cfg):
     dev = local
     torch.cuda.set_device(dev)
     if world > 1:
-        raise SystemExit("expert-parallel path not built yet")
+        return run_ep(args, cfg, world, rank, local)
     layer, x, host, info = build_gpu_layer(cfg, dev)
     layer.set_path({"auto": qgmoe.PATH_AUTO, "cuda_core": qgmoe.PATH_CUDA_CORE,
                     "tensor": qgmoe.PATH_TENSOR}[args.path])
@@ -525,7 +541,7 @@ def run_ours(args, cfg):
         line = {
             "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak" if world > 1 else "none",
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32 activations, int%d weights" % cfg["bits"]
             if cfg["bits"] != 32 else "f32", "data": "synthetic", "config": cfgj,
             "stage_ms": stages, "forward_ms_device": forward_ms,
@@ -538,6 +554,110 @@ def run_ours(args, cfg):
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_ep(args, cfg, world, rank, local):
+    """Config 3 over `world` GPUs: expert parallelism (experts round-robin,
+    E/W per rank) with the T tokens split evenly over the ranks; rows move
+    through NCCL all-to-all.  Strong scaling: total work is fixed."""
+    import torch
+    import torch.distributed as dist
+    import qgmoe
+    from qgmoe.ep import ExpertParallelMoE
+
+    dev = local
+    layer, x_all, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False)
+    T_all, H = cfg["T"], cfg["H"]
+    lo, hi = rank * T_all // world, (rank + 1) * T_all // world
+    x = x_all[lo:hi].contiguous()
+    del x_all
+    out = torch.empty_like(x)
+    ep = ExpertParallelMoE(layer)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            ep.forward(x, out, stream)
+    stream.synchronize()
+
+    # ---- timed region: device events on the launching stream, max over ranks
+    stages = {}
+    marks = []
+
+    def timer(name):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        marks.append((name, ev))
+
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                start = torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                marks.append(("start", start))
+                ep.forward(x, out, stream, timer=timer)
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    prev = None
+    for name, ev in marks:
+        if name != "start":
+            stages[name] = stages.get(name, 0.0) + prev.elapsed_time(ev)
+        prev = ev
+    stages = {kk: v / args.steps for kk, v in stages.items()}
+    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    value = T_all * args.steps / (total_ms / 1e3)
+
+    # ---- roofline: the expert stage (grouped GEMMs on this rank) ----
+    peaks, peak_src = load_peaks()
+    exp_ms = max_over_ranks(stages.get("experts", 0.0), world)
+    k, I = cfg["k"], cfg["I"]
+    flops = 2.0 * T_all * k * 3 * I * H / world  # average rows per rank
+    achieved = flops / (exp_ms / 1e3) / 1e12 if exp_ms > 0 else 0.0
+    roof = {"bound": "tensor", "kernel": "experts (gate_up + down grouped GEMMs, slowest rank)",
+            "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": achieved / peaks["bf16_tflops"],
+            "peak_source": f"{peak_src} bf16 dense (MEASURED_PEAKS.json bf16_tflops)",
+            "algorithmic_per_launch": f"{flops / 1e9:.1f} GFLOP per rank (mean)", "traffic": None}
+
+    # ---- end to end: pinned host shard -> device -> layer -> host ----
+    xh = x.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+    barrier(world)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            x.copy_(xh, non_blocking=True)
+            ep.forward(x, out, stream)
+            oh.copy_(out, non_blocking=True)
+            stream.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = {"value": T_all * e2e_steps / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": T_all * H * 4, "d2h_bytes_per_step": T_all * H * 4,
+           "api": "qgmoe_ep_* via qgmoe.ep.ExpertParallelMoE (pinned host shards)"}
+
+    if rank == 0:
+        cfgj = config_json(cfg, world)
+        cfgj.update(info)
+        cfgj["placement"] = "round-robin: expert e on rank e % N"
+        cfgj["tokens_per_rank"] = T_all // world
+        line = {
+            "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 activations, int%d weights" % cfg["bits"], "data": "synthetic",
+            "config": cfgj, "stage_ms_rank0": stages, "roofline": roof, "cpu_baseline": None,
+            "e2e": e2e, "gpu_launches": (4 + 3 + 1) * args.steps, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    del ep
+    layer.close()
+    dist.destroy_process_group()
 
 
 def main():

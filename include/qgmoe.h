@@ -58,9 +58,9 @@ typedef struct qgmoe qgmoe_t;
 /* Weights of one moeMLP (model/moe.go:10-25).  Layouts are the reference's:
  * rows are (out, in), row-major.  bits selects the expert + shared-expert
  * weight format: 32 = float32 (gateUpW/downW), 8 or 4 = quantLinear codes
- * (int8 [O, I] bytes, or int4 packed [O, I/2] with element 2c in the high
- * nibble of byte c, both stored +8 ... see quantizeInt4) plus group-32
- * scales [O, I/32].  The router (gate) and sharedGate stay float32.
+ * (int8 [O, I] two's-complement bytes, or int4 packed [O, I/2] with element
+ * 2c in the high nibble of byte c and element 2c+1 in the low nibble, each
+ * stored as code + 8, model/moe.go:190-217) plus group-32 scales [O, I/32].  The router (gate) and sharedGate stay float32.
  * All pointers are either host pointers (weights_on_device = 0) or device
  * pointers on `device` (1); create() copies them, the caller keeps
  * ownership of its buffers. */
@@ -94,6 +94,13 @@ typedef struct qgmoe_desc {
     const void *shared_up_scale;
     const uint8_t *shared_down_q;
     const void *shared_down_scale;
+    /* Expert parallelism (0 or 1 = off).  With ep_world = W > 1 this handle
+     * owns the experts e with e % W == ep_rank (local index e / W); the expert
+     * stacks above then hold only those E/W experts, in local order, while
+     * the router stays [E, H].  Forward then goes through the qgmoe_ep_*
+     * calls below. */
+    int32_t ep_world;
+    int32_t ep_rank;
 } qgmoe_desc;
 
 /* Uploads the weights (device copies owned by the handle). */
@@ -113,6 +120,32 @@ int qgmoe_forward(qgmoe_t *h, const float *x, int32_t T, float *out, int32_t *se
  * are reported by qgmoe_sync(). */
 int qgmoe_forward_device(qgmoe_t *h, const float *x, int32_t T, float *out, int32_t *sel_idx,
                          float *sel_w, void *stream);
+
+/* ---- expert-parallel forward --------------------------------------------
+ * One process (handle) per GPU; the host moves rows between ranks, e.g. with
+ * NCCL all-to-all.  No reference counterpart: qwen-go is one process with no
+ * multi-GPU code; the per-token math is still moeMLP.forward's.
+ *   1. qgmoe_ep_dispatch: route this rank's T tokens over all E experts and
+ *      write the fp16 activation rows of its T*k (token, rank) pairs to
+ *      send_rows [T*k, H], sorted by owner rank, then local expert.
+ *   2. qgmoe_ep_send_counts: blocking; counts [W][E/W] of those rows.
+ *   3. host: exchange counts, then rows (rank r gets its block of each peer).
+ *   4. qgmoe_ep_experts: this rank's experts on the R received rows
+ *      (recv_rows [R, H] fp16, source-rank-major, each source's rows sorted
+ *      by local expert; recv_counts [W][E/W] host array) -> out_rows [R, H]
+ *      fp16 in the same order (SwiGLU expert outputs, model/moe.go:64-81).
+ *   5. host: send out_rows back (the reverse exchange).
+ *   6. qgmoe_ep_combine: back_rows [T*k, H] fp16 in send order -> out [T, H]
+ *      f32, the rank-ordered weighted sum of model/moe.go:82-85; sel_idx /
+ *      sel_w optional as in qgmoe_forward.
+ * All pointers except recv_counts / counts are DEVICE pointers; calls are
+ * enqueued on `stream` (NULL = the handle's stream). */
+int qgmoe_ep_dispatch(qgmoe_t *h, const float *x, int32_t T, void *send_rows, void *stream);
+int qgmoe_ep_send_counts(qgmoe_t *h, int32_t *counts, void *stream);
+int qgmoe_ep_experts(qgmoe_t *h, const void *recv_rows, int32_t R, const int32_t *recv_counts,
+                     void *out_rows, void *stream);
+int qgmoe_ep_combine(qgmoe_t *h, const void *back_rows, int32_t T, float *out, int32_t *sel_idx,
+                     float *sel_w, void *stream);
 
 /* Waits for `stream` (NULL = the handle's stream) and reports any
  * device-side bounds flag raised since the last check. */

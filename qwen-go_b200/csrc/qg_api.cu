@@ -167,6 +167,18 @@ struct qgmoe {
     int *err_dev = nullptr;
     int hmax = 0;
     int last_launches = 0;
+    // expert parallelism: this rank owns experts e with e % ep_world == ep_rank
+    // (local index e / ep_world); G = expert groups held here (E or E/ep_world)
+    int ep_world = 1, ep_rank = 0, G = 0;
+    int last_T = 0;             // tokens of the last qgmoe_ep_dispatch
+    int cap_R = 0;              // receive-side capacity (rows)
+    Allocs ep_work;
+    __half *xg16 = nullptr;     // received rows regrouped by local expert
+    __half *eh16 = nullptr;     // their SwiGLU output
+    int32_t *grp2recv = nullptr;
+    int32_t *ep_tab = nullptr;  // per-call segment tables and local active list
+    std::vector<int32_t> ep_host;
+    CUtensorMap tmap_xg{}, tmap_eh{};
     // tensor-core path (qg_umma.cu): UMMA-tiled weight copies, fp16
     // activation buffers and their TMA descriptors
     bool tensor_ok = false;
@@ -264,7 +276,7 @@ static int ensure_capacity(qgmoe *m, int T) {
 // Tensor-core path: int8/int4 weights, no shared expert, H and I multiples
 // of 128 (128-row weight tiles, 64-wide K blocks).
 static int build_tensor_weights(qgmoe *m) {
-    const int E = m->E, H = m->H, I = m->I, bits = m->bits;
+    const int E = m->G, H = m->H, I = m->I, bits = m->bits;
     if (!((bits == 8 || bits == 4) && !m->has_shared && H % 128 == 0 && I % 128 == 0))
         return QGMOE_OK;
     Allocs &al = m->weights;
@@ -356,6 +368,9 @@ static int read_flag(qgmoe *m, cudaStream_t s) {
 }
 
 static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    if (m->ep_world > 1)
+        return set_error(QGMOE_ERR_UNSUPPORTED,
+                         "expert-parallel handle: use qgmoe_ep_dispatch / _experts / _combine");
     if (use_tensor(m, T)) return enqueue_forward_tensor(m, x, T, out, s);
     m->begin_timed();
     m->mark(0, nullptr, s);
@@ -420,6 +435,12 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
         return set_error(QGMOE_ERR_INVALID_ARG, "bad scale_dtype %d", d->scale_dtype);
     if (!d->router || (Is > 0 && !d->shared_gate))
         return set_error(QGMOE_ERR_INVALID_ARG, "router / shared_gate pointer missing");
+    const int W = d->ep_world > 1 ? d->ep_world : 1;
+    if (W > 1 && (E % W || d->ep_rank < 0 || d->ep_rank >= W || Is > 0 || bits == 32 ||
+                  H % 128 || I % 128))
+        return set_error(QGMOE_ERR_INVALID_ARG,
+                         "expert parallelism needs E %% ep_world == 0, 0 <= ep_rank < ep_world, "
+                         "int8/int4 experts, no shared expert, H and I multiples of 128");
     int rc = check_device(d->device);
     if (rc) return rc;
 
@@ -434,6 +455,10 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
     m->mode = d->router_mode;
     m->has_shared = Is > 0;
     m->hmax = I > Is ? I : Is;
+    m->ep_world = W;
+    m->ep_rank = W > 1 ? d->ep_rank : 0;
+    m->G = E / W;
+    m->st.ep_world = W;
     const bool dev = d->weights_on_device != 0;
     cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
@@ -449,11 +474,12 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             (rc = upload(m->weights, d->shared_gate, sizeof(float) * H, dev,
                          reinterpret_cast<void **>(&m->shared_gate), s)))
             break;
-        Part pgu{d->gate_up, d->gate_up_q, d->gate_up_scale, E * 2 * I};
-        if ((rc = build_set(m->weights, bits, H, 2 * I, E, &pgu, 1, d->scale_dtype, dev, &m->gu, s)))
+        const int G = m->G;  // expert stacks passed in: the experts this rank owns
+        Part pgu{d->gate_up, d->gate_up_q, d->gate_up_scale, G * 2 * I};
+        if ((rc = build_set(m->weights, bits, H, 2 * I, G, &pgu, 1, d->scale_dtype, dev, &m->gu, s)))
             break;
-        Part pdn{d->down, d->down_q, d->down_scale, E * H};
-        if ((rc = build_set(m->weights, bits, I, H, E, &pdn, 1, d->scale_dtype, dev, &m->dn, s)))
+        Part pdn{d->down, d->down_q, d->down_scale, G * H};
+        if ((rc = build_set(m->weights, bits, I, H, G, &pdn, 1, d->scale_dtype, dev, &m->dn, s)))
             break;
         if (m->has_shared) {
             Part psg[2] = {{d->shared_gate_proj, d->shared_gate_q, d->shared_gate_scale, Is},
@@ -472,6 +498,10 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             break;
         }
         if ((rc = build_tensor_weights(m))) break;
+        if (W > 1 && !m->tensor_ok) {
+            rc = set_error(QGMOE_ERR_UNSUPPORTED, "expert parallelism needs the tensor-core path");
+            break;
+        }
         if ((rc = ensure_capacity(m, 1))) break;
     } while (0);
     if (rc) {
@@ -487,6 +517,7 @@ int qgmoe_destroy(qgmoe_t *m) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     m->work.free_all();
+    m->ep_work.free_all();
     m->weights.free_all();
     for (auto &set : m->ev_sets)
         for (auto e : set)
@@ -591,6 +622,177 @@ int qgmoe_read_timing(qgmoe_t *m, float *ms, int32_t n, int32_t *n_forwards) {
 const char *qgmoe_stage_name(const qgmoe_t *m, int32_t i) {
     if (!m || i < 0 || i >= m->n_stages || !m->stage_names[i]) return "";
     return m->stage_names[i];
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Expert parallelism (one process per GPU; the host moves rows between ranks)
+// ---------------------------------------------------------------------------
+static int ep_capacity(qgmoe *m, int R) {
+    if (R <= m->cap_R) return QGMOE_OK;
+    cudaStreamSynchronize(m->stream);
+    m->ep_work.free_all();
+    int cap = m->cap_R ? m->cap_R : 256;
+    while (cap < R) cap *= 2;
+    const int W = m->ep_world, G = m->G;
+    const size_t tab = (size_t)2 * W * G + 1 + 3 * (G + 1) + 1 + (G + 2);
+    Allocs &w = m->ep_work;
+    int rc = 0;
+    if ((rc = w.alloc(reinterpret_cast<void **>(&m->xg16), sizeof(__half) * (size_t)cap * m->H)) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&m->eh16), sizeof(__half) * (size_t)cap * m->I)) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&m->grp2recv), sizeof(int32_t) * (size_t)cap)) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&m->ep_tab), sizeof(int32_t) * tab)))
+        return rc;
+    if ((rc = encode_act_map(&m->tmap_xg, m->xg16, cap, m->H))) return rc;
+    if ((rc = encode_act_map(&m->tmap_eh, m->eh16, cap, m->I))) return rc;
+    m->ep_host.assign(tab, 0);
+    m->cap_R = cap;
+    return QGMOE_OK;
+}
+
+extern "C" {
+
+int qgmoe_ep_dispatch(qgmoe_t *m, const float *x, int32_t T, void *send_rows, void *stream) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
+    if (T < 0 || (T > 0 && (!x || !send_rows)))
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad dispatch arguments");
+    QG_CUDA(cudaSetDevice(m->device));
+    m->last_T = T;
+    if (T == 0) return QGMOE_OK;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = ensure_capacity(m, T);
+    if (rc) return rc;
+    return launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
+                        static_cast<__half *>(send_rows), m->err_dev, s);
+}
+
+int qgmoe_ep_send_counts(qgmoe_t *m, int32_t *counts, void *stream) {
+    if (!m || !counts) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/counts");
+    if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
+    const int E = m->E;
+    if (m->last_T == 0) {
+        for (int i = 0; i < E; i++) counts[i] = 0;
+        return QGMOE_OK;
+    }
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    std::vector<int32_t> off(E);
+    QG_CUDA(cudaMemcpyAsync(off.data(), m->st.expert_off, sizeof(int32_t) * E,
+                            cudaMemcpyDeviceToHost, s));
+    QG_CUDA(cudaStreamSynchronize(s));
+    const int total = m->last_T * m->k;
+    for (int v = 0; v < E; v++) counts[v] = (v + 1 < E ? off[v + 1] : total) - off[v];
+    return read_flag(m, s);
+}
+
+int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t *recv_counts,
+                     void *out_rows, void *stream) {
+    if (!m || !recv_counts) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/counts");
+    if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
+    const int W = m->ep_world, G = m->G;
+    int64_t total = 0;
+    for (int i = 0; i < W * G; i++) {
+        if (recv_counts[i] < 0) return set_error(QGMOE_ERR_INVALID_ARG, "negative count");
+        total += recv_counts[i];
+    }
+    if (total != R) return set_error(QGMOE_ERR_INVALID_ARG, "counts sum %lld != R=%d", (long long)total, R);
+    if (R == 0) return QGMOE_OK;
+    if (!recv_rows || !out_rows) return set_error(QGMOE_ERR_INVALID_ARG, "null rows");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = ep_capacity(m, R);
+    if (rc) return rc;
+    // host tables: segments (source, local expert) in received order and in
+    // local-expert-major order, and the local active-expert list
+    int32_t *h = m->ep_host.data();
+    int32_t *seg_recv = h, *seg_grp = h + W * G + 1;
+    int32_t *act_group = seg_grp + W * G, *act_begin = act_group + (G + 1),
+            *act_n = act_begin + (G + 1), *n_act = act_n + (G + 1), *tile_prefix = n_act + 1;
+    int run = 0;
+    for (int i = 0; i < W * G; i++) {
+        seg_recv[i] = run;
+        run += recv_counts[i];
+    }
+    seg_recv[W * G] = run;
+    int base = 0, na = 0, tiles = 0;
+    for (int g = 0; g < G; g++) {
+        int ng = 0;
+        for (int src = 0; src < W; src++) {
+            seg_grp[src * G + g] = base + ng;
+            ng += recv_counts[src * G + g];
+        }
+        if (ng > 0) {
+            act_group[na] = g;
+            act_begin[na] = base;
+            act_n[na] = ng;
+            tile_prefix[na] = tiles;
+            tiles += (ng + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS;
+            na++;
+        }
+        base += ng;
+    }
+    tile_prefix[na] = tiles;
+    *n_act = na;
+    // pageable source: the copy has read the host table when this returns
+    QG_CUDA(cudaMemcpyAsync(m->ep_tab, h, sizeof(int32_t) * m->ep_host.size(),
+                            cudaMemcpyHostToDevice, s));
+    const int32_t *d = m->ep_tab;
+    const int32_t *d_seg_recv = d, *d_seg_grp = d + W * G + 1;
+    const int32_t *d_act_group = d_seg_grp + W * G, *d_act_begin = d_act_group + (G + 1),
+                  *d_act_n = d_act_begin + (G + 1), *d_n_act = d_act_n + (G + 1),
+                  *d_tile_prefix = d_n_act + 1;
+    if ((rc = launch_ep_regroup(static_cast<const __half *>(recv_rows), R, m->H, d_seg_recv,
+                                d_seg_grp, W * G, m->xg16, m->grp2recv, s)))
+        return rc;
+    UmmaLaunch l{};
+    l.act_group = d_act_group;
+    l.act_begin = d_act_begin;
+    l.act_n = d_act_n;
+    l.n_act = d_n_act;
+    l.tile_prefix = d_tile_prefix;
+    l.err = m->err_dev;
+    l.wq = m->gu_pq;
+    l.ws = m->gu_ps;
+    l.RT = m->I / 64;
+    l.KB = m->H / 64;
+    l.out = m->eh16;
+    l.out_stride = m->I;
+    l.grid = tiles * l.RT;
+    if ((rc = launch_umma(m->bits, true, &m->tmap_xg, l, s))) return rc;
+    l.wq = m->dn_pq;
+    l.ws = m->dn_ps;
+    l.RT = m->H / 128;
+    l.KB = m->I / 64;
+    l.out = static_cast<__half *>(out_rows);
+    l.out_stride = m->H;
+    l.out_map = m->grp2recv;  // results go back in received order
+    l.grid = tiles * l.RT;
+    if ((rc = launch_umma(m->bits, false, &m->tmap_eh, l, s))) return rc;
+    m->last_launches = 3;
+    return QGMOE_OK;
+}
+
+int qgmoe_ep_combine(qgmoe_t *m, const void *back_rows, int32_t T, float *out, int32_t *sel_idx,
+                     float *sel_w, void *stream) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
+    if (T != m->last_T) return set_error(QGMOE_ERR_INVALID_ARG, "T differs from the dispatch");
+    if (T == 0) return QGMOE_OK;
+    if (!back_rows || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null rows/out");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = launch_combine_f16(static_cast<const __half *>(back_rows), m->H, T, m->k,
+                                m->st.pair_slot, m->st.topk_w, m->st.shared_w, 0, out, s);
+    if (rc) return rc;
+    if (sel_idx)
+        QG_CUDA(cudaMemcpyAsync(sel_idx, m->st.topk_idx, sizeof(int32_t) * T * m->k,
+                                cudaMemcpyDeviceToDevice, s));
+    if (sel_w)
+        QG_CUDA(cudaMemcpyAsync(sel_w, m->st.topk_w, sizeof(float) * T * m->k,
+                                cudaMemcpyDeviceToDevice, s));
+    return QGMOE_OK;
 }
 
 }  // extern "C"

@@ -60,8 +60,16 @@ struct RouteState {
     int32_t *tile_prefix;  // [E+2] QG_TILE_TOKENS-token tiles before each routed group, total last
     float *logits;         // [splits][T][E+1] split-K partial router logits
     int32_t *hist;         // [ceil(T/32)][E] expert histogram of each top-k CTA
-    int32_t *expert_off;   // [E] first slot of each expert
+    int32_t *expert_off;   // [E] first slot of each dispatch key
+    // Expert parallelism over ep_world ranks (1 = off): expert e is owned by
+    // rank e % ep_world, and slots are sorted by the dispatch key
+    // (e % W) * (E / W) + e / W, i.e. by destination rank, then local expert.
+    int ep_world;
 };
+
+__device__ __forceinline__ int dispatch_key(int e, int E, int W) {
+    return W > 1 ? (e % W) * (E / W) + e / W : e;
+}
 
 // One launch of the tensor-core grouped GEMM (qg_umma.cu).
 struct UmmaLaunch {
@@ -71,6 +79,7 @@ struct UmmaLaunch {
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
     __half *out;                // GEMM1: h [slots, I]; GEMM2: d [slots, H] (fp16)
     int out_stride;
+    const int32_t *out_map;     // GEMM2 only: output row of each slot (null = same slot)
     int *err;
     int grid;                   // upper bound of work units
 };
@@ -125,5 +134,9 @@ int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_
 int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
                       cudaStream_t s);
 int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
+// Expert parallelism: copies received rows into local-expert-major order.
+int launch_ep_regroup(const __half *recv, int R, int H, const int32_t *seg_recv_off,
+                      const int32_t *seg_grp_off, int nseg, __half *grouped, int32_t *grp2recv,
+                      cudaStream_t s);
 
 }  // namespace qg

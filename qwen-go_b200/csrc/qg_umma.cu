@@ -137,6 +137,7 @@ struct UmmaArgs {
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
     __half *out;          // SWIGLU: h [slots, out_stride]; STORE: d [slots, out_stride]
     int out_stride;
+    const int32_t *out_map;  // STORE: output row of each slot (null = the slot itself)
     int *err;
 };
 
@@ -357,7 +358,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                             o[2 * q] = *reinterpret_cast<uint32_t *>(&a2);
                             o[2 * q + 1] = *reinterpret_cast<uint32_t *>(&b2);
                         }
-                        __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * UM_M + er;
+                        const int orow = a.out_map ? a.out_map[w.slot0 + t] : w.slot0 + t;
+                        __half *dst = a.out + (size_t)orow * a.out_stride + w.rt * UM_M + er;
                         reinterpret_cast<uint4 *>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
                         reinterpret_cast<uint4 *>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
                     }
@@ -488,6 +490,48 @@ __global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restr
             *reinterpret_cast<uint4 *>(dst + k) = *reinterpret_cast<uint4 *>(h);
         }
     }
+}
+
+// ---- expert parallelism: regroup received rows by local expert ------------
+// Received rows arrive source-rank-major (each source's rows sorted by local
+// expert).  Segment i = (source, local expert) starts at seg_recv_off[i] in
+// the received buffer and at seg_grp_off[i] in the expert-major buffer.  One
+// warp per row: find its segment, copy the 2H-byte row, record the mapping
+// back (GEMM2 writes its output rows in received order through it).
+__global__ void k_ep_regroup(const __half *__restrict__ recv, int R, int H,
+                             const int32_t *__restrict__ seg_recv_off,
+                             const int32_t *__restrict__ seg_grp_off, int nseg,
+                             __half *__restrict__ grouped, int32_t *__restrict__ grp2recv) {
+    const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int r = wg; r < R; r += nw) {
+        int lo = 0, hi = nseg - 1;  // last segment with seg_recv_off <= r
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (seg_recv_off[mid] <= r) lo = mid; else hi = mid - 1;
+        }
+        const int g = seg_grp_off[lo] + (r - seg_recv_off[lo]);
+        if (lane == 0) grp2recv[g] = r;
+        const uint4 *src = reinterpret_cast<const uint4 *>(recv + (size_t)r * H);
+        uint4 *dst = reinterpret_cast<uint4 *>(grouped + (size_t)g * H);
+        for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
+    }
+}
+
+int launch_ep_regroup(const __half *recv, int R, int H, const int32_t *seg_recv_off,
+                      const int32_t *seg_grp_off, int nseg, __half *grouped, int32_t *grp2recv,
+                      cudaStream_t s) {
+    if (R <= 0) return QGMOE_OK;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int blocks = (R + 7) / 8;
+    const int cap = num_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    k_ep_regroup<<<blocks, 256, 0, s>>>(recv, R, H, seg_recv_off, seg_grp_off, nseg, grouped,
+                                        grp2recv);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
 }
 
 // ---- weight repack into UMMA tiles --------------------------------------
@@ -635,6 +679,7 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.tile_prefix = l.tile_prefix;
     a.out = l.out;
     a.out_stride = l.out_stride;
+    a.out_map = l.out_map;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
     if (bits == 8 && swiglu) return launch_umma_t<8, true>(tmap, a, l.grid, s);

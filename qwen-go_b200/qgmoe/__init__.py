@@ -55,6 +55,7 @@ class _Desc(C.Structure):
         ("shared_gate_q", _vp), ("shared_gate_scale", _vp),
         ("shared_up_q", _vp), ("shared_up_scale", _vp),
         ("shared_down_q", _vp), ("shared_down_scale", _vp),
+        ("ep_world", C.c_int32), ("ep_rank", C.c_int32),
     ]
 
 
@@ -65,6 +66,10 @@ SIGNATURES = {
     "qgmoe_forward": ([_vp, _vp, C.c_int32, _vp, _vp, _vp], C.c_int),
     "qgmoe_forward_device": ([_vp, _vp, C.c_int32, _vp, _vp, _vp, _vp], C.c_int),
     "qgmoe_sync": ([_vp, _vp], C.c_int),
+    "qgmoe_ep_dispatch": ([_vp, _vp, C.c_int32, _vp, _vp], C.c_int),
+    "qgmoe_ep_send_counts": ([_vp, C.POINTER(C.c_int32), _vp], C.c_int),
+    "qgmoe_ep_experts": ([_vp, _vp, C.c_int32, C.POINTER(C.c_int32), _vp, _vp], C.c_int),
+    "qgmoe_ep_combine": ([_vp, _vp, C.c_int32, _vp, _vp, _vp, _vp], C.c_int),
     "qgmoe_last_launch_count": ([_vp], C.c_int),
     "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_timing": ([_vp, C.c_int32], C.c_int),
@@ -154,7 +159,8 @@ class MoeMLP:
     """
 
     def __init__(self, *, n_embed, n_experts, top_k, n_moe_mlp, n_shared_mlp=0, bits=32,
-                 router_mode=ROUTER_TOPK, scale_dtype=SCALE_F16, device=0, router, shared_gate=None,
+                 router_mode=ROUTER_TOPK, scale_dtype=SCALE_F16, device=0, ep_world=1, ep_rank=0,
+                 router, shared_gate=None,
                  gate_up=None, down=None, shared_gate_proj=None, shared_up_proj=None,
                  shared_down_proj=None, gate_up_q=None, gate_up_scale=None, down_q=None,
                  down_scale=None, shared_gate_q=None, shared_gate_scale=None, shared_up_q=None,
@@ -175,6 +181,7 @@ class MoeMLP:
         d.n_shared_mlp, d.bits, d.router_mode, d.scale_dtype = n_shared_mlp, bits, router_mode, \
             scale_dtype
         d.weights_on_device, d.device = int(on_dev), device
+        d.ep_world, d.ep_rank = ep_world, ep_rank
         for name, v in arrays.items():
             setattr(d, name, _ptr(v))
         self._keep = arrays  # alive until create() has copied them
@@ -184,6 +191,7 @@ class MoeMLP:
         self.h = h
         self.n_embed, self.top_k, self.n_experts = n_embed, top_k, n_experts
         self.device = device
+        self.ep_world, self.ep_rank = ep_world, ep_rank
 
     def close(self):
         if getattr(self, "h", None):

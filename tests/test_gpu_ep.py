@@ -1,0 +1,91 @@
+"""Expert-parallel forward on 2 GPUs (NCCL): each rank owns half the experts
+and a token shard; its output must match the single-GPU layer on the same
+tokens (same kernels, so the tolerance is the north-star one) and the oracle
+on a token sample.  Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+W = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, port, result_dir):
+    import datetime
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (os.path.join(repo, "qwen-go_b200"), os.path.join(repo, "oracle"),
+              os.path.join(repo, "tests")):
+        sys.path.insert(0, p)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    import torch.distributed as dist
+
+    import qg_oracle as O
+    import qgmoe
+    from qgmoe.ep import ExpertParallelMoE
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=W,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    H, E, k, I, bits, T_all = 256, 16, 4, 128, 8, 600
+    m = O.make_moe(H, E, k, I, 0, bits, seed=88)
+    x_all = O.randn(88, 100, (T_all, H))
+    lo, hi = rank * T_all // W, (rank + 1) * T_all // W
+    G = E // W
+    mine = [rank + W * j for j in range(G)]          # experts owned here, local order
+    gu_rows = np.concatenate([np.arange(e * 2 * I, (e + 1) * 2 * I) for e in mine])
+    dn_rows = np.concatenate([np.arange(e * H, (e + 1) * H) for e in mine])
+    layer = qgmoe.MoeMLP(n_embed=H, n_experts=E, top_k=k, n_moe_mlp=I, bits=bits, device=rank,
+                         ep_world=W, ep_rank=rank, router=m.router,
+                         gate_up_q=np.ascontiguousarray(m.q["gate_up"][gu_rows]),
+                         gate_up_scale=np.ascontiguousarray(m.s16["gate_up"][gu_rows]),
+                         down_q=np.ascontiguousarray(m.q["down"][dn_rows]),
+                         down_scale=np.ascontiguousarray(m.s16["down"][dn_rows]))
+    ep = ExpertParallelMoE(layer)
+    x = torch.from_numpy(x_all[lo:hi]).cuda()
+    out = torch.empty_like(x)
+    for _ in range(2):  # second pass checks the reused buffers
+        ep.forward(x, out)
+        torch.cuda.synchronize()
+    np.save(os.path.join(result_dir, f"ep{rank}.npy"), out.cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gpu_expert_parallel_matches_single_gpu(tmp_path):
+    import torch
+    if torch.cuda.device_count() < W:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    import qg_oracle as O
+    import qgmoe
+    from moe_cases import check_outputs, make_gpu_moe
+
+    mp.spawn(_rank_main, args=(_free_port(), str(tmp_path)), nprocs=W, join=True)
+    H, E, k, I, bits, T_all = 256, 16, 4, 128, 8, 600
+    m = O.make_moe(H, E, k, I, 0, bits, seed=88)
+    x_all = O.randn(88, 100, (T_all, H))
+    ep_out = np.concatenate([np.load(tmp_path / f"ep{r}.npy") for r in range(W)])
+    single = make_gpu_moe(m, O.ROUTER_TOPK)
+    single.set_path(qgmoe.PATH_TENSOR)
+    ref = single.forward_batch(x_all)
+    np.testing.assert_allclose(ep_out, ref, rtol=1e-3, atol=1e-3)
+    sample = np.arange(0, T_all, 37)
+    oref, *_ = O.moe_forward(m, x_all[sample])
+    check_outputs(ep_out[sample], oref, bits)

@@ -71,7 +71,7 @@ def test_tensor_one_expert_many_tiles():
 
 
 def test_config3_prefill_full_size_sampled():
-    """BASELINE config 3 shapes (H=2048, E=128, k=8, I=768, int8) at 4096
+    """Config 3 shapes (H=2048, E=128, k=8, I=768, int8) at 4096
     tokens, uniform inputs: 48 sampled tokens against the oracle, all
     4096 for finiteness, routing weights summing to ~1, and agreement with
     the CUDA-core path on the same handle."""
