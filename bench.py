@@ -406,7 +406,7 @@ def run_reference(args, cfg):
         "impl": "reference", "metric": "MoE-layer tokens/s", "value": val, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": config_json(cfg, world),
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{n} of {cfg['T']} tokens per step, token-parallel over "
@@ -425,7 +425,8 @@ def config_json(cfg, world):
             "scale": "fp16 group-32", "tokens": cfg["T"], "router": "topk f32",
             "l2": ("no flush: weights %.1f MB > 126 MB L2" % (cfg["E"] * wb / 1e6)
                    if cfg["E"] * wb > L2_BYTES else "L2 flushed between steps"),
-            "parallelism": "single GPU" if world == 1 else f"ep{world}"}
+            "parallelism": "single GPU" if world == 1 else f"ep{world}",
+            "batch": "T tokens per GPU (weak scaling over GPUs)"}
 
 
 def run_ours(args, cfg):
@@ -541,7 +542,7 @@ def run_ours(args, cfg):
         line = {
             "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "strong",
+            "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 activations, int%d weights" % cfg["bits"]
             if cfg["bits"] != 32 else "f32", "data": "synthetic", "config": cfgj,
             "stage_ms": stages, "forward_ms_device": forward_ms,
@@ -558,19 +559,23 @@ def run_ours(args, cfg):
 
 def run_ep(args, cfg, world, rank, local):
     """Config 3 over `world` GPUs: expert parallelism (experts round-robin,
-    E/W per rank) with the T tokens split evenly over the ranks; rows move
-    through NCCL all-to-all.  Strong scaling: total work is fixed."""
+    E/W per rank), every rank routing its own batch of T tokens (tokens
+    r*T .. (r+1)*T-1 of one generated stream); rows move through NCCL
+    all-to-all.  Weak scaling: the work per GPU stays one T-token layer."""
     import torch
     import torch.distributed as dist
     import qgmoe
     from qgmoe.ep import ExpertParallelMoE
 
     dev = local
-    layer, x_all, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False)
-    T_all, H = cfg["T"], cfg["H"]
-    lo, hi = rank * T_all // world, (rank + 1) * T_all // world
-    x = x_all[lo:hi].contiguous()
-    del x_all
+    layer, x0, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False)
+    T, H = cfg["T"], cfg["H"]
+    T_all = T * world
+    x = torch.empty((T, H), dtype=torch.float32, device=x0.device)
+    qgmoe.randn_device(x, cfg["seed"], 100, 1.0, offset=rank * T * H)
+    if cfg["zipf"]:
+        x += MU
+    del x0
     out = torch.empty_like(x)
     ep = ExpertParallelMoE(layer)
     stream = torch.cuda.Stream(dev)
@@ -614,7 +619,7 @@ def run_ep(args, cfg, world, rank, local):
     peaks, peak_src = load_peaks()
     exp_ms = max_over_ranks(stages.get("experts", 0.0), world)
     k, I = cfg["k"], cfg["I"]
-    flops = 2.0 * T_all * k * 3 * I * H / world  # average rows per rank
+    flops = 2.0 * T * k * 3 * I * H  # rows per rank on average = T*k
     achieved = flops / (exp_ms / 1e3) / 1e12 if exp_ms > 0 else 0.0
     roof = {"bound": "tensor", "kernel": "experts (gate_up + down grouped GEMMs, slowest rank)",
             "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -643,12 +648,13 @@ def run_ep(args, cfg, world, rank, local):
         cfgj = config_json(cfg, world)
         cfgj.update(info)
         cfgj["placement"] = "round-robin: expert e on rank e % N"
-        cfgj["tokens_per_rank"] = T_all // world
+        cfgj["tokens_per_rank"] = T
+        cfgj["tokens"] = T_all
         line = {
             "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None,
+            "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 activations, int%d weights" % cfg["bits"], "data": "synthetic",
             "config": cfgj, "stage_ms_rank0": stages, "roofline": roof, "cpu_baseline": None,
             "e2e": e2e, "gpu_launches": (4 + 3 + 1) * args.steps, "clocks": clk.summary(),

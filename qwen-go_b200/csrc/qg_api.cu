@@ -183,10 +183,11 @@ struct qgmoe {
     // activation buffers and their TMA descriptors
     bool tensor_ok = false;
     int path_mode = QGMOE_PATH_AUTO;
-    uint8_t *gu_pq = nullptr, *dn_pq = nullptr;
-    __half2 *gu_ps = nullptr, *dn_ps = nullptr;
+    uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
+    __half2 *gu_ps = nullptr, *dn_ps = nullptr, *sgu_ps = nullptr, *sdn_ps = nullptr;
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
-    CUtensorMap tmap_x{}, tmap_h{};
+    // [0]: 256-token boxes (prefill tiles), [1]: 64-token boxes (decode tiles)
+    CUtensorMap tmap_x[2]{}, tmap_h[2]{}, tmap_hs[2]{};
     // stage timing (qgmoe_set_timing): one event set per timed forward since
     // the last read, so a whole timed loop runs without host syncs.
     static constexpr int kMaxStages = 8;
@@ -239,6 +240,8 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(st.act_n, sizeof(int32_t) * (m->E + 1));
     QG_A(st.n_act, sizeof(int32_t));
     QG_A(st.tile_prefix, sizeof(int32_t) * (m->E + 2));
+    QG_A(st.n_act_routed, sizeof(int32_t));
+    QG_A(st.shared_act, sizeof(int32_t) * 6);
     {
         const int Ep = m->E + m->has_shared;
         size_t rows = 0;  // max over T' <= cap of splits(T') * T'
@@ -251,9 +254,9 @@ static int ensure_capacity(qgmoe *m, int T) {
         QG_A(st.expert_off, sizeof(int32_t) * m->E);
     }
     if (m->tensor_ok) {
-        QG_A(m->xp16, sizeof(__half) * pairs * m->H);
-        QG_A(m->h16, sizeof(__half) * pairs * m->I);
-        QG_A(m->d16, sizeof(__half) * pairs * m->H);
+        QG_A(m->xp16, sizeof(__half) * slots * m->H);
+        QG_A(m->h16, sizeof(__half) * slots * m->hmax);
+        QG_A(m->d16, sizeof(__half) * slots * m->H);
     }
     QG_A(m->h, sizeof(float) * slots * m->hmax);
     QG_A(m->d, sizeof(float) * slots * m->H);
@@ -266,18 +269,26 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream));
     QG_CUDA(cudaStreamSynchronize(m->stream));
     if (m->tensor_ok) {
-        if ((rc = encode_act_map(&m->tmap_x, m->xp16, (int)pairs, m->H))) return rc;
-        if ((rc = encode_act_map(&m->tmap_h, m->h16, (int)pairs, m->I))) return rc;
+        const int box[2] = {256, 64};
+        for (int i = 0; i < 2; i++) {
+            if ((rc = encode_act_map(&m->tmap_x[i], m->xp16, (int)slots, m->H, m->H, box[i])))
+                return rc;
+            if ((rc = encode_act_map(&m->tmap_h[i], m->h16, (int)slots, m->I, m->hmax, box[i])))
+                return rc;
+            if (m->has_shared &&
+                (rc = encode_act_map(&m->tmap_hs[i], m->h16, (int)slots, m->Is, m->hmax, box[i])))
+                return rc;
+        }
     }
     m->cap_T = cap;
     return QGMOE_OK;
 }
 
-// Tensor-core path: int8/int4 weights, no shared expert, H and I multiples
-// of 128 (128-row weight tiles, 64-wide K blocks).
+// Tensor-core path: int8/int4 weights, H, I (and the shared width) multiples
+// of 128 (128-row weight tiles of 64 gate + 64 up rows, 64-wide K blocks).
 static int build_tensor_weights(qgmoe *m) {
-    const int E = m->G, H = m->H, I = m->I, bits = m->bits;
-    if (!((bits == 8 || bits == 4) && !m->has_shared && H % 128 == 0 && I % 128 == 0))
+    const int E = m->G, H = m->H, I = m->I, Is = m->Is, bits = m->bits;
+    if (!((bits == 8 || bits == 4) && H % 128 == 0 && I % 128 == 0 && Is % 128 == 0))
         return QGMOE_OK;
     Allocs &al = m->weights;
     int rc;
@@ -298,6 +309,20 @@ static int build_tensor_weights(qgmoe *m) {
     if ((rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 0, 0, m->dn_pq, m->dn_ps,
                             m->stream)))
         return rc;
+    if (m->has_shared) {  // the shared expert as one more (single-expert) weight set
+        if ((rc = al.alloc(reinterpret_cast<void **>(&m->sgu_pq), (size_t)2 * Is * H * bits / 8)) ||
+            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_pq), (size_t)H * Is * bits / 8)) ||
+            (rc = al.alloc(reinterpret_cast<void **>(&m->sgu_ps),
+                           sizeof(__half2) * (size_t)2 * Is * (H / 64))) ||
+            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_ps),
+                           sizeof(__half2) * (size_t)H * (Is / 64))))
+            return rc;
+        if ((rc = launch_repack(m->sgu.q, m->sgu.s, bits, 1, 2 * Is, H, Is / 64, 1, Is, m->sgu_pq,
+                                m->sgu_ps, m->stream)) ||
+            (rc = launch_repack(m->sdn.q, m->sdn.s, bits, 1, H, Is, H / 128, 0, 0, m->sdn_pq,
+                                m->sdn_ps, m->stream)))
+            return rc;
+    }
     QG_CUDA(cudaStreamSynchronize(m->stream));
     m->tensor_ok = true;
     return QGMOE_OK;
@@ -306,10 +331,22 @@ static int build_tensor_weights(qgmoe *m) {
 static bool use_tensor(const qgmoe *m, int T) {
     if (!m->tensor_ok || m->path_mode == QGMOE_PATH_CUDA_CORE) return false;
     if (m->path_mode == QGMOE_PATH_TENSOR) return true;
-    return T * m->k >= 2048;
+    return T * m->k >= 64;
+}
+
+// Tokens per tensor-core work unit: 256 when experts average more than 96
+// tokens in this call (prefill), else 64 (decode: smaller activation stages,
+// deeper weight ring).
+static int tile_tokens_for(const qgmoe *m, int T) {
+    const int pairs = T * m->k;
+    const int groups = pairs < m->G ? pairs : m->G;
+    return pairs > 96 * groups ? 256 : 64;
 }
 
 static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    const int nt = tile_tokens_for(m, T);
+    const int ti = nt == 256 ? 0 : 1;
+    m->st.tile_tokens = nt;
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
@@ -317,24 +354,40 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     if (rc) return rc;
     m->mark(1, "route", s);
     const int pairs = T * m->k;
-    const int tiles =
-        (pairs + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS + (pairs < m->E ? pairs : m->E);
+    const int tiles = (pairs + nt - 1) / nt + (pairs < m->E ? pairs : m->E);
+    int launches = 4;  // logits, top-k, scatter, gather
     UmmaLaunch l{};
     l.act_group = m->st.act_group;
     l.act_begin = m->st.act_begin;
     l.act_n = m->st.act_n;
-    l.n_act = m->st.n_act;
+    l.n_act = m->st.n_act_routed;
     l.tile_prefix = m->st.tile_prefix;
     l.err = m->err_dev;
+    l.tile_tokens = nt;
     // gate_up + SwiGLU -> h16
     l.wq = m->gu_pq;
     l.ws = m->gu_ps;
     l.RT = m->I / 64;
     l.KB = m->H / 64;
     l.out = m->h16;
-    l.out_stride = m->I;
+    l.out_stride = m->hmax;
     l.grid = tiles * l.RT;
-    if ((rc = launch_umma(m->bits, true, &m->tmap_x, l, s))) return rc;
+    if ((rc = launch_umma(m->bits, true, &m->tmap_x[ti], l, s))) return rc;
+    // shared expert gate_up (one group: slots T*k .. T*k+T-1)
+    UmmaLaunch sl = l;
+    if (m->has_shared) {
+        sl.act_group = m->st.shared_act;
+        sl.act_begin = m->st.shared_act + 1;
+        sl.act_n = m->st.shared_act + 2;
+        sl.n_act = m->st.shared_act + 3;
+        sl.tile_prefix = m->st.shared_act + 4;
+        sl.wq = m->sgu_pq;
+        sl.ws = m->sgu_ps;
+        sl.RT = m->Is / 64;
+        sl.grid = ((T + nt - 1) / nt) * sl.RT;
+        if ((rc = launch_umma(m->bits, true, &m->tmap_x[ti], sl, s))) return rc;
+        launches++;
+    }
     m->mark(2, "gate_up", s);
     // down -> d16
     l.wq = m->dn_pq;
@@ -344,13 +397,24 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     l.out = m->d16;
     l.out_stride = m->H;
     l.grid = tiles * l.RT;
-    if ((rc = launch_umma(m->bits, false, &m->tmap_h, l, s))) return rc;
+    if ((rc = launch_umma(m->bits, false, &m->tmap_h[ti], l, s))) return rc;
+    if (m->has_shared) {
+        sl.wq = m->sdn_pq;
+        sl.ws = m->sdn_ps;
+        sl.RT = m->H / 128;
+        sl.KB = m->Is / 64;
+        sl.out = m->d16;
+        sl.out_stride = m->H;
+        sl.grid = ((T + nt - 1) / nt) * sl.RT;
+        if ((rc = launch_umma(m->bits, false, &m->tmap_hs[ti], sl, s))) return rc;
+        launches++;
+    }
     m->mark(3, "down", s);
     if ((rc = launch_combine_f16(m->d16, m->H, T, m->k, m->st.pair_slot, m->st.topk_w,
                                  m->st.shared_w, m->has_shared, out, s)))
         return rc;
     m->mark(4, "combine", s);
-    m->last_launches = 6;  // logits, top-k, scatter+gather, gate_up, down, combine
+    m->last_launches = launches + 3;  // + gate_up, down, combine
     return QGMOE_OK;
 }
 
@@ -644,8 +708,8 @@ static int ep_capacity(qgmoe *m, int R) {
         (rc = w.alloc(reinterpret_cast<void **>(&m->grp2recv), sizeof(int32_t) * (size_t)cap)) ||
         (rc = w.alloc(reinterpret_cast<void **>(&m->ep_tab), sizeof(int32_t) * tab)))
         return rc;
-    if ((rc = encode_act_map(&m->tmap_xg, m->xg16, cap, m->H))) return rc;
-    if ((rc = encode_act_map(&m->tmap_eh, m->eh16, cap, m->I))) return rc;
+    if ((rc = encode_act_map(&m->tmap_xg, m->xg16, cap, m->H, m->H, 256))) return rc;
+    if ((rc = encode_act_map(&m->tmap_eh, m->eh16, cap, m->I, m->I, 256))) return rc;
     m->ep_host.assign(tab, 0);
     m->cap_R = cap;
     return QGMOE_OK;
@@ -728,7 +792,7 @@ int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t
             act_begin[na] = base;
             act_n[na] = ng;
             tile_prefix[na] = tiles;
-            tiles += (ng + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS;
+            tiles += (ng + 255) / 256;  // 256-token tensor-core tiles
             na++;
         }
         base += ng;
@@ -753,6 +817,7 @@ int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t
     l.n_act = d_n_act;
     l.tile_prefix = d_tile_prefix;
     l.err = m->err_dev;
+    l.tile_tokens = 256;
     l.wq = m->gu_pq;
     l.ws = m->gu_ps;
     l.RT = m->I / 64;

@@ -57,7 +57,11 @@ struct RouteState {
     int32_t *act_begin;  // [E+1] first slot of the group
     int32_t *act_n;      // [E+1] tokens in the group
     int32_t *n_act;      // [1]
-    int32_t *tile_prefix;  // [E+2] QG_TILE_TOKENS-token tiles before each routed group, total last
+    int32_t *tile_prefix;  // [E+2] tile_tokens-token tiles before each routed group, total last
+    int32_t *n_act_routed; // [1] routed groups in the active list (the shared one excluded)
+    int32_t *shared_act;   // [6] the shared expert as a one-group list: group 0, first
+                           //     slot T*k, T tokens, count 1, tile prefix {0, tiles}
+    int tile_tokens;       // tile granularity of tile_prefix (256 or 64; 0 = 256)
     float *logits;         // [splits][T][E+1] split-K partial router logits
     int32_t *hist;         // [ceil(T/32)][E] expert histogram of each top-k CTA
     int32_t *expert_off;   // [E] first slot of each dispatch key
@@ -82,8 +86,8 @@ struct UmmaLaunch {
     const int32_t *out_map;     // GEMM2 only: output row of each slot (null = same slot)
     int *err;
     int grid;                   // upper bound of work units
+    int tile_tokens;            // max tokens per work unit: 256 (prefill) or 64 (decode)
 };
-constexpr int QG_TILE_TOKENS = 256;  // token rows per tensor-core work unit
 
 // Arguments of the grouped expert kernels.
 struct ExpertArgs {
@@ -127,7 +131,7 @@ int launch_f32_to_f16(const float *in, __half *out, int64_t n, cudaStream_t s);
 int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
                  float *out, cudaStream_t s);
 int num_sms(int device);
-int encode_act_map(void *map_out, const __half *ptr, int rows, int cols);
+int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld, int box_rows);
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
                   int RT, int interleave, int up_offset, uint8_t *qo, __half2 *so,
                   cudaStream_t s);

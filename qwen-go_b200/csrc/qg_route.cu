@@ -24,8 +24,8 @@
 
 namespace qg {
 
-constexpr int LG_TOK = 32;   // tokens per logits tile
-constexpr int LG_ROWS = 128; // router rows per logits tile
+constexpr int LG_TOK = 64;   // tokens per logits tile (8 per warp)
+constexpr int LG_ROWS = 128; // router rows per logits tile (4 per lane)
 constexpr int LG_KC = 32;    // K chunk staged in shared memory
 constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA
 constexpr int RT_THREADS = 1024;  // top-k and scatter CTAs: one warp per token
@@ -57,6 +57,10 @@ int route_splits(int T, int H, int Ep, int sms) {
 }
 
 // ---- 1. logits ------------------------------------------------------------------
+// CTA tile: 64 tokens x 128 router rows x one K slice.  Warp w owns tokens
+// 8w..8w+7, lane l owns rows 4l..4l+3: per K step two broadcast float4 reads
+// of x and one float4 read of the router feed 32 FMAs.  The next K chunk is
+// fetched into registers while the current one is consumed.
 __global__ void __launch_bounds__(256)
 k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *__restrict__ router,
          const float *__restrict__ shared_gate, int ksplit, float *__restrict__ part) {
@@ -66,61 +70,76 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
     const int t0 = blockIdx.x * LG_TOK, r0 = blockIdx.y * LG_ROWS, s = blockIdx.z;
     const int kc = ((H / LG_KC + ksplit - 1) / ksplit) * LG_KC;
     const int k0 = s * kc, k1 = min(H, k0 + kc);
-    float acc[4][4] = {};
-    // Each thread stages one float4 of x and four float4 of the router per
-    // chunk; the next chunk is fetched into registers while this one computes.
-    const int tok = tid >> 3, k4 = (tid & 7) * 4;
-    const float *xrow = (t0 + tok < T) ? x + (size_t)(t0 + tok) * H : nullptr;
+    float acc[8][4] = {};
+    const int lrow = tid >> 3, k4 = (tid & 7) * 4;  // loader: row / token, float4 column
+    const float *xrow[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const int t = t0 + lrow + 32 * j;
+        xrow[j] = t < T ? x + (size_t)t * H : nullptr;
+    }
     const float *wrow[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        const int r = r0 + tok + 32 * j;
+        const int r = r0 + lrow + 32 * j;
         wrow[j] = r < Ep ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
     }
-    auto fetch = [&](int kb, float4 &xv, float4 (&wv)[4]) {
-        xv = xrow ? *reinterpret_cast<const float4 *>(xrow + kb + k4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 xn[2], wn[4];
+    auto fetch = [&](int kb) {
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+            xn[j] = xrow[j] ? *reinterpret_cast<const float4 *>(xrow[j] + kb + k4) : zero;
 #pragma unroll
         for (int j = 0; j < 4; j++)
-            wv[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + k4))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + k4)) : zero;
     };
-    float4 xn, wn[4];
-    if (k0 < k1) fetch(k0, xn, wn);
+    if (k0 < k1) fetch(k0);
     for (int kb = k0; kb < k1; kb += LG_KC) {
-        xs[k4][tok] = xn.x;
-        xs[k4 + 1][tok] = xn.y;
-        xs[k4 + 2][tok] = xn.z;
-        xs[k4 + 3][tok] = xn.w;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int t = lrow + 32 * j;
+            xs[k4][t] = xn[j].x;
+            xs[k4 + 1][t] = xn[j].y;
+            xs[k4 + 2][t] = xn[j].z;
+            xs[k4 + 3][t] = xn[j].w;
+        }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const int row = tok + 32 * j;
+            const int row = lrow + 32 * j;
             ws[k4][row] = wn[j].x;
             ws[k4 + 1][row] = wn[j].y;
             ws[k4 + 2][row] = wn[j].z;
             ws[k4 + 3][row] = wn[j].w;
         }
         __syncthreads();
-        if (kb + LG_KC < k1) fetch(kb + LG_KC, xn, wn);
-#pragma unroll 8
+        if (kb + LG_KC < k1) fetch(kb + LG_KC);
+#pragma unroll 4
         for (int kk = 0; kk < LG_KC; kk++) {
-            const float4 a = *reinterpret_cast<const float4 *>(&xs[kk][4 * warp]);
+            const float4 a0 = *reinterpret_cast<const float4 *>(&xs[kk][8 * warp]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&xs[kk][8 * warp + 4]);
             const float4 b = *reinterpret_cast<const float4 *>(&ws[kk][4 * lane]);
-            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int i = 0; i < 8; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int t = t0 + 4 * warp + i;
+    for (int i = 0; i < 8; i++) {
+        const int t = t0 + 8 * warp + i;
         if (t >= T) continue;
+        const int r = r0 + 4 * lane;
+        float *dst = part + ((size_t)s * T + t) * Ep + r;
+        if (r + 3 < Ep && (Ep & 3) == 0) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int r = r0 + 4 * lane + j;
-            if (r < Ep) part[((size_t)s * T + t) * Ep + r] = acc[i][j];
+            for (int j = 0; j < 4; j++)
+                if (r + j < Ep) dst[j] = acc[i][j];
         }
     }
 }
@@ -293,13 +312,23 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
         }
         int total_act = __shfl_sync(0xffffffffu, nzi, 31);
         if (lane == 0) {
+            const int tt = st.tile_tokens > 0 ? st.tile_tokens : 256;
             int tiles = 0, ai = 0;
             for (int e = 0; e < E; e++)
                 if (cnt[e] > 0) {
                     st.tile_prefix[ai++] = tiles;
-                    tiles += (cnt[e] + QG_TILE_TOKENS - 1) / QG_TILE_TOKENS;
+                    tiles += (cnt[e] + tt - 1) / tt;
                 }
             st.tile_prefix[ai] = tiles;
+            if (st.n_act_routed) *st.n_act_routed = ai;
+            if (has_shared && st.shared_act) {
+                st.shared_act[0] = 0;
+                st.shared_act[1] = T * k;
+                st.shared_act[2] = T;
+                st.shared_act[3] = 1;
+                st.shared_act[4] = 0;
+                st.shared_act[5] = (T + tt - 1) / tt;
+            }
             if (has_shared) {
                 st.act_group[total_act] = E;
                 st.act_begin[total_act] = T * k;
@@ -429,7 +458,7 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     QG_CUDA(cudaGetLastError());
     k_scatter<<<nc, RT_THREADS, sm3, s>>>(T, E, k, has_shared, st, err);
     QG_CUDA(cudaGetLastError());
-    if (xp) return launch_gather_f16(x, st.slot_token, T * k, H, xp, s);
+    if (xp) return launch_gather_f16(x, st.slot_token, T * k + (has_shared ? T : 0), H, xp, s);
     return QGMOE_OK;
 }
 

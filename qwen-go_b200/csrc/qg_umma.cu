@@ -46,22 +46,24 @@ constexpr int UM_ACT_WARP = 14;    // tiled TMA of the activation (B) tiles
 constexpr int UM_THREADS = 15 * 32;
 constexpr int UM_CONV = UM_CONV_WARPS * 32;
 constexpr int UM_M = 128;          // weight rows per tile (= TMEM lanes)
-constexpr int UM_N = 256;          // max tokens per tile (= TMEM columns per buffer)
+// Max tokens per tile NT (= TMEM columns per accumulator buffer) is a template
+// parameter: 256 for prefill batches, 64 for decode batches (smaller activation
+// stages leave room for a deeper weight-code ring).
 constexpr int UM_BK = 64;          // K elements per stage (one 128-byte fp16 row)
 constexpr int UM_XS = UM_M + 4;    // epilogue staging row stride (floats, 16 B aligned)
 constexpr int UM_EC = 16;          // token columns per epilogue chunk
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
-template <int BITS>
+template <int BITS, int NT>
 struct UmCfg {
-    static constexpr int STAGES = 3;
-    static constexpr int RAW_STAGES = BITS == 8 ? 6 : 8;
+    static constexpr int STAGES = NT == 256 ? 3 : 4;
+    static constexpr int RAW_STAGES = NT == 256 ? (BITS == 8 ? 6 : 8) : (BITS == 8 ? 12 : 20);
     static constexpr int A_BYTES = UM_M * UM_BK * 2;            // 16 KB fp16
-    static constexpr int B_BYTES = UM_N * UM_BK * 2;            // 32 KB fp16
+    static constexpr int B_BYTES = NT * UM_BK * 2;              // 32 KB / 8 KB fp16
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int RAW_CODE = UM_M * UM_BK * BITS / 8;    // codes of one k block
     static constexpr int RAW_BYTES = RAW_CODE + UM_M * 4;       // + 2 fp16 scales per row
-    static constexpr int ACC_COLS = UM_N;
+    static constexpr int ACC_COLS = NT;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
     static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 5) + 16;
@@ -145,6 +147,7 @@ struct UmmaArgs {
 struct Unit {
     int e, rt, slot0, nval, N;
 };
+template <int NT>
 __device__ __forceinline__ Unit decode_unit(const UmmaArgs &a, int n_act, int u) {
     Unit w;
     const int ti = u / a.RT;
@@ -156,16 +159,16 @@ __device__ __forceinline__ Unit decode_unit(const UmmaArgs &a, int n_act, int u)
     }
     w.e = a.act_group[lo];
     const int tt = ti - a.tile_prefix[lo];
-    w.slot0 = a.act_begin[lo] + tt * UM_N;
-    w.nval = min(UM_N, a.act_n[lo] - tt * UM_N);
+    w.slot0 = a.act_begin[lo] + tt * NT;
+    w.nval = min(NT, a.act_n[lo] - tt * NT);
     w.N = (w.nval + 15) & ~15;
     return w;
 }
 
-template <int BITS, bool SWIGLU>
+template <int BITS, bool SWIGLU, int NT>
 __global__ void __launch_bounds__(UM_THREADS, 1)
 k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
-    using Cfg = UmCfg<BITS>;
+    using Cfg = UmCfg<BITS, NT>;
     constexpr int S = Cfg::STAGES;
     constexpr int R = Cfg::RAW_STAGES;
     constexpr int U4_TILE = Cfg::RAW_CODE / 16;
@@ -322,7 +325,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 break;
             }
             tc_fence_after();
-            const Unit w = decode_unit(a, n_act, u);
+            const Unit w = decode_unit<NT>(a, n_act, u);
             const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
             for (int c0 = 0; c0 < w.N; c0 += UM_EC) {
                 float v[16];
@@ -376,7 +379,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             int g = 0, last = -1;
             bool ok = true;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit w = decode_unit(a, n_act, u);
+                const Unit w = decode_unit<NT>(a, n_act, u);
                 const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
                 const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
                 const __half2 *scales = a.ws + tb * UM_M;
@@ -405,7 +408,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             int g = 0, last = -1;
             bool ok = true;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit w = decode_unit(a, n_act, u);
+                const Unit w = decode_unit<NT>(a, n_act, u);
                 for (int kb = 0; kb < a.KB; kb++, g++) {
                     const int s = g % S;
                     if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -428,7 +431,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             int g = 0, lt = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, lt++) {
-                const Unit w = decode_unit(a, n_act, u);
+                const Unit w = decode_unit<NT>(a, n_act, u);
                 const uint32_t idesc = idesc_f16_f32(UM_M, w.N);
                 const int buf = lt & 1;
                 if (!mbar_wait(&accEmpty[buf], ((lt >> 1) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -605,15 +608,16 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D fp16 row-major [rows, cols] tensor, box 64 cols x 256 rows, 128B swizzle.
-int encode_act_map(void *map_out, const __half *ptr, int rows, int cols) {
+// 2-D fp16 [rows, cols] tensor with row pitch `ld` elements, box 64 cols x
+// box_rows rows, 128B swizzle.
+int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return set_error(QGMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16 || cols > ld)
         return set_error(QGMOE_ERR_INVALID_ARG, "activation buffer not 16-byte aligned");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {UM_BK, UM_N};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {UM_BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                     const_cast<__half *>(ptr), dims, strides, box, estr,
@@ -647,20 +651,20 @@ int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int
     return QGMOE_OK;
 }
 
-template <int BITS, bool SWIGLU>
+template <int BITS, bool SWIGLU, int NT>
 static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStream_t s) {
-    using Cfg = UmCfg<BITS>;
+    using Cfg = UmCfg<BITS, NT>;
     int dev = 0;
     cudaGetDevice(&dev);
     static bool done[64] = {false};
     if (dev < 64 && !done[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, SWIGLU>,
+        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, SWIGLU, NT>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
         done[dev] = true;
     }
     int g = num_sms(dev);
     if (grid < g) g = grid;
-    k_umma<BITS, SWIGLU><<<g, UM_THREADS, Cfg::SMEM, s>>>(
+    k_umma<BITS, SWIGLU, NT><<<g, UM_THREADS, Cfg::SMEM, s>>>(
         *reinterpret_cast<const CUtensorMap *>(tmap), a);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
@@ -682,10 +686,16 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.out_map = l.out_map;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
-    if (bits == 8 && swiglu) return launch_umma_t<8, true>(tmap, a, l.grid, s);
-    if (bits == 8 && !swiglu) return launch_umma_t<8, false>(tmap, a, l.grid, s);
-    if (bits == 4 && swiglu) return launch_umma_t<4, true>(tmap, a, l.grid, s);
-    if (bits == 4 && !swiglu) return launch_umma_t<4, false>(tmap, a, l.grid, s);
+    const bool big = l.tile_tokens != 64;
+#define QG_UMMA_CASE(B, SW)                                                        \
+    if (bits == B && swiglu == SW)                                                 \
+        return big ? launch_umma_t<B, SW, 256>(tmap, a, l.grid, s)                 \
+                   : launch_umma_t<B, SW, 64>(tmap, a, l.grid, s);
+    QG_UMMA_CASE(8, true)
+    QG_UMMA_CASE(8, false)
+    QG_UMMA_CASE(4, true)
+    QG_UMMA_CASE(4, false)
+#undef QG_UMMA_CASE
     return set_error(QGMOE_ERR_UNSUPPORTED, "tensor path needs int8/int4 weights");
 }
 

@@ -50,11 +50,26 @@ def test_tensor_matches_cuda_core_path(bits):
     assert np.array_equal(g.forward_batch(x), b)
 
 
-def test_tensor_path_unavailable_with_shared_expert():
-    m = host_case(H=256, E=8, k=2, I=128, Is=128, bits=8, seed=71)
+def test_tensor_path_needs_128_multiples():
+    m = host_case(H=256, E=8, k=2, I=128, Is=96, bits=8, seed=71)
     g = make_gpu_moe(m, O.ROUTER_TOPK)
     with pytest.raises(qgmoe.QgmoeError):
         g.set_path(qgmoe.PATH_TENSOR)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("T", [2, 40, 300])
+def test_tensor_with_shared_expert(bits, T):
+    """The gated shared expert runs as a one-group tensor-core GEMM pair over
+    all T tokens (slots T*k..T*k+T-1); 64- and 256-token tiles both occur."""
+    m = host_case(H=256, E=8, k=2, I=128, Is=256, bits=bits, seed=73 + T)
+    x = O.randn(73, T, (T, 256))
+    g = tensor_moe(m)
+    out, idx, w = g.forward_batch(x, return_routing=True)
+    assert g.last_launch_count() == 9
+    ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
+    flipped = check_routing(idx, w, ridx, rw, probs)
+    check_outputs(out, ref, bits, skip_tokens=flipped)
 
 
 def test_tensor_one_expert_many_tiles():
