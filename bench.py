@@ -466,7 +466,7 @@ def run_ours(args, cfg):
     distinct = int((hist > 0).sum())
 
     # ---- timed region (device events, max over ranks) ----
-    layer.set_timing(True)
+    # Repeated identical forwards replay a CUDA graph inside the library.
     barrier(world)
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -476,12 +476,19 @@ def run_ours(args, cfg):
             step()
         ev1.record(stream)
         torch.cuda.synchronize(dev)
+    layer.sync(stream)
+    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    ms_per_step = total_ms / args.steps
+    # ---- second timed region: the same K steps with a CUDA event between
+    # consecutive launches (graphs off), for the per-kernel durations ----
+    layer.set_timing(True)
+    torch.cuda.synchronize(dev)
+    for _ in range(args.steps):
+        step()
     stage_ms, nf = layer.read_timing()
     layer.set_timing(False)
     layer.sync(stream)
-    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
     forward_ms = sum(stage_ms.values()) / max(nf, 1)
-    ms_per_step = total_ms / args.steps
     value = T * world * args.steps / (total_ms / 1e3)
 
     # ---- roofline of the dominant kernel ----

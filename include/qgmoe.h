@@ -159,6 +159,12 @@ int qgmoe_last_launch_count(const qgmoe_t *h);
  * experts, no shared expert, H and I multiples of 128) and the CUDA-core
  * streaming GEMV otherwise.  CUDA_CORE / TENSOR force one path (TENSOR
  * returns QGMOE_ERR_UNSUPPORTED when the layer does not allow it). */
+/* CUDA graphs (default on): the second forward with the same T, x, out and
+ * stream is captured into a graph and later identical calls replay it, which
+ * removes the per-launch host cost of decode-sized calls.  Disabled while
+ * stage timing is on.  enable = 0 turns graphs off and drops cached ones. */
+int qgmoe_set_graphs(qgmoe_t *h, int32_t enable);
+
 #define QGMOE_PATH_AUTO 0
 #define QGMOE_PATH_CUDA_CORE 1
 #define QGMOE_PATH_TENSOR 2

@@ -10,6 +10,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <tuple>
 #include <vector>
 
 #include "qg_common.cuh"
@@ -183,11 +185,23 @@ struct qgmoe {
     // activation buffers and their TMA descriptors
     bool tensor_ok = false;
     int path_mode = QGMOE_PATH_AUTO;
+    // CUDA graphs of whole forwards, keyed by (T, x, out, stream): captured on
+    // the second identical call, replayed after that (launch latency dominates
+    // decode-sized calls).  Invalidated when workspace or path changes.
+    bool graphs = true;
+    using GraphKey = std::tuple<int, const void *, void *, cudaStream_t>;
+    std::map<GraphKey, cudaGraphExec_t> graph_exec;
+    std::map<GraphKey, int> graph_seen;
+    void drop_graphs() {
+        for (auto &kv : graph_exec) cudaGraphExecDestroy(kv.second);
+        graph_exec.clear();
+        graph_seen.clear();
+    }
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
     __half2 *gu_ps = nullptr, *dn_ps = nullptr, *sgu_ps = nullptr, *sdn_ps = nullptr;
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
-    // [0]: 256-token boxes (prefill tiles), [1]: 64-token boxes (decode tiles)
-    CUtensorMap tmap_x[2]{}, tmap_h[2]{}, tmap_hs[2]{};
+    // boxes of 256 / 64 / 16 token rows (prefill and decode tile sizes)
+    CUtensorMap tmap_x[3]{}, tmap_h[3]{}, tmap_hs[3]{};
     // stage timing (qgmoe_set_timing): one event set per timed forward since
     // the last read, so a whole timed loop runs without host syncs.
     static constexpr int kMaxStages = 8;
@@ -218,6 +232,7 @@ struct qgmoe {
 static int ensure_capacity(qgmoe *m, int T) {
     if (T <= m->cap_T) return QGMOE_OK;
     cudaStreamSynchronize(m->stream);
+    m->drop_graphs();  // captured graphs point into the old workspace
     m->work.free_all();
     int cap = m->cap_T ? m->cap_T : 1;
     while (cap < T) cap *= 2;
@@ -269,8 +284,8 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream));
     QG_CUDA(cudaStreamSynchronize(m->stream));
     if (m->tensor_ok) {
-        const int box[2] = {256, 64};
-        for (int i = 0; i < 2; i++) {
+        const int box[3] = {256, 64, 16};
+        for (int i = 0; i < 3; i++) {
             if ((rc = encode_act_map(&m->tmap_x[i], m->xp16, (int)slots, m->H, m->H, box[i])))
                 return rc;
             if ((rc = encode_act_map(&m->tmap_h[i], m->h16, (int)slots, m->I, m->hmax, box[i])))
@@ -334,18 +349,18 @@ static bool use_tensor(const qgmoe *m, int T) {
     return T * m->k >= 64;
 }
 
-// Tokens per tensor-core work unit: 256 when experts average more than 96
-// tokens in this call (prefill), else 64 (decode: smaller activation stages,
-// deeper weight ring).
+// Tokens per tensor-core work unit from the average tokens per expert in this
+// call: > 96 -> 256 (prefill), > 16 -> 64, else 16 (decode: small activation
+// stages, deeper rings).
 static int tile_tokens_for(const qgmoe *m, int T) {
     const int pairs = T * m->k;
     const int groups = pairs < m->G ? pairs : m->G;
-    return pairs > 96 * groups ? 256 : 64;
+    return pairs > 96 * groups ? 256 : (pairs > 16 * groups ? 64 : 16);
 }
 
 static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
     const int nt = tile_tokens_for(m, T);
-    const int ti = nt == 256 ? 0 : 1;
+    const int ti = nt == 256 ? 0 : (nt == 64 ? 1 : 2);
     m->st.tile_tokens = nt;
     m->begin_timed();
     m->mark(0, nullptr, s);
@@ -478,6 +493,37 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     return QGMOE_OK;
 }
 
+// Enqueues one forward, through a cached CUDA graph when possible.
+static int run_forward(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    if (!m->graphs || m->timing || m->ep_world > 1) return enqueue_forward(m, x, T, out, s);
+    const qgmoe::GraphKey key{T, x, out, s};
+    auto it = m->graph_exec.find(key);
+    if (it != m->graph_exec.end()) {
+        QG_CUDA(cudaGraphLaunch(it->second, s));
+        return QGMOE_OK;
+    }
+    if (++m->graph_seen[key] < 2) return enqueue_forward(m, x, T, out, s);  // first call: warm
+    cudaStreamCaptureStatus cs;
+    QG_CUDA(cudaStreamIsCapturing(s, &cs));
+    if (cs != cudaStreamCaptureStatusNone) return enqueue_forward(m, x, T, out, s);
+    QG_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(m, x, T, out, s);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return set_error(QGMOE_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_error(QGMOE_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    m->graph_exec[key] = ex;
+    QG_CUDA(cudaGraphLaunch(ex, s));
+    return QGMOE_OK;
+}
+
 extern "C" {
 
 int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
@@ -580,6 +626,7 @@ int qgmoe_destroy(qgmoe_t *m) {
     if (!m) return QGMOE_OK;
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    m->drop_graphs();
     m->work.free_all();
     m->ep_work.free_all();
     m->weights.free_all();
@@ -601,7 +648,7 @@ int qgmoe_forward_device(qgmoe_t *m, const float *x, int32_t T, float *out, int3
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
     int rc = ensure_capacity(m, T);
     if (rc) return rc;
-    if ((rc = enqueue_forward(m, x, T, out, s))) return rc;
+    if ((rc = run_forward(m, x, T, out, s))) return rc;
     if (sel_idx)
         QG_CUDA(cudaMemcpyAsync(sel_idx, m->st.topk_idx, sizeof(int32_t) * T * m->k,
                                 cudaMemcpyDeviceToDevice, s));
@@ -622,7 +669,7 @@ int qgmoe_forward(qgmoe_t *m, const float *x, int32_t T, float *out, int32_t *se
     if (rc) return rc;
     cudaStream_t s = m->stream;
     QG_CUDA(cudaMemcpyAsync(m->x_dev, x, sizeof(float) * T * m->H, cudaMemcpyHostToDevice, s));
-    if ((rc = enqueue_forward(m, m->x_dev, T, m->out_dev, s))) return rc;
+    if ((rc = run_forward(m, m->x_dev, T, m->out_dev, s))) return rc;
     QG_CUDA(cudaMemcpyAsync(out, m->out_dev, sizeof(float) * T * m->H, cudaMemcpyDeviceToHost, s));
     if (sel_idx)
         QG_CUDA(cudaMemcpyAsync(sel_idx, m->st.topk_idx, sizeof(int32_t) * T * m->k,
@@ -643,6 +690,15 @@ int qgmoe_sync(qgmoe_t *m, void *stream) {
 
 int qgmoe_last_launch_count(const qgmoe_t *m) { return m ? m->last_launches : 0; }
 
+int qgmoe_set_graphs(qgmoe_t *m, int32_t enable) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStreamSynchronize(m->stream);
+    m->graphs = enable != 0;
+    m->drop_graphs();
+    return QGMOE_OK;
+}
+
 int qgmoe_set_path(qgmoe_t *m, int32_t mode) {
     if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
     if (mode != QGMOE_PATH_AUTO && mode != QGMOE_PATH_CUDA_CORE && mode != QGMOE_PATH_TENSOR)
@@ -652,6 +708,7 @@ int qgmoe_set_path(qgmoe_t *m, int32_t mode) {
                          "tensor-core path needs int8/int4 experts, no shared expert, "
                          "H and I multiples of 128");
     m->path_mode = mode;
+    m->drop_graphs();
     return QGMOE_OK;
 }
 

@@ -47,8 +47,8 @@ constexpr int UM_THREADS = 15 * 32;
 constexpr int UM_CONV = UM_CONV_WARPS * 32;
 constexpr int UM_M = 128;          // weight rows per tile (= TMEM lanes)
 // Max tokens per tile NT (= TMEM columns per accumulator buffer) is a template
-// parameter: 256 for prefill batches, 64 for decode batches (smaller activation
-// stages leave room for a deeper weight-code ring).
+// parameter: 256 for prefill batches, 64 or 16 for decode batches (smaller
+// activation stages leave room for deeper rings).
 constexpr int UM_BK = 64;          // K elements per stage (one 128-byte fp16 row)
 constexpr int UM_XS = UM_M + 4;    // epilogue staging row stride (floats, 16 B aligned)
 constexpr int UM_EC = 16;          // token columns per epilogue chunk
@@ -56,10 +56,12 @@ constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 template <int BITS, int NT>
 struct UmCfg {
-    static constexpr int STAGES = NT == 256 ? 3 : 4;
-    static constexpr int RAW_STAGES = NT == 256 ? (BITS == 8 ? 6 : 8) : (BITS == 8 ? 12 : 20);
+    static constexpr int STAGES = NT == 256 ? 3 : (NT == 64 ? 4 : (BITS == 8 ? 6 : 8));
+    static constexpr int RAW_STAGES = NT == 256 ? (BITS == 8 ? 6 : 8)
+                                    : NT == 64  ? (BITS == 8 ? 12 : 20)
+                                                : (BITS == 8 ? 12 : 14);
     static constexpr int A_BYTES = UM_M * UM_BK * 2;            // 16 KB fp16
-    static constexpr int B_BYTES = NT * UM_BK * 2;              // 32 KB / 8 KB fp16
+    static constexpr int B_BYTES = NT * UM_BK * 2;              // 32 / 8 / 2 KB fp16
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int RAW_CODE = UM_M * UM_BK * BITS / 8;    // codes of one k block
     static constexpr int RAW_BYTES = RAW_CODE + UM_M * 4;       // + 2 fp16 scales per row
@@ -686,11 +688,12 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.out_map = l.out_map;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
-    const bool big = l.tile_tokens != 64;
+    const int nt = l.tile_tokens == 64 || l.tile_tokens == 16 ? l.tile_tokens : 256;
 #define QG_UMMA_CASE(B, SW)                                                        \
     if (bits == B && swiglu == SW)                                                 \
-        return big ? launch_umma_t<B, SW, 256>(tmap, a, l.grid, s)                 \
-                   : launch_umma_t<B, SW, 64>(tmap, a, l.grid, s);
+        return nt == 256 ? launch_umma_t<B, SW, 256>(tmap, a, l.grid, s)           \
+               : nt == 64 ? launch_umma_t<B, SW, 64>(tmap, a, l.grid, s)           \
+                          : launch_umma_t<B, SW, 16>(tmap, a, l.grid, s);
     QG_UMMA_CASE(8, true)
     QG_UMMA_CASE(8, false)
     QG_UMMA_CASE(4, true)

@@ -72,6 +72,7 @@ SIGNATURES = {
     "qgmoe_ep_combine": ([_vp, _vp, C.c_int32, _vp, _vp, _vp, _vp], C.c_int),
     "qgmoe_last_launch_count": ([_vp], C.c_int),
     "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
+    "qgmoe_set_graphs": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_timing": ([_vp, C.c_int32], C.c_int),
     "qgmoe_read_timing": ([_vp, C.POINTER(C.c_float), C.c_int32, C.POINTER(C.c_int32)], C.c_int),
     "qgmoe_stage_name": ([_vp, C.c_int32], C.c_char_p),
@@ -236,6 +237,10 @@ class MoeMLP:
     def set_path(self, mode: int):
         """PATH_AUTO, PATH_CUDA_CORE or PATH_TENSOR (see include/qgmoe.h)."""
         _check(lib().qgmoe_set_path(self.h, mode), "qgmoe_set_path")
+
+    def set_graphs(self, enable: bool = True):
+        """CUDA-graph replay of repeated identical forwards (default on)."""
+        _check(lib().qgmoe_set_graphs(self.h, int(enable)), "qgmoe_set_graphs")
 
     def set_timing(self, enable: bool = True):
         _check(lib().qgmoe_set_timing(self.h, int(enable)), "qgmoe_set_timing")
