@@ -144,6 +144,22 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
     }
 }
 
+// Sum of the split-K partials of one logit, in a fixed order; four
+// independent accumulators keep the loads in flight together.
+__device__ __forceinline__ float sum_splits(const float *__restrict__ part, int ksplit,
+                                            size_t stride, size_t off) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= ksplit; s += 4) {
+        a0 += part[off + s * stride];
+        a1 += part[off + (s + 1) * stride];
+        a2 += part[off + (s + 2) * stride];
+        a3 += part[off + (s + 3) * stride];
+    }
+    for (; s < ksplit; s++) a0 += part[off + s * stride];
+    return (a0 + a1) + (a2 + a3);
+}
+
 // ---- 2. softmax + top-k + histograms --------------------------------------------
 // A warp holds one token's probabilities in registers: lane l owns experts
 // l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
@@ -165,10 +181,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
-            float acc = 0.f;
-            if (e < E)
-                for (int s = 0; s < ksplit; s++) acc += part[((size_t)s * T + t) * Ep + e];
-            v[j] = e < E ? acc : -INFINITY;
+            v[j] = e < E ? sum_splits(part, ksplit, (size_t)T * Ep, (size_t)t * Ep + e) : -INFINITY;
         }
         float mx = v[0];
 #pragma unroll
@@ -255,8 +268,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
         }
         if (has_shared && lane == 0) {
-            float g = 0.f;
-            for (int s = 0; s < ksplit; s++) g += part[((size_t)s * T + t) * Ep + E];
+            const float g = sum_splits(part, ksplit, (size_t)T * Ep, (size_t)t * Ep + E);
             st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)g));
         }
         __syncwarp();

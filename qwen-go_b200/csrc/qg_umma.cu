@@ -52,6 +52,7 @@ constexpr int UM_M = 128;          // weight rows per tile (= TMEM lanes)
 constexpr int UM_BK = 64;          // K elements per stage (one 128-byte fp16 row)
 constexpr int UM_XS = UM_M + 4;    // epilogue staging row stride (floats, 16 B aligned)
 constexpr int UM_EC = 16;          // token columns per epilogue chunk
+constexpr int UM_MAX_UNITS = 64;   // work units per CTA decoded once into shared memory
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 template <int BITS, int NT>
@@ -68,9 +69,10 @@ struct UmCfg {
     static constexpr int ACC_COLS = NT;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
+    static constexpr int UNIT_BYTES = UM_MAX_UNITS * 16;
     static constexpr int BAR_BYTES = 8 * (3 * STAGES + 2 * RAW_STAGES + 5) + 16;
     static constexpr int SMEM =
-        STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + XCH_BYTES + BAR_BYTES + 1024;
+        STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(STAGE_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
 };
@@ -189,7 +191,9 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     uint8_t *raw = base + S * Cfg::STAGE_BYTES;
     const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_BYTES;
     const uint32_t xch_u32 = raw_u32 + R * Cfg::RAW_BYTES;  // [UM_EC tokens][UM_XS] f32
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES);
+    const uint32_t utab_u32 = xch_u32 + Cfg::XCH_BYTES;      // this CTA's decoded units
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES +
+                                                   Cfg::UNIT_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
     uint64_t *rawFull = empty + S;
@@ -222,6 +226,20 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
+    // Decode this CTA's units once (one binary search per unit, in parallel),
+    // so no role walks the active-expert tables in global memory per unit.
+    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const bool utab = n_mine <= UM_MAX_UNITS;
+    if (utab)
+        for (int i = tid; i < n_mine; i += UM_THREADS) {
+            const Unit w = decode_unit<NT>(a, n_act, blockIdx.x + i * gridDim.x);
+            st_shared_v4(utab_u32 + i * 16, w.e, w.rt, w.slot0, w.nval);
+        }
+    auto unit_at = [&](int i, int u) -> Unit {
+        if (!utab) return decode_unit<NT>(a, n_act, u);
+        const uint4 v = ld_shared_v4(utab_u32 + i * 16);
+        return Unit{(int)v.x, (int)v.y, (int)v.z, (int)v.w, ((int)v.w + 15) & ~15};
+    };
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -327,7 +345,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 break;
             }
             tc_fence_after();
-            const Unit w = decode_unit<NT>(a, n_act, u);
+            const Unit w = unit_at(lt, u);
             const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
             for (int c0 = 0; c0 < w.N; c0 += UM_EC) {
                 float v[16];
@@ -380,8 +398,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         if (lane == 0) {
             int g = 0, last = -1;
             bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit w = decode_unit<NT>(a, n_act, u);
+            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
+                const Unit w = unit_at(i, u);
                 const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
                 const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
                 const __half2 *scales = a.ws + tb * UM_M;
@@ -409,8 +427,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             prefetch_tmap(&tmap_b);
             int g = 0, last = -1;
             bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-                const Unit w = decode_unit<NT>(a, n_act, u);
+            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
+                const Unit w = unit_at(i, u);
                 for (int kb = 0; kb < a.KB; kb++, g++) {
                     const int s = g % S;
                     if (!mbar_wait(&empty[s], ((g / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -433,7 +451,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             int g = 0, lt = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, lt++) {
-                const Unit w = decode_unit<NT>(a, n_act, u);
+                const Unit w = unit_at(lt, u);
                 const uint32_t idesc = idesc_f16_f32(UM_M, w.N);
                 const int buf = lt & 1;
                 if (!mbar_wait(&accEmpty[buf], ((lt >> 1) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
