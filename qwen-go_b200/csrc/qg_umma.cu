@@ -1,15 +1,20 @@
 // Grouped expert GEMMs on the 5th-generation tensor cores (kernels K3'/K4',
 // prefill-sized token counts; also used for decode batches when forced).
 //
-// Swap-AB formulation per work unit (expert e, 128-row weight tile, <=256
+// Swap-AB formulation per work unit (expert e, 128-row weight tile, <=NT
 // token tile):
 //   D[rows, tokens] = W[rows, K] * X[tokens, K]^T      (tcgen05.mma kind::f16)
 // A = expert weights, dequantised from int8/int4 group-32 codes with fp16
-//     scales (model/moe.go:134-157) by eight converter warps straight into
-//     the 128B-swizzled UMMA layout in shared memory; the raw codes and
-//     scales arrive through a deep ring of bulk TMA copies;
+//     scales (model/moe.go:134-157) by converter warps; the raw codes and
+//     scales arrive through a deep ring of bulk TMA copies.  Two variants:
+//       k_umma    (NT = 256, prefill): A goes to shared memory in the
+//                 128B-swizzled UMMA layout;
+//       k_umma_ts (NT = 64 / 16, decode): A goes straight to TMEM with
+//                 tcgen05.st and the MMA reads it from there, which halves
+//                 the shared-memory traffic per weight byte -- the limit for
+//                 weight-streaming batches;
 // B = the expert's token rows in fp16, brought in by tiled TMA (SWIZZLE_128B);
-// D = fp32 accumulators in TMEM, double-buffered (2 x 256 columns): a
+// D = fp32 accumulators in TMEM, double-buffered (2 x NT columns): a
 //     dedicated epilogue warpgroup drains one buffer (tcgen05.ld) while the
 //     next unit accumulates into the other.
 //
@@ -55,17 +60,25 @@ constexpr int UM_EC = 16;          // token columns per epilogue chunk
 constexpr int UM_MAX_UNITS = 64;   // work units per CTA decoded once into shared memory
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
+// Raw code tile of one k block (128 rows x 64 codes): four 16-code chunks per
+// row, stored chunk-major ([chunk][row][CB bytes]) so that consecutive rows
+// are consecutive in shared memory; then the rows' two fp16 group scales.
+template <int BITS>
+struct RawTile {
+    static constexpr int CB = BITS == 8 ? 16 : 8;            // bytes of one 16-code chunk
+    static constexpr int CODE = UM_M * UM_BK * BITS / 8;     // 8 KB int8, 4 KB int4
+    static constexpr int BYTES = CODE + UM_M * 4;
+};
+
 template <int BITS, int NT>
 struct UmCfg {
-    static constexpr int STAGES = NT == 256 ? 3 : (NT == 64 ? 4 : (BITS == 8 ? 6 : 8));
-    static constexpr int RAW_STAGES = NT == 256 ? (BITS == 8 ? 6 : 8)
-                                    : NT == 64  ? (BITS == 8 ? 12 : 20)
-                                                : (BITS == 8 ? 12 : 14);
+    static constexpr int STAGES = 3;
+    static constexpr int RAW_STAGES = BITS == 8 ? 6 : 8;
     static constexpr int A_BYTES = UM_M * UM_BK * 2;            // 16 KB fp16
-    static constexpr int B_BYTES = NT * UM_BK * 2;              // 32 / 8 / 2 KB fp16
+    static constexpr int B_BYTES = NT * UM_BK * 2;              // 32 KB fp16
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int RAW_CODE = UM_M * UM_BK * BITS / 8;    // codes of one k block
-    static constexpr int RAW_BYTES = RAW_CODE + UM_M * 4;       // + 2 fp16 scales per row
+    static constexpr int RAW_CODE = RawTile<BITS>::CODE;
+    static constexpr int RAW_BYTES = RawTile<BITS>::BYTES;
     static constexpr int ACC_COLS = NT;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
@@ -75,6 +88,35 @@ struct UmCfg {
         STAGES * STAGE_BYTES + RAW_STAGES * RAW_BYTES + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(STAGE_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
+};
+
+// Decode-tile variant (A in TMEM): warp roles.  Converter warp w writes K
+// chunk w >> 2 (16 codes = 8 TMEM columns) of TMEM lane quarter w & 3.
+constexpr int TS_CONV_WARPS = 16;  // warps 0-15
+constexpr int TS_EPI_WARP0 = 16;   // warps 16-19 (lane quarter = warp & 3)
+constexpr int TS_CODE_WARP = 20;
+constexpr int TS_MMA_WARP = 21;
+constexpr int TS_ACT_WARP = 22;
+constexpr int TS_THREADS = 23 * 32;
+constexpr int TS_S = 6;            // stages of two k blocks: A 64 TMEM columns, B 2 tiles
+
+template <int BITS, int NT>
+struct TsCfg {
+    static constexpr int B_BYTES = NT * UM_BK * 2;                    // one tile: 8 / 2 KB fp16
+    static constexpr int STAGE_B = 2 * B_BYTES;
+    static constexpr int R = NT == 64 ? (BITS == 8 ? 12 : 24) : (BITS == 8 ? 20 : 32);
+    static constexpr int RAW_CODE = RawTile<BITS>::CODE;
+    static constexpr int RAW_BYTES = RawTile<BITS>::BYTES;
+    static constexpr int A_COL0 = 2 * NT;                             // after the accumulators
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
+    static constexpr int UNIT_BYTES = UM_MAX_UNITS * 16;
+    static constexpr int BAR_BYTES = 8 * (3 * TS_S + 2 * R + 5) + 16;
+    static constexpr int SMEM =
+        TS_S * STAGE_B + R * RAW_BYTES + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(B_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
+    static_assert(A_COL0 + TS_S * 64 <= TMEM_COLS, "TMEM budget");
 };
 
 // int8 x4 stored biased (q + 128, repacked at create time) -> two fp16x2
@@ -96,6 +138,33 @@ __device__ __forceinline__ uint32_t cvt_i4_pair(uint32_t w, int j, __half2 s2) {
     uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
     __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), bias), s2);
     return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// One 16-code chunk of a raw tile (at shared address `code`) -> eight fp16x2
+// words (K pairs 0-1, 2-3, ..., 14-15), scaled by the group scale `s2`.
+template <int BITS>
+__device__ __forceinline__ void cvt_chunk(uint32_t code, __half2 s2, uint32_t (&o)[8]) {
+    if constexpr (BITS == 8) {
+        const uint4 q = ld_shared_v4(code);
+        cvt_i8x4(q.x, s2, o[0], o[1]);
+        cvt_i8x4(q.y, s2, o[2], o[3]);
+        cvt_i8x4(q.z, s2, o[4], o[5]);
+        cvt_i8x4(q.w, s2, o[6], o[7]);
+    } else {
+        const uint2 q = ld_shared_v2(code);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            o[p] = cvt_i4_pair(q.x, p, s2);
+            o[4 + p] = cvt_i4_pair(q.y, p, s2);
+        }
+    }
+}
+
+// Group scale of tile row `row` for K chunk `q` (chunks 0-1: group 0, 2-3: group 1).
+__device__ __forceinline__ __half2 chunk_scale(uint32_t scales, int row, int q) {
+    uint32_t w = ld_shared_u32(scales + row * 4);
+    const __half2 sc = *reinterpret_cast<__half2 *>(&w);
+    return q >= 2 ? __high2half2(sc) : __low2half2(sc);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -169,15 +238,66 @@ __device__ __forceinline__ Unit decode_unit(const UmmaArgs &a, int n_act, int u)
     return w;
 }
 
+// Drains one accumulator buffer (this warp's TMEM lane quarter, token
+// columns from lane_addr) into h rows (SwiGLU) or d rows.  Per chunk of 16
+// token columns: every thread copies its TMEM lane (tile row) into a
+// [token][row] staging buffer; then each thread takes one token and 8
+// (SwiGLU) or 16 (store) consecutive rows and writes them as 16-byte vectors,
+// so each token row of h / d goes out in coalesced 128-256 byte runs.  The
+// four epilogue warps call it together (named barrier 1).
+template <bool SWIGLU>
+__device__ __forceinline__ void epi_unit(const UmmaArgs &a, const Unit &w, uint32_t lane_addr,
+                                         uint32_t xch_u32, int L, int ej, int er) {
+    for (int c0 = 0; c0 < w.N; c0 += UM_EC) {
+        float v[16];
+        tmem_ld16(lane_addr + c0, v);
+#pragma unroll
+        for (int j = 0; j < UM_EC; j++) st_shared_f32(xch_u32 + (j * UM_XS + L) * 4, v[j]);
+        epi_bar();
+        const int t = c0 + ej;
+        if (t < w.nval) {
+            const uint32_t rowp = xch_u32 + (ej * UM_XS + er) * 4;
+            if constexpr (SWIGLU) {
+                const float4 g0 = ld_shared_f4(rowp), g1 = ld_shared_f4(rowp + 16);
+                const float4 u0 = ld_shared_f4(rowp + 256), u1 = ld_shared_f4(rowp + 272);
+                const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+                const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+                uint32_t o[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float h0 = __fdividef(gv[2 * q], 1.f + __expf(-gv[2 * q])) * uv[2 * q];
+                    const float h1 =
+                        __fdividef(gv[2 * q + 1], 1.f + __expf(-gv[2 * q + 1])) * uv[2 * q + 1];
+                    __half2 hh = __floats2half2_rn(h0, h1);
+                    o[q] = *reinterpret_cast<uint32_t *>(&hh);
+                }
+                __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * 64 + er;
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+                uint32_t o[8];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float4 f = ld_shared_f4(rowp + 16 * q);
+                    __half2 a2 = __floats2half2_rn(f.x, f.y), b2 = __floats2half2_rn(f.z, f.w);
+                    o[2 * q] = *reinterpret_cast<uint32_t *>(&a2);
+                    o[2 * q + 1] = *reinterpret_cast<uint32_t *>(&b2);
+                }
+                const int orow = a.out_map ? a.out_map[w.slot0 + t] : w.slot0 + t;
+                __half *dst = a.out + (size_t)orow * a.out_stride + w.rt * UM_M + er;
+                reinterpret_cast<uint4 *>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                reinterpret_cast<uint4 *>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+        }
+        epi_bar();
+    }
+}
+
 template <int BITS, bool SWIGLU, int NT>
 __global__ void __launch_bounds__(UM_THREADS, 1)
 k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     using Cfg = UmCfg<BITS, NT>;
     constexpr int S = Cfg::STAGES;
     constexpr int R = Cfg::RAW_STAGES;
-    constexpr int U4_TILE = Cfg::RAW_CODE / 16;
-    constexpr int PER_THREAD = U4_TILE / UM_CONV;
-    constexpr int CHUNKS = BITS == 8 ? 2 : 4;  // 16-byte fp16 chunks written per uint4 of codes
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -254,22 +374,22 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     if (warp < UM_CONV_WARPS) {
         // ============ converters: raw ring -> fp16 swizzled A tiles ==========
-        // Each thread always converts the same rows/chunks of a k block, so
-        // its shared-memory offsets are fixed.
-        uint32_t code_off[PER_THREAD], scale_off[PER_THREAD], st_off[PER_THREAD][CHUNKS];
-        bool hi_half[PER_THREAD];
+        // Thread i of 256 converts chunks i and i + 256 (chunk c = (q, row) with
+        // q = c / 128): 16 codes -> two 16-byte fp16 runs of the row's 128-byte
+        // swizzled line.  Its shared-memory offsets are fixed.
+        constexpr int PER_THREAD = 4 * UM_M / UM_CONV;
+        constexpr int CB = RawTile<BITS>::CB;
+        uint32_t code_off[PER_THREAD], st_off[PER_THREAD][2];
+        int row_of[PER_THREAD], q_of[PER_THREAD];
 #pragma unroll
         for (int j = 0; j < PER_THREAD; j++) {
             const int i = tid + UM_CONV * j;
-            const int row = BITS == 8 ? (i >> 2) : (i >> 1);
-            const int sub = BITS == 8 ? (i & 3) : (i & 1);  // 16-code chunk / 32-code half
-            code_off[j] = i * 16;
-            scale_off[j] = Cfg::RAW_CODE + row * 4;
-            hi_half[j] = BITS == 8 ? (sub >= 2) : (sub == 1);
-            const int x7 = row & 7;
-#pragma unroll
-            for (int q = 0; q < CHUNKS; q++)
-                st_off[j][q] = row * 128 + (((CHUNKS * sub + q) ^ x7) << 4);
+            const int q = i / UM_M, row = i % UM_M;
+            row_of[j] = row;
+            q_of[j] = q;
+            code_off[j] = i * CB;
+            st_off[j][0] = row * 128 + (((2 * q) ^ (row & 7)) << 4);
+            st_off[j][1] = row * 128 + (((2 * q + 1) ^ (row & 7)) << 4);
         }
         int g = 0;  // running k-block counter across this CTA's units
         bool ok = true;
@@ -286,32 +406,11 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 const uint32_t A = base_u32 + s * Cfg::STAGE_BYTES;
 #pragma unroll
                 for (int j = 0; j < PER_THREAD; j++) {
-                    const uint4 q = ld_shared_v4(rs + code_off[j]);
-                    uint32_t scw = ld_shared_u32(rs + scale_off[j]);
-                    const __half2 sc = *reinterpret_cast<__half2 *>(&scw);
-                    const __half2 s2 = hi_half[j] ? __high2half2(sc) : __low2half2(sc);
-                    if constexpr (BITS == 8) {
-                        uint32_t o[8];
-                        cvt_i8x4(q.x, s2, o[0], o[1]);
-                        cvt_i8x4(q.y, s2, o[2], o[3]);
-                        cvt_i8x4(q.z, s2, o[4], o[5]);
-                        cvt_i8x4(q.w, s2, o[6], o[7]);
-                        st_shared_v4(A + st_off[j][0], o[0], o[1], o[2], o[3]);
-                        st_shared_v4(A + st_off[j][1], o[4], o[5], o[6], o[7]);
-                    } else {
-                        st_shared_v4(A + st_off[j][0], cvt_i4_pair(q.x, 0, s2),
-                                     cvt_i4_pair(q.x, 1, s2), cvt_i4_pair(q.x, 2, s2),
-                                     cvt_i4_pair(q.x, 3, s2));
-                        st_shared_v4(A + st_off[j][1], cvt_i4_pair(q.y, 0, s2),
-                                     cvt_i4_pair(q.y, 1, s2), cvt_i4_pair(q.y, 2, s2),
-                                     cvt_i4_pair(q.y, 3, s2));
-                        st_shared_v4(A + st_off[j][2], cvt_i4_pair(q.z, 0, s2),
-                                     cvt_i4_pair(q.z, 1, s2), cvt_i4_pair(q.z, 2, s2),
-                                     cvt_i4_pair(q.z, 3, s2));
-                        st_shared_v4(A + st_off[j][3], cvt_i4_pair(q.w, 0, s2),
-                                     cvt_i4_pair(q.w, 1, s2), cvt_i4_pair(q.w, 2, s2),
-                                     cvt_i4_pair(q.w, 3, s2));
-                    }
+                    uint32_t o[8];
+                    cvt_chunk<BITS>(rs + code_off[j],
+                                    chunk_scale(rs + Cfg::RAW_CODE, row_of[j], q_of[j]), o);
+                    st_shared_v4(A + st_off[j][0], o[0], o[1], o[2], o[3]);
+                    st_shared_v4(A + st_off[j][1], o[4], o[5], o[6], o[7]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -323,11 +422,6 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         }
     } else if (warp < UM_EPI_WARP0 + 4) {
         // ============ epilogue: TMEM -> SwiGLU / store ============================
-        // Per chunk of 16 token columns: every thread copies its TMEM lane
-        // (tile row) into a [token][row] staging buffer; then each thread
-        // takes one token and 8 (SwiGLU) or 16 (store) consecutive rows and
-        // writes them as 16-byte vectors, so each token row of h / d goes out
-        // in coalesced 128-256 byte runs.
         const int ew = warp - UM_EPI_WARP0;  // TMEM lane quarter
         const int L = ew * 32 + lane;        // TMEM lane = tile row
         const int et = tid - UM_EPI_WARP0 * 32;  // 0..127
@@ -347,48 +441,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             tc_fence_after();
             const Unit w = unit_at(lt, u);
             const uint32_t lane_addr = tmem + buf * Cfg::ACC_COLS + ((uint32_t)(ew * 32) << 16);
-            for (int c0 = 0; c0 < w.N; c0 += UM_EC) {
-                float v[16];
-                tmem_ld16(lane_addr + c0, v);
-#pragma unroll
-                for (int j = 0; j < UM_EC; j++) st_shared_f32(xch_u32 + (j * UM_XS + L) * 4, v[j]);
-                epi_bar();
-                const int t = c0 + ej;
-                if (t < w.nval) {
-                    const uint32_t rowp = xch_u32 + (ej * UM_XS + er) * 4;
-                    if constexpr (SWIGLU) {
-                        const float4 g0 = ld_shared_f4(rowp), g1 = ld_shared_f4(rowp + 16);
-                        const float4 u0 = ld_shared_f4(rowp + 256), u1 = ld_shared_f4(rowp + 272);
-                        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-                        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-                        uint32_t o[4];
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const float h0 = __fdividef(gv[2 * q], 1.f + __expf(-gv[2 * q])) * uv[2 * q];
-                            const float h1 =
-                                __fdividef(gv[2 * q + 1], 1.f + __expf(-gv[2 * q + 1])) * uv[2 * q + 1];
-                            __half2 hh = __floats2half2_rn(h0, h1);
-                            o[q] = *reinterpret_cast<uint32_t *>(&hh);
-                        }
-                        __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * 64 + er;
-                        *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
-                    } else {
-                        uint32_t o[8];
-#pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            const float4 f = ld_shared_f4(rowp + 16 * q);
-                            __half2 a2 = __floats2half2_rn(f.x, f.y), b2 = __floats2half2_rn(f.z, f.w);
-                            o[2 * q] = *reinterpret_cast<uint32_t *>(&a2);
-                            o[2 * q + 1] = *reinterpret_cast<uint32_t *>(&b2);
-                        }
-                        const int orow = a.out_map ? a.out_map[w.slot0 + t] : w.slot0 + t;
-                        __half *dst = a.out + (size_t)orow * a.out_stride + w.rt * UM_M + er;
-                        reinterpret_cast<uint4 *>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                        reinterpret_cast<uint4 *>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-                    }
-                }
-                epi_bar();
-            }
+            epi_unit<SWIGLU>(a, w, lane_addr, xch_u32, L, ej, er);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&accEmpty[buf]);
@@ -496,6 +549,267 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     }
 }
 
+// ---- decode tiles: A operand in TMEM ---------------------------------------------
+// Same unit sequence and roles as k_umma, with the dequantised weight tile
+// written to TMEM (tcgen05.st.32x32b: thread = tile row = TMEM lane, 16 K
+// codes -> 8 columns of fp16 pairs) instead of shared memory.  A pipeline
+// stage covers two k blocks (A: 64 TMEM columns, B: two activation tiles),
+// so the MMA issuer waits once, issues 8 MMAs and commits once per stage:
+// with N <= 64 an MMA takes about as long to issue as to run, and the
+// per-stage barrier work would otherwise pace the weight stream.
+// TMEM columns: [0, NT) and [NT, 2NT) accumulators, then 6 A stages of 64.
+// Barriers: fullA[s] completes when the 16 converter warps have stored A,
+// fullB[s] when both activation tiles have landed, empty[s] when the stage's
+// MMAs have completed (one tcgen05.commit frees A and B together).
+template <int BITS, bool SWIGLU, int NT>
+__global__ void __launch_bounds__(TS_THREADS, 1)
+k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
+    using Cfg = TsCfg<BITS, NT>;
+    constexpr int S = TS_S, R = Cfg::R;
+    constexpr int CB = RawTile<BITS>::CB;
+    extern __shared__ uint8_t smem_raw[];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_act = *a.n_act;
+    const int n_units = a.tile_prefix[n_act] * a.RT;
+    if ((int)blockIdx.x >= n_units) return;
+    const int KP = a.KB >> 1;  // stages per unit (K is a multiple of 128)
+
+    uint8_t *base = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t base_u32 = smem_u32(base);                 // activation stages
+    uint8_t *raw = base + S * Cfg::STAGE_B;
+    const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_B;
+    const uint32_t xch_u32 = raw_u32 + R * Cfg::RAW_BYTES;
+    const uint32_t utab_u32 = xch_u32 + Cfg::XCH_BYTES;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES +
+                                                   Cfg::UNIT_BYTES);
+    uint64_t *fullB = fullA + S;
+    uint64_t *empty = fullB + S;
+    uint64_t *rawFull = empty + S;
+    uint64_t *rawEmpty = rawFull + R;
+    uint64_t *accFull = rawEmpty + R;   // [2]
+    uint64_t *accEmpty = accFull + 2;   // [2]
+    uint64_t *drain = accEmpty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    const uint32_t abort_addr = smem_u32(tmem_slot + 1);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&fullA[s], TS_CONV_WARPS);
+            mbar_init(&fullB[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < R; r++) {
+            mbar_init(&rawFull[r], 1);
+            mbar_init(&rawEmpty[r], TS_CONV_WARPS);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accFull[b], 1);
+            mbar_init(&accEmpty[b], 4);
+        }
+        mbar_init(drain, 1);
+        st_volatile_shared(abort_addr, 0);
+        fence_mbar_init();
+    }
+    if (warp == TS_MMA_WARP) {
+        tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const bool utab = n_mine <= UM_MAX_UNITS;
+    if (utab)
+        for (int i = tid; i < n_mine; i += TS_THREADS) {
+            const Unit w = decode_unit<NT>(a, n_act, blockIdx.x + i * gridDim.x);
+            st_shared_v4(utab_u32 + i * 16, w.e, w.rt, w.slot0, w.nval);
+        }
+    auto unit_at = [&](int i, int u) -> Unit {
+        if (!utab) return decode_unit<NT>(a, n_act, u);
+        const uint4 v = ld_shared_v4(utab_u32 + i * 16);
+        return Unit{(int)v.x, (int)v.y, (int)v.z, (int)v.w, ((int)v.w + 15) & ~15};
+    };
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto fail = [&]() {
+        if (!ld_volatile_shared(abort_addr)) {
+            st_volatile_shared(abort_addr, 1);
+            atomicOr(a.err, QG_FLAG_TIMEOUT);
+        }
+    };
+
+    if (warp < TS_CONV_WARPS) {
+        // ============ converters: raw ring -> fp16 A tiles in TMEM ===========
+        const int qd = warp & 3, q = warp >> 2;
+        const int row = qd * 32 + lane;
+        const uint32_t code_off = (uint32_t)(q * UM_M + row) * CB;
+        const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + Cfg::A_COL0 + q * 8;
+        int g = 0, gs = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            for (int kp = 0; kp < KP; kp++, gs++) {
+                const int s = gs % S;
+                if (!mbar_wait(&empty[s], ((gs / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int h = 0; h < 2; h++, g++) {
+                    const int r = g % R;
+                    if (!mbar_wait(&rawFull[r], (g / R) & 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t rs = raw_u32 + r * Cfg::RAW_BYTES;
+                    uint32_t o[8];
+                    cvt_chunk<BITS>(rs + code_off, chunk_scale(rs + Cfg::RAW_CODE, row, q), o);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&rawEmpty[r]);  // the codes are in registers
+                    tmem_st8(ta + s * 64 + h * 32, o);
+                }
+                if (!ok) break;
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&fullA[s]);
+            }
+        }
+    } else if (warp < TS_EPI_WARP0 + 4) {
+        // ============ epilogue: TMEM -> SwiGLU / store ============================
+        const int ew = warp & 3;                 // TMEM lane quarter
+        const int L = ew * 32 + lane;            // TMEM lane = tile row
+        const int et = tid - TS_EPI_WARP0 * 32;  // 0..127
+        const int ej = et >> 3;
+        const int er = (et & 7) * (SWIGLU ? 8 : 16);
+        int lt = 0;
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, lt++) {
+            const int buf = lt & 1;
+            bool bad = !mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES);
+            bad = epi_bar_or(bad || ld_volatile_shared(abort_addr));
+            if (bad) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const Unit w = unit_at(lt, u);
+            const uint32_t lane_addr = tmem + buf * NT + ((uint32_t)(ew * 32) << 16);
+            epi_unit<SWIGLU>(a, w, lane_addr, xch_u32, L, ej, er);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accEmpty[buf]);
+        }
+    } else if (warp == TS_CODE_WARP) {
+        // ============ code/scale producer (bulk TMA) ==============================
+        if (lane == 0) {
+            int g = 0, last = -1;
+            bool ok = true;
+            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
+                const Unit w = unit_at(i, u);
+                const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
+                const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
+                const __half2 *scales = a.ws + tb * UM_M;
+                for (int kb = 0; kb < a.KB; kb++, g++) {
+                    const int r = g % R;
+                    if (!mbar_wait(&rawEmpty[r], ((g / R) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *dst = raw + r * Cfg::RAW_BYTES;
+                    mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
+                    bulk_load(dst, codes + (size_t)kb * Cfg::RAW_CODE, Cfg::RAW_CODE, &rawFull[r]);
+                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * UM_M, UM_M * 4,
+                              &rawFull[r]);
+                    last = g;
+                }
+            }
+            if (!ok && last >= 0)
+                mbar_wait(&rawFull[last % R], (last / R) & 1, 0, UM_WAIT_CYCLES);
+        }
+    } else if (warp == TS_ACT_WARP) {
+        // ============ activation producer (tiled TMA, two tiles per stage) =========
+        if (lane == 0) {
+            prefetch_tmap(&tmap_b);
+            int gs = 0, last = -1;
+            bool ok = true;
+            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
+                const Unit w = unit_at(i, u);
+                for (int kp = 0; kp < KP; kp++, gs++) {
+                    const int s = gs % S;
+                    if (!mbar_wait(&empty[s], ((gs / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&fullB[s], Cfg::STAGE_B);
+                    uint8_t *dst = base + s * Cfg::STAGE_B;
+                    tma_load_2d(dst, &tmap_b, 2 * kp * UM_BK, w.slot0, &fullB[s]);
+                    tma_load_2d(dst + Cfg::B_BYTES, &tmap_b, (2 * kp + 1) * UM_BK, w.slot0,
+                                &fullB[s]);
+                    last = gs;
+                }
+            }
+            if (!ok && last >= 0)  // let our own last copies land before smem goes away
+                mbar_wait(&fullB[last % S], (last / S) & 1, 0, UM_WAIT_CYCLES);
+        }
+    } else {
+        // ============ MMA issuer =====================================================
+        if (lane == 0) {
+            int gs = 0, lt = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, lt++) {
+                const Unit w = unit_at(lt, u);
+                const uint32_t idesc = idesc_f16_f32(UM_M, w.N);
+                const int buf = lt & 1;
+                if (!mbar_wait(&accEmpty[buf], ((lt >> 1) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + buf * NT;
+                for (int kp = 0; kp < KP; kp++, gs++) {
+                    const int s = gs % S;
+                    if (!mbar_wait(&fullB[s], (gs / S) & 1, abort_addr, UM_WAIT_CYCLES) ||
+                        !mbar_wait(&fullA[s], (gs / S) & 1, abort_addr, UM_WAIT_CYCLES)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t at = tmem + Cfg::A_COL0 + s * 64;
+                    const uint32_t bsm = base_u32 + s * Cfg::STAGE_B;
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int k16 = 0; k16 < UM_BK / 16; k16++)
+                            umma_f16_ts(acc, at + h * 32 + k16 * 8,
+                                        desc_k_sw128(bsm + h * Cfg::B_BYTES + k16 * 32), idesc,
+                                        (kp | h | k16) != 0);
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&accFull[buf]);
+            }
+            if (!ok) {
+                umma_commit(drain);
+                mbar_wait(drain, 0, 0, UM_WAIT_CYCLES);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == TS_MMA_WARP) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
 // ---- activation gather: xp[s, :] = fp16(x[slot_token[s], :]) -------------
 __global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restrict__ slot_token,
                              int nslots, int H, __half *__restrict__ xp) {
@@ -562,9 +876,11 @@ int launch_ep_regroup(const __half *recv, int R, int H, const int32_t *seg_recv_
 //   interleave (SWIGLU): row < 64 -> rt*64 + row (gate),
 //                        row >= 64 -> up_offset + rt*64 + row - 64 (up);
 //   plain (STORE):       rt*128 + row.
-// int8 codes are stored biased (q + 128) for the converter's byte splice;
-// int4 words are reordered so element 2j sits in bits [4j, 4j+4) and element
-// 2j+1 in bits [16+4j, 20+4j): one shift+mask per fp16 pair.
+// The tile's codes are stored as four 16-code chunks per row, chunk-major
+// ([chunk][row]).  int8 codes are stored biased (q + 128) for the
+// converter's byte splice; int4 words are reordered so element 2j sits in
+// bits [4j, 4j+4) and element 2j+1 in bits [16+4j, 20+4j): one shift+mask
+// per fp16 pair.
 __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict__ sc, int bits,
                          int E, int rows_per_e, int K, int RT, int interleave, int up_offset,
                          uint8_t *__restrict__ qo, __half2 *__restrict__ so) {
@@ -585,29 +901,32 @@ __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict
         srow = (int64_t)e * rows_per_e + rt * UM_M + row;
     const int row_bytes = bits == 8 ? K : K / 2;
     const int blk_bytes = bits == 8 ? UM_BK : UM_BK / 2;
+    const int cb = blk_bytes / 4;  // bytes of one 16-code chunk
     const uint8_t *s = q + srow * row_bytes + (int64_t)kb * blk_bytes;
     const int64_t tile = ((int64_t)e * RT + rt) * KB + kb;
-    uint8_t *d = qo + tile * (UM_M * blk_bytes) + (int64_t)row * blk_bytes;
-    if (bits == 8) {
-        for (int b = 0; b < blk_bytes; b += 16) {
-            uint4 v = *reinterpret_cast<const uint4 *>(s + b);
+    uint8_t *d = qo + tile * (UM_M * blk_bytes);
+    for (int c = 0; c < 4; c++) {
+        uint8_t *dc = d + ((int64_t)c * UM_M + row) * cb;  // [chunk][row][cb]
+        const uint8_t *sc4 = s + c * cb;
+        if (bits == 8) {
+            uint4 v = *reinterpret_cast<const uint4 *>(sc4);
             v.x ^= 0x80808080u;
             v.y ^= 0x80808080u;
             v.z ^= 0x80808080u;
             v.w ^= 0x80808080u;
-            *reinterpret_cast<uint4 *>(d + b) = v;
-        }
-    } else {
-        for (int w = 0; w < blk_bytes / 4; w++) {
-            uint32_t src = *reinterpret_cast<const uint32_t *>(s + 4 * w);
-            uint32_t out = 0;
+            *reinterpret_cast<uint4 *>(dc) = v;
+        } else {
+            for (int w = 0; w < 2; w++) {
+                const uint32_t src = *reinterpret_cast<const uint32_t *>(sc4 + 4 * w);
+                uint32_t out = 0;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const uint32_t byte = (src >> (8 * j)) & 0xFFu;
-                out |= (byte >> 4) << (4 * j);          // element 2j
-                out |= (byte & 0xFu) << (16 + 4 * j);   // element 2j+1
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t byte = (src >> (8 * j)) & 0xFFu;
+                    out |= (byte >> 4) << (4 * j);          // element 2j
+                    out |= (byte & 0xFu) << (16 + 4 * j);   // element 2j+1
+                }
+                *reinterpret_cast<uint32_t *>(dc + 4 * w) = out;
             }
-            *reinterpret_cast<uint32_t *>(d + 4 * w) = out;
         }
     }
     const __half *ss = sc + srow * (K / QG_GROUP) + kb * 2;
@@ -673,19 +992,28 @@ int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int
 
 template <int BITS, bool SWIGLU, int NT>
 static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStream_t s) {
-    using Cfg = UmCfg<BITS, NT>;
+    // NT = 256: A in shared memory; NT = 64 / 16: A in TMEM.
+    int smem, threads;
+    void (*kern)(const CUtensorMap, const UmmaArgs);
+    if constexpr (NT != 256) {
+        smem = TsCfg<BITS, NT>::SMEM;
+        threads = TS_THREADS;
+        kern = k_umma_ts<BITS, SWIGLU, NT>;
+    } else {
+        smem = UmCfg<BITS, NT>::SMEM;
+        threads = UM_THREADS;
+        kern = k_umma<BITS, SWIGLU, NT>;
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     static bool done[64] = {false};
     if (dev < 64 && !done[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(k_umma<BITS, SWIGLU, NT>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        QG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         done[dev] = true;
     }
     int g = num_sms(dev);
     if (grid < g) g = grid;
-    k_umma<BITS, SWIGLU, NT><<<g, UM_THREADS, Cfg::SMEM, s>>>(
-        *reinterpret_cast<const CUtensorMap *>(tmap), a);
+    kern<<<g, threads, smem, s>>>(*reinterpret_cast<const CUtensorMap *>(tmap), a);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
