@@ -198,7 +198,6 @@ struct qgmoe {
         graph_seen.clear();
     }
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
-    __half2 *gu_ps = nullptr, *dn_ps = nullptr, *sgu_ps = nullptr, *sdn_ps = nullptr;
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
     // boxes of 256 / 64 / 16 token rows (prefill and decode tile sizes)
     CUtensorMap tmap_x[3]{}, tmap_h[3]{}, tmap_hs[3]{};
@@ -259,12 +258,7 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(st.shared_act, sizeof(int32_t) * 6);
     {
         const int Ep = m->E + m->has_shared;
-        size_t rows = 0;  // max over T' <= cap of splits(T') * T'
-        for (int t = 1; t <= cap; t++) {
-            const size_t r = (size_t)route_splits(t, m->H, Ep, num_sms(m->device)) * t;
-            if (r > rows) rows = r;
-        }
-        QG_A(st.logits, sizeof(float) * rows * Ep);
+        QG_A(st.logits, sizeof(float) * (size_t)cap * Ep);
         QG_A(st.hist, sizeof(int32_t) * (size_t)((cap + 31) / 32) * m->E);
         QG_A(st.expert_off, sizeof(int32_t) * m->E);
     }
@@ -307,35 +301,22 @@ static int build_tensor_weights(qgmoe *m) {
         return QGMOE_OK;
     Allocs &al = m->weights;
     int rc;
-    const size_t gu_bytes = (size_t)E * 2 * I * H * bits / 8;
-    const size_t dn_bytes = (size_t)E * H * I * bits / 8;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&m->gu_pq), gu_bytes))) return rc;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&m->dn_pq), dn_bytes))) return rc;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&m->gu_ps),
-                       sizeof(__half2) * (size_t)E * 2 * I * (H / 64))))
-        return rc;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&m->dn_ps),
-                       sizeof(__half2) * (size_t)E * H * (I / 64))))
-        return rc;
     // gate_up tiles: 64 gate rows + the matching 64 up rows; down: 128 rows
-    if ((rc = launch_repack(m->gu.q, m->gu.s, bits, E, 2 * I, H, I / 64, 1, I, m->gu_pq,
-                            m->gu_ps, m->stream)))
+    if ((rc = al.alloc(reinterpret_cast<void **>(&m->gu_pq), packed_bytes(bits, E, 2 * I, H))) ||
+        (rc = al.alloc(reinterpret_cast<void **>(&m->dn_pq), packed_bytes(bits, E, H, I))))
         return rc;
-    if ((rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 0, 0, m->dn_pq, m->dn_ps,
-                            m->stream)))
+    if ((rc = launch_repack(m->gu.q, m->gu.s, bits, E, 2 * I, H, I / 64, 1, I, m->gu_pq,
+                            m->stream)) ||
+        (rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 0, 0, m->dn_pq, m->stream)))
         return rc;
     if (m->has_shared) {  // the shared expert as one more (single-expert) weight set
-        if ((rc = al.alloc(reinterpret_cast<void **>(&m->sgu_pq), (size_t)2 * Is * H * bits / 8)) ||
-            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_pq), (size_t)H * Is * bits / 8)) ||
-            (rc = al.alloc(reinterpret_cast<void **>(&m->sgu_ps),
-                           sizeof(__half2) * (size_t)2 * Is * (H / 64))) ||
-            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_ps),
-                           sizeof(__half2) * (size_t)H * (Is / 64))))
+        if ((rc = al.alloc(reinterpret_cast<void **>(&m->sgu_pq), packed_bytes(bits, 1, 2 * Is, H))) ||
+            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_pq), packed_bytes(bits, 1, H, Is))))
             return rc;
         if ((rc = launch_repack(m->sgu.q, m->sgu.s, bits, 1, 2 * Is, H, Is / 64, 1, Is, m->sgu_pq,
-                                m->sgu_ps, m->stream)) ||
+                                m->stream)) ||
             (rc = launch_repack(m->sdn.q, m->sdn.s, bits, 1, H, Is, H / 128, 0, 0, m->sdn_pq,
-                                m->sdn_ps, m->stream)))
+                                m->stream)))
             return rc;
     }
     QG_CUDA(cudaStreamSynchronize(m->stream));
@@ -381,7 +362,6 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     l.tile_tokens = nt;
     // gate_up + SwiGLU -> h16
     l.wq = m->gu_pq;
-    l.ws = m->gu_ps;
     l.RT = m->I / 64;
     l.KB = m->H / 64;
     l.out = m->h16;
@@ -397,7 +377,6 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
         sl.n_act = m->st.shared_act + 3;
         sl.tile_prefix = m->st.shared_act + 4;
         sl.wq = m->sgu_pq;
-        sl.ws = m->sgu_ps;
         sl.RT = m->Is / 64;
         sl.grid = ((T + nt - 1) / nt) * sl.RT;
         if ((rc = launch_umma(m->bits, true, &m->tmap_x[ti], sl, s))) return rc;
@@ -406,7 +385,6 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     m->mark(2, "gate_up", s);
     // down -> d16
     l.wq = m->dn_pq;
-    l.ws = m->dn_ps;
     l.RT = m->H / 128;
     l.KB = m->I / 64;
     l.out = m->d16;
@@ -415,7 +393,6 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     if ((rc = launch_umma(m->bits, false, &m->tmap_h[ti], l, s))) return rc;
     if (m->has_shared) {
         sl.wq = m->sdn_pq;
-        sl.ws = m->sdn_ps;
         sl.RT = m->H / 128;
         sl.KB = m->Is / 64;
         sl.out = m->d16;
@@ -876,7 +853,6 @@ int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t
     l.err = m->err_dev;
     l.tile_tokens = 256;
     l.wq = m->gu_pq;
-    l.ws = m->gu_ps;
     l.RT = m->I / 64;
     l.KB = m->H / 64;
     l.out = m->eh16;
@@ -884,7 +860,6 @@ int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t
     l.grid = tiles * l.RT;
     if ((rc = launch_umma(m->bits, true, &m->tmap_xg, l, s))) return rc;
     l.wq = m->dn_pq;
-    l.ws = m->dn_ps;
     l.RT = m->H / 128;
     l.KB = m->I / 64;
     l.out = static_cast<__half *>(out_rows);

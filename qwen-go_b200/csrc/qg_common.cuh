@@ -77,8 +77,8 @@ __device__ __forceinline__ int dispatch_key(int e, int E, int W) {
 
 // One launch of the tensor-core grouped GEMM (qg_umma.cu).
 struct UmmaLaunch {
-    const uint8_t *wq;          // packed codes
-    const __half2 *ws;          // packed scales
+    const uint8_t *wq;          // packed tiles: per (expert, row tile, k block) the codes
+                                // then the rows' fp16 scales, contiguous
     int RT, KB;                 // row tiles per expert, 64-wide K blocks
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
     __half *out;                // GEMM1: h [slots, I]; GEMM2: d [slots, H] (fp16)
@@ -133,8 +133,9 @@ int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, flo
 int num_sms(int device);
 int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld, int box_rows);
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
-                  int RT, int interleave, int up_offset, uint8_t *qo, __half2 *so,
-                  cudaStream_t s);
+                  int RT, int interleave, int up_offset, uint8_t *qo, cudaStream_t s);
+// Bytes of the packed tensor-core copy of a weight set (codes + scales).
+size_t packed_bytes(int bits, int E, int rows_per_e, int K);
 int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
                       cudaStream_t s);
 int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s);

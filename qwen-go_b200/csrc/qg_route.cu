@@ -2,13 +2,14 @@
 //
 // Launches: k_logits, k_topk, k_scatter (+ k_gather_f16 for the tensor path).
 // 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...), model/moe.go:42)
-//    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 32 tokens x 128
-//    router rows x one K slice, writes its partial sums.  The shared-expert
-//    gate vector rides along as router row E (model/moe.go:87-93).  Split-K
-//    keeps decode-sized batches (T = 1..64) spread over the SMs while the
-//    1 MiB router matrix is read about once.
-// 2. k_topk: one warp per token adds the partials in a fixed order, then
-//    softmax (model/tensors.go:106-121: max-subtract, exp in float64 rounded
+//    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 64 tokens x 128
+//    router rows x one K slice.  The shared-expert gate vector rides along as
+//    router row E (model/moe.go:87-93).  Split-K keeps decode-sized batches
+//    (T = 1..64) spread over the SMs while the 1 MiB router matrix is read
+//    about once; the K slices of one tile form a thread-block cluster and add
+//    their partial tiles through distributed shared memory in rank order
+//    (deterministic), so only final logits reach global memory.
+// 2. k_topk: one warp per token reads its logits, then softmax (model/tensors.go:106-121: max-subtract, exp in float64 rounded
 //    to float32, divide by the sum), top-k (model/moe.go:44-52, TOPK or the
 //    literal PREFIX bound), w = p / (wSum + 1e-9) (model/moe.go:53-63) and
 //    sigmoid of the shared gate.  Each CTA writes its expert histogram; the
@@ -21,12 +22,18 @@
 //    pass.  For the tensor-core path k_gather_f16 then writes each slot's fp16
 //    activation row.
 #include "qg_common.cuh"
+#include "qg_sm100.cuh"
 
 namespace qg {
+using sm100::cluster_ctarank;
+using sm100::cluster_sync;
+using sm100::ld_cluster_f32;
+using sm100::mapa_shared;
+using sm100::smem_u32;
 
-constexpr int LG_TOK = 64;   // tokens per logits tile (8 per warp)
-constexpr int LG_ROWS = 128; // router rows per logits tile (4 per lane)
 constexpr int LG_KC = 32;    // K chunk staged in shared memory
+constexpr int LG_MAX_SPLIT = 16; // K slices per tile = cluster size (16: non-portable opt-in)
+constexpr int LG_SMALL_T = 8;    // up to this many tokens: 8 x 32 tiles, else 64 x 128
 constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA
 constexpr int RT_THREADS = 1024;  // top-k and scatter CTAs: one warp per token
 constexpr int RT_WARPS = RT_THREADS / 32;
@@ -47,117 +54,162 @@ __device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
 }
 
 int route_splits(int T, int H, int Ep, int sms) {
-    const int tt = (T + LG_TOK - 1) / LG_TOK;
-    const int te = (Ep + LG_ROWS - 1) / LG_ROWS;
-    int s = (2 * sms) / (tt * te);
-    const int smax = H / LG_KC < 32 ? H / LG_KC : 32;
-    if (s > smax) s = smax;
-    if (s < 1) s = 1;
+    const int TT = T <= LG_SMALL_T ? 8 : 64, RR = T <= LG_SMALL_T ? 32 : 128;
+    const int tiles = ((T + TT - 1) / TT) * ((Ep + RR - 1) / RR);
+    int s = 1;  // a power of two: the cluster size
+    while (s < LG_MAX_SPLIT && 2 * s * tiles <= sms && 2 * s * LG_KC <= H) s *= 2;
     return s;
 }
 
 // ---- 1. logits ------------------------------------------------------------------
-// CTA tile: 64 tokens x 128 router rows x one K slice.  Warp w owns tokens
-// 8w..8w+7, lane l owns rows 4l..4l+3: per K step two broadcast float4 reads
-// of x and one float4 read of the router feed 32 FMAs.  The next K chunk is
-// fetched into registers while the current one is consumed.
+// CTA tile: TT tokens x RR router rows x one K slice (TT x RR = 64 x 128 for
+// prefill batches, 8 x 32 for decode batches, so that a handful of tokens
+// still spreads over many CTAs).  Warp w owns tokens w*TT/8 ..., lane l owns
+// rows l*RR/32 ...: per K step the warp's x values and the lane's router
+// values come from shared memory and feed (TT/8) x (RR/32) FMAs.  The next K
+// chunk is fetched into registers while the current one is consumed.  With
+// KS > 1 the KS slices of a tile are one cluster: each CTA parks its partial
+// tile in its shared memory, and CTA c then sums elements
+// [c*TT*RR/KS, (c+1)*TT*RR/KS) of the tile over the ranks 0..KS-1 in order.
+template <int TT, int RR>
+struct LgTile {
+    static constexpr int TPW = TT / 8;   // tokens per warp
+    static constexpr int RPL = RR / 32;  // rows per lane
+    static constexpr int STAGE_FLOATS = LG_KC * (TT + 4) + LG_KC * (RR + 4);
+    static constexpr int SMEM =
+        4 * (STAGE_FLOATS > TT * RR ? STAGE_FLOATS : TT * RR);
+};
+
+template <int TT, int RR, int KS>
 __global__ void __launch_bounds__(256)
 k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *__restrict__ router,
-         const float *__restrict__ shared_gate, int ksplit, float *__restrict__ part) {
-    __shared__ __align__(16) float xs[LG_KC][LG_TOK + 4];
-    __shared__ __align__(16) float ws[LG_KC][LG_ROWS + 4];
+         const float *__restrict__ shared_gate, float *__restrict__ logits) {
+    using Tl = LgTile<TT, RR>;
+    constexpr int TPW = Tl::TPW, RPL = Tl::RPL;
+    constexpr int XV = TT * LG_KC / 4;   // float4 loads of x per K chunk
+    constexpr int WV = RR * LG_KC / 4;   // float4 loads of router rows per K chunk
+    constexpr int XPT = (XV + 255) / 256, WPT = WV / 256;
+    static_assert(WV % 256 == 0, "router chunk must split evenly over the CTA");
+    extern __shared__ __align__(16) float lg_smem[];
+    float (*xs)[TT + 4] = reinterpret_cast<float (*)[TT + 4]>(lg_smem);
+    float (*ws)[RR + 4] = reinterpret_cast<float (*)[RR + 4]>(lg_smem + LG_KC * (TT + 4));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t0 = blockIdx.x * LG_TOK, r0 = blockIdx.y * LG_ROWS, s = blockIdx.z;
-    const int kc = ((H / LG_KC + ksplit - 1) / ksplit) * LG_KC;
+    const int t0 = blockIdx.x * TT, r0 = blockIdx.y * RR, s = blockIdx.z;
+    const int kc = ((H / LG_KC + KS - 1) / KS) * LG_KC;
     const int k0 = s * kc, k1 = min(H, k0 + kc);
-    float acc[8][4] = {};
-    const int lrow = tid >> 3, k4 = (tid & 7) * 4;  // loader: row / token, float4 column
-    const float *xrow[2];
+    float acc[TPW][RPL] = {};
+    // loaders: float4 i of a chunk covers item i / 8 (token or row), column (i % 8) * 4
+    const float *xrow[XPT];
+    int xi[XPT];
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const int t = t0 + lrow + 32 * j;
-        xrow[j] = t < T ? x + (size_t)t * H : nullptr;
+    for (int j = 0; j < XPT; j++) {
+        xi[j] = tid + 256 * j;
+        const int t = t0 + xi[j] / 8;
+        xrow[j] = (xi[j] < XV && t < T) ? x + (size_t)t * H : nullptr;
     }
-    const float *wrow[4];
+    const float *wrow[WPT];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int r = r0 + lrow + 32 * j;
+    for (int j = 0; j < WPT; j++) {
+        const int r = r0 + (tid + 256 * j) / 8;
         wrow[j] = r < Ep ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
     }
+    const int c4 = (tid % 8) * 4;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 xn[2], wn[4];
+    float4 xn[XPT], wn[WPT];
     auto fetch = [&](int kb) {
 #pragma unroll
-        for (int j = 0; j < 2; j++)
-            xn[j] = xrow[j] ? *reinterpret_cast<const float4 *>(xrow[j] + kb + k4) : zero;
+        for (int j = 0; j < XPT; j++)
+            xn[j] = xrow[j] ? *reinterpret_cast<const float4 *>(xrow[j] + kb + c4) : zero;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + k4)) : zero;
+        for (int j = 0; j < WPT; j++)
+            wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + c4)) : zero;
     };
     if (k0 < k1) fetch(k0);
     for (int kb = k0; kb < k1; kb += LG_KC) {
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const int t = lrow + 32 * j;
-            xs[k4][t] = xn[j].x;
-            xs[k4 + 1][t] = xn[j].y;
-            xs[k4 + 2][t] = xn[j].z;
-            xs[k4 + 3][t] = xn[j].w;
-        }
+        for (int j = 0; j < XPT; j++)
+            if (xi[j] < XV) {
+                const int t = xi[j] / 8;
+                xs[c4][t] = xn[j].x;
+                xs[c4 + 1][t] = xn[j].y;
+                xs[c4 + 2][t] = xn[j].z;
+                xs[c4 + 3][t] = xn[j].w;
+            }
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int row = lrow + 32 * j;
-            ws[k4][row] = wn[j].x;
-            ws[k4 + 1][row] = wn[j].y;
-            ws[k4 + 2][row] = wn[j].z;
-            ws[k4 + 3][row] = wn[j].w;
+        for (int j = 0; j < WPT; j++) {
+            const int row = (tid + 256 * j) / 8;
+            ws[c4][row] = wn[j].x;
+            ws[c4 + 1][row] = wn[j].y;
+            ws[c4 + 2][row] = wn[j].z;
+            ws[c4 + 3][row] = wn[j].w;
         }
         __syncthreads();
         if (kb + LG_KC < k1) fetch(kb + LG_KC);
 #pragma unroll 4
         for (int kk = 0; kk < LG_KC; kk++) {
-            const float4 a0 = *reinterpret_cast<const float4 *>(&xs[kk][8 * warp]);
-            const float4 a1 = *reinterpret_cast<const float4 *>(&xs[kk][8 * warp + 4]);
-            const float4 b = *reinterpret_cast<const float4 *>(&ws[kk][4 * lane]);
-            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const float bv[4] = {b.x, b.y, b.z, b.w};
+            float av[TPW], bv[RPL];
+            if constexpr (TPW % 4 == 0) {
 #pragma unroll
-            for (int i = 0; i < 8; i++)
+                for (int i = 0; i < TPW; i += 4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(&xs[kk][TPW * warp + i]);
+                    av[i] = v.x, av[i + 1] = v.y, av[i + 2] = v.z, av[i + 3] = v.w;
+                }
+            } else {
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                for (int i = 0; i < TPW; i++) av[i] = xs[kk][TPW * warp + i];
+            }
+            if constexpr (RPL % 4 == 0) {
+#pragma unroll
+                for (int j = 0; j < RPL; j += 4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(&ws[kk][RPL * lane + j]);
+                    bv[j] = v.x, bv[j + 1] = v.y, bv[j + 2] = v.z, bv[j + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < RPL; j++) bv[j] = ws[kk][RPL * lane + j];
+            }
+#pragma unroll
+            for (int i = 0; i < TPW; i++)
+#pragma unroll
+                for (int j = 0; j < RPL; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
         }
         __syncthreads();
     }
+    if constexpr (KS == 1) {
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int t = t0 + 8 * warp + i;
-        if (t >= T) continue;
-        const int r = r0 + 4 * lane;
-        float *dst = part + ((size_t)s * T + t) * Ep + r;
-        if (r + 3 < Ep && (Ep & 3) == 0) {
-            *reinterpret_cast<float4 *>(dst) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-        } else {
+        for (int i = 0; i < TPW; i++) {
+            const int t = t0 + TPW * warp + i;
+            if (t >= T) continue;
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (r + j < Ep) dst[j] = acc[i][j];
+            for (int j = 0; j < RPL; j++) {
+                const int r = r0 + RPL * lane + j;
+                if (r < Ep) logits[(size_t)t * Ep + r] = acc[i][j];
+            }
         }
+    } else {
+        // partial tile [TT tokens][RR rows] over the staging buffers (the K
+        // loop ended with a barrier)
+        float *red = lg_smem;
+#pragma unroll
+        for (int i = 0; i < TPW; i++)
+#pragma unroll
+            for (int j = 0; j < RPL; j++) red[(TPW * warp + i) * RR + RPL * lane + j] = acc[i][j];
+        cluster_sync();
+        constexpr int EPC = TT * RR / KS;  // tile elements reduced by this CTA
+        const int c = (int)cluster_ctarank();
+        for (int idx = c * EPC + tid; idx < (c + 1) * EPC; idx += 256) {
+            const uint32_t off = smem_u32(red + idx);
+            float v[KS];
+#pragma unroll
+            for (int q = 0; q < KS; q++) v[q] = ld_cluster_f32(mapa_shared(off, q));
+            float sum = v[0];
+#pragma unroll
+            for (int q = 1; q < KS; q++) sum += v[q];
+            const int t = t0 + idx / RR, row = r0 + idx % RR;
+            if (t < T && row < Ep) logits[(size_t)t * Ep + row] = sum;
+        }
+        cluster_sync();  // no CTA leaves while others still read its tile
     }
-}
-
-// Sum of the split-K partials of one logit, in a fixed order; four
-// independent accumulators keep the loads in flight together.
-__device__ __forceinline__ float sum_splits(const float *__restrict__ part, int ksplit,
-                                            size_t stride, size_t off) {
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int s = 0;
-    for (; s + 4 <= ksplit; s += 4) {
-        a0 += part[off + s * stride];
-        a1 += part[off + (s + 1) * stride];
-        a2 += part[off + (s + 2) * stride];
-        a3 += part[off + (s + 3) * stride];
-    }
-    for (; s < ksplit; s++) a0 += part[off + s * stride];
-    return (a0 + a1) + (a2 + a3);
 }
 
 // ---- 2. softmax + top-k + histograms --------------------------------------------
@@ -165,7 +217,7 @@ __device__ __forceinline__ float sum_splits(const float *__restrict__ part, int 
 // l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
 template <int NJ>
 __global__ void __launch_bounds__(RT_THREADS)
-k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, int mode,
+k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
        int has_shared, RouteState st, int *err) {
     extern __shared__ int hist_s[];  // [E]
     __shared__ int s_idx[RT_WARPS][QG_MAX_TOPK];
@@ -181,7 +233,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
-            v[j] = e < E ? sum_splits(part, ksplit, (size_t)T * Ep, (size_t)t * Ep + e) : -INFINITY;
+            v[j] = e < E ? logits[(size_t)t * Ep + e] : -INFINITY;
         }
         float mx = v[0];
 #pragma unroll
@@ -268,7 +320,7 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
         }
         if (has_shared && lane == 0) {
-            const float g = sum_splits(part, ksplit, (size_t)T * Ep, (size_t)t * Ep + E);
+            const float g = logits[(size_t)t * Ep + E];
             st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)g));
         }
         __syncwarp();
@@ -294,52 +346,58 @@ k_topk(const float *__restrict__ part, int ksplit, int T, int E, int Ep, int k, 
     }
     __syncthreads();
     if (warp == 0) {
+        // one warp-wide exclusive scan of (pairs, active experts, tiles) over
+        // contiguous per-lane expert ranges; every lane then writes its own
+        // experts' offsets, active-list entries and tile prefixes
+        const int tt = st.tile_tokens > 0 ? st.tile_tokens : 256;  // a power of two
+        const int tsh = __ffs(tt) - 1;
         const int per = (E + 31) / 32;
-        const int lo = lane * per, hi = min(E, lo + per);
-        int run = 0, nz = 0;
+        const int lo = min(E, lane * per), hi = min(E, lo + per);
+        int run = 0, nz = 0, tl = 0;
         for (int e = lo; e < hi; e++) {
-            run += cnt[e];
-            nz += cnt[e] > 0;
+            const int c = cnt[e];
+            run += c;
+            nz += c > 0;
+            tl += (c + tt - 1) >> tsh;
         }
-        int incl = run, nzi = nz;
+        int incl = run, nzi = nz, tli = tl;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int v = __shfl_up_sync(0xffffffffu, incl, o);
             const int w = __shfl_up_sync(0xffffffffu, nzi, o);
+            const int x = __shfl_up_sync(0xffffffffu, tli, o);
             if (lane >= o) {
                 incl += v;
                 nzi += w;
+                tli += x;
             }
         }
-        int base = incl - run, a = nzi - nz;
+        int base = incl - run, a = nzi - nz, tb = tli - tl;
         for (int e = lo; e < hi; e++) {
+            const int c = cnt[e];
             st.expert_off[e] = base;
-            if (cnt[e] > 0) {
+            if (c > 0) {
                 st.act_group[a] = e;
                 st.act_begin[a] = base;
-                st.act_n[a] = cnt[e];
+                st.act_n[a] = c;
+                st.tile_prefix[a] = tb;
+                tb += (c + tt - 1) >> tsh;
                 a++;
             }
-            base += cnt[e];
+            base += c;
         }
-        int total_act = __shfl_sync(0xffffffffu, nzi, 31);
-        if (lane == 0) {
-            const int tt = st.tile_tokens > 0 ? st.tile_tokens : 256;
-            int tiles = 0, ai = 0;
-            for (int e = 0; e < E; e++)
-                if (cnt[e] > 0) {
-                    st.tile_prefix[ai++] = tiles;
-                    tiles += (cnt[e] + tt - 1) / tt;
-                }
-            st.tile_prefix[ai] = tiles;
-            if (st.n_act_routed) *st.n_act_routed = ai;
+        const int routed_act = __shfl_sync(0xffffffffu, nzi, 31);
+        if (lane == 31) {
+            st.tile_prefix[routed_act] = tli;
+            if (st.n_act_routed) *st.n_act_routed = routed_act;
+            int total_act = routed_act;
             if (has_shared && st.shared_act) {
                 st.shared_act[0] = 0;
                 st.shared_act[1] = T * k;
                 st.shared_act[2] = T;
                 st.shared_act[3] = 1;
                 st.shared_act[4] = 0;
-                st.shared_act[5] = (T + tt - 1) / tt;
+                st.shared_act[5] = (T + tt - 1) >> tsh;
             }
             if (has_shared) {
                 st.act_group[total_act] = E;
@@ -443,9 +501,35 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     cudaGetDevice(&dev);
     const int Ep = E + (has_shared ? 1 : 0);
     const int ks = route_splits(T, H, Ep, num_sms(dev));
-    dim3 g1((T + LG_TOK - 1) / LG_TOK, (Ep + LG_ROWS - 1) / LG_ROWS, ks);
-    k_logits<<<g1, 256, 0, s>>>(x, T, H, E, Ep, router, shared_gate, ks, st.logits);
-    QG_CUDA(cudaGetLastError());
+    const bool small = T <= LG_SMALL_T;
+    using LgKern = void (*)(const float *, int, int, int, int, const float *, const float *, float *);
+    static const LgKern kerns[2][5] = {
+        {k_logits<64, 128, 1>, k_logits<64, 128, 2>, k_logits<64, 128, 4>, k_logits<64, 128, 8>,
+         k_logits<64, 128, 16>},
+        {k_logits<8, 32, 1>, k_logits<8, 32, 2>, k_logits<8, 32, 4>, k_logits<8, 32, 8>,
+         k_logits<8, 32, 16>}};
+    const int ki = ks == 1 ? 0 : ks == 2 ? 1 : ks == 4 ? 2 : ks == 8 ? 3 : 4;
+    const LgKern kern = kerns[small][ki];
+    static bool wide[64] = {false};  // 16-CTA clusters need the non-portable opt-in
+    if (dev < 64 && !wide[dev]) {
+        QG_CUDA(cudaFuncSetAttribute(kerns[0][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        QG_CUDA(cudaFuncSetAttribute(kerns[1][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        wide[dev] = true;
+    }
+    const int TT = small ? 8 : 64, RR = small ? 32 : 128;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = small ? LgTile<8, 32>::SMEM : LgTile<64, 128>::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute cl[1];
+    cl[0].id = cudaLaunchAttributeClusterDimension;
+    cl[0].val.clusterDim.x = 1;
+    cl[0].val.clusterDim.y = 1;
+    cl[0].val.clusterDim.z = ks;
+    cfg.attrs = cl;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
+    QG_CUDA(cudaLaunchKernelEx(&cfg, kern, x, T, H, E, Ep, router, shared_gate, st.logits));
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
@@ -456,17 +540,17 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     }
     const int nj = (E + 31) / 32;
     if (nj <= 1)
-        k_topk<1><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<1><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 2)
-        k_topk<2><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<2><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 4)
-        k_topk<4><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<4><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 8)
-        k_topk<8><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<8><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     else if (nj <= 16)
-        k_topk<16><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<16><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     else
-        k_topk<32><<<nc, RT_THREADS, sm2, s>>>(st.logits, ks, T, E, Ep, k, mode, has_shared, st, err);
+        k_topk<32><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
     QG_CUDA(cudaGetLastError());
     k_scatter<<<nc, RT_THREADS, sm3, s>>>(T, E, k, has_shared, st, err);
     QG_CUDA(cudaGetLastError());

@@ -42,11 +42,10 @@ static int scratch_for_device(int dev, unsigned char **out) {
 
 // Bytes of scratch a route of T tokens needs, laid out in 256-byte aligned
 // pieces (mirrors the carve-up in qgmoe_route_static).
-static size_t route_scratch_bytes(int T, int H, int E, int k, int sms) {
+static size_t route_scratch_bytes(int T, int E, int k) {
     auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
-    const size_t splits = (size_t)route_splits(T, H, E, sms);
     size_t n = 0;
-    n += al(sizeof(float) * splits * T * E);             // logits partials
+    n += al(sizeof(float) * (size_t)T * E);              // logits
     n += al(sizeof(int32_t) * (size_t)((T + 31) / 32) * E);  // per-CTA histograms
     n += al(sizeof(int32_t) * E);                        // counts (zeroed per call)
     n += al(sizeof(int32_t) * 2);                        // ticket + error word (zeroed)
@@ -78,7 +77,7 @@ extern "C" int qgmoe_route_static(const float *x, const float *router, int32_t T
         return set_error(QGMOE_ERR_INVALID_ARG, "null pointer argument");
     int dev = 0;
     QG_CUDA(cudaGetDevice(&dev));
-    const size_t need = route_scratch_bytes(T, H, E, k, num_sms(dev));
+    const size_t need = route_scratch_bytes(T, E, k);
     if (need > QGMOE_ROUTE_STATIC_SCRATCH)
         return set_error(QGMOE_ERR_INVALID_ARG,
                          "route of T=%d tokens over E=%d experts needs %zu bytes of scratch; "
@@ -95,11 +94,10 @@ extern "C" int qgmoe_route_static(const float *x, const float *router, int32_t T
         return p;
     };
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const size_t splits = (size_t)route_splits(T, H, E, num_sms(dev));
     RouteState st{};
     st.topk_idx = sel_idx;  // outputs go straight to the caller's arrays
     st.topk_w = sel_w;
-    st.logits = static_cast<float *>(take(sizeof(float) * splits * T * E));
+    st.logits = static_cast<float *>(take(sizeof(float) * (size_t)T * E));
     st.hist = static_cast<int32_t *>(take(sizeof(int32_t) * (size_t)((T + 31) / 32) * E));
     st.counts = static_cast<int32_t *>(take(sizeof(int32_t) * E));
     int32_t *flags = static_cast<int32_t *>(take(sizeof(int32_t) * 2));

@@ -60,9 +60,13 @@ constexpr int UM_EC = 16;          // token columns per epilogue chunk
 constexpr int UM_MAX_UNITS = 64;   // work units per CTA decoded once into shared memory
 constexpr long long UM_WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
-// Raw code tile of one k block (128 rows x 64 codes): four 16-code chunks per
-// row, stored chunk-major ([chunk][row][CB bytes]) so that consecutive rows
-// are consecutive in shared memory; then the rows' two fp16 group scales.
+// Raw tile of one k block (128 rows x 64 codes), the unit of the packed
+// weight layout in HBM and of the code ring in shared memory: four 16-code
+// chunks per row, stored chunk-major ([chunk][row][CB bytes]) so that
+// consecutive rows are consecutive in shared memory, then the rows' two fp16
+// group scales.  A tile's k blocks follow each other, so several k blocks
+// travel as one bulk copy (copies of 4 KB reach only about half the HBM
+// bandwidth that 8 KB and larger copies do).
 template <int BITS>
 struct RawTile {
     static constexpr int CB = BITS == 8 ? 16 : 8;            // bytes of one 16-code chunk
@@ -98,25 +102,27 @@ constexpr int TS_CODE_WARP = 20;
 constexpr int TS_MMA_WARP = 21;
 constexpr int TS_ACT_WARP = 22;
 constexpr int TS_THREADS = 23 * 32;
-constexpr int TS_S = 6;            // stages of two k blocks: A 64 TMEM columns, B 2 tiles
+constexpr int TS_KS = 4;           // k blocks per pipeline stage
+constexpr int TS_S = 3;            // stages: A 4 x 32 TMEM columns, B 4 activation tiles
 
 template <int BITS, int NT>
 struct TsCfg {
     static constexpr int B_BYTES = NT * UM_BK * 2;                    // one tile: 8 / 2 KB fp16
-    static constexpr int STAGE_B = 2 * B_BYTES;
-    static constexpr int R = NT == 64 ? (BITS == 8 ? 12 : 24) : (BITS == 8 ? 20 : 32);
+    static constexpr int STAGE_B = TS_KS * B_BYTES;
     static constexpr int RAW_CODE = RawTile<BITS>::CODE;
     static constexpr int RAW_BYTES = RawTile<BITS>::BYTES;
+    static constexpr int RAW_SLOT = TS_KS * RAW_BYTES;                // one stage of codes
+    static constexpr int R = NT == 64 ? (BITS == 8 ? 3 : 6) : (BITS == 8 ? 5 : 9);
     static constexpr int A_COL0 = 2 * NT;                             // after the accumulators
     static constexpr int TMEM_COLS = 512;
     static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
     static constexpr int UNIT_BYTES = UM_MAX_UNITS * 16;
     static constexpr int BAR_BYTES = 8 * (3 * TS_S + 2 * R + 5) + 16;
     static constexpr int SMEM =
-        TS_S * STAGE_B + R * RAW_BYTES + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
+        TS_S * STAGE_B + R * RAW_SLOT + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(B_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
-    static_assert(A_COL0 + TS_S * 64 <= TMEM_COLS, "TMEM budget");
+    static_assert(A_COL0 + TS_S * TS_KS * 32 <= TMEM_COLS, "TMEM budget");
 };
 
 // int8 x4 stored biased (q + 128, repacked at create time) -> two fp16x2
@@ -132,12 +138,27 @@ __device__ __forceinline__ void cvt_i8x4(uint32_t u, __half2 s2, uint32_t &o0, u
 }
 
 // int4 word in the repacked nibble order (element 2j in bits [4j, 4j+4),
-// element 2j+1 in bits [16+4j, 20+4j)) -> fp16x2 ((code - 8) * s) of pair j.
-__device__ __forceinline__ uint32_t cvt_i4_pair(uint32_t w, int j, __half2 s2) {
-    const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
-    uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
-    __half2 h = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p), bias), s2);
-    return *reinterpret_cast<uint32_t *>(&h);
+// element 2j+1 in bits [16+4j, 20+4j)) -> four fp16x2 ((code - 8) * s), pairs
+// j = 0..3.  Pairs 1 and 3 are taken in place (mask 0x00F0: 1024 + 16 code)
+// and scaled back by an exact fma, so the word needs one shift and four masks:
+// integer ops slow the tensor pipe of the same SM far more than fp16x2 ops.
+__device__ __forceinline__ void cvt_i4_word(uint32_t w, __half2 s2, uint32_t *o) {
+    const __half2 b1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));
+    const __half2 r16 = __halves2half2(__ushort_as_half(0x2C00), __ushort_as_half(0x2C00));  // 1/16
+    const __half2 m72 = __halves2half2(__ushort_as_half(0xD480), __ushort_as_half(0xD480));  // -72
+    const uint32_t w8 = w >> 8;
+    uint32_t p0 = (w & 0x000F000Fu) | 0x64006400u;   // 1024 + code
+    uint32_t p1 = (w & 0x00F000F0u) | 0x64006400u;   // 1024 + 16 code
+    uint32_t p2 = (w8 & 0x000F000Fu) | 0x64006400u;
+    uint32_t p3 = (w8 & 0x00F000F0u) | 0x64006400u;
+    __half2 h0 = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p0), b1032), s2);
+    __half2 h1 = __hmul2(__hfma2(*reinterpret_cast<__half2 *>(&p1), r16, m72), s2);
+    __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2 *>(&p2), b1032), s2);
+    __half2 h3 = __hmul2(__hfma2(*reinterpret_cast<__half2 *>(&p3), r16, m72), s2);
+    o[0] = *reinterpret_cast<uint32_t *>(&h0);
+    o[1] = *reinterpret_cast<uint32_t *>(&h1);
+    o[2] = *reinterpret_cast<uint32_t *>(&h2);
+    o[3] = *reinterpret_cast<uint32_t *>(&h3);
 }
 
 // One 16-code chunk of a raw tile (at shared address `code`) -> eight fp16x2
@@ -152,11 +173,8 @@ __device__ __forceinline__ void cvt_chunk(uint32_t code, __half2 s2, uint32_t (&
         cvt_i8x4(q.w, s2, o[6], o[7]);
     } else {
         const uint2 q = ld_shared_v2(code);
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-            o[p] = cvt_i4_pair(q.x, p, s2);
-            o[4 + p] = cvt_i4_pair(q.y, p, s2);
-        }
+        cvt_i4_word(q.x, s2, o);
+        cvt_i4_word(q.y, s2, o + 4);
     }
 }
 
@@ -206,8 +224,7 @@ __device__ __forceinline__ bool epi_bar_or(bool p) {
 }
 
 struct UmmaArgs {
-    const uint8_t *wq;    // packed codes [E][RT][KB][128 rows][64 or 32 B]
-    const __half2 *ws;    // packed scales [E][RT][KB][128] (the row's 2 groups)
+    const uint8_t *wq;    // packed tiles [E][RT][KB] x RawTile<BITS>::BYTES
     int RT, KB;
     const int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix;
     __half *out;          // SWIGLU: h [slots, out_stride]; STORE: d [slots, out_stride]
@@ -453,9 +470,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             bool ok = true;
             for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
                 const Unit w = unit_at(i, u);
-                const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
-                const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
-                const __half2 *scales = a.ws + tb * UM_M;
+                const uint8_t *tile =
+                    a.wq + (size_t)(w.e * a.RT + w.rt) * a.KB * Cfg::RAW_BYTES;
                 for (int kb = 0; kb < a.KB; kb++, g++) {
                     const int r = g % R;
                     if (!mbar_wait(&rawEmpty[r], ((g / R) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -463,11 +479,9 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                         ok = false;
                         break;
                     }
-                    uint8_t *dst = raw + r * Cfg::RAW_BYTES;
                     mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
-                    bulk_load(dst, codes + (size_t)kb * Cfg::RAW_CODE, Cfg::RAW_CODE, &rawFull[r]);
-                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * UM_M, UM_M * 4,
-                              &rawFull[r]);
+                    bulk_load(raw + r * Cfg::RAW_BYTES, tile + (size_t)kb * Cfg::RAW_BYTES,
+                              Cfg::RAW_BYTES, &rawFull[r]);
                     last = g;
                 }
             }
@@ -525,11 +539,8 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                     }
                     tc_fence_after();
                     const uint32_t asm_ = base_u32 + s * Cfg::STAGE_BYTES;
-                    const uint32_t bsm = asm_ + Cfg::A_BYTES;
-#pragma unroll
-                    for (int k16 = 0; k16 < UM_BK / 16; k16++)
-                        umma_f16(acc, desc_k_sw128(asm_ + k16 * 32), desc_k_sw128(bsm + k16 * 32),
-                                 idesc, (kb | k16) != 0);
+                    umma_ss_k64(acc, desc_k_sw128(asm_), desc_k_sw128(asm_ + Cfg::A_BYTES), idesc,
+                                kb != 0);
                     umma_commit(&empty[s]);
                 }
                 if (ok) umma_commit(&accFull[buf]);
@@ -553,11 +564,12 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 // Same unit sequence and roles as k_umma, with the dequantised weight tile
 // written to TMEM (tcgen05.st.32x32b: thread = tile row = TMEM lane, 16 K
 // codes -> 8 columns of fp16 pairs) instead of shared memory.  A pipeline
-// stage covers two k blocks (A: 64 TMEM columns, B: two activation tiles),
-// so the MMA issuer waits once, issues 8 MMAs and commits once per stage:
-// with N <= 64 an MMA takes about as long to issue as to run, and the
-// per-stage barrier work would otherwise pace the weight stream.
-// TMEM columns: [0, NT) and [NT, 2NT) accumulators, then 6 A stages of 64.
+// stage covers four k blocks (A: 128 TMEM columns, B: four activation
+// tiles), so the MMA issuer waits once, issues 16 MMAs and commits once per
+// stage, and each converter thread loads and converts four independent
+// chunks before storing them: at N <= 64 the per-stage barrier and latency
+// chains, not the MMAs, would otherwise pace the weight stream.
+// TMEM columns: [0, NT) and [NT, 2NT) accumulators, then 3 A stages of 128.
 // Barriers: fullA[s] completes when the 16 converter warps have stored A,
 // fullB[s] when both activation tiles have landed, empty[s] when the stage's
 // MMAs have completed (one tcgen05.commit frees A and B together).
@@ -573,16 +585,16 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const int n_act = *a.n_act;
     const int n_units = a.tile_prefix[n_act] * a.RT;
     if ((int)blockIdx.x >= n_units) return;
-    const int KP = a.KB >> 1;  // stages per unit (K is a multiple of 128)
+    const int KP = (a.KB + TS_KS - 1) / TS_KS;  // stages per unit (the last may be partial)
 
     uint8_t *base = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base_u32 = smem_u32(base);                 // activation stages
     uint8_t *raw = base + S * Cfg::STAGE_B;
     const uint32_t raw_u32 = base_u32 + S * Cfg::STAGE_B;
-    const uint32_t xch_u32 = raw_u32 + R * Cfg::RAW_BYTES;
+    const uint32_t xch_u32 = raw_u32 + R * Cfg::RAW_SLOT;
     const uint32_t utab_u32 = xch_u32 + Cfg::XCH_BYTES;
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_BYTES + Cfg::XCH_BYTES +
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(raw + R * Cfg::RAW_SLOT + Cfg::XCH_BYTES +
                                                    Cfg::UNIT_BYTES);
     uint64_t *fullB = fullA + S;
     uint64_t *empty = fullB + S;
@@ -651,28 +663,35 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             for (int kp = 0; kp < KP; kp++, gs++) {
                 const int s = gs % S;
+                const int nk = min(TS_KS, a.KB - kp * TS_KS);
                 if (!mbar_wait(&empty[s], ((gs / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
                     fail();
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-#pragma unroll
-                for (int h = 0; h < 2; h++, g++) {
-                    const int r = g % R;
-                    if (!mbar_wait(&rawFull[r], (g / R) & 1, abort_addr, UM_WAIT_CYCLES)) {
-                        fail();
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t rs = raw_u32 + r * Cfg::RAW_BYTES;
-                    uint32_t o[8];
-                    cvt_chunk<BITS>(rs + code_off, chunk_scale(rs + Cfg::RAW_CODE, row, q), o);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&rawEmpty[r]);  // the codes are in registers
-                    tmem_st8(ta + s * 64 + h * 32, o);
+                // the stage's code tiles (one ring slot), converted as four
+                // independent chains, then stored to TMEM
+                const int r = g % R;
+                if (!mbar_wait(&rawFull[r], (g / R) & 1, abort_addr, UM_WAIT_CYCLES)) {
+                    fail();
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
+                uint32_t o[TS_KS][8];
+#pragma unroll
+                for (int h = 0; h < TS_KS; h++)
+                    if (h < nk) {
+                        const uint32_t rs = raw_u32 + r * Cfg::RAW_SLOT + h * Cfg::RAW_BYTES;
+                        cvt_chunk<BITS>(rs + code_off, chunk_scale(rs + Cfg::RAW_CODE, row, q),
+                                        o[h]);
+                    }
+#pragma unroll
+                for (int h = 0; h < TS_KS; h++)
+                    if (h < nk) tmem_st8(ta + s * (TS_KS * 32) + h * 32, o[h]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rawEmpty[r]);  // codes consumed by the stores
+                g++;
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -710,21 +729,19 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             bool ok = true;
             for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
                 const Unit w = unit_at(i, u);
-                const size_t tb = (size_t)(w.e * a.RT + w.rt) * a.KB;
-                const uint8_t *codes = a.wq + tb * Cfg::RAW_CODE;
-                const __half2 *scales = a.ws + tb * UM_M;
-                for (int kb = 0; kb < a.KB; kb++, g++) {
+                const uint8_t *tile =
+                    a.wq + (size_t)(w.e * a.RT + w.rt) * a.KB * Cfg::RAW_BYTES;
+                for (int kp = 0; kp < KP; kp++, g++) {
                     const int r = g % R;
+                    const int nk = min(TS_KS, a.KB - kp * TS_KS);
                     if (!mbar_wait(&rawEmpty[r], ((g / R) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
                         fail();
                         ok = false;
                         break;
                     }
-                    uint8_t *dst = raw + r * Cfg::RAW_BYTES;
-                    mbar_arrive_expect_tx(&rawFull[r], Cfg::RAW_BYTES);
-                    bulk_load(dst, codes + (size_t)kb * Cfg::RAW_CODE, Cfg::RAW_CODE, &rawFull[r]);
-                    bulk_load(dst + Cfg::RAW_CODE, scales + (size_t)kb * UM_M, UM_M * 4,
-                              &rawFull[r]);
+                    mbar_arrive_expect_tx(&rawFull[r], nk * Cfg::RAW_BYTES);
+                    bulk_load(raw + r * Cfg::RAW_SLOT, tile + (size_t)kp * Cfg::RAW_SLOT,
+                              nk * Cfg::RAW_BYTES, &rawFull[r]);
                     last = g;
                 }
             }
@@ -741,16 +758,17 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 const Unit w = unit_at(i, u);
                 for (int kp = 0; kp < KP; kp++, gs++) {
                     const int s = gs % S;
+                    const int nk = min(TS_KS, a.KB - kp * TS_KS);
                     if (!mbar_wait(&empty[s], ((gs / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
                         fail();
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&fullB[s], Cfg::STAGE_B);
+                    mbar_arrive_expect_tx(&fullB[s], nk * Cfg::B_BYTES);
                     uint8_t *dst = base + s * Cfg::STAGE_B;
-                    tma_load_2d(dst, &tmap_b, 2 * kp * UM_BK, w.slot0, &fullB[s]);
-                    tma_load_2d(dst + Cfg::B_BYTES, &tmap_b, (2 * kp + 1) * UM_BK, w.slot0,
-                                &fullB[s]);
+                    for (int h = 0; h < nk; h++)
+                        tma_load_2d(dst + h * Cfg::B_BYTES, &tmap_b, (kp * TS_KS + h) * UM_BK,
+                                    w.slot0, &fullB[s]);
                     last = gs;
                 }
             }
@@ -782,15 +800,14 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t at = tmem + Cfg::A_COL0 + s * 64;
-                    const uint32_t bsm = base_u32 + s * Cfg::STAGE_B;
+                    const int nk = min(TS_KS, a.KB - kp * TS_KS);
+                    const uint32_t at = tmem + Cfg::A_COL0 + s * (TS_KS * 32);
+                    const uint64_t bd = desc_k_sw128(base_u32 + s * Cfg::STAGE_B);
+                    umma_ts_k64(acc, at, bd, idesc, kp != 0);
 #pragma unroll
-                    for (int h = 0; h < 2; h++)
-#pragma unroll
-                        for (int k16 = 0; k16 < UM_BK / 16; k16++)
-                            umma_f16_ts(acc, at + h * 32 + k16 * 8,
-                                        desc_k_sw128(bsm + h * Cfg::B_BYTES + k16 * 32), idesc,
-                                        (kp | h | k16) != 0);
+                    for (int h = 1; h < TS_KS; h++)
+                        if (h < nk)
+                            umma_ts_k64(acc, at + h * 32, bd + ((h * Cfg::B_BYTES) >> 4), idesc, 1);
                     umma_commit(&empty[s]);
                 }
                 if (ok) umma_commit(&accFull[buf]);
@@ -876,14 +893,14 @@ int launch_ep_regroup(const __half *recv, int R, int H, const int32_t *seg_recv_
 //   interleave (SWIGLU): row < 64 -> rt*64 + row (gate),
 //                        row >= 64 -> up_offset + rt*64 + row - 64 (up);
 //   plain (STORE):       rt*128 + row.
-// The tile's codes are stored as four 16-code chunks per row, chunk-major
-// ([chunk][row]).  int8 codes are stored biased (q + 128) for the
+// Output: one RawTile block per (e, rt, kb), codes chunk-major then the
+// rows' two group scales.  int8 codes are stored biased (q + 128) for the
 // converter's byte splice; int4 words are reordered so element 2j sits in
 // bits [4j, 4j+4) and element 2j+1 in bits [16+4j, 20+4j): one shift+mask
 // per fp16 pair.
 __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict__ sc, int bits,
                          int E, int rows_per_e, int K, int RT, int interleave, int up_offset,
-                         uint8_t *__restrict__ qo, __half2 *__restrict__ so) {
+                         uint8_t *__restrict__ qo) {
     const int KB = K / UM_BK;
     const int64_t n = (int64_t)E * RT * KB * UM_M;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -901,10 +918,11 @@ __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict
         srow = (int64_t)e * rows_per_e + rt * UM_M + row;
     const int row_bytes = bits == 8 ? K : K / 2;
     const int blk_bytes = bits == 8 ? UM_BK : UM_BK / 2;
+    const int code_bytes = UM_M * blk_bytes;
     const int cb = blk_bytes / 4;  // bytes of one 16-code chunk
     const uint8_t *s = q + srow * row_bytes + (int64_t)kb * blk_bytes;
     const int64_t tile = ((int64_t)e * RT + rt) * KB + kb;
-    uint8_t *d = qo + tile * (UM_M * blk_bytes);
+    uint8_t *d = qo + tile * (code_bytes + UM_M * 4);
     for (int c = 0; c < 4; c++) {
         uint8_t *dc = d + ((int64_t)c * UM_M + row) * cb;  // [chunk][row][cb]
         const uint8_t *sc4 = s + c * cb;
@@ -930,7 +948,7 @@ __global__ void k_repack(const uint8_t *__restrict__ q, const __half *__restrict
         }
     }
     const __half *ss = sc + srow * (K / QG_GROUP) + kb * 2;
-    so[tile * UM_M + row] = __halves2half2(ss[0], ss[1]);
+    reinterpret_cast<__half2 *>(d + code_bytes)[row] = __halves2half2(ss[0], ss[1]);
 }
 
 // ---- host side --------------------------------------------------------------
@@ -966,13 +984,18 @@ int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld,
     return QGMOE_OK;
 }
 
+size_t packed_bytes(int bits, int E, int rows_per_e, int K) {
+    // rows_per_e / 128 row tiles x K / 64 k blocks per expert
+    const size_t tiles = (size_t)E * (rows_per_e / UM_M) * (K / UM_BK);
+    return tiles * (size_t)(bits == 8 ? RawTile<8>::BYTES : RawTile<4>::BYTES);
+}
+
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
-                  int RT, int interleave, int up_offset, uint8_t *qo, __half2 *so,
-                  cudaStream_t s) {
+                  int RT, int interleave, int up_offset, uint8_t *qo, cudaStream_t s) {
     const int64_t n = (int64_t)E * RT * (K / UM_BK) * UM_M;
     if (n == 0) return QGMOE_OK;
     k_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, sc, bits, E, rows_per_e, K, RT,
-                                                          interleave, up_offset, qo, so);
+                                                          interleave, up_offset, qo);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
@@ -1021,7 +1044,6 @@ static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStre
 int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s) {
     UmmaArgs a{};
     a.wq = l.wq;
-    a.ws = l.ws;
     a.RT = l.RT;
     a.KB = l.KB;
     a.act_group = l.act_group;
