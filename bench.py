@@ -575,12 +575,14 @@ def run_ours(args, cfg):
 def run_ep(args, cfg, world, rank, local):
     """Config 3 over `world` GPUs: expert parallelism (experts round-robin,
     E/W per rank), every rank routing its own batch of T tokens (tokens
-    r*T .. (r+1)*T-1 of one generated stream); rows move through NCCL
-    all-to-all.  Weak scaling: the work per GPU stays one T-token layer."""
+    r*T .. (r+1)*T-1 of one generated stream).  Rows move through the
+    library's peer-memory exchange (default) or, with --ep-nccl, through NCCL
+    all-to-all driven by the host.  Weak scaling: the work per GPU stays one
+    T-token layer."""
     import torch
     import torch.distributed as dist
     import qgmoe
-    from qgmoe.ep import ExpertParallelMoE
+    from qgmoe.ep import ExpertParallelMoE, PeerExpertParallelMoE
 
     dev = local
     layer, x0, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False)
@@ -592,22 +594,16 @@ def run_ep(args, cfg, world, rank, local):
         x += MU
     del x0
     out = torch.empty_like(x)
-    ep = ExpertParallelMoE(layer)
+    peer = not args.ep_nccl
+    ep = PeerExpertParallelMoE(layer, T) if peer else ExpertParallelMoE(layer)
     stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize(dev)
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
             ep.forward(x, out, stream)
     stream.synchronize()
 
     # ---- timed region: device events on the launching stream, max over ranks
-    stages = {}
-    marks = []
-
-    def timer(name):
-        ev = torch.cuda.Event(enable_timing=True)
-        ev.record(stream)
-        marks.append((name, ev))
-
     barrier(world)
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -615,20 +611,45 @@ def run_ep(args, cfg, world, rank, local):
         with torch.cuda.stream(stream):
             ev0.record(stream)
             for _ in range(args.steps):
+                ep.forward(x, out, stream)
+            ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    value = T_all * args.steps / (total_ms / 1e3)
+
+    # ---- stage durations: a second pass with events between the stages ----
+    stages = {}
+    if peer:
+        layer.set_timing(True)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                ep.forward(x, out, stream)
+        stream.synchronize()
+        st_ms, nf = layer.read_timing()
+        layer.set_timing(False)
+        stages = {kk: v / max(nf, 1) for kk, v in st_ms.items()}
+    else:
+        marks = []
+
+        def timer(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            marks.append((name, ev))
+
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
                 start = torch.cuda.Event(enable_timing=True)
                 start.record(stream)
                 marks.append(("start", start))
                 ep.forward(x, out, stream, timer=timer)
-            ev1.record(stream)
         torch.cuda.synchronize(dev)
-    prev = None
-    for name, ev in marks:
-        if name != "start":
-            stages[name] = stages.get(name, 0.0) + prev.elapsed_time(ev)
-        prev = ev
-    stages = {kk: v / args.steps for kk, v in stages.items()}
-    total_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
-    value = T_all * args.steps / (total_ms / 1e3)
+        prev = None
+        for name, ev in marks:
+            if name != "start":
+                stages[name] = stages.get(name, 0.0) + prev.elapsed_time(ev)
+            prev = ev
+        stages = {kk: v / args.steps for kk, v in stages.items()}
+    barrier(world)
 
     # ---- roofline: the expert stage (grouped GEMMs on this rank) ----
     peaks, peak_src = load_peaks()
@@ -657,12 +678,15 @@ def run_ep(args, cfg, world, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     e2e = {"value": T_all * e2e_steps / e2e_s, "unit": "tokens/s",
            "h2d_bytes_per_step": T_all * H * 4, "d2h_bytes_per_step": T_all * H * 4,
-           "api": "qgmoe_ep_* via qgmoe.ep.ExpertParallelMoE (pinned host shards)"}
+           "api": ("qgmoe_ep_px_forward via qgmoe.ep.PeerExpertParallelMoE" if peer else
+                   "qgmoe_ep_* via qgmoe.ep.ExpertParallelMoE") + " (pinned host shards)"}
 
     if rank == 0:
         cfgj = config_json(cfg, world)
         cfgj.update(info)
         cfgj["placement"] = "round-robin: expert e on rank e % N"
+        cfgj["exchange"] = ("library kernels over NVLink peer memory (CUDA IPC), no host sync"
+                            if peer else "NCCL all_to_all_single (host-side split sizes)")
         cfgj["tokens_per_rank"] = T
         cfgj["tokens"] = T_all
         line = {
@@ -672,7 +696,8 @@ def run_ep(args, cfg, world, rank, local):
             "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 activations, int%d weights" % cfg["bits"], "data": "synthetic",
             "config": cfgj, "stage_ms_rank0": stages, "roofline": roof, "cpu_baseline": None,
-            "e2e": e2e, "gpu_launches": (4 + 3 + 1) * args.steps, "clocks": clk.summary(),
+            "e2e": e2e, "gpu_launches": (layer.last_launch_count() if peer else 4 + 3 + 1)
+            * args.steps, "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
     barrier(world)
@@ -692,6 +717,8 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "cuda_core", "tensor"],
                     help="expert-product path (qgmoe_set_path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-nccl", action="store_true",
+                    help="N > 1: move rows with NCCL all-to-all instead of peer memory")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.tokens:

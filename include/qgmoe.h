@@ -147,6 +147,29 @@ int qgmoe_ep_experts(qgmoe_t *h, const void *recv_rows, int32_t R, const int32_t
 int qgmoe_ep_combine(qgmoe_t *h, const void *back_rows, int32_t T, float *out, int32_t *sel_idx,
                      float *sel_w, void *stream);
 
+/* ---- expert-parallel forward over NVLink peer memory ----------------------
+ * The same expert-parallel layer with the row exchange done by the library's
+ * own kernels through CUDA IPC mappings of every rank's exchange region: no
+ * host synchronisation and no collective library in the data path (rows are
+ * stored straight into their owner's grouped buffer; the down GEMM stores its
+ * outputs straight into the source rank's buffer).  No reference counterpart
+ * (qwen-go has no multi-GPU code).  Setup, collective over the W ranks:
+ *   1. qgmoe_ep_px_setup: allocate this rank's region for up to max_tokens
+ *      tokens per rank and forward; writes its IPC handle
+ *      (QGMOE_IPC_HANDLE_BYTES bytes) to ipc_handle;
+ *   2. the host gathers all W handles in rank order (e.g. all_gather);
+ *   3. qgmoe_ep_px_connect: map the peers' regions.
+ * Then every rank calls qgmoe_ep_px_forward once per step (each with its own
+ * T <= max_tokens, T = 0 allowed): x [T, H] f32 -> out [T, H] f32, DEVICE
+ * pointers, enqueued on `stream`.  Ranks wait for each other on the GPU
+ * (bounded waits, ~2 s; a timeout is reported by qgmoe_sync).  Every rank
+ * must take the same number of steps; destroy handles only after all ranks
+ * finished their last step. */
+#define QGMOE_IPC_HANDLE_BYTES 64
+int qgmoe_ep_px_setup(qgmoe_t *h, int32_t max_tokens, void *ipc_handle);
+int qgmoe_ep_px_connect(qgmoe_t *h, const void *ipc_handles);
+int qgmoe_ep_px_forward(qgmoe_t *h, const float *x, int32_t T, float *out, void *stream);
+
 /* Waits for `stream` (NULL = the handle's stream) and reports any
  * device-side bounds flag raised since the last check. */
 int qgmoe_sync(qgmoe_t *h, void *stream);

@@ -181,6 +181,17 @@ struct qgmoe {
     int32_t *ep_tab = nullptr;  // per-call segment tables and local active list
     std::vector<int32_t> ep_host;
     CUtensorMap tmap_xg{}, tmap_eh{};
+    // expert-parallel exchange over NVLink peer memory (qg_peer.cu)
+    uint8_t *px_region = nullptr;   // this rank's exchange region (IPC-exported)
+    int px_cap = 0;                 // max tokens per rank and forward
+    PxArgs px{};                    // layout; bases filled by qgmoe_ep_px_connect
+    std::vector<void *> px_opened;  // peers' regions opened in this process
+    uint8_t **px_bases = nullptr;   // device array [W]
+    bool px_ready = false;
+    Allocs px_work;
+    PxTables pxt{};
+    __half *px_h16 = nullptr;       // SwiGLU outputs of the received rows
+    CUtensorMap tmap_px_recv[3]{}, tmap_px_h[3]{};
     // tensor-core path (qg_umma.cu): UMMA-tiled weight copies, fp16
     // activation buffers and their TMA descriptors
     bool tensor_ok = false;
@@ -604,6 +615,9 @@ int qgmoe_destroy(qgmoe_t *m) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     m->drop_graphs();
+    for (void *p : m->px_opened) cudaIpcCloseMemHandle(p);
+    if (m->px_region) cudaFree(m->px_region);
+    m->px_work.free_all();
     m->work.free_all();
     m->ep_work.free_all();
     m->weights.free_all();
@@ -889,6 +903,169 @@ int qgmoe_ep_combine(qgmoe_t *m, const void *back_rows, int32_t T, float *out, i
     if (sel_w)
         QG_CUDA(cudaMemcpyAsync(sel_w, m->st.topk_w, sizeof(float) * T * m->k,
                                 cudaMemcpyDeviceToDevice, s));
+    return QGMOE_OK;
+}
+
+// ---- expert parallelism over peer memory -----------------------------------
+static size_t px_align(size_t b) { return (b + 255) & ~size_t(255); }
+
+int qgmoe_ep_px_setup(qgmoe_t *m, int32_t max_tokens, void *ipc_handle) {
+    if (!m || !ipc_handle) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/ipc_handle");
+    if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
+    if (m->ep_world > PX_MAX_WORLD)
+        return set_error(QGMOE_ERR_UNSUPPORTED, "ep_world %d > %d", m->ep_world, PX_MAX_WORLD);
+    if (m->px_region) return set_error(QGMOE_ERR_INVALID_ARG, "exchange region already set up");
+    if (max_tokens <= 0) return set_error(QGMOE_ERR_INVALID_ARG, "max_tokens must be > 0");
+    const int64_t rows = (int64_t)max_tokens * m->k;
+    if (rows * m->ep_world >= (1 << 24))
+        return set_error(QGMOE_ERR_INVALID_ARG, "max_tokens * top_k * ep_world must be < 2^24");
+    QG_CUDA(cudaSetDevice(m->device));
+    const int W = m->ep_world, G = m->G, H = m->H;
+    PxArgs &a = m->px;
+    a.W = W;
+    a.me = m->ep_rank;
+    a.G = G;
+    a.H = H;
+    a.k = m->k;
+    a.recv_cap = rows * W;
+    a.off_epoch = 3 * PX_FLAG_BLOCK;
+    a.off_ticket = a.off_epoch + 8;
+    a.off_inbox = 1024;
+    a.off_recv = px_align(a.off_inbox + sizeof(int32_t) * (size_t)W * W * G);
+    a.off_back = px_align(a.off_recv + sizeof(__half) * (size_t)a.recv_cap * H);
+    const size_t bytes = px_align(a.off_back + sizeof(__half) * (size_t)rows * H);
+    int rc = ensure_capacity(m, max_tokens);
+    if (rc) return rc;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&m->px_region), bytes);
+    if (e != cudaSuccess) {
+        m->px_region = nullptr;
+        return set_error(QGMOE_ERR_CUDA, "exchange region cudaMalloc(%zu): %s", bytes,
+                         cudaGetErrorString(e));
+    }
+    QG_CUDA(cudaMemset(m->px_region, 0, a.off_recv));
+    cudaIpcMemHandle_t hnd;
+    QG_CUDA(cudaIpcGetMemHandle(&hnd, m->px_region));
+    memcpy(ipc_handle, &hnd, sizeof(hnd));
+    Allocs &w = m->px_work;
+    PxTables &t = m->pxt;
+    if ((rc = w.alloc(reinterpret_cast<void **>(&t.act_group), sizeof(int32_t) * (G + 1))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.act_begin), sizeof(int32_t) * (G + 1))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.act_n), sizeof(int32_t) * (G + 1))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.n_act), sizeof(int32_t))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.n_rows), sizeof(int32_t))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.tile_prefix), sizeof(int32_t) * (G + 2))) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&t.out_map), sizeof(int32_t) * a.recv_cap)) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&m->px_h16),
+                      sizeof(__half) * (size_t)a.recv_cap * m->I)) ||
+        (rc = w.alloc(reinterpret_cast<void **>(&m->px_bases), sizeof(uint8_t *) * W)))
+        return rc;
+    const int box[3] = {256, 64, 16};
+    for (int i = 0; i < 3; i++) {
+        if ((rc = encode_act_map(&m->tmap_px_recv[i],
+                                 reinterpret_cast<const __half *>(m->px_region + a.off_recv),
+                                 (int)a.recv_cap, H, H, box[i])) ||
+            (rc = encode_act_map(&m->tmap_px_h[i], m->px_h16, (int)a.recv_cap, m->I, m->I, box[i])))
+            return rc;
+    }
+    m->px_cap = max_tokens;
+    return QGMOE_OK;
+}
+
+int qgmoe_ep_px_connect(qgmoe_t *m, const void *ipc_handles) {
+    if (!m || !ipc_handles) return set_error(QGMOE_ERR_INVALID_ARG, "null handle/ipc_handles");
+    if (!m->px_region) return set_error(QGMOE_ERR_INVALID_ARG, "call qgmoe_ep_px_setup first");
+    if (m->px_ready) return set_error(QGMOE_ERR_INVALID_ARG, "already connected");
+    QG_CUDA(cudaSetDevice(m->device));
+    const int W = m->ep_world;
+    std::vector<uint8_t *> bases(W, nullptr);
+    const unsigned char *hb = static_cast<const unsigned char *>(ipc_handles);
+    for (int r = 0; r < W; r++) {
+        if (r == m->ep_rank) {
+            bases[r] = m->px_region;
+            continue;
+        }
+        cudaIpcMemHandle_t hnd;
+        memcpy(&hnd, hb + (size_t)r * QGMOE_IPC_HANDLE_BYTES, sizeof(hnd));
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, hnd, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error(QGMOE_ERR_CUDA, "cudaIpcOpenMemHandle(rank %d): %s", r,
+                             cudaGetErrorString(e));
+        m->px_opened.push_back(p);
+        bases[r] = static_cast<uint8_t *>(p);
+    }
+    QG_CUDA(cudaMemcpy(m->px_bases, bases.data(), sizeof(uint8_t *) * W, cudaMemcpyHostToDevice));
+    m->px.bases = m->px_bases;
+    m->px_ready = true;
+    return QGMOE_OK;
+}
+
+int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void *stream) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (!m->px_ready) return set_error(QGMOE_ERR_INVALID_ARG, "exchange not connected");
+    if (T < 0 || T > m->px_cap)
+        return set_error(QGMOE_ERR_INVALID_ARG, "T=%d outside [0, %d]", T, m->px_cap);
+    if (T > 0 && (!x || !out)) return set_error(QGMOE_ERR_INVALID_ARG, "null x/out");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = 0;
+    // every rank takes every step, T = 0 included (its counts are zero)
+    const int nt = T > 0 ? tile_tokens_for(m, T) : 256;
+    const int ti = nt == 256 ? 0 : (nt == 64 ? 1 : 2);
+    m->st.tile_tokens = nt;
+    m->begin_timed();
+    m->mark(0, nullptr, s);
+    if (T > 0) {
+        if ((rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
+                               nullptr, m->err_dev, s)))
+            return rc;
+    } else {
+        QG_CUDA(cudaMemsetAsync(m->st.expert_off, 0, sizeof(int32_t) * m->E, s));
+    }
+    m->mark(1, "route", s);
+    PxArgs a = m->px;
+    a.T = T;
+    if ((rc = launch_px_counts(a, m->st.expert_off, m->err_dev, s)) ||
+        (rc = launch_px_send(a, x, m->st.expert_off, m->st.slot_token, m->err_dev, s)))
+        return rc;
+    m->mark(2, "dispatch", s);
+    if ((rc = launch_px_tables(a, nt, m->pxt, m->err_dev, s))) return rc;
+    int dev_sms = num_sms(m->device);
+    UmmaLaunch l{};
+    l.act_group = m->pxt.act_group;
+    l.act_begin = m->pxt.act_begin;
+    l.act_n = m->pxt.act_n;
+    l.n_act = m->pxt.n_act;
+    l.tile_prefix = m->pxt.tile_prefix;
+    l.err = m->err_dev;
+    l.tile_tokens = nt;
+    l.wq = m->gu_pq;
+    l.RT = m->I / 64;
+    l.KB = m->H / 64;
+    l.out = m->px_h16;
+    l.out_stride = m->I;
+    l.grid = dev_sms;
+    if ((rc = launch_umma(m->bits, true, &m->tmap_px_recv[ti], l, s))) return rc;
+    l.wq = m->dn_pq;
+    l.RT = m->H / 128;
+    l.KB = m->I / 64;
+    l.out = nullptr;
+    l.out_stride = m->H;
+    l.out_map = m->pxt.out_map;
+    l.out_peers = m->px_bases;
+    l.out_peer_off = m->px.off_back;
+    if ((rc = launch_umma(m->bits, false, &m->tmap_px_h[ti], l, s))) return rc;
+    m->mark(3, "experts", s);
+    if ((rc = launch_px_signal(a, s)) || (rc = launch_px_wait(a, m->err_dev, s))) return rc;
+    m->mark(4, "return", s);
+    if (T > 0) {
+        const __half *back = reinterpret_cast<const __half *>(m->px_region + m->px.off_back);
+        if ((rc = launch_combine_f16(back, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, nullptr,
+                                     0, out, s)))
+            return rc;
+    }
+    m->mark(5, "combine", s);
+    m->last_launches = (T > 0 ? 3 : 0) + 2 + 1 + 2 + 2 + (T > 0 ? 1 : 0);
     return QGMOE_OK;
 }
 

@@ -75,6 +75,28 @@ __device__ __forceinline__ int dispatch_key(int e, int E, int W) {
     return W > 1 ? (e % W) * (E / W) + e / W : e;
 }
 
+// Expert-parallel exchange over NVLink peer memory (qg_peer.cu): every
+// rank's exchange region, mapped into this process, and its layout.
+constexpr int PX_CNT = 0, PX_DATA = 1, PX_BACK = 2;  // flag kinds
+constexpr int PX_FLAG_BLOCK = 256;                   // bytes per flag kind (W <= 32)
+constexpr int PX_MAX_WORLD = 32;
+struct PxArgs {
+    uint8_t *const *bases;  // device array [W]: every rank's region as mapped here
+    int W, me, G, H, k, T;
+    int64_t recv_cap;       // rows of a region's recv buffer
+    size_t off_epoch, off_ticket, off_inbox, off_recv, off_back;
+};
+struct PxTables {  // this rank's grouped-row tables (device)
+    int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix, *out_map, *n_rows;
+};
+int launch_px_counts(const PxArgs &a, const int32_t *expert_off, int *err, cudaStream_t s);
+int launch_px_send(const PxArgs &a, const float *x, const int32_t *expert_off,
+                   const int32_t *slot_token, int *err, cudaStream_t s);
+int launch_px_tables(const PxArgs &a, int tile_tokens, const PxTables &t, int *err,
+                     cudaStream_t s);
+int launch_px_signal(const PxArgs &a, cudaStream_t s);
+int launch_px_wait(const PxArgs &a, int *err, cudaStream_t s);
+
 // One launch of the tensor-core grouped GEMM (qg_umma.cu).
 struct UmmaLaunch {
     const uint8_t *wq;          // packed tiles: per (expert, row tile, k block) the codes
@@ -84,6 +106,10 @@ struct UmmaLaunch {
     __half *out;                // GEMM1: h [slots, I]; GEMM2: d [slots, H] (fp16)
     int out_stride;
     const int32_t *out_map;     // GEMM2 only: output row of each slot (null = same slot)
+    // GEMM2 only, expert parallelism over peer memory: out_map holds
+    // (rank << 24 | row) and row goes to out_peers[rank] + out_peer_off
+    uint8_t *const *out_peers;
+    size_t out_peer_off;
     int *err;
     int grid;                   // upper bound of work units
     int tile_tokens;            // max tokens per work unit: 256 (prefill) or 64 (decode)

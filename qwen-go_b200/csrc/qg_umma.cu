@@ -230,6 +230,8 @@ struct UmmaArgs {
     __half *out;          // SWIGLU: h [slots, out_stride]; STORE: d [slots, out_stride]
     int out_stride;
     const int32_t *out_map;  // STORE: output row of each slot (null = the slot itself)
+    uint8_t *const *out_peers;  // STORE over peers: out_map = rank << 24 | row
+    size_t out_peer_off;
     int *err;
 };
 
@@ -299,8 +301,15 @@ __device__ __forceinline__ void epi_unit(const UmmaArgs &a, const Unit &w, uint3
                     o[2 * q] = *reinterpret_cast<uint32_t *>(&a2);
                     o[2 * q + 1] = *reinterpret_cast<uint32_t *>(&b2);
                 }
-                const int orow = a.out_map ? a.out_map[w.slot0 + t] : w.slot0 + t;
-                __half *dst = a.out + (size_t)orow * a.out_stride + w.rt * UM_M + er;
+                __half *dst;
+                if (a.out_peers) {  // expert parallelism: straight into the source rank
+                    const int code = a.out_map[w.slot0 + t];
+                    dst = reinterpret_cast<__half *>(a.out_peers[code >> 24] + a.out_peer_off) +
+                          (size_t)(code & 0xFFFFFF) * a.out_stride + w.rt * UM_M + er;
+                } else {
+                    const int orow = a.out_map ? a.out_map[w.slot0 + t] : w.slot0 + t;
+                    dst = a.out + (size_t)orow * a.out_stride + w.rt * UM_M + er;
+                }
                 reinterpret_cast<uint4 *>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
                 reinterpret_cast<uint4 *>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
             }
@@ -1054,6 +1063,8 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.out = l.out;
     a.out_stride = l.out_stride;
     a.out_map = l.out_map;
+    a.out_peers = l.out_peers;
+    a.out_peer_off = l.out_peer_off;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
     const int nt = l.tile_tokens == 64 || l.tile_tokens == 16 ? l.tile_tokens : 256;

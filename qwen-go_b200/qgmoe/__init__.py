@@ -70,6 +70,9 @@ SIGNATURES = {
     "qgmoe_ep_send_counts": ([_vp, C.POINTER(C.c_int32), _vp], C.c_int),
     "qgmoe_ep_experts": ([_vp, _vp, C.c_int32, C.POINTER(C.c_int32), _vp, _vp], C.c_int),
     "qgmoe_ep_combine": ([_vp, _vp, C.c_int32, _vp, _vp, _vp, _vp], C.c_int),
+    "qgmoe_ep_px_setup": ([_vp, C.c_int32, _vp], C.c_int),
+    "qgmoe_ep_px_connect": ([_vp, _vp], C.c_int),
+    "qgmoe_ep_px_forward": ([_vp, _vp, C.c_int32, _vp, _vp], C.c_int),
     "qgmoe_last_launch_count": ([_vp], C.c_int),
     "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_graphs": ([_vp, C.c_int32], C.c_int),

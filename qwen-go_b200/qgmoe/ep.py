@@ -81,6 +81,44 @@ def run_exchange(dispatch, experts, combine, group=None, device=None, timer=None
     return res
 
 
+IPC_HANDLE_BYTES = 64
+
+
+class PeerExpertParallelMoE:
+    """The GPU layer with the row exchange over NVLink peer memory
+    (qgmoe_ep_px_*): the library maps every rank's exchange region and moves
+    rows with its own kernels, so a forward is one stream of kernels with no
+    host synchronisation.  Construction is collective (all ranks, same
+    max_tokens); forward(x, out) works on this rank's token shard."""
+
+    def __init__(self, layer, max_tokens: int, group=None):
+        import torch
+        import torch.distributed as dist
+        from . import _check, lib
+        self.layer = layer
+        self.W = layer.ep_world
+        L = lib()
+        mine = np.zeros(IPC_HANDLE_BYTES, np.uint8)
+        _check(L.qgmoe_ep_px_setup(layer.h, int(max_tokens), mine.ctypes.data_as(C.c_void_p)),
+               "qgmoe_ep_px_setup")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        t = torch.from_numpy(mine).to(dev)
+        parts = [torch.empty_like(t) for _ in range(self.W)]
+        dist.all_gather(parts, t, group=group)
+        allh = np.ascontiguousarray(torch.cat(parts).cpu().numpy())
+        _check(L.qgmoe_ep_px_connect(layer.h, allh.ctypes.data_as(C.c_void_p)),
+               "qgmoe_ep_px_connect")
+        dist.barrier(group=group)
+
+    def forward(self, x, out, stream=None):
+        import torch
+        from . import _check, _ptr, _stream_ptr, lib
+        s = stream or torch.cuda.current_stream(x.device)
+        _check(lib().qgmoe_ep_px_forward(self.layer.h, _ptr(x), x.shape[0], _ptr(out),
+                                         _stream_ptr(s)), "qgmoe_ep_px_forward")
+        return out
+
+
 class ExpertParallelMoE:
     """The GPU layer: an expert-parallel MoeMLP handle (ep_world = W) plus
     the NCCL exchanges.  forward(x, out) works on this rank's token shard."""

@@ -1,7 +1,10 @@
-"""Expert-parallel forward on 2 GPUs (NCCL): each rank owns half the experts
-and a token shard; its output must match the single-GPU layer on the same
-tokens (same kernels, so the tolerance is the north-star one) and the oracle
-on a token sample.  Skipped when fewer than 2 GPUs are visible."""
+"""Expert-parallel forward on 2 GPUs: each rank owns half the experts and a
+token shard; its output must match the single-GPU layer on the same tokens
+(same kernels, so the tolerance is the north-star one) and the oracle on a
+token sample.  Two exchanges: NCCL all-to-all driven by the host
+(qgmoe.ep.ExpertParallelMoE) and the library's own peer-memory exchange
+(qgmoe.ep.PeerExpertParallelMoE, uneven shards, repeated steps).  Skipped
+when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -21,7 +24,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, port, result_dir):
+def _rank_main(rank, port, result_dir, mode="nccl"):
     import datetime
     import sys
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -34,7 +37,7 @@ def _rank_main(rank, port, result_dir):
 
     import qg_oracle as O
     import qgmoe
-    from qgmoe.ep import ExpertParallelMoE
+    from qgmoe.ep import ExpertParallelMoE, PeerExpertParallelMoE
 
     torch.cuda.set_device(rank)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -45,7 +48,11 @@ def _rank_main(rank, port, result_dir):
     H, E, k, I, bits, T_all = 256, 16, 4, 128, 8, 600
     m = O.make_moe(H, E, k, I, 0, bits, seed=88)
     x_all = O.randn(88, 100, (T_all, H))
-    lo, hi = rank * T_all // W, (rank + 1) * T_all // W
+    if mode == "nccl":
+        lo, hi = rank * T_all // W, (rank + 1) * T_all // W
+    else:  # uneven shards: 220 / 380 tokens
+        cut = 220
+        lo, hi = (0, cut) if rank == 0 else (cut, T_all)
     G = E // W
     mine = [rank + W * j for j in range(G)]          # experts owned here, local order
     gu_rows = np.concatenate([np.arange(e * 2 * I, (e + 1) * 2 * I) for e in mine])
@@ -56,18 +63,26 @@ def _rank_main(rank, port, result_dir):
                          gate_up_scale=np.ascontiguousarray(m.s16["gate_up"][gu_rows]),
                          down_q=np.ascontiguousarray(m.q["down"][dn_rows]),
                          down_scale=np.ascontiguousarray(m.s16["down"][dn_rows]))
-    ep = ExpertParallelMoE(layer)
+    ep = ExpertParallelMoE(layer) if mode == "nccl" else PeerExpertParallelMoE(layer, 400)
     x = torch.from_numpy(x_all[lo:hi]).cuda()
     out = torch.empty_like(x)
-    for _ in range(2):  # second pass checks the reused buffers
-        ep.forward(x, out)
-        torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    for _ in range(3):  # later passes check the reused buffers (and exchange epochs)
+        with torch.cuda.stream(s):
+            out.zero_()
+            ep.forward(x, out, s)
+        s.synchronize()
+    if mode == "peer":
+        rc = qgmoe.lib().qgmoe_sync(layer.h, None)
+        assert rc == 0, qgmoe.last_error()
     np.save(os.path.join(result_dir, f"ep{rank}.npy"), out.cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_two_gpu_expert_parallel_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_two_gpu_expert_parallel_matches_single_gpu(tmp_path, mode):
     import torch
     if torch.cuda.device_count() < W:
         pytest.skip("needs 2 GPUs")
@@ -77,7 +92,7 @@ def test_two_gpu_expert_parallel_matches_single_gpu(tmp_path):
     import qgmoe
     from moe_cases import check_outputs, make_gpu_moe
 
-    mp.spawn(_rank_main, args=(_free_port(), str(tmp_path)), nprocs=W, join=True)
+    mp.spawn(_rank_main, args=(_free_port(), str(tmp_path), mode), nprocs=W, join=True)
     H, E, k, I, bits, T_all = 256, 16, 4, 128, 8, 600
     m = O.make_moe(H, E, k, I, 0, bits, seed=88)
     x_all = O.randn(88, 100, (T_all, H))
