@@ -128,11 +128,14 @@ def zipf_bias_rows(E, H, c):
 # --------------------------------------------------------------------------
 
 
-def build_gpu_layer(cfg, device, ep_world=1, ep_rank=0, keep_host=True):
+def build_gpu_layer(cfg, device, ep_world=1, ep_rank=0, keep_host=True, placement="balanced"):
     """Generates the layer on the GPU with the library's generator/quantiser.
-    With ep_world > 1 only the experts this rank owns (e % W == rank) are
-    generated, from the same counter-based streams at their offsets, so every
-    rank holds exactly the slice of the single-GPU layer.
+    With ep_world > 1 only the experts this rank owns are generated, from the
+    same counter-based streams at their offsets, so every rank holds exactly
+    its slice of the single-GPU layer.  Placement: "balanced" (skewed
+    routing: experts spread over the ranks by the expert loads measured on the
+    calibration sample, rank 0's choice broadcast to all ranks) or
+    "round-robin" (expert e on rank e % W).
     Returns (MoeMLP, x [T, H] for all tokens, host copies, routing info)."""
     import torch
     import qgmoe
@@ -156,7 +159,29 @@ def build_gpu_layer(cfg, device, ep_world=1, ep_rank=0, keep_host=True):
         info["zipf_c"] = c
     args = dict(router=router)
     host = {"router": router.cpu().numpy()} if keep_host else {}
-    mine = list(range(ep_rank, E, ep_world))  # local expert order
+    slot = None
+    if ep_world > 1:
+        from qgmoe.ep import balanced_slots, owned_experts, round_robin_slots
+        if placement == "balanced" and cfg["zipf"]:
+            slot = balanced_slots(hist, ep_world)
+            import torch.distributed as dist
+            if dist.is_initialized():  # every rank takes rank 0's placement
+                t = torch.from_numpy(slot.astype(np.int64)).to(dev)
+                dist.broadcast(t, 0)
+                slot = t.cpu().numpy().astype(np.int32)
+            info["placement"] = "balanced by calibration-sample expert load"
+        else:
+            slot = round_robin_slots(E, ep_world).astype(np.int32)
+            info["placement"] = "round-robin: expert e on rank e % N"
+        mine = owned_experts(slot, ep_rank, ep_world)  # local expert order
+        G = E // ep_world
+        if cfg["zipf"]:
+            load = np.zeros(ep_world)
+            for e in range(E):
+                load[slot[e] // G] += hist[e]
+            info["rank_load_share"] = [round(float(v) / float(load.sum()), 4) for v in load]
+    else:
+        mine = list(range(E))
 
     def expert_stack(stream, rows_per_e, cols):
         if ep_world == 1:
@@ -189,7 +214,7 @@ def build_gpu_layer(cfg, device, ep_world=1, ep_rank=0, keep_host=True):
     torch.cuda.synchronize(dev)
     layer = qgmoe.MoeMLP(n_embed=H, n_experts=E, top_k=k, n_moe_mlp=I, n_shared_mlp=Is, bits=bits,
                          router_mode=qgmoe.ROUTER_TOPK, device=device, ep_world=ep_world,
-                         ep_rank=ep_rank, **args)
+                         ep_rank=ep_rank, ep_slot=slot, **args)
     del args
     torch.cuda.empty_cache()
     return layer, x, host, info
@@ -585,7 +610,8 @@ def run_ep(args, cfg, world, rank, local):
     from qgmoe.ep import ExpertParallelMoE, PeerExpertParallelMoE
 
     dev = local
-    layer, x0, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False)
+    layer, x0, _host, info = build_gpu_layer(cfg, dev, world, rank, keep_host=False,
+                                             placement=args.ep_placement)
     T, H = cfg["T"], cfg["H"]
     T_all = T * world
     x = torch.empty((T, H), dtype=torch.float32, device=x0.device)
@@ -684,7 +710,6 @@ def run_ep(args, cfg, world, rank, local):
     if rank == 0:
         cfgj = config_json(cfg, world)
         cfgj.update(info)
-        cfgj["placement"] = "round-robin: expert e on rank e % N"
         cfgj["exchange"] = ("library kernels over NVLink peer memory (CUDA IPC), no host sync"
                             if peer else "NCCL all_to_all_single (host-side split sizes)")
         cfgj["tokens_per_rank"] = T
@@ -717,6 +742,8 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "cuda_core", "tensor"],
                     help="expert-product path (qgmoe_set_path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "round-robin"],
+                    help="N > 1: expert placement over the ranks")
     ap.add_argument("--ep-nccl", action="store_true",
                     help="N > 1: move rows with NCCL all-to-all instead of peer memory")
     args = ap.parse_args()

@@ -94,13 +94,17 @@ typedef struct qgmoe_desc {
     const void *shared_up_scale;
     const uint8_t *shared_down_q;
     const void *shared_down_scale;
-    /* Expert parallelism (0 or 1 = off).  With ep_world = W > 1 this handle
-     * owns the experts e with e % W == ep_rank (local index e / W); the expert
-     * stacks above then hold only those E/W experts, in local order, while
-     * the router stays [E, H].  Forward then goes through the qgmoe_ep_*
-     * calls below. */
+    /* Expert parallelism (0 or 1 = off).  With ep_world = W > 1 each rank
+     * owns E/W experts; the expert stacks above then hold only this rank's
+     * experts, in local order, while the router stays [E, H].  Forward then
+     * goes through the qgmoe_ep_* calls below. */
     int32_t ep_world;
     int32_t ep_rank;
+    /* Placement (host array [E], may be NULL): ep_slot[e] = owner rank *
+     * (E/W) + local index of expert e, a permutation of 0..E-1 identical on
+     * every rank (e.g. balanced by measured expert load).  NULL = round-robin:
+     * expert e on rank e % W, local index e / W. */
+    const int32_t *ep_slot;
 } qgmoe_desc;
 
 /* Uploads the weights (device copies owned by the handle). */

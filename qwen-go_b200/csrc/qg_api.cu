@@ -595,6 +595,28 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             rc = set_error(QGMOE_ERR_CUDA, "weight upload: %s", cudaGetErrorString(e));
             break;
         }
+        if (W > 1 && d->ep_slot) {  // placement table: a permutation of 0..E-1
+            std::vector<char> seen(E, 0);
+            for (int e2 = 0; e2 < E; e2++) {
+                const int v = d->ep_slot[e2];
+                if (v < 0 || v >= E || seen[v]) {
+                    rc = set_error(QGMOE_ERR_INVALID_ARG, "ep_slot is not a permutation of 0..E-1");
+                    break;
+                }
+                seen[v] = 1;
+            }
+            if (rc) break;
+            int32_t *slot_dev = nullptr;
+            if ((rc = m->weights.alloc(reinterpret_cast<void **>(&slot_dev), sizeof(int32_t) * E)))
+                break;
+            const cudaError_t ce =
+                cudaMemcpy(slot_dev, d->ep_slot, sizeof(int32_t) * E, cudaMemcpyHostToDevice);
+            if (ce != cudaSuccess) {
+                rc = set_error(QGMOE_ERR_CUDA, "ep_slot upload: %s", cudaGetErrorString(ce));
+                break;
+            }
+            m->st.ep_slot = slot_dev;
+        }
         if ((rc = build_tensor_weights(m))) break;
         if (W > 1 && !m->tensor_ok) {
             rc = set_error(QGMOE_ERR_UNSUPPORTED, "expert parallelism needs the tensor-core path");

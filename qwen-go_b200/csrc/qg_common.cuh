@@ -65,13 +65,17 @@ struct RouteState {
     float *logits;         // [splits][T][E+1] split-K partial router logits
     int32_t *hist;         // [ceil(T/32)][E] expert histogram of each top-k CTA
     int32_t *expert_off;   // [E] first slot of each dispatch key
-    // Expert parallelism over ep_world ranks (1 = off): expert e is owned by
-    // rank e % ep_world, and slots are sorted by the dispatch key
-    // (e % W) * (E / W) + e / W, i.e. by destination rank, then local expert.
+    // Expert parallelism over ep_world ranks (1 = off): slots are sorted by
+    // the dispatch key = owner rank * (E / W) + local index of the expert,
+    // i.e. by destination rank, then local expert.  ep_slot [E] (device)
+    // holds the key of each expert; null = round-robin (expert e on rank
+    // e % W, local index e / W).
     int ep_world;
+    const int32_t *ep_slot;
 };
 
-__device__ __forceinline__ int dispatch_key(int e, int E, int W) {
+__device__ __forceinline__ int dispatch_key(int e, int E, int W, const int32_t *slot) {
+    if (slot) return slot[e];
     return W > 1 ? (e % W) * (E / W) + e / W : e;
 }
 

@@ -315,7 +315,7 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
             st.topk_idx[(size_t)t * k + lane] = e;
             st.topk_w[(size_t)t * k + lane] = __fdiv_rn(selp, den);
             if (e >= 0 && e < E)
-                atomicAdd(&hist_s[dispatch_key(e, E, st.ep_world)], 1);
+                atomicAdd(&hist_s[dispatch_key(e, E, st.ep_world, st.ep_slot)], 1);
             else
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
         }
@@ -464,7 +464,7 @@ k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
                 e = -1;
             } else {
-                e = dispatch_key(e, E, st.ep_world);
+                e = dispatch_key(e, E, st.ep_world, st.ep_slot);
             }
         }
         const unsigned peers = __match_any_sync(0xffffffffu, e);

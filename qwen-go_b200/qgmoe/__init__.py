@@ -56,6 +56,7 @@ class _Desc(C.Structure):
         ("shared_up_q", _vp), ("shared_up_scale", _vp),
         ("shared_down_q", _vp), ("shared_down_scale", _vp),
         ("ep_world", C.c_int32), ("ep_rank", C.c_int32),
+        ("ep_slot", _vp),
     ]
 
 
@@ -164,7 +165,7 @@ class MoeMLP:
 
     def __init__(self, *, n_embed, n_experts, top_k, n_moe_mlp, n_shared_mlp=0, bits=32,
                  router_mode=ROUTER_TOPK, scale_dtype=SCALE_F16, device=0, ep_world=1, ep_rank=0,
-                 router, shared_gate=None,
+                 ep_slot=None, router, shared_gate=None,
                  gate_up=None, down=None, shared_gate_proj=None, shared_up_proj=None,
                  shared_down_proj=None, gate_up_q=None, gate_up_scale=None, down_q=None,
                  down_scale=None, shared_gate_q=None, shared_gate_scale=None, shared_up_q=None,
@@ -186,9 +187,13 @@ class MoeMLP:
             scale_dtype
         d.weights_on_device, d.device = int(on_dev), device
         d.ep_world, d.ep_rank = ep_world, ep_rank
+        slot = None
+        if ep_slot is not None:
+            slot = np.ascontiguousarray(ep_slot, np.int32)
+            d.ep_slot = slot.ctypes.data_as(_vp)
         for name, v in arrays.items():
             setattr(d, name, _ptr(v))
-        self._keep = arrays  # alive until create() has copied them
+        self._keep = (arrays, slot)  # alive until create() has copied them
         h = _vp()
         _check(lib().qgmoe_create(C.byref(d), C.byref(h)), "qgmoe_create")
         self._keep = None

@@ -26,9 +26,72 @@ import ctypes as C
 import numpy as np
 
 
-def dispatch_key(e, E: int, W: int):
-    """Sort key of expert e: (owner rank, local index) = (e % W, e // W)."""
+def dispatch_key(e, E: int, W: int, slot=None):
+    """Sort key of expert e: owner rank * (E/W) + local index; `slot` (the
+    placement, a permutation of 0..E-1) or round-robin (e % W, e // W)."""
+    if slot is not None:
+        return np.asarray(slot)[e]
     return (e % W) * (E // W) + e // W
+
+
+def round_robin_slots(E: int, W: int) -> np.ndarray:
+    e = np.arange(E)
+    return dispatch_key(e, E, W)
+
+
+def balanced_slots(load, W: int) -> np.ndarray:
+    """Placement by measured load: experts in decreasing load, each to the
+    rank with the least load so far among those with a free place (E/W
+    places per rank); local indices in increasing expert id.  Returns
+    slot[e] = rank * (E/W) + local index."""
+    load = np.asarray(load, np.float64)
+    E = load.size
+    G = E // W
+    tot = np.zeros(W)
+    owned = [[] for _ in range(W)]
+    for e in np.argsort(-load, kind="stable"):
+        free = [r for r in range(W) if len(owned[r]) < G]
+        r = min(free, key=lambda q: (tot[q], q))
+        owned[r].append(int(e))
+        tot[r] += load[e]
+    # then swap pairs between the most loaded rank and the others while that
+    # lowers the maximum (the greedy pass must also fill every rank to E/W)
+    for _ in range(4 * E):
+        a = int(np.argmax(tot))
+        best = None
+        for b in range(W):
+            if b == a:
+                continue
+            for i, x in enumerate(owned[a]):
+                for j, y in enumerate(owned[b]):
+                    d = load[x] - load[y]
+                    if d <= 0:
+                        continue
+                    m = max(tot[a] - d, tot[b] + d)
+                    if m < tot[a] - 1e-9 and (best is None or m < best[0]):
+                        best = (m, b, i, j, d)
+        if best is None:
+            break
+        _, b, i, j, d = best
+        owned[a][i], owned[b][j] = owned[b][j], owned[a][i]
+        tot[a] -= d
+        tot[b] += d
+    slot = np.empty(E, np.int32)
+    for r in range(W):
+        for j, e in enumerate(sorted(owned[r])):
+            slot[e] = r * G + j
+    return slot
+
+
+def owned_experts(slot, rank: int, W: int):
+    """Experts of `rank` in local order under placement `slot`."""
+    slot = np.asarray(slot)
+    G = slot.size // W
+    mine = np.empty(G, np.int64)
+    for e in range(slot.size):
+        if slot[e] // G == rank:
+            mine[slot[e] % G] = e
+    return mine.tolist()
 
 
 def exchange_counts(counts: np.ndarray, group=None, device=None) -> np.ndarray:

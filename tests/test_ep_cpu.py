@@ -20,7 +20,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, port, result_dir):
+def _rank_main(rank, port, result_dir, placement="rr"):
     import sys
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for p in (os.path.join(repo, "qwen-go_b200"), os.path.join(repo, "oracle")):
@@ -29,13 +29,16 @@ def _rank_main(rank, port, result_dir):
     import torch.distributed as dist
 
     import qg_oracle as O
-    from qgmoe.ep import dispatch_key, run_exchange
+    from qgmoe.ep import dispatch_key, owned_experts, round_robin_slots, run_exchange
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=W)
     H, E, k, I, bits, T_all = 64, 8, 3, 32, 8, 26
     G = E // W
+    place = (round_robin_slots(E, W) if placement == "rr"
+             else np.array([5, 2, 7, 0, 4, 1, 6, 3], np.int32))  # any permutation
+    mine = owned_experts(place, rank, W)
     m = O.make_moe(H, E, k, I, 0, bits, seed=77)
     x_all = O.randn(77, 100, (T_all, H))
     lo, hi = rank * T_all // W, (rank + 1) * T_all // W
@@ -46,7 +49,7 @@ def _rank_main(rank, port, result_dir):
     state = {}
 
     def dispatch():
-        keys = dispatch_key(idx.reshape(-1), E, W)
+        keys = dispatch_key(idx.reshape(-1), E, W, place)
         order = np.argsort(keys, kind="stable")       # pair ids in slot order
         slot = np.empty_like(order)
         slot[order] = np.arange(order.size)
@@ -72,7 +75,7 @@ def _rank_main(rank, port, result_dir):
             for j in range(G):
                 n = int(recv_counts[src, j])
                 if n:
-                    e = rank + W * j            # the global id of local expert j
+                    e = mine[j]                 # the global id of local expert j
                     out[off:off + n] = expert_rows(e, rows[off:off + n])
                 off += n
         return torch.from_numpy(out)
@@ -92,10 +95,11 @@ def _rank_main(rank, port, result_dir):
     dist.destroy_process_group()
 
 
-def test_two_rank_exchange_reproduces_oracle(tmp_path):
+@pytest.mark.parametrize("placement", ["rr", "permuted"])
+def test_two_rank_exchange_reproduces_oracle(tmp_path, placement):
     import torch.multiprocessing as mp
     port = _free_port()
-    mp.spawn(_rank_main, args=(port, str(tmp_path)), nprocs=W, join=True)
+    mp.spawn(_rank_main, args=(port, str(tmp_path), placement), nprocs=W, join=True)
     for r in range(W):
         out, ref = np.load(tmp_path / f"rank{r}.npy")
         np.testing.assert_allclose(out, ref, rtol=1e-6, atol=1e-7)
@@ -108,3 +112,26 @@ def test_dispatch_key_groups_by_owner_then_local_index():
     assert sorted(keys) == list(range(E))
     for e in range(E):
         assert keys[e] // (E // W) == e % W and keys[e] % (E // W) == e // W
+
+
+def test_balanced_placement_is_a_permutation_and_evens_the_load():
+    from qgmoe.ep import balanced_slots, owned_experts, round_robin_slots
+    E, W = 128, 8
+    load = (np.arange(E) + 1.0) ** -0.7 * 4096  # skewed expert loads whose hottest
+    assert load.max() < 0.75 * load.sum() / W   # expert fits well inside one rank
+    slot = balanced_slots(load, W)
+    assert sorted(slot.tolist()) == list(range(E))
+    G = E // W
+    per_rank = np.zeros(W)
+    for r in range(W):
+        mine = owned_experts(slot, r, W)
+        assert len(mine) == G and all(slot[e] // G == r for e in mine)
+        assert all(slot[e] % G == j for j, e in enumerate(mine))
+        per_rank[r] = load[mine].sum()
+    rr = round_robin_slots(E, W)
+    rr_rank = np.array([load[[e for e in range(E) if rr[e] // G == r]].sum() for r in range(W)])
+    # lower bound with E/W experts per rank: the mean, and the hottest expert
+    # together with the E/W - 1 lightest others
+    lb = max(load.sum() / W, load.max() + np.sort(load)[:G - 1].sum())
+    assert per_rank.max() <= 1.01 * lb
+    assert rr_rank.max() > 1.2 * per_rank.max()

@@ -48,22 +48,26 @@ def _rank_main(rank, port, result_dir, mode="nccl"):
     H, E, k, I, bits, T_all = 256, 16, 4, 128, 8, 600
     m = O.make_moe(H, E, k, I, 0, bits, seed=88)
     x_all = O.randn(88, 100, (T_all, H))
-    if mode == "nccl":
+    if mode != "peer":
         lo, hi = rank * T_all // W, (rank + 1) * T_all // W
     else:  # uneven shards: 220 / 380 tokens
         cut = 220
         lo, hi = (0, cut) if rank == 0 else (cut, T_all)
     G = E // W
-    mine = [rank + W * j for j in range(G)]          # experts owned here, local order
+    from qgmoe.ep import owned_experts, round_robin_slots
+    slot = (np.random.default_rng(5).permutation(E).astype(np.int32) if mode == "peer_perm"
+            else round_robin_slots(E, W).astype(np.int32))
+    mine = owned_experts(slot, rank, W)              # experts owned here, local order
     gu_rows = np.concatenate([np.arange(e * 2 * I, (e + 1) * 2 * I) for e in mine])
     dn_rows = np.concatenate([np.arange(e * H, (e + 1) * H) for e in mine])
     layer = qgmoe.MoeMLP(n_embed=H, n_experts=E, top_k=k, n_moe_mlp=I, bits=bits, device=rank,
-                         ep_world=W, ep_rank=rank, router=m.router,
+                         ep_world=W, ep_rank=rank, ep_slot=slot, router=m.router,
                          gate_up_q=np.ascontiguousarray(m.q["gate_up"][gu_rows]),
                          gate_up_scale=np.ascontiguousarray(m.s16["gate_up"][gu_rows]),
                          down_q=np.ascontiguousarray(m.q["down"][dn_rows]),
                          down_scale=np.ascontiguousarray(m.s16["down"][dn_rows]))
     ep = ExpertParallelMoE(layer) if mode == "nccl" else PeerExpertParallelMoE(layer, 400)
+    peer = mode != "nccl"
     x = torch.from_numpy(x_all[lo:hi]).cuda()
     out = torch.empty_like(x)
     s = torch.cuda.Stream()
@@ -73,7 +77,7 @@ def _rank_main(rank, port, result_dir, mode="nccl"):
             out.zero_()
             ep.forward(x, out, s)
         s.synchronize()
-    if mode == "peer":
+    if peer:
         rc = qgmoe.lib().qgmoe_sync(layer.h, None)
         assert rc == 0, qgmoe.last_error()
     np.save(os.path.join(result_dir, f"ep{rank}.npy"), out.cpu().numpy())
@@ -81,7 +85,7 @@ def _rank_main(rank, port, result_dir, mode="nccl"):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "peer"])
+@pytest.mark.parametrize("mode", ["nccl", "peer", "peer_perm"])
 def test_two_gpu_expert_parallel_matches_single_gpu(tmp_path, mode):
     import torch
     if torch.cuda.device_count() < W:
