@@ -181,11 +181,12 @@ int qgmoe_sync(qgmoe_t *h, void *stream);
 /* Number of kernel launches the last forward enqueued (instrumentation). */
 int qgmoe_last_launch_count(const qgmoe_t *h);
 
-/* Expert-product path.  AUTO picks the tcgen05 tensor-core grouped GEMM for
- * large token batches (T*k >= 2048) when the layer allows it (int8/int4
- * experts, no shared expert, H and I multiples of 128) and the CUDA-core
- * streaming GEMV otherwise.  CUDA_CORE / TENSOR force one path (TENSOR
- * returns QGMOE_ERR_UNSUPPORTED when the layer does not allow it). */
+/* Expert-product path.  AUTO picks the tcgen05 tensor-core grouped GEMMs
+ * whenever the layer allows them (int8/int4 experts; H, I and the shared
+ * width multiples of 128), except for the smallest batches of a layer with
+ * a shared expert (T*k < 16), and the CUDA-core streaming GEMV otherwise.
+ * CUDA_CORE / TENSOR force one path (TENSOR returns QGMOE_ERR_UNSUPPORTED
+ * when the layer does not allow it). */
 /* CUDA graphs (default on): the second forward with the same T, x, out and
  * stream is captured into a graph and later identical calls replay it, which
  * removes the per-launch host cost of decode-sized calls.  Disabled while

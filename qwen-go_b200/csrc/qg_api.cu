@@ -335,10 +335,15 @@ static int build_tensor_weights(qgmoe *m) {
     return QGMOE_OK;
 }
 
+// AUTO: the tensor-core path whenever the layer allows it, except the
+// smallest batches of a layer with a shared expert (T*k < 16), where the
+// CUDA-core path's fewer launches win (measured on B200: config 1 at T=1
+// 50 us on CUDA cores vs 64 us on tensor cores; at T=8 the tensor path is
+// 1.6x faster, and without a shared expert it wins from T=1 on).
 static bool use_tensor(const qgmoe *m, int T) {
     if (!m->tensor_ok || m->path_mode == QGMOE_PATH_CUDA_CORE) return false;
     if (m->path_mode == QGMOE_PATH_TENSOR) return true;
-    return T * m->k >= 64;
+    return !m->has_shared || T * m->k >= 16;
 }
 
 // Tokens per tensor-core work unit from the average tokens per expert in this
