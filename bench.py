@@ -675,11 +675,16 @@ def run_ep(args, cfg, world, rank, local):
                 stages[name] = stages.get(name, 0.0) + prev.elapsed_time(ev)
             prev = ev
         stages = {kk: v / args.steps for kk, v in stages.items()}
+    all_stages = [None] * world  # every rank's stage durations (ms), rank order
+    dist.all_gather_object(all_stages, stages)
+    stage_range = {kk: [round(min(r.get(kk, 0.0) for r in all_stages), 4),
+                        round(max(r.get(kk, 0.0) for r in all_stages), 4)] for kk in stages}
     barrier(world)
 
     # ---- roofline: the expert stage (grouped GEMMs on this rank) ----
     peaks, peak_src = load_peaks()
-    exp_ms = max_over_ranks(stages.get("experts", 0.0), world)
+    exp_ms = max_over_ranks(stages.get("experts", stages.get("gate_up", 0.0) +
+                                       stages.get("down_return", 0.0)), world)
     k, I = cfg["k"], cfg["I"]
     flops = 2.0 * T * k * 3 * I * H  # rows per rank on average = T*k
     achieved = flops / (exp_ms / 1e3) / 1e12 if exp_ms > 0 else 0.0
@@ -720,7 +725,8 @@ def run_ep(args, cfg, world, rank, local):
             "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 activations, int%d weights" % cfg["bits"], "data": "synthetic",
-            "config": cfgj, "stage_ms_rank0": stages, "roofline": roof, "cpu_baseline": None,
+            "config": cfgj, "stage_ms_rank0": stages, "stage_ms_min_max_over_ranks": stage_range,
+            "roofline": roof, "cpu_baseline": None,
             "e2e": e2e, "gpu_launches": (layer.last_launch_count() if peer else 4 + 3 + 1)
             * args.steps, "clocks": clk.summary(),
         }

@@ -1057,6 +1057,7 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
         return rc;
     m->mark(2, "dispatch", s);
     if ((rc = launch_px_tables(a, nt, m->pxt, m->err_dev, s))) return rc;
+    m->mark(3, "receive", s);  // the tables wait for every rank's rows
     int dev_sms = num_sms(m->device);
     UmmaLaunch l{};
     l.act_group = m->pxt.act_group;
@@ -1073,6 +1074,7 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     l.out_stride = m->I;
     l.grid = dev_sms;
     if ((rc = launch_umma(m->bits, true, &m->tmap_px_recv[ti], l, s))) return rc;
+    m->mark(4, "gate_up", s);
     l.wq = m->dn_pq;
     l.RT = m->H / 128;
     l.KB = m->I / 64;
@@ -1082,16 +1084,16 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     l.out_peers = m->px_bases;
     l.out_peer_off = m->px.off_back;
     if ((rc = launch_umma(m->bits, false, &m->tmap_px_h[ti], l, s))) return rc;
-    m->mark(3, "experts", s);
+    m->mark(5, "down_return", s);  // down GEMM, outputs stored into the sources
     if ((rc = launch_px_signal(a, s)) || (rc = launch_px_wait(a, m->err_dev, s))) return rc;
-    m->mark(4, "return", s);
+    m->mark(6, "wait", s);
     if (T > 0) {
         const __half *back = reinterpret_cast<const __half *>(m->px_region + m->px.off_back);
         if ((rc = launch_combine_f16(back, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, nullptr,
                                      0, out, s)))
             return rc;
     }
-    m->mark(5, "combine", s);
+    m->mark(7, "combine", s);
     m->last_launches = (T > 0 ? 3 : 0) + 2 + 1 + 2 + 2 + (T > 0 ? 1 : 0);
     return QGMOE_OK;
 }

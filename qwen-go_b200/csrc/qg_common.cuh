@@ -24,6 +24,42 @@ int set_error(int code, const char *fmt, ...);
                                    #call, cudaGetErrorString(e_));                    \
     } while (0)
 
+// Programmatic dependent launch.  The forward's kernels are launched with
+// launch_pdl: the next kernel of the stream may be scheduled while this one
+// is still running, and each kernel opens with pdl_enter(), which lets its
+// own successor be scheduled and then waits until every earlier kernel of
+// the stream has completed and its writes are visible.  Nothing is read or
+// written before that wait, so the only effect is that launch latency and
+// CTA start-up overlap the previous kernel's tail.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, int cluster_z, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    int n = 1;
+    if (cluster_z > 1) {
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = 1;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = cluster_z;
+        n = 2;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Device-side error word bits (an int in device memory, read back by the host).
 enum : int {
     QG_FLAG_BAD_EXPERT = 1,   // router produced an expert id out of [0, E)

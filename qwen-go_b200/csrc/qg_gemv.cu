@@ -130,6 +130,7 @@ __device__ __forceinline__ float silu_ref(float g) {
 template <int BITS, bool GATEUP>
 __global__ void __launch_bounds__(GEMV_THREADS)
 k_expert_gemv(ExpertArgs a) {
+    pdl_enter();
     extern __shared__ __align__(16) float xs[];
     constexpr int V = Chunk<BITS>::V;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -243,7 +244,7 @@ static int launch_t(const ExpertArgs &a, int max_items, cudaStream_t s) {
     int grid = num_sms(dev) * per_sm;
     if (max_items < grid) grid = max_items;
     if (grid < 1) grid = 1;
-    k_expert_gemv<BITS, GATEUP><<<grid, GEMV_THREADS, smem, s>>>(a);
+    QG_CUDA(launch_pdl(k_expert_gemv<BITS, GATEUP>, dim3(grid), dim3(GEMV_THREADS), smem, s, 1, a));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
@@ -286,6 +287,7 @@ __global__ void k_combine(const D *__restrict__ d, int H, int T, int k,
                           const int32_t *__restrict__ pair_slot,
                           const float *__restrict__ topk_w, const float *__restrict__ shared_w,
                           int has_shared, float *__restrict__ out) {
+    pdl_enter();
     const int t = blockIdx.y;
     const int j4 = blockIdx.x * blockDim.x + threadIdx.x;
     if (j4 * 4 >= H) return;
@@ -316,8 +318,8 @@ static int launch_combine_t(const D *d, int H, int T, int k, const int32_t *pair
                             cudaStream_t s) {
     const int threads = 128;
     dim3 grid((H / 4 + threads - 1) / threads, T);
-    k_combine<D><<<grid, threads, 0, s>>>(d, H, T, k, pair_slot, topk_w, shared_w, has_shared,
-                                          out);
+    QG_CUDA(launch_pdl(k_combine<D>, grid, dim3(threads), 0, s, 1, d, H, T, k, pair_slot, topk_w,
+                       shared_w, has_shared, out));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }

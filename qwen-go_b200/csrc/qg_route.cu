@@ -90,6 +90,7 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
     constexpr int WV = RR * LG_KC / 4;   // float4 loads of router rows per K chunk
     constexpr int XPT = (XV + 255) / 256, WPT = WV / 256;
     static_assert(WV % 256 == 0, "router chunk must split evenly over the CTA");
+    pdl_enter();
     extern __shared__ __align__(16) float lg_smem[];
     float (*xs)[TT + 4] = reinterpret_cast<float (*)[TT + 4]>(lg_smem);
     float (*ws)[RR + 4] = reinterpret_cast<float (*)[RR + 4]>(lg_smem + LG_KC * (TT + 4));
@@ -219,6 +220,7 @@ template <int NJ>
 __global__ void __launch_bounds__(RT_THREADS)
 k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
        int has_shared, RouteState st, int *err) {
+    pdl_enter();
     extern __shared__ int hist_s[];  // [E]
     __shared__ int s_idx[RT_WARPS][QG_MAX_TOPK];
     __shared__ int s_last;
@@ -414,6 +416,7 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
 // ---- 3. scatter (+ fp16 gather) ---------------------------------------------------
 __global__ void __launch_bounds__(RT_THREADS)
 k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
+    pdl_enter();
     extern __shared__ int sm[];
     int *cur = sm;            // [E] next slot per expert for this CTA
     int *wcnt = sm + E;       // [RT_WARPS][E]
@@ -517,19 +520,9 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
         wide[dev] = true;
     }
     const int TT = small ? 8 : 64, RR = small ? 32 : 128;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = small ? LgTile<8, 32>::SMEM : LgTile<64, 128>::SMEM;
-    cfg.stream = s;
-    cudaLaunchAttribute cl[1];
-    cl[0].id = cudaLaunchAttributeClusterDimension;
-    cl[0].val.clusterDim.x = 1;
-    cl[0].val.clusterDim.y = 1;
-    cl[0].val.clusterDim.z = ks;
-    cfg.attrs = cl;
-    cfg.numAttrs = ks > 1 ? 1 : 0;
-    QG_CUDA(cudaLaunchKernelEx(&cfg, kern, x, T, H, E, Ep, router, shared_gate, st.logits));
+    QG_CUDA(launch_pdl(kern, dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks), dim3(256),
+                       small ? LgTile<8, 32>::SMEM : LgTile<64, 128>::SMEM, s, ks, x, T, H, E,
+                       Ep, router, shared_gate, st.logits));
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
@@ -539,20 +532,18 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
         attr[dev] = true;
     }
     const int nj = (E + 31) / 32;
-    if (nj <= 1)
-        k_topk<1><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
-    else if (nj <= 2)
-        k_topk<2><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
-    else if (nj <= 4)
-        k_topk<4><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
-    else if (nj <= 8)
-        k_topk<8><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
-    else if (nj <= 16)
-        k_topk<16><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
-    else
-        k_topk<32><<<nc, RT_THREADS, sm2, s>>>(st.logits, T, E, Ep, k, mode, has_shared, st, err);
+    void (*topk)(const float *, int, int, int, int, int, int, RouteState, int *) =
+        nj <= 1    ? k_topk<1>
+        : nj <= 2  ? k_topk<2>
+        : nj <= 4  ? k_topk<4>
+        : nj <= 8  ? k_topk<8>
+        : nj <= 16 ? k_topk<16>
+                   : k_topk<32>;
+    QG_CUDA(launch_pdl(topk, dim3(nc), dim3(RT_THREADS), sm2, s, 1, (const float *)st.logits, T, E,
+                       Ep, k, mode, has_shared, st, err));
     QG_CUDA(cudaGetLastError());
-    k_scatter<<<nc, RT_THREADS, sm3, s>>>(T, E, k, has_shared, st, err);
+    QG_CUDA(launch_pdl(k_scatter, dim3(nc), dim3(RT_THREADS), sm3, s, 1, T, E, k, has_shared, st,
+                       err));
     QG_CUDA(cudaGetLastError());
     if (xp) return launch_gather_f16(x, st.slot_token, T * k + (has_shared ? T : 0), H, xp, s);
     return QGMOE_OK;

@@ -321,6 +321,7 @@ __device__ __forceinline__ void epi_unit(const UmmaArgs &a, const Unit &w, uint3
 template <int BITS, bool SWIGLU, int NT>
 __global__ void __launch_bounds__(UM_THREADS, 1)
 k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
+    pdl_enter();
     using Cfg = UmCfg<BITS, NT>;
     constexpr int S = Cfg::STAGES;
     constexpr int R = Cfg::RAW_STAGES;
@@ -585,6 +586,7 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 template <int BITS, bool SWIGLU, int NT>
 __global__ void __launch_bounds__(TS_THREADS, 1)
 k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
+    pdl_enter();
     using Cfg = TsCfg<BITS, NT>;
     constexpr int S = TS_S, R = Cfg::R;
     constexpr int CB = RawTile<BITS>::CB;
@@ -839,6 +841,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 // ---- activation gather: xp[s, :] = fp16(x[slot_token[s], :]) -------------
 __global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restrict__ slot_token,
                              int nslots, int H, __half *__restrict__ xp) {
+    pdl_enter();
     const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const int nw = (gridDim.x * blockDim.x) >> 5;
@@ -1017,7 +1020,8 @@ int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int
     int blocks = (nslots + 7) / 8;
     const int cap = num_sms(dev) * 8;
     if (blocks > cap) blocks = cap;
-    k_gather_f16<<<blocks, 256, 0, s>>>(x, slot_token, nslots, H, xp);
+    QG_CUDA(launch_pdl(k_gather_f16, dim3(blocks), dim3(256), 0, s, 1, x, slot_token, nslots, H,
+                       xp));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
@@ -1045,7 +1049,8 @@ static int launch_umma_t(const void *tmap, const UmmaArgs &a, int grid, cudaStre
     }
     int g = num_sms(dev);
     if (grid < g) g = grid;
-    kern<<<g, threads, smem, s>>>(*reinterpret_cast<const CUtensorMap *>(tmap), a);
+    QG_CUDA(launch_pdl(kern, dim3(g), dim3(threads), smem, s, 1,
+                       *reinterpret_cast<const CUtensorMap *>(tmap), a));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
