@@ -209,6 +209,13 @@ struct qgmoe {
         graph_seen.clear();
     }
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
+    // router logits on the tensor cores (qg_router_tc.cu): split router rows
+    // at create time, split activations per call (workspace)
+    bool rtc_ok = false;
+    RouterTC rtc{};
+    const RouterTC *rtc_for(int T) const {
+        return rtc_ok && T >= RTC_MIN_T && T <= rtc.cap ? &rtc : nullptr;
+    }
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
     // boxes of 256 / 64 / 16 token rows (prefill and decode tile sizes)
     CUtensorMap tmap_x[3]{}, tmap_h[3]{}, tmap_hs[3]{};
@@ -278,6 +285,10 @@ static int ensure_capacity(qgmoe *m, int T) {
         QG_A(m->h16, sizeof(__half) * slots * m->hmax);
         QG_A(m->d16, sizeof(__half) * slots * m->H);
     }
+    if (m->rtc_ok && cap >= RTC_MIN_T) {
+        QG_A(m->rtc.xh, sizeof(__half) * (size_t)cap * m->H);
+        QG_A(m->rtc.xl, sizeof(__half) * (size_t)cap * m->H);
+    }
     QG_A(m->h, sizeof(float) * slots * m->hmax);
     QG_A(m->d, sizeof(float) * slots * m->H);
     QG_A(m->x_dev, sizeof(float) * (size_t)cap * m->H);
@@ -300,7 +311,45 @@ static int ensure_capacity(qgmoe *m, int T) {
                 return rc;
         }
     }
+    m->rtc.cap = 0;
+    if (m->rtc_ok && cap >= RTC_MIN_T) {
+        if ((rc = encode_act_map(&m->rtc.map_xh, m->rtc.xh, cap, m->H, m->H, 256)) ||
+            (rc = encode_act_map(&m->rtc.map_xl, m->rtc.xl, cap, m->H, m->H, 256)))
+            return rc;
+        m->rtc.cap = cap;
+    }
     m->cap_T = cap;
+    return QGMOE_OK;
+}
+
+// Tensor-core router: the router rows (and the shared-gate row) split into
+// fp16 heads and tails once.  Rows beyond fp16 range keep the CUDA-core
+// router for this handle.
+static int build_router_tc(qgmoe *m) {
+    if (m->H % 64) return QGMOE_OK;
+    const int Ep = m->E + m->has_shared;
+    const int rows_pad = (Ep + 127) / 128 * 128;
+    Allocs &al = m->weights;
+    __half *wh = nullptr, *wl = nullptr;
+    int rc;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&wh), sizeof(__half) * (size_t)rows_pad * m->H)) ||
+        (rc = al.alloc(reinterpret_cast<void **>(&wl), sizeof(__half) * (size_t)rows_pad * m->H)))
+        return rc;
+    int *flag = nullptr;
+    if ((rc = al.alloc(reinterpret_cast<void **>(&flag), sizeof(int)))) return rc;
+    QG_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), m->stream));
+    if ((rc = launch_split_rows(m->router, m->shared_gate, m->E, Ep, m->H, rows_pad, wh, wl, flag,
+                                m->stream)))
+        return rc;
+    int h_flag = 0;
+    QG_CUDA(cudaMemcpyAsync(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    QG_CUDA(cudaStreamSynchronize(m->stream));
+    if (h_flag) return QGMOE_OK;  // router weights beyond fp16 range
+    if ((rc = encode_act_map(&m->rtc.map_wh, wh, rows_pad, m->H, m->H, 128)) ||
+        (rc = encode_act_map(&m->rtc.map_wl, wl, rows_pad, m->H, m->H, 128)))
+        return rc;
+    m->rtc.rows_pad = rows_pad;
+    m->rtc_ok = true;
     return QGMOE_OK;
 }
 
@@ -362,7 +411,7 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, m->xp16, m->err_dev, s);
+                          m->has_shared, m->st, m->xp16, m->err_dev, s, m->rtc_for(T));
     if (rc) return rc;
     m->mark(1, "route", s);
     const int pairs = T * m->k;
@@ -433,7 +482,9 @@ static int read_flag(qgmoe *m, cudaStream_t s) {
     if (flag) {
         cudaMemsetAsync(m->err_dev, 0, sizeof(int), s);
         cudaStreamSynchronize(s);
-        return set_error(QGMOE_ERR_DEVICE_FLAG, "device bounds flag 0x%x (1=expert id, 2=slot, 4=group)",
+        return set_error(QGMOE_ERR_DEVICE_FLAG,
+                         "device flag 0x%x (1=expert id, 2=slot, 4=group, 8=wait timeout, "
+                         "16=activation beyond fp16 range in the tensor-core router)",
                          flag);
     }
     return QGMOE_OK;
@@ -447,7 +498,7 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, nullptr, m->err_dev, s);
+                          m->has_shared, m->st, nullptr, m->err_dev, s, m->rtc_for(T));
     if (rc) return rc;
     m->mark(1, "route", s);
     ExpertArgs a{};
@@ -622,6 +673,7 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             }
             m->st.ep_slot = slot_dev;
         }
+        if ((rc = build_router_tc(m))) break;
         if ((rc = build_tensor_weights(m))) break;
         if (W > 1 && !m->tensor_ok) {
             rc = set_error(QGMOE_ERR_UNSUPPORTED, "expert parallelism needs the tensor-core path");
@@ -804,7 +856,7 @@ int qgmoe_ep_dispatch(qgmoe_t *m, const float *x, int32_t T, void *send_rows, vo
     int rc = ensure_capacity(m, T);
     if (rc) return rc;
     return launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
-                        static_cast<__half *>(send_rows), m->err_dev, s);
+                        static_cast<__half *>(send_rows), m->err_dev, s, m->rtc_for(T));
 }
 
 int qgmoe_ep_send_counts(qgmoe_t *m, int32_t *counts, void *stream) {
@@ -1044,7 +1096,7 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     m->mark(0, nullptr, s);
     if (T > 0) {
         if ((rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
-                               nullptr, m->err_dev, s)))
+                               nullptr, m->err_dev, s, m->rtc_for(T))))
             return rc;
     } else {
         QG_CUDA(cudaMemsetAsync(m->st.expert_off, 0, sizeof(int32_t) * m->E, s));

@@ -1,5 +1,6 @@
 // Shared definitions for the qgmoe CUDA library (sm_100a only).
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -66,6 +67,7 @@ enum : int {
     QG_FLAG_BAD_SLOT = 2,     // dispatch slot out of range
     QG_FLAG_BAD_GROUP = 4,    // expert kernel saw an active group out of range
     QG_FLAG_TIMEOUT = 8,      // a bounded mbarrier wait in the tensor-core kernel ran out
+    QG_FLAG_RANGE = 16,       // an activation beyond fp16 range reached the tensor-core router
 };
 
 // One stacked weight family (e.g. all experts' gate_up) in device memory.
@@ -177,9 +179,29 @@ struct ExpertArgs {
 // Launch helpers implemented in the .cu files.
 // Router + dispatch: logits, top-k, scatter; with xp set, a 4th launch writes
 // every slot's fp16 activation row for the tensor-core path.
+// Router logits on the tensor cores (qg_router_tc.cu), for batches of at
+// least RTC_MIN_T tokens: the router rows split once into fp16 hi + lo
+// parts, x split per call, logits = xh.Wh + xh.Wl + xl.Wh accumulated in f32.
+constexpr int RTC_MIN_T = 256;
+struct RouterTC {
+    CUtensorMap map_wh, map_wl;  // [rows_pad, H] fp16, boxes of 64 x 128
+    CUtensorMap map_xh, map_xl;  // [cap, H] fp16, boxes of 64 x 256
+    __half *xh, *xl;             // [cap, H]
+    int rows_pad;                // router rows (+ shared-gate row) padded to 128
+    int cap;                     // tokens xh / xl hold
+};
+int launch_split_rows(const float *router, const float *shared_gate, int E, int Ep, int H,
+                      int rows_pad, __half *wh, __half *wl, int *err, cudaStream_t s);
+int launch_logits_tc(const RouterTC &tc, const float *x, int T, int H, int Ep, float *logits,
+                     int *err, cudaStream_t s);
+int launch_gather_h16(const __half *xh, const int32_t *slot_token, int nslots, int H, __half *xp,
+                      cudaStream_t s);
+
+// The router (logits, top-k, dispatch; fp16 gathered rows when xp is set).
+// With tc (and T >= RTC_MIN_T) the logits run on the tensor cores.
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
                  const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
-                 cudaStream_t s);
+                 cudaStream_t s, const RouterTC *tc = nullptr);
 int route_splits(int T, int H, int Ep, int sms);
 int launch_expert(bool gateup, const ExpertArgs &a, int max_items, cudaStream_t s);
 // d rows are f32 (CUDA-core path) or fp16 (tensor-core path).

@@ -497,12 +497,9 @@ k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
             st.slot_token[T * k + t] = t;
 }
 
-int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
-                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
-                 cudaStream_t s) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int Ep = E + (has_shared ? 1 : 0);
+// CUDA-core logits: the split-K tiled f32 GEMM above.
+static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
+                         const float *shared_gate, float *logits, int dev, cudaStream_t s) {
     const int ks = route_splits(T, H, Ep, num_sms(dev));
     const bool small = T <= LG_SMALL_T;
     using LgKern = void (*)(const float *, int, int, int, int, const float *, const float *, float *);
@@ -522,7 +519,24 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     const int TT = small ? 8 : 64, RR = small ? 32 : 128;
     QG_CUDA(launch_pdl(kern, dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks), dim3(256),
                        small ? LgTile<8, 32>::SMEM : LgTile<64, 128>::SMEM, s, ks, x, T, H, E,
-                       Ep, router, shared_gate, st.logits));
+                       Ep, router, shared_gate, logits));
+    return QGMOE_OK;
+}
+
+int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
+                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
+                 cudaStream_t s, const RouterTC *tc) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int Ep = E + (has_shared ? 1 : 0);
+    const bool on_tc = tc && T >= RTC_MIN_T && T <= tc->cap && Ep <= tc->rows_pad;
+    if (on_tc) {
+        int rc = launch_logits_tc(*tc, x, T, H, Ep, st.logits, err, s);
+        if (rc) return rc;
+    } else {
+        int rc = launch_logits(x, T, H, E, Ep, router, shared_gate, st.logits, dev, s);
+        if (rc) return rc;
+    }
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
@@ -545,7 +559,12 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     QG_CUDA(launch_pdl(k_scatter, dim3(nc), dim3(RT_THREADS), sm3, s, 1, T, E, k, has_shared, st,
                        err));
     QG_CUDA(cudaGetLastError());
-    if (xp) return launch_gather_f16(x, st.slot_token, T * k + (has_shared ? T : 0), H, xp, s);
+    if (xp) {
+        const int nslots = T * k + (has_shared ? T : 0);
+        // after the tensor-core logits the fp16 rows exist already (xh = fp16(x))
+        return on_tc ? launch_gather_h16(tc->xh, st.slot_token, nslots, H, xp, s)
+                     : launch_gather_f16(x, st.slot_token, nslots, H, xp, s);
+    }
     return QGMOE_OK;
 }
 

@@ -154,3 +154,44 @@ def test_graph_replay_matches_eager():
         assert np.array_equal(gpu.forward_batch(x), ref)
     x2 = O.randn(48, 2, (5, 128))  # same buffers, new contents: replay reads them
     assert np.array_equal(gpu.forward_batch(x2), eager_gpu.forward_batch(x2))
+
+
+# ---- router logits on the tensor cores (T >= 256) -----------------------
+
+
+@pytest.mark.parametrize("bits,Is,T", [(8, 96, 300), (4, 0, 512), (32, 0, 257)])
+def test_tensor_core_router_matches_oracle(bits, Is, T):
+    """From 256 tokens on the logits run as three fp16 products of split
+    operands on the tensor cores; routing and outputs must still meet the
+    oracle bar (the shared-gate row rides along when Is > 0)."""
+    m = host_case(H=256, E=8, k=3, I=64, Is=Is, bits=bits, seed=50 + T)
+    x = O.randn(50, T, (T, 256))
+    _, flipped = run_both(m, x, O.ROUTER_TOPK)
+    assert len(flipped) <= T // 50  # near-ties only
+
+
+def test_tensor_core_router_agrees_with_cuda_core_router():
+    """The same tokens routed in one batch of 300 (tensor-core logits) and in
+    batches of 100 (CUDA-core logits) select the same experts, and the
+    weights agree to float rounding."""
+    m = host_case(H=512, E=16, k=4, I=64, Is=0, bits=8, seed=60)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(60, 1, (300, 512))
+    _, idx_a, w_a = gpu.forward_batch(x, return_routing=True)
+    parts = [gpu.forward_batch(x[i:i + 100], return_routing=True) for i in range(0, 300, 100)]
+    idx_b = np.concatenate([p[1] for p in parts])
+    w_b = np.concatenate([p[2] for p in parts])
+    same = np.all(idx_a == idx_b, axis=1)
+    assert same.mean() > 0.98
+    np.testing.assert_allclose(w_a[same], w_b[same], rtol=1e-5, atol=1e-6)
+
+
+def test_tensor_core_router_flags_activations_beyond_fp16():
+    m = host_case(H=256, E=8, k=2, I=64, Is=0, bits=8, seed=61)
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(61, 1, (300, 256))
+    x[7, 3] = 1.0e5
+    with pytest.raises(qgmoe.QgmoeError):
+        gpu.forward_batch(x)
+    ok = gpu.forward_batch(x[:100])  # the CUDA-core router (T < 256) takes it; the error cleared
+    assert np.all(np.isfinite(ok[np.arange(100) != 7]))
