@@ -619,13 +619,13 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&fullA[s], TS_CONV_WARPS);
+            mbar_init(&fullA[s], TS_CONV_WARPS / 2);  // the stage's converter group
             mbar_init(&fullB[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < R; r++) {
             mbar_init(&rawFull[r], 1);
-            mbar_init(&rawEmpty[r], TS_CONV_WARPS);
+            mbar_init(&rawEmpty[r], TS_CONV_WARPS / 2);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&accFull[b], 1);
@@ -665,14 +665,19 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 
     if (warp < TS_CONV_WARPS) {
         // ============ converters: raw ring -> fp16 A tiles in TMEM ===========
-        const int qd = warp & 3, q = warp >> 2;
+        // Two groups of 8 warps take alternate stages, so one group converts
+        // stage s+1 while the other's stores for stage s drain.  In a group,
+        // warp w covers TMEM lane quarter w & 3 and K chunks 2c, 2c+1
+        // (c = (w >> 2) & 1) of every k block of the stage.
+        const int grp = warp >> 3;
+        const int qd = warp & 3, c2 = ((warp >> 2) & 1) * 2;
         const int row = qd * 32 + lane;
-        const uint32_t code_off = (uint32_t)(q * UM_M + row) * CB;
-        const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + Cfg::A_COL0 + q * 8;
-        int g = 0, gs = 0;
+        const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + Cfg::A_COL0;
+        int gs = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             for (int kp = 0; kp < KP; kp++, gs++) {
+                if ((gs & 1) != grp) continue;
                 const int s = gs % S;
                 const int nk = min(TS_KS, a.KB - kp * TS_KS);
                 if (!mbar_wait(&empty[s], ((gs / S) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
@@ -681,28 +686,34 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                     break;
                 }
                 tc_fence_after();
-                // the stage's code tiles (one ring slot), converted as four
-                // independent chains, then stored to TMEM
-                const int r = g % R;
-                if (!mbar_wait(&rawFull[r], (g / R) & 1, abort_addr, UM_WAIT_CYCLES)) {
+                const int r = gs % R;  // one raw slot per stage
+                if (!mbar_wait(&rawFull[r], (gs / R) & 1, abort_addr, UM_WAIT_CYCLES)) {
                     fail();
                     ok = false;
                     break;
                 }
-                uint32_t o[TS_KS][8];
+                // per half of the stage: the two chunks of two k blocks,
+                // converted as independent chains, then stored to TMEM
 #pragma unroll
-                for (int h = 0; h < TS_KS; h++)
-                    if (h < nk) {
-                        const uint32_t rs = raw_u32 + r * Cfg::RAW_SLOT + h * Cfg::RAW_BYTES;
-                        cvt_chunk<BITS>(rs + code_off, chunk_scale(rs + Cfg::RAW_CODE, row, q),
-                                        o[h]);
+                for (int hh = 0; hh < TS_KS; hh += 2) {
+                    uint32_t o[4][8];
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int h = hh + (j >> 1), q = c2 + (j & 1);
+                        if (h < nk) {
+                            const uint32_t rs = raw_u32 + r * Cfg::RAW_SLOT + h * Cfg::RAW_BYTES;
+                            cvt_chunk<BITS>(rs + (uint32_t)(q * UM_M + row) * CB,
+                                            chunk_scale(rs + Cfg::RAW_CODE, row, q), o[j]);
+                        }
                     }
 #pragma unroll
-                for (int h = 0; h < TS_KS; h++)
-                    if (h < nk) tmem_st8(ta + s * (TS_KS * 32) + h * 32, o[h]);
+                    for (int j = 0; j < 4; j++) {
+                        const int h = hh + (j >> 1), q = c2 + (j & 1);
+                        if (h < nk) tmem_st8(ta + s * (TS_KS * 32) + h * 32 + q * 8, o[j]);
+                    }
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&rawEmpty[r]);  // codes consumed by the stores
-                g++;
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
