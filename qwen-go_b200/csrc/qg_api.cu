@@ -211,6 +211,10 @@ struct qgmoe {
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
     // router logits on the tensor cores (qg_router_tc.cu): split router rows
     // at create time, split activations per call (workspace)
+    // copy streams of the pipelined host-pointer forward (qgmoe_forward)
+    static constexpr int kMaxChunks = 8;
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t ev_in[kMaxChunks] = {}, ev_out[kMaxChunks] = {};
     bool rtc_ok = false;
     RouterTC rtc{};
     const RouterTC *rtc_for(int T) const {
@@ -703,6 +707,16 @@ int qgmoe_destroy(qgmoe_t *m) {
     for (auto &set : m->ev_sets)
         for (auto e : set)
             if (e) cudaEventDestroy(e);
+    if (m->h2d) {
+        cudaStreamSynchronize(m->h2d);
+        cudaStreamSynchronize(m->d2h);
+        for (int i = 0; i < qgmoe::kMaxChunks; i++) {
+            if (m->ev_in[i]) cudaEventDestroy(m->ev_in[i]);
+            if (m->ev_out[i]) cudaEventDestroy(m->ev_out[i]);
+        }
+        cudaStreamDestroy(m->h2d);
+        cudaStreamDestroy(m->d2h);
+    }
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
     return QGMOE_OK;
@@ -728,6 +742,31 @@ int qgmoe_forward_device(qgmoe_t *m, const float *x, int32_t T, float *out, int3
     return QGMOE_OK;
 }
 
+}  // extern "C"
+
+// Chunks of a blocking host-pointer forward: about 2048 tokens each (large
+// enough for full 256-token expert tiles at top-8 over 128 experts), at most
+// kMaxChunks; 1 (no pipelining) for smaller batches or when the routing is
+// also returned (it lives in the per-call workspace that each chunk reuses).
+static int pipeline_chunks(const qgmoe *m, int T, bool want_routing) {
+    if (want_routing || m->ep_world > 1 || T < 4096) return 1;
+    const int nc = T / 2048;
+    return nc < qgmoe::kMaxChunks ? nc : qgmoe::kMaxChunks;
+}
+
+static int ensure_copy_streams(qgmoe *m) {
+    if (m->h2d) return QGMOE_OK;
+    QG_CUDA(cudaStreamCreateWithFlags(&m->h2d, cudaStreamNonBlocking));
+    QG_CUDA(cudaStreamCreateWithFlags(&m->d2h, cudaStreamNonBlocking));
+    for (int i = 0; i < qgmoe::kMaxChunks; i++) {
+        QG_CUDA(cudaEventCreateWithFlags(&m->ev_in[i], cudaEventDisableTiming));
+        QG_CUDA(cudaEventCreateWithFlags(&m->ev_out[i], cudaEventDisableTiming));
+    }
+    return QGMOE_OK;
+}
+
+extern "C" {
+
 int qgmoe_forward(qgmoe_t *m, const float *x, int32_t T, float *out, int32_t *sel_idx,
                   float *sel_w) {
     if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
@@ -738,6 +777,33 @@ int qgmoe_forward(qgmoe_t *m, const float *x, int32_t T, float *out, int32_t *se
     int rc = ensure_capacity(m, T);
     if (rc) return rc;
     cudaStream_t s = m->stream;
+    const int nc = pipeline_chunks(m, T, sel_idx || sel_w);
+    if (nc > 1) {
+        // Large batches: token chunks, so the copy of chunk i+1 in and of
+        // chunk i-1 out run on their own streams under chunk i's forward
+        // (tokens are independent in moeMLP.forward, so chunking changes
+        // nothing in the result).
+        if ((rc = ensure_copy_streams(m))) return rc;
+        const int64_t H = m->H;
+        for (int i = 0; i < nc; i++) {
+            const int64_t t0 = (int64_t)T * i / nc, t1 = (int64_t)T * (i + 1) / nc;
+            QG_CUDA(cudaMemcpyAsync(m->x_dev + t0 * H, x + t0 * H, sizeof(float) * (t1 - t0) * H,
+                                    cudaMemcpyHostToDevice, m->h2d));
+            QG_CUDA(cudaEventRecord(m->ev_in[i], m->h2d));
+        }
+        for (int i = 0; i < nc; i++) {
+            const int64_t t0 = (int64_t)T * i / nc, t1 = (int64_t)T * (i + 1) / nc;
+            QG_CUDA(cudaStreamWaitEvent(s, m->ev_in[i], 0));
+            if ((rc = run_forward(m, m->x_dev + t0 * H, (int)(t1 - t0), m->out_dev + t0 * H, s)))
+                return rc;
+            QG_CUDA(cudaEventRecord(m->ev_out[i], s));
+            QG_CUDA(cudaStreamWaitEvent(m->d2h, m->ev_out[i], 0));
+            QG_CUDA(cudaMemcpyAsync(out + t0 * H, m->out_dev + t0 * H, sizeof(float) * (t1 - t0) * H,
+                                    cudaMemcpyDeviceToHost, m->d2h));
+        }
+        QG_CUDA(cudaStreamSynchronize(m->d2h));
+        return read_flag(m, s);
+    }
     QG_CUDA(cudaMemcpyAsync(m->x_dev, x, sizeof(float) * T * m->H, cudaMemcpyHostToDevice, s));
     if ((rc = run_forward(m, m->x_dev, T, m->out_dev, s))) return rc;
     QG_CUDA(cudaMemcpyAsync(out, m->out_dev, sizeof(float) * T * m->H, cudaMemcpyDeviceToHost, s));
