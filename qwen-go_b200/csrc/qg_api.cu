@@ -191,7 +191,7 @@ struct qgmoe {
     Allocs px_work;
     PxTables pxt{};
     __half *px_h16 = nullptr;       // SwiGLU outputs of the received rows
-    CUtensorMap tmap_px_recv[3]{}, tmap_px_h[3]{};
+    CUtensorMap tmap_px_recv[4]{}, tmap_px_h[4]{};
     // tensor-core path (qg_umma.cu): UMMA-tiled weight copies, fp16
     // activation buffers and their TMA descriptors
     bool tensor_ok = false;
@@ -221,8 +221,8 @@ struct qgmoe {
         return rtc_ok && T >= RTC_MIN_T && T <= rtc.cap ? &rtc : nullptr;
     }
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
-    // boxes of 256 / 64 / 16 token rows (prefill and decode tile sizes)
-    CUtensorMap tmap_x[3]{}, tmap_h[3]{}, tmap_hs[3]{};
+    // boxes of 256 / 64 / 16 / 128 token rows (the tile sizes)
+    CUtensorMap tmap_x[4]{}, tmap_h[4]{}, tmap_hs[4]{};
     // stage timing (qgmoe_set_timing): one event set per timed forward since
     // the last read, so a whole timed loop runs without host syncs.
     static constexpr int kMaxStages = 8;
@@ -304,8 +304,8 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_CUDA(cudaMemsetAsync(m->err_dev, 0, sizeof(int), m->stream));
     QG_CUDA(cudaStreamSynchronize(m->stream));
     if (m->tensor_ok) {
-        const int box[3] = {256, 64, 16};
-        for (int i = 0; i < 3; i++) {
+        const int box[4] = {256, 64, 16, 128};
+        for (int i = 0; i < 4; i++) {
             if ((rc = encode_act_map(&m->tmap_x[i], m->xp16, (int)slots, m->H, m->H, box[i])))
                 return rc;
             if ((rc = encode_act_map(&m->tmap_h[i], m->h16, (int)slots, m->I, m->hmax, box[i])))
@@ -400,17 +400,22 @@ static bool use_tensor(const qgmoe *m, int T) {
 }
 
 // Tokens per tensor-core work unit from the average tokens per expert in this
-// call: > 96 -> 256 (prefill), > 16 -> 64, else 16 (decode: small activation
-// stages, deeper rings).
+// call: > 96 -> 128 (prefill), > 16 -> 64, else 16 (decode).  All three use
+// the kernel that keeps the dequantised weights in TMEM; measured on B200 it
+// beats the 256-token shared-memory kernel at prefill sizes too (config 3,
+// 4096 tokens: 0.526 vs 0.574 ms per forward).
 static int tile_tokens_for(const qgmoe *m, int T) {
     const int pairs = T * m->k;
     const int groups = pairs < m->G ? pairs : m->G;
-    return pairs > 96 * groups ? 256 : (pairs > 16 * groups ? 64 : 16);
+    return pairs > 96 * groups ? 128 : (pairs > 16 * groups ? 64 : 16);
 }
+
+// Index of the activation tensor maps whose box height is nt token rows.
+static int tile_map_index(int nt) { return nt == 256 ? 0 : nt == 64 ? 1 : nt == 16 ? 2 : 3; }
 
 static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
     const int nt = tile_tokens_for(m, T);
-    const int ti = nt == 256 ? 0 : (nt == 64 ? 1 : 2);
+    const int ti = tile_map_index(nt);
     m->st.tile_tokens = nt;
     m->begin_timed();
     m->mark(0, nullptr, s);
@@ -1104,8 +1109,8 @@ int qgmoe_ep_px_setup(qgmoe_t *m, int32_t max_tokens, void *ipc_handle) {
                       sizeof(__half) * (size_t)a.recv_cap * m->I)) ||
         (rc = w.alloc(reinterpret_cast<void **>(&m->px_bases), sizeof(uint8_t *) * W)))
         return rc;
-    const int box[3] = {256, 64, 16};
-    for (int i = 0; i < 3; i++) {
+    const int box[4] = {256, 64, 16, 128};
+    for (int i = 0; i < 4; i++) {
         if ((rc = encode_act_map(&m->tmap_px_recv[i],
                                  reinterpret_cast<const __half *>(m->px_region + a.off_recv),
                                  (int)a.recv_cap, H, H, box[i])) ||
@@ -1156,7 +1161,7 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     int rc = 0;
     // every rank takes every step, T = 0 included (its counts are zero)
     const int nt = T > 0 ? tile_tokens_for(m, T) : 256;
-    const int ti = nt == 256 ? 0 : (nt == 64 ? 1 : 2);
+    const int ti = tile_map_index(nt);
     m->st.tile_tokens = nt;
     m->begin_timed();
     m->mark(0, nullptr, s);

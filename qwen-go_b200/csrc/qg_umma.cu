@@ -112,17 +112,20 @@ struct TsCfg {
     static constexpr int RAW_CODE = RawTile<BITS>::CODE;
     static constexpr int RAW_BYTES = RawTile<BITS>::BYTES;
     static constexpr int RAW_SLOT = TS_KS * RAW_BYTES;                // one stage of codes
-    static constexpr int R = NT == 64 ? (BITS == 8 ? 3 : 6) : (BITS == 8 ? 5 : 9);
+    static constexpr int S = NT == 128 ? 2 : TS_S;                   // stages (TMEM budget)
+    static constexpr int R = NT == 128 ? (BITS == 8 ? 2 : 4)
+                           : NT == 64  ? (BITS == 8 ? 3 : 6)
+                                       : (BITS == 8 ? 5 : 9);
     static constexpr int A_COL0 = 2 * NT;                             // after the accumulators
     static constexpr int TMEM_COLS = 512;
     static constexpr int XCH_BYTES = UM_EC * UM_XS * 4;
     static constexpr int UNIT_BYTES = UM_MAX_UNITS * 16;
-    static constexpr int BAR_BYTES = 8 * (3 * TS_S + 2 * R + 5) + 16;
+    static constexpr int BAR_BYTES = 8 * (3 * S + 2 * R + 5) + 16;
     static constexpr int SMEM =
-        TS_S * STAGE_B + R * RAW_SLOT + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
+        S * STAGE_B + R * RAW_SLOT + XCH_BYTES + UNIT_BYTES + BAR_BYTES + 1024;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(B_BYTES % 1024 == 0, "UMMA tiles must stay 1024-byte aligned");
-    static_assert(A_COL0 + TS_S * TS_KS * 32 <= TMEM_COLS, "TMEM budget");
+    static_assert(A_COL0 + S * TS_KS * 32 <= TMEM_COLS, "TMEM budget");
 };
 
 // int8 x4 stored biased (q + 128, repacked at create time) -> two fp16x2
@@ -588,7 +591,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     pdl_enter();
     using Cfg = TsCfg<BITS, NT>;
-    constexpr int S = TS_S, R = Cfg::R;
+    constexpr int S = Cfg::S, R = Cfg::R;
     constexpr int CB = RawTile<BITS>::CB;
     extern __shared__ uint8_t smem_raw[];
 
@@ -1083,12 +1086,14 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.out_peer_off = l.out_peer_off;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
-    const int nt = l.tile_tokens == 64 || l.tile_tokens == 16 ? l.tile_tokens : 256;
+    const int nt = l.tile_tokens == 128 || l.tile_tokens == 64 || l.tile_tokens == 16
+                       ? l.tile_tokens : 256;
 #define QG_UMMA_CASE(B, SW)                                                        \
     if (bits == B && swiglu == SW)                                                 \
-        return nt == 256 ? launch_umma_t<B, SW, 256>(tmap, a, l.grid, s)           \
-               : nt == 64 ? launch_umma_t<B, SW, 64>(tmap, a, l.grid, s)           \
-                          : launch_umma_t<B, SW, 16>(tmap, a, l.grid, s);
+        return nt == 256   ? launch_umma_t<B, SW, 256>(tmap, a, l.grid, s)         \
+               : nt == 128 ? launch_umma_t<B, SW, 128>(tmap, a, l.grid, s)         \
+               : nt == 64  ? launch_umma_t<B, SW, 64>(tmap, a, l.grid, s)          \
+                           : launch_umma_t<B, SW, 16>(tmap, a, l.grid, s);
     QG_UMMA_CASE(8, true)
     QG_UMMA_CASE(8, false)
     QG_UMMA_CASE(4, true)
