@@ -599,6 +599,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     const int n_act = *a.n_act;
     const int n_units = a.tile_prefix[n_act] * a.RT;
     if ((int)blockIdx.x >= n_units) return;
+    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const int KP = (a.KB + TS_KS - 1) / TS_KS;  // stages per unit (the last may be partial)
 
     uint8_t *base = reinterpret_cast<uint8_t *>(
@@ -642,15 +643,15 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
-    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const bool utab = n_mine <= UM_MAX_UNITS;
     if (utab)
         for (int i = tid; i < n_mine; i += TS_THREADS) {
             const Unit w = decode_unit<NT>(a, n_act, blockIdx.x + i * gridDim.x);
             st_shared_v4(utab_u32 + i * 16, w.e, w.rt, w.slot0, w.nval);
         }
-    auto unit_at = [&](int i, int u) -> Unit {
-        if (!utab) return decode_unit<NT>(a, n_act, u);
+    // this CTA's i-th unit (units b, b + grid, b + 2 grid, ...)
+    auto unit_at = [&](int i) -> Unit {
+        if (!utab) return decode_unit<NT>(a, n_act, blockIdx.x + i * gridDim.x);
         const uint4 v = ld_shared_v4(utab_u32 + i * 16);
         return Unit{(int)v.x, (int)v.y, (int)v.z, (int)v.w, ((int)v.w + 15) & ~15};
     };
@@ -678,7 +679,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         const uint32_t ta = tmem + ((uint32_t)(qd * 32) << 16) + Cfg::A_COL0;
         int gs = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        for (int i = 0; i < n_mine && ok; i++) {
             for (int kp = 0; kp < KP; kp++, gs++) {
                 if ((gs & 1) != grp) continue;
                 const int s = gs % S;
@@ -730,8 +731,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         const int et = tid - TS_EPI_WARP0 * 32;  // 0..127
         const int ej = et >> 3;
         const int er = (et & 7) * (SWIGLU ? 8 : 16);
-        int lt = 0;
-        for (int u = blockIdx.x; u < n_units; u += gridDim.x, lt++) {
+        for (int lt = 0; lt < n_mine; lt++) {
             const int buf = lt & 1;
             bool bad = !mbar_wait(&accFull[buf], (lt >> 1) & 1, abort_addr, UM_WAIT_CYCLES);
             bad = epi_bar_or(bad || ld_volatile_shared(abort_addr));
@@ -740,7 +740,7 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
                 break;
             }
             tc_fence_after();
-            const Unit w = unit_at(lt, u);
+            const Unit w = unit_at(lt);
             const uint32_t lane_addr = tmem + buf * NT + ((uint32_t)(ew * 32) << 16);
             epi_unit<SWIGLU>(a, w, lane_addr, xch_u32, L, ej, er);
             tc_fence_before();
@@ -752,8 +752,8 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         if (lane == 0) {
             int g = 0, last = -1;
             bool ok = true;
-            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
-                const Unit w = unit_at(i, u);
+            for (int i = 0; i < n_mine && ok; i++) {
+                const Unit w = unit_at(i);
                 const uint8_t *tile =
                     a.wq + (size_t)(w.e * a.RT + w.rt) * a.KB * Cfg::RAW_BYTES;
                 for (int kp = 0; kp < KP; kp++, g++) {
@@ -779,8 +779,8 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
             prefetch_tmap(&tmap_b);
             int gs = 0, last = -1;
             bool ok = true;
-            for (int u = blockIdx.x, i = 0; u < n_units && ok; u += gridDim.x, i++) {
-                const Unit w = unit_at(i, u);
+            for (int i = 0; i < n_mine && ok; i++) {
+                const Unit w = unit_at(i);
                 for (int kp = 0; kp < KP; kp++, gs++) {
                     const int s = gs % S;
                     const int nk = min(TS_KS, a.KB - kp * TS_KS);
@@ -803,10 +803,10 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     } else {
         // ============ MMA issuer =====================================================
         if (lane == 0) {
-            int gs = 0, lt = 0;
+            int gs = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, lt++) {
-                const Unit w = unit_at(lt, u);
+            for (int lt = 0; lt < n_mine && ok; lt++) {
+                const Unit w = unit_at(lt);
                 const uint32_t idesc = idesc_f16_f32(UM_M, w.N);
                 const int buf = lt & 1;
                 if (!mbar_wait(&accEmpty[buf], ((lt >> 1) & 1) ^ 1, abort_addr, UM_WAIT_CYCLES)) {
