@@ -8,7 +8,10 @@
 //   ticket  last-CTA counter of k_px_send (local)
 //   inbox   [W src][W dst][G] int32: every rank's count matrix (broadcast)
 //   recv    [W*cap][H] fp16: rows received for this rank's experts, grouped
-//           by local expert, sources in rank order within an expert
+//           by local expert; within an expert the sources follow each other
+//           starting at this rank (me, me+1, ..., me-1 mod W), so that the
+//           owners' down GEMMs, which walk their experts' rows in this
+//           order, start by returning rows to different sources
 //   back    [cap][H] fp16: expert outputs of this rank's own rows, returned
 //           by their owners in this rank's send order
 // One forward (rank me, epoch e):
@@ -16,7 +19,10 @@
 //                expert g) into every rank's inbox, then cnt[me] = e there;
 //   k_px_send    wait for every cnt flag; from the W count matrices compute
 //                where each of my rows lands in its owner's grouped buffer
-//                and store it there (fp16, converted from x on the fly);
+//                and store it there (fp16, converted from x on the fly); the
+//                warps are split evenly over the destinations, rotated by
+//                rank, so every destination receives from every source at
+//                once instead of all sources sending to one rank at a time;
 //                the last CTA sets data[me] = e on every rank;
 //   k_px_tables  wait for every data flag; build this rank's active-expert
 //                list, tile prefix and, per received row, the (source rank,
@@ -127,25 +133,30 @@ k_px_send(PxArgs a, const float *__restrict__ x, const int32_t *__restrict__ exp
     for (int i = tid; i < WG; i += blockDim.x) off[i] = expert_off[i];
     __syncthreads();
     // position at d of my rows for d's local expert g: the rows of d's local
-    // experts before g (all sources), then the rows of lower sources for g
+    // experts before g (all sources), then the rows of the sources that come
+    // before me in d's order (d, d+1, ..., d-1 mod W) for g
     for (int key = tid; key < WG; key += blockDim.x) {
         const int d = key / G, g = key - d * G;
         int p = 0;
         for (int g2 = 0; g2 < g; g2++)
             for (int s = 0; s < W; s++) p += cnt[(s * W + d) * G + g2];
-        for (int s = 0; s < a.me; s++) p += cnt[(s * W + d) * G + g];
+        for (int s = d; s != a.me; s = s + 1 == W ? 0 : s + 1) p += cnt[(s * W + d) * G + g];
         pos[key] = p;
     }
     __syncthreads();
-    const int n = a.T * a.k;
+    // warp slot j (global warp index mod W) sends to destination (me + j) mod W
     const int nw = gridDim.x * (blockDim.x >> 5);
-    for (int p = blockIdx.x * (blockDim.x >> 5) + warp; p < n; p += nw) {
-        int lo = 0, hi = WG - 1;  // last key with off[key] <= p
+    const int wg = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int j = wg % W;
+    const int d = (a.me + j) % W;
+    const int wi = wg / W, nwd = (nw - j + W - 1) / W;  // my index among d's warps
+    const int p_end = d + 1 < W ? off[(d + 1) * G] : a.T * a.k;
+    for (int p = off[d * G] + wi; p < p_end; p += nwd) {
+        int lo = d * G, hi = d * G + G - 1;  // last key of d with off[key] <= p
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
             if (off[mid] <= p) lo = mid; else hi = mid - 1;
         }
-        const int d = lo / G;
         const int64_t row = pos[lo] + (p - off[lo]);
         if (row < 0 || row >= (int64_t)a.recv_cap) {
             if (lane == 0) atomicOr(err, QG_FLAG_BAD_SLOT);
@@ -181,8 +192,8 @@ k_px_tables(PxArgs a, int tile_tokens, PxTables t, int *err) {
     const int W = a.W, G = a.G, WG = W * G;
     int32_t *cnt = px_sm;                  // [W][W][G]
     int32_t *gbase = cnt + W * WG;         // [G+1] first grouped row of local expert g
-    int32_t *seg = gbase + G + 1;          // [G][W] first grouped row of (g, source s)
-    int32_t *dst0 = seg + WG;              // [G][W] send position at s of (g, s) row 0
+    int32_t *seg = gbase + G + 1;          // [G][W] first grouped row of (g, j-th source)
+    int32_t *dst0 = seg + WG;              // [G][W] send position of that source's row 0
     __shared__ int s_ok;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
@@ -220,10 +231,11 @@ k_px_tables(PxArgs a, int tile_tokens, PxTables t, int *err) {
         if (lane == 0) gbase[G] = carry;
     }
     __syncthreads();
+    // within expert g the sources follow each other as me, me+1, ..., me-1 (mod W)
     for (int i = tid; i < WG; i += blockDim.x) {
-        const int g = i / W, s = i - g * W;
+        const int g = i / W, j = i - g * W, s = (me + j) % W;
         int r = gbase[g];
-        for (int s2 = 0; s2 < s; s2++) r += cnt[(s2 * W + me) * G + g];
+        for (int s2 = me; s2 != s; s2 = s2 + 1 == W ? 0 : s2 + 1) r += cnt[(s2 * W + me) * G + g];
         seg[i] = r;
         // position of s's first row for (me, g) in s's send order: s's rows
         // for ranks before me, then for my experts before g
@@ -274,9 +286,10 @@ k_px_tables(PxArgs a, int tile_tokens, PxTables t, int *err) {
             const int mid = (lo + hi + 1) >> 1;
             if (gbase[mid] <= r) lo = mid; else hi = mid - 1;
         }
-        int s = W - 1;
-        while (s > 0 && seg[lo * W + s] > r) s--;
-        t.out_map[r] = (s << 24) | (dst0[lo * W + s] + (r - seg[lo * W + s]));
+        int j = W - 1;
+        while (j > 0 && seg[lo * W + j] > r) j--;
+        const int s = (me + j) % W;
+        t.out_map[r] = (s << 24) | (dst0[lo * W + j] + (r - seg[lo * W + j]));
     }
 }
 
@@ -311,7 +324,7 @@ int launch_px_send(const PxArgs &a, const float *x, const int32_t *expert_off,
     int blocks = (rows + 7) / 8;
     const int cap = num_sms(dev) * 4;
     if (blocks > cap) blocks = cap;
-    if (blocks < 1) blocks = 1;
+    if (blocks < (a.W + 7) / 8) blocks = (a.W + 7) / 8;  // at least one warp per destination
     k_px_send<<<blocks, 256, px_smem(a), s>>>(a, x, expert_off, slot_token, err);
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
