@@ -33,7 +33,8 @@ using sm100::smem_u32;
 
 constexpr int LG_KC = 32;    // K chunk staged in shared memory
 constexpr int LG_MAX_SPLIT = 16; // K slices per tile = cluster size (16: non-portable opt-in)
-constexpr int LG_SMALL_T = 8;    // up to this many tokens: 8 x 32 tiles, else 64 x 128
+constexpr int LG_SMALL_T = 8;    // up to this many tokens: 8 x 32 tiles,
+constexpr int LG_MID_T = 64;     // up to this many: 32 x 32, else 64 x 128
 constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA
 constexpr int RT_THREADS = 1024;  // top-k and scatter CTAs: one warp per token
 constexpr int RT_WARPS = RT_THREADS / 32;
@@ -53,8 +54,12 @@ __device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
     }
 }
 
+// logits tile tier: 0 = 64 x 128, 1 = 8 x 32, 2 = 32 x 32
+static int lg_tier(int T) { return T <= LG_SMALL_T ? 1 : T <= LG_MID_T ? 2 : 0; }
+
 int route_splits(int T, int H, int Ep, int sms) {
-    const int TT = T <= LG_SMALL_T ? 8 : 64, RR = T <= LG_SMALL_T ? 32 : 128;
+    static const int tts[3] = {64, 8, 32}, rrs[3] = {128, 32, 32};
+    const int TT = tts[lg_tier(T)], RR = rrs[lg_tier(T)];
     const int tiles = ((T + TT - 1) / TT) * ((Ep + RR - 1) / RR);
     int s = 1;  // a power of two: the cluster size
     while (s < LG_MAX_SPLIT && 2 * s * tiles <= sms && 2 * s * LG_KC <= H) s *= 2;
@@ -63,8 +68,8 @@ int route_splits(int T, int H, int Ep, int sms) {
 
 // ---- 1. logits ------------------------------------------------------------------
 // CTA tile: TT tokens x RR router rows x one K slice (TT x RR = 64 x 128 for
-// prefill batches, 8 x 32 for decode batches, so that a handful of tokens
-// still spreads over many CTAs).  Warp w owns tokens w*TT/8 ..., lane l owns
+// prefill batches, 8 x 32 or 32 x 32 for decode batches, so that a handful
+// of tokens still spreads over many CTAs).  Warp w owns tokens w*TT/8 ..., lane l owns
 // rows l*RR/32 ...: per K step the warp's x values and the lane's router
 // values come from shared memory and feed (TT/8) x (RR/32) FMAs.  The next K
 // chunk is fetched into registers while the current one is consumed.  With
@@ -501,25 +506,28 @@ k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
 static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
                          const float *shared_gate, float *logits, int dev, cudaStream_t s) {
     const int ks = route_splits(T, H, Ep, num_sms(dev));
-    const bool small = T <= LG_SMALL_T;
+    const int tier = lg_tier(T);
     using LgKern = void (*)(const float *, int, int, int, int, const float *, const float *, float *);
-    static const LgKern kerns[2][5] = {
+    static const LgKern kerns[3][5] = {
         {k_logits<64, 128, 1>, k_logits<64, 128, 2>, k_logits<64, 128, 4>, k_logits<64, 128, 8>,
          k_logits<64, 128, 16>},
         {k_logits<8, 32, 1>, k_logits<8, 32, 2>, k_logits<8, 32, 4>, k_logits<8, 32, 8>,
-         k_logits<8, 32, 16>}};
+         k_logits<8, 32, 16>},
+        {k_logits<32, 32, 1>, k_logits<32, 32, 2>, k_logits<32, 32, 4>, k_logits<32, 32, 8>,
+         k_logits<32, 32, 16>}};
+    static const int tts[3] = {64, 8, 32}, rrs[3] = {128, 32, 32};
+    static const int smems[3] = {LgTile<64, 128>::SMEM, LgTile<8, 32>::SMEM, LgTile<32, 32>::SMEM};
     const int ki = ks == 1 ? 0 : ks == 2 ? 1 : ks == 4 ? 2 : ks == 8 ? 3 : 4;
-    const LgKern kern = kerns[small][ki];
+    const LgKern kern = kerns[tier][ki];
     static bool wide[64] = {false};  // 16-CTA clusters need the non-portable opt-in
     if (dev < 64 && !wide[dev]) {
-        QG_CUDA(cudaFuncSetAttribute(kerns[0][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        QG_CUDA(cudaFuncSetAttribute(kerns[1][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        for (int i = 0; i < 3; i++)
+            QG_CUDA(cudaFuncSetAttribute(kerns[i][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
         wide[dev] = true;
     }
-    const int TT = small ? 8 : 64, RR = small ? 32 : 128;
+    const int TT = tts[tier], RR = rrs[tier];
     QG_CUDA(launch_pdl(kern, dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks), dim3(256),
-                       small ? LgTile<8, 32>::SMEM : LgTile<64, 128>::SMEM, s, ks, x, T, H, E,
-                       Ep, router, shared_gate, logits));
+                       smems[tier], s, ks, x, T, H, E, Ep, router, shared_gate, logits));
     return QGMOE_OK;
 }
 
