@@ -58,6 +58,21 @@ def load_peaks():
         return PEAKS_FALLBACK, "fallback"
 
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch
+# of the dominant kernel, from the ncu --set full captures summarised in
+# profiles/ (same workload, same kernel build): (config, tokens, kernel) ->
+# (bytes, summary file).  Other workloads report null.
+NCU_TRAFFIC = {
+    ("c3", 4096, "gate_up"): (562.258944e6 + 52.420352e6, "profiles/full_c3_prefill_t4096.md"),
+    ("c2", 64, "gate_up"): (219.808000e6 + 5.256704e6, "profiles/full_c2_decode_t64.md"),
+}
+
+
+def ncu_traffic(config, T, kernel):
+    hit = NCU_TRAFFIC.get((config, T, kernel))
+    return (hit[0], hit[1]) if hit else (None, None)
+
+
 def weight_bytes(cfg):
     """Bytes of one expert's gate_up + down weights (codes + fp16 scales)."""
     H, I, bits = cfg["H"], cfg["I"], cfg["bits"]
@@ -528,6 +543,7 @@ def run_ours(args, cfg):
     dom = max(stages, key=stages.get)
     dom_ms = stages[dom]
     prefill = cfg["T"] >= 512
+    traffic, traffic_src = ncu_traffic(args.config, T, dom)
     if prefill:
         Iw = 2 * cfg["I"] if dom == "gate_up" else cfg["I"]
         flops = 2.0 * T * k * Iw * H if dom in ("gate_up", "down") else 2.0 * T * cfg["E"] * H
@@ -536,7 +552,7 @@ def run_ours(args, cfg):
         roof = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{peak_src} bf16 dense (MEASURED_PEAKS.json bf16_tflops)",
-                "algorithmic_per_launch": f"{flops / 1e9:.1f} GFLOP", "traffic": None}
+                "algorithmic_per_launch": f"{flops / 1e9:.1f} GFLOP", "traffic": traffic}
     else:
         frac_w = (2 / 3) if dom == "gate_up" else (1 / 3)
         bytes_ = distinct * weight_bytes(cfg) * frac_w + T * H * 4 * 2
@@ -544,7 +560,10 @@ def run_ours(args, cfg):
         peak = peaks["hbm_gbs"]
         roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_source": f"{peak_src} HBM copy",
-                "algorithmic_per_launch": f"{bytes_ / 1e6:.2f} MB", "traffic": None}
+                "algorithmic_per_launch": f"{bytes_ / 1e6:.2f} MB", "traffic": traffic}
+    if traffic is not None:
+        roof["traffic_unit"] = "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)"
+        roof["traffic_source"] = traffic_src
 
     # ---- end to end through the public host API (pinned buffers) ----
     xh = x.cpu().pin_memory()

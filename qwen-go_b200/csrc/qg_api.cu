@@ -425,7 +425,9 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     m->mark(1, "route", s);
     const int pairs = T * m->k;
     const int tiles = (pairs + nt - 1) / nt + (pairs < m->E ? pairs : m->E);
-    int launches = 4;  // logits, top-k, scatter, gather
+    // logits (+ the x split on the tensor-core router), top-k, scatter (fused
+    // into top-k for <= 32 tokens), gather
+    int launches = (m->rtc_for(T) ? 2 : 1) + 1 + (T > 32 ? 1 : 0) + 1;
     UmmaLaunch l{};
     l.act_group = m->st.act_group;
     l.act_begin = m->st.act_begin;

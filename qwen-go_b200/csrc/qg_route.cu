@@ -221,7 +221,13 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *
 // ---- 2. softmax + top-k + histograms --------------------------------------------
 // A warp holds one token's probabilities in registers: lane l owns experts
 // l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
-template <int NJ>
+__device__ __forceinline__ void scatter_chunk(int c, int T, int E, int k, int has_shared,
+                                              const RouteState &st, int *err, int *sm,
+                                              int *partial);
+
+// FUSED (T <= TK_TOK, one CTA): the scatter of the single token chunk
+// follows in the same CTA once the expert offsets are known.
+template <int NJ, bool FUSED>
 __global__ void __launch_bounds__(RT_THREADS)
 k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
        int has_shared, RouteState st, int *err) {
@@ -416,18 +422,22 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
             *st.done_ctr = 0;
         }
     }
+    if constexpr (FUSED) {
+        __shared__ int partial[RT_THREADS];
+        __syncthreads();  // expert offsets and top-k pairs written by this CTA
+        scatter_chunk(0, T, E, k, has_shared, st, err, hist_s, partial);
+    }
 }
 
-// ---- 3. scatter (+ fp16 gather) ---------------------------------------------------
-__global__ void __launch_bounds__(RT_THREADS)
-k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
-    pdl_enter();
-    extern __shared__ int sm[];
+// ---- 3. scatter ---------------------------------------------------------------------
+// Slots of token chunk c (TK_TOK tokens, one CTA of RT_THREADS threads); sm
+// holds (RT_WARPS + 1) * E ints.
+__device__ __forceinline__ void scatter_chunk(int c, int T, int E, int k, int has_shared,
+                                              const RouteState &st, int *err, int *sm,
+                                              int *partial) {
     int *cur = sm;            // [E] next slot per expert for this CTA
     int *wcnt = sm + E;       // [RT_WARPS][E]
-    __shared__ int partial[RT_THREADS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int c = blockIdx.x;
     // Slots of this CTA's pairs start after the earlier CTAs' pairs of the
     // same expert: sum histogram rows 0..c-1, split over nparts threads per
     // expert with independent accumulators so the loads overlap.
@@ -502,6 +512,14 @@ k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
             st.slot_token[T * k + t] = t;
 }
 
+__global__ void __launch_bounds__(RT_THREADS)
+k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
+    pdl_enter();
+    extern __shared__ int sm[];
+    __shared__ int partial[RT_THREADS];
+    scatter_chunk(blockIdx.x, T, E, k, has_shared, st, err, sm, partial);
+}
+
 // CUDA-core logits: the split-K tiled f32 GEMM above.
 static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
                          const float *shared_gate, float *logits, int dev, cudaStream_t s) {
@@ -548,25 +566,34 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
-    static bool attr[64] = {false};
+    static bool attr[64] = {false}, attr_f[64] = {false};
     if (dev < 64 && !attr[dev]) {
         QG_CUDA(cudaFuncSetAttribute(k_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
         attr[dev] = true;
     }
     const int nj = (E + 31) / 32;
-    void (*topk)(const float *, int, int, int, int, int, int, RouteState, int *) =
-        nj <= 1    ? k_topk<1>
-        : nj <= 2  ? k_topk<2>
-        : nj <= 4  ? k_topk<4>
-        : nj <= 8  ? k_topk<8>
-        : nj <= 16 ? k_topk<16>
-                   : k_topk<32>;
-    QG_CUDA(launch_pdl(topk, dim3(nc), dim3(RT_THREADS), sm2, s, 1, (const float *)st.logits, T, E,
-                       Ep, k, mode, has_shared, st, err));
+    using TkKern = void (*)(const float *, int, int, int, int, int, int, RouteState, int *);
+    static const TkKern tk[2][6] = {
+        {k_topk<1, false>, k_topk<2, false>, k_topk<4, false>, k_topk<8, false>,
+         k_topk<16, false>, k_topk<32, false>},
+        {k_topk<1, true>, k_topk<2, true>, k_topk<4, true>, k_topk<8, true>, k_topk<16, true>,
+         k_topk<32, true>}};
+    const int ji = nj <= 1 ? 0 : nj <= 2 ? 1 : nj <= 4 ? 2 : nj <= 8 ? 3 : nj <= 16 ? 4 : 5;
+    const bool fused = nc == 1;  // one token chunk: top-k and scatter in one CTA
+    if (fused && dev < 64 && !attr_f[dev]) {
+        for (int i = 0; i < 6; i++)
+            QG_CUDA(cudaFuncSetAttribute(tk[1][i], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         160 * 1024));
+        attr_f[dev] = true;
+    }
+    QG_CUDA(launch_pdl(tk[fused][ji], dim3(nc), dim3(RT_THREADS), fused ? sm3 : sm2, s, 1,
+                       (const float *)st.logits, T, E, Ep, k, mode, has_shared, st, err));
     QG_CUDA(cudaGetLastError());
-    QG_CUDA(launch_pdl(k_scatter, dim3(nc), dim3(RT_THREADS), sm3, s, 1, T, E, k, has_shared, st,
-                       err));
-    QG_CUDA(cudaGetLastError());
+    if (!fused) {
+        QG_CUDA(launch_pdl(k_scatter, dim3(nc), dim3(RT_THREADS), sm3, s, 1, T, E, k, has_shared,
+                           st, err));
+        QG_CUDA(cudaGetLastError());
+    }
     if (xp) {
         const int nslots = T * k + (has_shared ? T : 0);
         // after the tensor-core logits the fp16 rows exist already (xh = fp16(x))
