@@ -22,7 +22,8 @@ namespace qg {
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
-constexpr int GEMV_ROWS = 32;  // output rows per work item (4 per warp)
+constexpr int GEMV_ROWS = 8;   // output rows per work item (1 per warp)
+constexpr int GEMV_UNR = 4;    // 16-byte chunks per lane loaded ahead
 constexpr int GEMV_NT = 4;     // tokens staged per pass
 
 // Elements carried by one 16-byte weight chunk.
@@ -82,35 +83,57 @@ __device__ __forceinline__ int stage_pos(int c, int j) {
     return (((c >> 5) * (V / 4) + (j >> 2)) * 32 + (c & 31)) * 4 + (j & 3);
 }
 
-// Dot products of one weight row against the staged rows: acc[t] += row . x_t
-template <int BITS>
-__device__ __forceinline__ void row_dot(const uint8_t *__restrict__ row_bytes,
-                                        const __half *__restrict__ row_scales, int nchunks,
-                                        const float *xs, int kpad, int nt, int lane,
-                                        float (&acc)[GEMV_NT]) {
+// Dot products of NR weight rows (gate and up for GATEUP) against the staged
+// rows: acc[r][t] += row_r . x_t.  Each lane takes chunks lane, lane+32, ...;
+// the loads of up to GEMV_UNR chunks of every row are issued before any is
+// used, so a row pair of a few KB costs one memory round trip, not one per
+// chunk and row.
+template <int BITS, int NR>
+__device__ __forceinline__ void rows_dot(const uint8_t *const (&row_bytes)[NR],
+                                         const __half *const (&row_scales)[NR], int nchunks,
+                                         const float *xs, int kpad, int nt, int lane,
+                                         float (&acc)[NR][GEMV_NT]) {
     constexpr int V = Chunk<BITS>::V;
-    const uint4 *rp = reinterpret_cast<const uint4 *>(row_bytes);
-    for (int c = lane; c < nchunks; c += 32) {
-        const uint4 raw = __ldcs(rp + c);  // streamed once: evict-first
-        float v[V];
-        decode_chunk<BITS>(raw, v);
-        float sc = 1.f;
-        if constexpr (BITS != 32) sc = __half2float(row_scales[(c * V) / QG_GROUP]);
+    for (int c0 = lane; c0 < nchunks; c0 += 32 * GEMV_UNR) {
+        uint4 raw[NR][GEMV_UNR];
+        float sc[NR][GEMV_UNR];
 #pragma unroll
-        for (int t = 0; t < GEMV_NT; t++) {
-            if (t < nt) {
-                const float *xt = xs + t * kpad;
-                float part = 0.f;
+        for (int u = 0; u < GEMV_UNR; u++) {
+            const int c = c0 + 32 * u;
 #pragma unroll
-                for (int j4 = 0; j4 < V / 4; j4++) {
-                    const float4 xv =
-                        *reinterpret_cast<const float4 *>(xt + stage_pos<V>(c, j4 * 4));
-                    part = fmaf(v[j4 * 4 + 0], xv.x, part);
-                    part = fmaf(v[j4 * 4 + 1], xv.y, part);
-                    part = fmaf(v[j4 * 4 + 2], xv.z, part);
-                    part = fmaf(v[j4 * 4 + 3], xv.w, part);
+            for (int r = 0; r < NR; r++) {
+                sc[r][u] = 1.f;
+                if (c < nchunks) {
+                    raw[r][u] = __ldcs(reinterpret_cast<const uint4 *>(row_bytes[r]) + c);  // evict-first
+                    if constexpr (BITS != 32) sc[r][u] = __half2float(row_scales[r][(c * V) / QG_GROUP]);
                 }
-                acc[t] = fmaf(part, sc, acc[t]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < GEMV_UNR; u++) {
+            const int c = c0 + 32 * u;
+            if (c >= nchunks) break;
+#pragma unroll
+            for (int r = 0; r < NR; r++) {
+                float v[V];
+                decode_chunk<BITS>(raw[r][u], v);
+#pragma unroll
+                for (int t = 0; t < GEMV_NT; t++) {
+                    if (t < nt) {
+                        const float *xt = xs + t * kpad;
+                        float part = 0.f;
+#pragma unroll
+                        for (int j4 = 0; j4 < V / 4; j4++) {
+                            const float4 xv =
+                                *reinterpret_cast<const float4 *>(xt + stage_pos<V>(c, j4 * 4));
+                            part = fmaf(v[j4 * 4 + 0], xv.x, part);
+                            part = fmaf(v[j4 * 4 + 1], xv.y, part);
+                            part = fmaf(v[j4 * 4 + 2], xv.z, part);
+                            part = fmaf(v[j4 * 4 + 3], xv.w, part);
+                        }
+                        acc[r][t] = fmaf(part, sc[r][u], acc[r][t]);
+                    }
+                }
             }
         }
     }
@@ -186,32 +209,32 @@ k_expert_gemv(ExpertArgs a) {
             for (int rr = warp; rr < GEMV_ROWS; rr += GEMV_WARPS) {
                 const int r = r0 + rr;
                 if (r >= out_rows) break;
-                float acc[GEMV_NT];
-#pragma unroll
-                for (int t = 0; t < GEMV_NT; t++) acc[t] = 0.f;
-                row_dot<BITS>(wbase + (size_t)r * row_bytes,
-                              sbase ? sbase + (size_t)r * (K / QG_GROUP) : nullptr, nchunks, xs,
-                              kpad, nt, lane, acc);
                 if constexpr (GATEUP) {
-                    float accu[GEMV_NT];
-#pragma unroll
-                    for (int t = 0; t < GEMV_NT; t++) accu[t] = 0.f;
                     const int ru = r + out_rows;  // up rows follow the gate rows
-                    row_dot<BITS>(wbase + (size_t)ru * row_bytes,
-                                  sbase ? sbase + (size_t)ru * (K / QG_GROUP) : nullptr, nchunks,
-                                  xs, kpad, nt, lane, accu);
+                    const uint8_t *const rows[2] = {wbase + (size_t)r * row_bytes,
+                                                    wbase + (size_t)ru * row_bytes};
+                    const __half *const scs[2] = {
+                        sbase ? sbase + (size_t)r * (K / QG_GROUP) : nullptr,
+                        sbase ? sbase + (size_t)ru * (K / QG_GROUP) : nullptr};
+                    float acc[2][GEMV_NT] = {};
+                    rows_dot<BITS, 2>(rows, scs, nchunks, xs, kpad, nt, lane, acc);
 #pragma unroll
                     for (int t = 0; t < GEMV_NT; t++) {
-                        const float gsum = warp_allsum(acc[t]);
-                        const float usum = warp_allsum(accu[t]);
+                        const float gsum = warp_allsum(acc[0][t]);
+                        const float usum = warp_allsum(acc[1][t]);
                         if (lane == t && t < nt)
                             a.out[(size_t)(slot0 + tc + t) * a.out_stride + r] =
                                 __fmul_rn(silu_ref(gsum), usum);
                     }
                 } else {
+                    const uint8_t *const rows[1] = {wbase + (size_t)r * row_bytes};
+                    const __half *const scs[1] = {
+                        sbase ? sbase + (size_t)r * (K / QG_GROUP) : nullptr};
+                    float acc[1][GEMV_NT] = {};
+                    rows_dot<BITS, 1>(rows, scs, nchunks, xs, kpad, nt, lane, acc);
 #pragma unroll
                     for (int t = 0; t < GEMV_NT; t++) {
-                        const float s = warp_allsum(acc[t]);
+                        const float s = warp_allsum(acc[0][t]);
                         if (lane == t && t < nt)
                             a.out[(size_t)(slot0 + tc + t) * a.out_stride + r] = s;
                     }
