@@ -589,17 +589,13 @@ k_umma(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
 template <int BITS, bool SWIGLU, int NT>
 __global__ void __launch_bounds__(TS_THREADS, 1)
 k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
-    pdl_enter();
+    pdl_launch_dependents();
     using Cfg = TsCfg<BITS, NT>;
     constexpr int S = Cfg::S, R = Cfg::R;
     constexpr int CB = RawTile<BITS>::CB;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_act = *a.n_act;
-    const int n_units = a.tile_prefix[n_act] * a.RT;
-    if ((int)blockIdx.x >= n_units) return;
-    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const int KP = (a.KB + TS_KS - 1) / TS_KS;  // stages per unit (the last may be partial)
 
     uint8_t *base = reinterpret_cast<uint8_t *>(
@@ -643,6 +639,19 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
         tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
+    // everything above reads no global memory; the routing tables below come
+    // from the previous kernels
+    pdl_wait();
+    const int n_act = *a.n_act;
+    const int n_units = a.tile_prefix[n_act] * a.RT;
+    if ((int)blockIdx.x >= n_units) {  // no work: give the TMEM back and leave
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (warp == TS_MMA_WARP) tmem_dealloc(*tmem_slot, Cfg::TMEM_COLS);
+        return;
+    }
+    const int n_mine = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const bool utab = n_mine <= UM_MAX_UNITS;
     if (utab)
         for (int i = tid; i < n_mine; i += TS_THREADS) {
