@@ -1,9 +1,11 @@
 // Router + dispatch (kernels K1 and K2).
 //
-// Launches: k_logits, k_topk, k_scatter (+ k_gather_f16 for the tensor path).
+// Launches: k_logits, k_topk, k_scatter (fused into k_topk for <= 32 tokens)
+// (+ k_gather_f16 for the tensor path).
 // 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...), model/moe.go:42)
 //    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 64 tokens x 128
-//    router rows x one K slice.  The shared-expert gate vector rides along as
+//    router rows (32 x 32 for 9-64 tokens, 8 x 32 for up to 8) x one K
+//    slice.  The shared-expert gate vector rides along as
 //    router row E (model/moe.go:87-93).  Split-K keeps decode-sized batches
 //    (T = 1..64) spread over the SMs while the 1 MiB router matrix is read
 //    about once; the K slices of one tile form a thread-block cluster and add
@@ -19,7 +21,8 @@
 // 3. k_scatter: each CTA ranks its own (token, rank) pairs per expert in pair
 //    order (warp match + per-warp counts) and adds the histograms of the CTAs
 //    before it, so slots are expert-sorted and deterministic without a serial
-//    pass.  For the tensor-core path k_gather_f16 then writes each slot's fp16
+//    pass.  With one token chunk (<= 32 tokens) the single top-k CTA does this
+//    itself once the offsets are known, one launch fewer.  For the tensor-core path k_gather_f16 then writes each slot's fp16
 //    activation row.
 #include "qg_common.cuh"
 #include "qg_sm100.cuh"
