@@ -242,10 +242,28 @@ int qgql_create(int32_t bits, int32_t out_features, int32_t in_features, const v
 int qgql_destroy(qgql_t *h);
 
 /* proj(x, T, nil, q, out) / quantLinear.forward: y[T, out] = x[T, in] W^T
- * with the dequantisation fused into the weight load.  HOST pointers. */
+ * with the dequantisation fused into the weight load.  HOST pointers;
+ * blocking; reports device error flags like qgql_sync.
+ * Paths (qgql_set_path): AUTO and CUDA_CORE run the CUDA-core GEMV (f32
+ * arithmetic, the reference's dequantise-then-dot within f32 rounding).
+ * TENSOR (opt-in; int8 / int4 weights with out % 128 == 0 and in % 64 == 0,
+ * 16-byte aligned x and y, else the GEMV) runs on the tensor cores: x
+ * rounded to fp16, fp16 dequantised weights, f32 accumulation and f32 y, so
+ * each output is within about 2^-10 * sum_k |w_k x_k| of the f32 result,
+ * which for unit-scale activations over rows of 1024+ can exceed the 1e-3
+ * element-wise bar of the GEMV path.  A finite activation beyond fp16 range
+ * on the tensor path raises QGMOE_ERR_DEVICE_FLAG instead of producing
+ * infinities.  The tensor path keeps per-handle workspace: calls of one
+ * handle must not overlap on the GPU (order them on one stream). */
 int qgql_forward(qgql_t *h, const float *x, int32_t T, float *y);
 /* Same on DEVICE pointers, enqueued on `stream` (NULL = handle stream). */
 int qgql_forward_device(qgql_t *h, const float *x, int32_t T, float *y, void *stream);
+/* QGMOE_PATH_AUTO / _CUDA_CORE / _TENSOR (UNSUPPORTED when the shape or
+ * bits exclude the tensor path). */
+int qgql_set_path(qgql_t *h, int32_t mode);
+/* Waits for `stream` (NULL = handle stream) and returns
+ * QGMOE_ERR_DEVICE_FLAG (clearing the flag) if a kernel raised one. */
+int qgql_sync(qgql_t *h, void *stream);
 /* quantLinear.dequantize (model/moe.go:134-157) into w_dev [out, in] f32. */
 int qgql_dequantize_device(qgql_t *h, float *w_dev, void *stream);
 

@@ -1238,7 +1238,61 @@ struct qgql {
     float *x_dev = nullptr, *y_dev = nullptr;
     int cap_T = 0;
     Allocs work;
+    // tensor-core path (int8/int4, out % 128 == 0, in % 64 == 0): the weights
+    // repacked into UMMA tiles once, fp16 rows of x and the one-group tables
+    // per call, activation maps with 128 / 64 / 16-row boxes
+    bool tensor_ok = false;
+    int path_mode = QGMOE_PATH_AUTO;
+    uint8_t *pq = nullptr;
+    __half *xp16 = nullptr;
+    int32_t *tab = nullptr;
+    int cap_tc = 0;
+    Allocs tc;
+    CUtensorMap tmap[3]{};
 };
+
+static int ql_tile_tokens(int T) { return T > 96 ? 128 : (T > 16 ? 64 : 16); }
+static int ql_map_index(int nt) { return nt == 128 ? 0 : nt == 64 ? 1 : 2; }
+
+static int ql_ensure_tc(qgql *h, int T) {
+    if (T <= h->cap_tc) return QGMOE_OK;
+    cudaDeviceSynchronize();  // earlier calls may still read the old buffers on any stream
+    h->tc.free_all();
+    h->cap_tc = 0;
+    int cap = 256;
+    while (cap < T) cap *= 2;
+    int rc = h->tc.alloc(reinterpret_cast<void **>(&h->xp16), sizeof(__half) * (size_t)cap * h->I);
+    if (!rc) rc = h->tc.alloc(reinterpret_cast<void **>(&h->tab), sizeof(int32_t) * 8);
+    const int box[3] = {128, 64, 16};
+    for (int i = 0; i < 3 && !rc; i++) rc = encode_act_map(&h->tmap[i], h->xp16, cap, h->I, h->I, box[i]);
+    if (rc) return rc;
+    h->cap_tc = cap;
+    return QGMOE_OK;
+}
+
+// y[T, O] = x W^T on the tensor cores: x -> fp16 rows, then the A-in-TMEM
+// GEMM (weights as A, dequantised in TMEM; token rows as B) with f32 rows out.
+static int ql_forward_tensor(qgql *h, const float *x, int T, float *y, cudaStream_t s) {
+    int rc = ql_ensure_tc(h, T);
+    if (rc) return rc;
+    const int nt = ql_tile_tokens(T);
+    if ((rc = launch_ql_prep(x, T, h->I, nt, h->xp16, h->tab, h->err_dev, s))) return rc;
+    UmmaLaunch l{};
+    l.wq = h->pq;
+    l.RT = h->O / 128;
+    l.KB = h->I / 64;
+    l.act_group = h->tab;
+    l.act_begin = h->tab + 1;
+    l.act_n = h->tab + 2;
+    l.n_act = h->tab + 3;
+    l.tile_prefix = h->tab + 4;
+    l.out32 = y;
+    l.out_stride = h->O;
+    l.err = h->err_dev;
+    l.tile_tokens = nt;
+    l.grid = ((T + nt - 1) / nt) * l.RT;
+    return launch_umma(h->bits, false, &h->tmap[ql_map_index(nt)], l, s);
+}
 
 extern "C" {
 
@@ -1268,6 +1322,11 @@ int qgql_create(int32_t bits, int32_t O, int32_t I, const void *q, const void *s
     Part p{bits == 32 ? static_cast<const float *>(q) : nullptr,
            bits == 32 ? nullptr : static_cast<const uint8_t *>(q), scale, O};
     rc = build_set(h->weights, bits, I, O, 1, &p, 1, scale_dtype, on_device != 0, &h->ws, h->stream);
+    h->tensor_ok = (bits == 8 || bits == 4) && O % 128 == 0 && I % 64 == 0;
+    if (!rc && h->tensor_ok) {
+        rc = h->weights.alloc(reinterpret_cast<void **>(&h->pq), packed_bytes(bits, 1, O, I));
+        if (!rc) rc = launch_repack(h->ws.q, h->ws.s, bits, 1, O, I, O / 128, 0, 0, h->pq, h->stream);
+    }
     if (!rc) rc = h->weights.alloc(reinterpret_cast<void **>(&h->err_dev), sizeof(int));
     if (!rc && cudaMemsetAsync(h->err_dev, 0, sizeof(int), h->stream) != cudaSuccess)
         rc = set_error(QGMOE_ERR_CUDA, "memset");
@@ -1286,6 +1345,7 @@ int qgql_destroy(qgql_t *h) {
     cudaSetDevice(h->device);
     if (h->stream) cudaStreamSynchronize(h->stream);
     h->work.free_all();
+    h->tc.free_all();
     h->weights.free_all();
     if (h->stream) cudaStreamDestroy(h->stream);
     delete h;
@@ -1299,6 +1359,12 @@ int qgql_forward_device(qgql_t *h, const float *x, int32_t T, float *y, void *st
     if (!x || !y) return set_error(QGMOE_ERR_INVALID_ARG, "null x/y");
     QG_CUDA(cudaSetDevice(h->device));
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    // The tensor path is opt-in (QGMOE_PATH_TENSOR): its fp16 operands give
+    // errors of order 2^-11 * sum_k |w_k x_k|, outside the f32 parity bar for
+    // unit-scale activations over long rows; AUTO keeps the f32 GEMV.
+    const bool aligned = !(reinterpret_cast<uintptr_t>(x) & 15) && !(reinterpret_cast<uintptr_t>(y) & 15);
+    if (h->tensor_ok && aligned && h->path_mode == QGMOE_PATH_TENSOR)
+        return ql_forward_tensor(h, x, T, y, s);
     ExpertArgs a{};
     a.routed = h->ws;
     a.shared = h->ws;
@@ -1335,7 +1401,35 @@ int qgql_forward(qgql_t *h, const float *x, int32_t T, float *y) {
     int rc = qgql_forward_device(h, h->x_dev, T, h->y_dev, s);
     if (rc) return rc;
     QG_CUDA(cudaMemcpyAsync(y, h->y_dev, sizeof(float) * T * h->O, cudaMemcpyDeviceToHost, s));
+    return qgql_sync(h, nullptr);
+}
+
+int qgql_sync(qgql_t *h, void *stream) {
+    if (!h) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    QG_CUDA(cudaSetDevice(h->device));
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    int flag = 0;
+    QG_CUDA(cudaMemcpyAsync(&flag, h->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
     QG_CUDA(cudaStreamSynchronize(s));
+    if (flag) {
+        QG_CUDA(cudaMemsetAsync(h->err_dev, 0, sizeof(int), s));
+        QG_CUDA(cudaStreamSynchronize(s));
+        return set_error(QGMOE_ERR_DEVICE_FLAG, "device error flag 0x%x%s", flag,
+                         (flag & QG_FLAG_RANGE) ? " (an activation beyond fp16 range reached the "
+                                                  "tensor-core path)" : "");
+    }
+    return QGMOE_OK;
+}
+
+int qgql_set_path(qgql_t *h, int32_t mode) {
+    if (!h) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (mode != QGMOE_PATH_AUTO && mode != QGMOE_PATH_CUDA_CORE && mode != QGMOE_PATH_TENSOR)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bad path mode %d", mode);
+    if (mode == QGMOE_PATH_TENSOR && !h->tensor_ok)
+        return set_error(QGMOE_ERR_UNSUPPORTED,
+                         "tensor-core QuantLinear needs int8/int4 weights, out_features %% 128 == 0 "
+                         "and in_features %% 64 == 0");
+    h->path_mode = mode;
     return QGMOE_OK;
 }
 

@@ -159,6 +159,7 @@ struct UmmaLaunch {
     // (rank << 24 | row) and row goes to out_peers[rank] + out_peer_off
     uint8_t *const *out_peers;
     size_t out_peer_off;
+    float *out32;               // GEMM2 only: f32 output rows instead of fp16 (QuantLinear)
     int *err;
     int grid;                   // upper bound of work units
     int tile_tokens;            // max tokens per work unit: 256 (prefill) or 64 (decode)
@@ -234,6 +235,12 @@ size_t packed_bytes(int bits, int E, int rows_per_e, int K);
 int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
                       cudaStream_t s);
 int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
+// QuantLinear on the tensor cores: x [T, K] f32 -> fp16 rows xp (a finite
+// value beyond fp16 range raises QG_FLAG_RANGE) and the one-group work
+// tables tab = {group 0, first slot 0, T slots, 1 group, tile prefix 0,
+// ceil(T / nt)}.
+int launch_ql_prep(const float *x, int T, int K, int nt, __half *xp, int32_t *tab, int *err,
+                   cudaStream_t s);
 // Expert parallelism: copies received rows into local-expert-major order.
 int launch_ep_regroup(const __half *recv, int R, int H, const int32_t *seg_recv_off,
                       const int32_t *seg_grp_off, int nseg, __half *grouped, int32_t *grp2recv,

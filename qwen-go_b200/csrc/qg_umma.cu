@@ -235,6 +235,7 @@ struct UmmaArgs {
     const int32_t *out_map;  // STORE: output row of each slot (null = the slot itself)
     uint8_t *const *out_peers;  // STORE over peers: out_map = rank << 24 | row
     size_t out_peer_off;
+    float *out32;         // STORE: f32 rows [slots, out_stride] instead of fp16 (QuantLinear)
     int *err;
 };
 
@@ -295,6 +296,11 @@ __device__ __forceinline__ void epi_unit(const UmmaArgs &a, const Unit &w, uint3
                 }
                 __half *dst = a.out + (size_t)(w.slot0 + t) * a.out_stride + w.rt * 64 + er;
                 *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else if (a.out32) {  // f32 rows (QuantLinear): 16 rows as four 16-byte stores
+                float4 *dst = reinterpret_cast<float4 *>(
+                    a.out32 + (size_t)(w.slot0 + t) * a.out_stride + w.rt * UM_M + er);
+#pragma unroll
+                for (int q = 0; q < 4; q++) dst[q] = ld_shared_f4(rowp + 16 * q);
             } else {
                 uint32_t o[8];
 #pragma unroll
@@ -881,6 +887,47 @@ __global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restr
     }
 }
 
+// ---- QuantLinear on the tensor cores: fp16 rows + one-group tables ----------
+__global__ void k_ql_prep(const float *__restrict__ x, int64_t n4, __half *__restrict__ xp, int T,
+                          int nt, int32_t *__restrict__ tab, int *err) {
+    pdl_enter();
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        tab[0] = 0;                  // act_group: the one weight matrix
+        tab[1] = 0;                  // act_begin: slot of token 0
+        tab[2] = T;                  // act_n
+        tab[3] = 1;                  // n_act
+        tab[4] = 0;                  // tile_prefix[0]
+        tab[5] = (T + nt - 1) / nt;  // tile_prefix[1]
+    }
+    bool bad = false;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4 *>(x)[i];
+        const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+        const float2 fa = __half22float2(a), fb = __half22float2(b);
+        bad |= (isfinite(v.x) && !isfinite(fa.x)) || (isfinite(v.y) && !isfinite(fa.y)) ||
+               (isfinite(v.z) && !isfinite(fb.x)) || (isfinite(v.w) && !isfinite(fb.y));
+        reinterpret_cast<__half2 *>(xp)[2 * i] = a;
+        reinterpret_cast<__half2 *>(xp)[2 * i + 1] = b;
+    }
+    if (bad) atomicOr(err, QG_FLAG_RANGE);
+}
+
+int launch_ql_prep(const float *x, int T, int K, int nt, __half *xp, int32_t *tab, int *err,
+                   cudaStream_t s) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int64_t n4 = (int64_t)T * K / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    const int64_t cap = (int64_t)num_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    QG_CUDA(launch_pdl(k_ql_prep, dim3((unsigned)blocks), dim3(256), 0, s, 1, x, n4, xp, T, nt,
+                       tab, err));
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
 // ---- expert parallelism: regroup received rows by local expert ------------
 // Received rows arrive source-rank-major (each source's rows sorted by local
 // expert).  Segment i = (source, local expert) starts at seg_recv_off[i] in
@@ -1093,6 +1140,7 @@ int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cu
     a.out_map = l.out_map;
     a.out_peers = l.out_peers;
     a.out_peer_off = l.out_peer_off;
+    a.out32 = l.out32;
     a.err = l.err;
     if (l.grid <= 0) return QGMOE_OK;
     const int nt = l.tile_tokens == 128 || l.tile_tokens == 64 || l.tile_tokens == 16

@@ -85,6 +85,8 @@ SIGNATURES = {
     "qgql_destroy": ([_vp], C.c_int),
     "qgql_forward": ([_vp, _vp, C.c_int32, _vp], C.c_int),
     "qgql_forward_device": ([_vp, _vp, C.c_int32, _vp, _vp], C.c_int),
+    "qgql_set_path": ([_vp, C.c_int32], C.c_int),
+    "qgql_sync": ([_vp, _vp], C.c_int),
     "qgql_dequantize_device": ([_vp, _vp, _vp], C.c_int),
     "qgql_quantize_device": ([C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "qg_randn_device": ([C.c_uint64, C.c_uint64, C.c_uint64, C.c_int64, C.c_float, _vp, _vp],
@@ -300,6 +302,14 @@ class QuantLinear:
     def forward_device(self, x, y, stream=None):
         _check(lib().qgql_forward_device(self.h, _ptr(x), x.shape[0], _ptr(y),
                                          _stream_ptr(stream)), "qgql_forward_device")
+
+    def set_path(self, mode: int):
+        """PATH_AUTO, PATH_CUDA_CORE or PATH_TENSOR (qgql_set_path)."""
+        _check(lib().qgql_set_path(self.h, mode), "qgql_set_path")
+
+    def sync(self, stream=None):
+        """Waits for the stream; raises on a device error flag (qgql_sync)."""
+        _check(lib().qgql_sync(self.h, _stream_ptr(stream)), "qgql_sync")
 
     def dequantize(self):
         """quantLinear.dequantize: the [out, in] float32 matrix (torch CUDA)."""

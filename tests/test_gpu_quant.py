@@ -86,6 +86,69 @@ def test_quantlinear_forward(bits, T, shape):
     assert np.array_equal(ql.forward(x[0]), y[0])
 
 
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("T", [1, 16, 100, 300])
+@pytest.mark.parametrize("shape", [(256, 384), (1024, 2048)])
+def test_quantlinear_tensor_path(bits, T, shape):
+    """The opt-in tensor-core QuantLinear (fp16 x, fp16 dequantised weights,
+    f32 accumulation and output) against the oracle, at 16-, 64- and
+    128-token tiles.  Its bound is the fp16 rounding of both operands: each
+    product is off by at most ~2^-10 of |w_k x_k| (the f32 accumulation adds
+    far less), so |y - ref| <= 2^-10 * sum_k |w_k x_k| per output.  Also
+    deterministic from call to call."""
+    Od, Id = shape
+    w = O.randn(31, 1, (Od, Id), 0.02)
+    x = O.randn(31, 2 + T, (T, Id))
+    q, s = O.quantize(w, bits)
+    ql = qgmoe.QuantLinear(bits, Od, Id, q, O.f16_bits(s))
+    ql.set_path(qgmoe.PATH_TENSOR)
+    y = ql.forward(x)
+    ref = O.linear_rows(bits, None, q, O.f16_round(s), x, Od)
+    wd = np.abs(O.dequantize(bits, q, O.f16_round(s), Id)).astype(np.float64)
+    bound = 1.25 * 2.0 ** -10 * (np.abs(x).astype(np.float64) @ wd.T) + 1e-6
+    err = np.abs(y.astype(np.float64) - ref)
+    assert np.all(err <= bound), (err / bound).max()
+    # and at the level of fp16 rounding on average, not merely inside the bound
+    assert np.sqrt(np.mean(err ** 2)) <= 1e-3 * np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+    assert np.array_equal(ql.forward(x), y)
+
+
+def test_quantlinear_tensor_path_on_device_buffers():
+    torch = _torch()
+    Od, Id, T = 512, 1024, 200
+    w = O.randn(33, 1, (Od, Id), 0.02)
+    q, s = O.quantize(w, 8)
+    ql = qgmoe.QuantLinear(8, Od, Id, q, O.f16_bits(s))
+    x = O.randn(33, 2, (T, Id))
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((T, Od), dtype=torch.float32, device="cuda")
+    ql.set_path(qgmoe.PATH_TENSOR)
+    ql.forward_device(xd, yd)
+    ql.sync()
+    assert np.array_equal(yd.cpu().numpy(), ql.forward(x))
+
+
+def test_quantlinear_tensor_path_shape_and_range_checks():
+    w = O.randn(34, 1, (300, 96), 0.02)
+    q, s = O.quantize(w, 8)
+    ql = qgmoe.QuantLinear(8, 300, 96, q, O.f16_bits(s))
+    with pytest.raises(qgmoe.QgmoeError):
+        ql.set_path(qgmoe.PATH_TENSOR)  # out_features not a multiple of 128
+    w = O.randn(34, 2, (128, 128), 0.02)
+    q, s = O.quantize(w, 8)
+    ql = qgmoe.QuantLinear(8, 128, 128, q, O.f16_bits(s))
+    ql.set_path(qgmoe.PATH_TENSOR)
+    x = O.randn(34, 3, (20, 128))
+    x[3, 7] = 1e6  # finite, beyond fp16: flagged, not turned into infinities
+    with pytest.raises(qgmoe.QgmoeError):
+        ql.forward(x)
+    x[3, 7] = 1.0
+    ref = O.linear_rows(8, None, q, O.f16_round(s), x, 128)
+    y = ql.forward(x)  # the flag was cleared
+    wd = np.abs(O.dequantize(8, q, O.f16_round(s), 128)).astype(np.float64)
+    assert np.all(np.abs(y - ref) <= 1.25 * 2.0 ** -10 * (np.abs(x) @ wd.T) + 1e-6)
+
+
 def test_quantlinear_T0_is_noop():
     w = O.randn(1, 1, (32, 64))
     ql = qgmoe.QuantLinear(32, 32, 64, w)
