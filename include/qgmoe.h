@@ -230,6 +230,48 @@ const char *qgmoe_stage_name(const qgmoe_t *h, int32_t i);
 int qgmoe_route_static(const float *x, const float *router, int32_t T, int32_t H, int32_t E,
                        int32_t k, int32_t mode, int32_t *sel_idx, float *sel_w, void *stream);
 
+/* ---- on-disk quantised MoE layers --------------------------------------
+ * The reference's quantised checkpoint convention (quant.json + safetensors
+ * with <name>.qweight / <name>.scale, model/load.go:478-582) extended to the
+ * stacked expert tensors its loader cannot read (model/load.go:419-449 only
+ * takes them as f32/bf16), so a quantised layer goes from the file to the
+ * device without an intermediate host copy.  Tensor names, with a caller
+ * prefix such as "model.layers.3.mlp." (the reference's mlp.* names,
+ * model/load.go:415-456):
+ *   gate.weight                          F32 [E, H]           router
+ *   experts.gate_up_proj.qweight         I8/U8 [E, 2I, H]     int8 codes, or
+ *                                        U8 [E, 2I, H/2]      int4 pairs
+ *   experts.gate_up_proj.scale           F16/F32 [E, 2I, H/32]
+ *   experts.down_proj.qweight / .scale   [E, H, I] or [E, H, I/2] / [E, H, I/32]
+ *   shared_expert.gate_proj, .up_proj, .down_proj (.qweight / .scale; all
+ *   three or none), [Is, H], [Is, H], [H, Is] as above
+ *   shared_expert_gate.weight            F32 [1, H] or [H]    (with the shared expert)
+ * int8 vs int4 follows from the code and scale shapes; every tensor must
+ * have the same scale dtype.  Safetensors layout: u64 little-endian header
+ * size, JSON header {name: {dtype, shape, data_offsets}}, data. */
+typedef struct qgmoe_file qgmoe_file_t;
+#define QGMOE_DT_F32 0
+#define QGMOE_DT_F16 1
+#define QGMOE_DT_BF16 2
+#define QGMOE_DT_I8 3
+#define QGMOE_DT_U8 4
+#define QGMOE_DT_I32 5
+#define QGMOE_DT_OTHER 6
+/* Maps a safetensors file read-only and parses its header (host only; no
+ * CUDA call). */
+int qgmoe_file_open(const char *path, qgmoe_file_t **out);
+int qgmoe_file_close(qgmoe_file_t *f);
+/* One tensor: dtype (QGMOE_DT_*), rank (<= 8) and shape, its bytes inside
+ * the mapping.  Any out pointer may be NULL.  INVALID_ARG if absent. */
+int qgmoe_file_tensor(const qgmoe_file_t *f, const char *name, int32_t *dtype, int32_t *rank,
+                      int64_t *shape, const void **data, int64_t *nbytes);
+/* Fills desc for the layer at `prefix`: shapes, bits and scale dtype from
+ * the tensors, host pointers into the mapping (weights_on_device = 0, no
+ * expert parallelism); top_k, router_mode and device from the caller.  The
+ * mapping must stay open until qgmoe_create has returned. */
+int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top_k,
+                          int32_t router_mode, int32_t device, qgmoe_desc *desc);
+
 /* ---- QuantLinear -------------------------------------------------------- */
 typedef struct qgql qgql_t;
 

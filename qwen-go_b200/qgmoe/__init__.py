@@ -11,6 +11,8 @@ module exposes the same objects over the C ABI in include/qgmoe.h:
     MoeMLP.forward_device(x, out, ...)  torch CUDA tensors, async on a stream
     QuantLinear(bits, q, scale).forward(x) / .dequantize()
     quantize_int8(w) / quantize_int4(w) -> (codes, scales)  on the GPU
+    MoeMLP.from_file(path, prefix, top_k)  a quantised layer from a safetensors
+                                        file (qgmoe.checkpoint writes them)
 
 Every call goes to the CUDA library; there is no CPU fallback.  A failing
 status raises QgmoeError with the library's message.
@@ -87,6 +89,12 @@ SIGNATURES = {
     "qgql_forward_device": ([_vp, _vp, C.c_int32, _vp, _vp], C.c_int),
     "qgql_set_path": ([_vp, C.c_int32], C.c_int),
     "qgql_sync": ([_vp, _vp], C.c_int),
+    "qgmoe_file_open": ([C.c_char_p, C.POINTER(_vp)], C.c_int),
+    "qgmoe_file_close": ([_vp], C.c_int),
+    "qgmoe_file_tensor": ([_vp, C.c_char_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                           C.POINTER(C.c_int64), C.POINTER(_vp), C.POINTER(C.c_int64)], C.c_int),
+    "qgmoe_file_layer_desc": ([_vp, C.c_char_p, C.c_int32, C.c_int32, C.c_int32,
+                               C.POINTER(_Desc)], C.c_int),
     "qgql_dequantize_device": ([_vp, _vp, _vp], C.c_int),
     "qgql_quantize_device": ([C.c_int32, C.c_int32, C.c_int32, _vp, _vp, _vp, _vp, _vp], C.c_int),
     "qg_randn_device": ([C.c_uint64, C.c_uint64, C.c_uint64, C.c_int64, C.c_float, _vp, _vp],
@@ -203,6 +211,27 @@ class MoeMLP:
         self.n_embed, self.top_k, self.n_experts = n_embed, top_k, n_experts
         self.device = device
         self.ep_world, self.ep_rank = ep_world, ep_rank
+
+    @classmethod
+    def from_file(cls, path: str, prefix: str, top_k: int, router_mode: int = ROUTER_TOPK,
+                  device: int = 0) -> "MoeMLP":
+        """The quantised layer stored under `prefix` in a safetensors file
+        (qgmoe_file_layer_desc): the tensors are mapped, not read, and
+        create() copies them from the mapping to the device."""
+        f = LayerFile(path)
+        try:
+            d = f.layer_desc(prefix, top_k, router_mode, device)
+            h = _vp()
+            _check(lib().qgmoe_create(C.byref(d), C.byref(h)), "qgmoe_create")
+        finally:
+            f.close()
+        self = cls.__new__(cls)
+        self._keep = None
+        self.h = h
+        self.n_embed, self.top_k, self.n_experts = d.n_embed, top_k, d.n_experts
+        self.device = device
+        self.ep_world, self.ep_rank = 1, 0
+        return self
 
     def close(self):
         if getattr(self, "h", None):
@@ -348,3 +377,49 @@ def randn_device(out, seed: int, stream_id: int, std: float = 1.0, offset: int =
     _check(lib().qg_randn_device(seed, stream_id, offset, out.numel(), std, _ptr(out),
                                  _stream_ptr(cuda_stream)), "qg_randn_device")
     return out
+
+
+DT_F32, DT_F16, DT_BF16, DT_I8, DT_U8, DT_I32, DT_OTHER = range(7)
+
+
+class LayerFile:
+    """A safetensors file mapped by the library (qgmoe_file_open): tensor
+    lookup and the qgmoe_desc of one quantised MoE layer (host only)."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(lib().qgmoe_file_open(os.fsencode(path), C.byref(h)), "qgmoe_file_open")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().qgmoe_file_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def tensor(self, name: str):
+        """(dtype code, shape tuple, address inside the mapping, bytes)."""
+        dt, rank = C.c_int32(), C.c_int32()
+        shape = (C.c_int64 * 8)()
+        data, nbytes = _vp(), C.c_int64()
+        _check(lib().qgmoe_file_tensor(self.h, name.encode(), C.byref(dt), C.byref(rank), shape,
+                                       C.byref(data), C.byref(nbytes)), "qgmoe_file_tensor")
+        return dt.value, tuple(shape[i] for i in range(rank.value)), data.value or 0, nbytes.value
+
+    def layer_desc(self, prefix: str, top_k: int, router_mode: int = ROUTER_TOPK,
+                   device: int = 0) -> _Desc:
+        d = _Desc()
+        _check(lib().qgmoe_file_layer_desc(self.h, prefix.encode(), top_k, router_mode, device,
+                                           C.byref(d)), "qgmoe_file_layer_desc")
+        return d

@@ -1,0 +1,124 @@
+"""Quantised MoE layers on disk: the writer for the layout qgmoe_file_*
+reads (include/qgmoe.h).
+
+qwen-go stores quantised linears as <name>.qweight / <name>.scale tensor
+pairs in safetensors shards listed by quant.json ({"bits": ..., "quantized":
+[...]}, model/load.go:478-582, written by cmd/qwen-quant); its MoE loader
+takes the stacked expert tensors only as float blobs (model/load.go:
+415-456).  save_layer writes one MoE layer with the stacked expert codes
+and fp16 (or f32) group scales under the same mlp.* names:
+
+    <prefix>gate.weight                      F32 [E, H]
+    <prefix>experts.gate_up_proj.qweight     I8 [E, 2I, H] (int8) / U8 [E, 2I, H/2] (int4)
+    <prefix>experts.gate_up_proj.scale       F16 or F32 [E, 2I, H/32]
+    <prefix>experts.down_proj.qweight/.scale [E, H, I] ... / [E, H, I/32]
+    <prefix>shared_expert.{gate,up,down}_proj.qweight/.scale   (optional)
+    <prefix>shared_expert_gate.weight        F32 [1, H]        (with the shared expert)
+
+Tensor data starts on 64-byte boundaries (the header is space-padded), so
+the mapped tensors are aligned for any element type.
+"""
+from __future__ import annotations
+
+import json
+import os
+import struct
+
+import numpy as np
+
+_DTYPES = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np.int8): "I8",
+           np.dtype(np.uint8): "U8", np.dtype(np.int32): "I32"}
+_ALIGN = 64
+
+
+def write_safetensors(path: str, tensors: dict, metadata: dict | None = None) -> None:
+    """tensors: name -> numpy array (float32/float16/int8/uint8/int32), in
+    the order given; fp16 scales may also come as uint16 bit patterns."""
+    header = {}
+    if metadata:
+        header["__metadata__"] = {str(k): str(v) for k, v in metadata.items()}
+    blobs, off = [], 0
+    for name, a in tensors.items():
+        a = np.ascontiguousarray(a)
+        if a.dtype == np.uint16:  # fp16 bit patterns
+            a = a.view(np.float16)
+        if a.dtype not in _DTYPES:
+            raise TypeError(f"{name}: unsupported dtype {a.dtype}")
+        pad = (-off) % _ALIGN
+        if pad:
+            blobs.append(b"\0" * pad)
+            off += pad
+        raw = a.tobytes()
+        header[name] = {"dtype": _DTYPES[a.dtype], "shape": list(a.shape),
+                        "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    hj = json.dumps(header, separators=(",", ":")).encode()
+    hj += b" " * ((-(8 + len(hj))) % _ALIGN)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for b in blobs:
+            f.write(b)
+
+
+def read_header(path: str) -> dict:
+    """The JSON header of a safetensors file (independent of the library)."""
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        return json.loads(f.read(n))
+
+
+def save_layer(path: str, prefix: str, *, router, gate_up_q, gate_up_scale, down_q, down_scale,
+               bits: int, shared_gate=None, shared_gate_q=None, shared_gate_scale=None,
+               shared_up_q=None, shared_up_scale=None, shared_down_q=None,
+               shared_down_scale=None, quant_json: str | None = None, append: dict | None = None):
+    """Writes one quantised MoE layer (the arrays qgmoe.MoeMLP takes for bits
+    8/4, with E, 2I, H / E, H, I leading shapes) to `path`; `append` adds
+    more tensors to the same file (other layers).  With quant_json, also
+    writes the reference's manifest listing the quantised tensors."""
+    if bits not in (8, 4):
+        raise ValueError("bits must be 8 or 4")
+    router = np.asarray(router, np.float32)
+    E, H = router.shape
+    t = dict(append or {})
+    t[prefix + "gate.weight"] = router
+
+    def codes(q, lead_shape):
+        q = np.asarray(q)
+        q = q.view(np.int8) if bits == 8 else q.view(np.uint8)
+        return q.reshape(lead_shape + (-1,))
+
+    def scales(s, lead_shape):
+        s = np.asarray(s)
+        if s.dtype not in (np.float32, np.float16, np.uint16):
+            raise TypeError("scales: float32, float16 or fp16 bits (uint16)")
+        return s.reshape(lead_shape + (-1,))
+
+    gu_rows = np.asarray(gate_up_scale).size // (E * (H // 32))
+    I = gu_rows // 2
+    t[prefix + "experts.gate_up_proj.qweight"] = codes(gate_up_q, (E, 2 * I))
+    t[prefix + "experts.gate_up_proj.scale"] = scales(gate_up_scale, (E, 2 * I))
+    t[prefix + "experts.down_proj.qweight"] = codes(down_q, (E, H))
+    t[prefix + "experts.down_proj.scale"] = scales(down_scale, (E, H))
+    names = [prefix + "experts.gate_up_proj.weight", prefix + "experts.down_proj.weight"]
+    if shared_gate_q is not None:
+        Is = np.asarray(shared_gate_scale).size // (H // 32)
+        for base, q, s, rows in (("shared_expert.gate_proj", shared_gate_q, shared_gate_scale, Is),
+                                 ("shared_expert.up_proj", shared_up_q, shared_up_scale, Is),
+                                 ("shared_expert.down_proj", shared_down_q, shared_down_scale, H)):
+            t[prefix + base + ".qweight"] = codes(q, (rows,))
+            t[prefix + base + ".scale"] = scales(s, (rows,))
+            names.append(prefix + base + ".weight")
+        t[prefix + "shared_expert_gate.weight"] = np.asarray(shared_gate, np.float32).reshape(1, H)
+    write_safetensors(path, t, {"format": "pt", "qgmoe_bits": bits})
+    if quant_json:
+        man = {"bits": bits, "quantized": names}
+        if os.path.exists(quant_json):
+            with open(quant_json) as f:
+                old = json.load(f)
+            if old.get("bits") != bits:
+                raise ValueError("quant.json already lists another bit width")
+            man["quantized"] = list(dict.fromkeys(old.get("quantized", []) + names))
+        with open(quant_json, "w") as f:
+            json.dump(man, f, indent=1)

@@ -1,0 +1,210 @@
+"""On-disk quantised MoE layers (qgmoe_file_*, qgmoe.checkpoint): the writer's
+safetensors layout, the library's header parser and tensor lookup, and the
+qgmoe_desc it builds, checked byte for byte against the arrays written.
+Host only (no CUDA call); the device side is qgmoe_create, tested elsewhere."""
+import ctypes as C
+import json
+import struct
+
+import numpy as np
+import pytest
+
+import qg_oracle as O
+import qgmoe
+from qgmoe import checkpoint as ck
+
+
+def _layer(bits, Is, seed=5):
+    return O.make_moe(H=128, E=4, k=2, I=64, Is=Is, bits=bits, seed=seed)
+
+
+def _save(tmp_path, m, prefix="model.layers.0.mlp.", scale="f16", **kw):
+    sc = (lambda n: m.s16[n]) if scale == "f16" else (lambda n: m.s[n].astype(np.float32))
+    args = dict(router=m.router, gate_up_q=m.q["gate_up"], gate_up_scale=sc("gate_up"),
+                down_q=m.q["down"], down_scale=sc("down"), bits=m.bits)
+    if m.Is:
+        args.update(shared_gate=m.shared_gate, shared_gate_q=m.q["sh_gate"],
+                    shared_gate_scale=sc("sh_gate"), shared_up_q=m.q["sh_up"],
+                    shared_up_scale=sc("sh_up"), shared_down_q=m.q["sh_down"],
+                    shared_down_scale=sc("sh_down"))
+    args.update(kw)
+    path = str(tmp_path / "layer.safetensors")
+    ck.save_layer(path, prefix, **args)
+    return path
+
+
+def _bytes(addr, a):
+    a = np.ascontiguousarray(a)
+    return C.string_at(addr, a.nbytes) == a.tobytes()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("Is", [0, 128])
+@pytest.mark.parametrize("scale", ["f16", "f32"])
+def test_layer_desc_points_at_the_written_arrays(tmp_path, bits, Is, scale):
+    m = _layer(bits, Is)
+    qj = str(tmp_path / "quant.json")
+    path = _save(tmp_path, m, scale=scale, quant_json=qj)
+    with qgmoe.LayerFile(path) as f:
+        d = f.layer_desc("model.layers.0.mlp.", top_k=2, router_mode=qgmoe.ROUTER_PREFIX, device=3)
+        assert (d.n_embed, d.n_experts, d.top_k, d.n_moe_mlp, d.n_shared_mlp) == (128, 4, 2, 64, Is)
+        assert (d.bits, d.router_mode, d.device, d.weights_on_device) == (bits, 1, 3, 0)
+        assert d.scale_dtype == (qgmoe.SCALE_F16 if scale == "f16" else qgmoe.SCALE_F32)
+        assert d.ep_world == 0 and not d.ep_slot and not d.gate_up and not d.down
+        assert _bytes(d.router, m.router)
+        pairs = [("gate_up", d.gate_up_q, d.gate_up_scale), ("down", d.down_q, d.down_scale)]
+        if Is:
+            pairs += [("sh_gate", d.shared_gate_q, d.shared_gate_scale),
+                      ("sh_up", d.shared_up_q, d.shared_up_scale),
+                      ("sh_down", d.shared_down_q, d.shared_down_scale)]
+            assert _bytes(d.shared_gate, m.shared_gate)
+        else:
+            assert not d.shared_gate_q and not d.shared_gate
+        for name, q, s in pairs:
+            assert _bytes(q, m.q[name]), name
+            want = m.s16[name] if scale == "f16" else m.s[name].astype(np.float32)
+            assert _bytes(s, want), name
+            assert q % 64 == 0 and s % 64 == 0  # aligned for any element type
+    man = json.load(open(qj))
+    assert man["bits"] == bits
+    assert "model.layers.0.mlp.experts.gate_up_proj.weight" in man["quantized"]
+    assert ("model.layers.0.mlp.shared_expert.down_proj.weight" in man["quantized"]) == bool(Is)
+
+
+def test_tensor_lookup_matches_an_independent_header_parse(tmp_path):
+    m = _layer(4, 128)
+    path = _save(tmp_path, m)
+    hdr = ck.read_header(path)
+    codes = {"F32": qgmoe.DT_F32, "F16": qgmoe.DT_F16, "I8": qgmoe.DT_I8, "U8": qgmoe.DT_U8}
+    with open(path, "rb") as fh:
+        n = struct.unpack("<Q", fh.read(8))[0]
+        raw = fh.read()
+    data = raw[n:]
+    with qgmoe.LayerFile(path) as f:
+        for name, t in hdr.items():
+            if name == "__metadata__":
+                continue
+            dt, shape, addr, nbytes = f.tensor(name)
+            assert dt == codes[t["dtype"]] and list(shape) == t["shape"], name
+            b0, b1 = t["data_offsets"]
+            assert nbytes == b1 - b0
+            assert C.string_at(addr, nbytes) == data[b0:b1]
+        with pytest.raises(qgmoe.QgmoeError):
+            f.tensor("model.layers.0.mlp.no_such.weight")
+    assert hdr["__metadata__"]["qgmoe_bits"] == "4"
+    assert hdr["model.layers.0.mlp.experts.gate_up_proj.qweight"]["shape"] == [4, 128, 64]
+
+
+def test_two_layers_in_one_file(tmp_path):
+    a, b = _layer(8, 0, seed=7), _layer(8, 0, seed=8)
+    first = {}
+    pa = _save(tmp_path, a, prefix="model.layers.1.mlp.")
+    hdr = ck.read_header(pa)
+    with open(pa, "rb") as fh:
+        n = struct.unpack("<Q", fh.read(8))[0]
+        data = fh.read()[n:]
+    for name, t in hdr.items():
+        if name != "__metadata__":
+            dt = {"F32": np.float32, "F16": np.float16, "I8": np.int8, "U8": np.uint8}[t["dtype"]]
+            b0, b1 = t["data_offsets"]
+            first[name] = np.frombuffer(data[b0:b1], dt).reshape(t["shape"])
+    path = _save(tmp_path, b, prefix="model.layers.2.mlp.", append=first)
+    with qgmoe.LayerFile(path) as f:
+        d1 = f.layer_desc("model.layers.1.mlp.", 2)
+        d2 = f.layer_desc("model.layers.2.mlp.", 2)
+        assert _bytes(d1.gate_up_q, a.q["gate_up"]) and _bytes(d2.gate_up_q, b.q["gate_up"])
+        assert _bytes(d1.router, a.router) and _bytes(d2.router, b.router)
+        with pytest.raises(qgmoe.QgmoeError):
+            f.layer_desc("model.layers.3.mlp.", 2)
+
+
+def _write_raw(path, header: dict, data: bytes = b"", pad=True):
+    hj = json.dumps(header).encode()
+    if pad:
+        hj += b" " * ((-(8 + len(hj))) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)) + hj + data)
+
+
+def test_malformed_files_are_rejected(tmp_path):
+    p = str(tmp_path / "bad.safetensors")
+    for content in (b"", b"\x01\x02", struct.pack("<Q", 1 << 40) + b"{}", struct.pack("<Q", 3) + b"{x}",
+                    struct.pack("<Q", 2) + b"[]"):
+        with open(p, "wb") as f:
+            f.write(content)
+        with pytest.raises(qgmoe.QgmoeError):
+            qgmoe.LayerFile(p)
+    # data beyond the file, byte count not matching the shape, missing keys
+    for hdr, data in (({"a": {"dtype": "F32", "shape": [4], "data_offsets": [0, 16]}}, b"\0" * 8),
+                      ({"a": {"dtype": "F32", "shape": [3], "data_offsets": [0, 16]}}, b"\0" * 16),
+                      ({"a": {"dtype": "F32", "shape": [4]}}, b"\0" * 16),
+                      ({"a": {"dtype": "F32", "shape": [-4], "data_offsets": [0, 16]}}, b"\0" * 16)):
+        _write_raw(p, hdr, data)
+        with pytest.raises(qgmoe.QgmoeError):
+            qgmoe.LayerFile(p)
+    # a well-formed file with escapes, metadata and an unknown dtype opens
+    # (json.dumps writes the non-ASCII key as a \u escape)
+    _write_raw(p, {"__metadata__": {"k": "v\"\u00e9"},
+                   "n\u00e9": {"dtype": "F8_E4M3", "shape": [2], "data_offsets": [0, 2]}}, b"\0\0")
+    with qgmoe.LayerFile(p) as f:
+        dt, shape, _, nbytes = f.tensor("né")
+        assert dt == qgmoe.DT_OTHER and shape == (2,) and nbytes == 2
+
+
+def test_layer_desc_rejects_inconsistent_layers(tmp_path):
+    m = _layer(8, 0)
+    p = _save(tmp_path, m)
+    hdr = ck.read_header(p)
+    with open(p, "rb") as fh:
+        n = struct.unpack("<Q", fh.read(8))[0]
+        data = fh.read()[n:]
+    arrays = {}
+    for name, t in hdr.items():
+        if name != "__metadata__":
+            dt = {"F32": np.float32, "F16": np.float16, "I8": np.int8, "U8": np.uint8}[t["dtype"]]
+            b0, b1 = t["data_offsets"]
+            arrays[name] = np.frombuffer(data[b0:b1], dt).reshape(t["shape"])
+    pre = "model.layers.0.mlp."
+    cases = [
+        # router in fp16
+        {pre + "gate.weight": arrays[pre + "gate.weight"].astype(np.float16)},
+        # down stack with the wrong number of experts
+        {pre + "experts.down_proj.qweight": arrays[pre + "experts.down_proj.qweight"][:3],
+         pre + "experts.down_proj.scale": arrays[pre + "experts.down_proj.scale"][:3]},
+        # gate_up scales for a different input width
+        {pre + "experts.gate_up_proj.scale": arrays[pre + "experts.gate_up_proj.scale"][:, :, :2]},
+        # int4-width codes stored as I8
+        {pre + "experts.gate_up_proj.qweight": arrays[pre + "experts.gate_up_proj.qweight"][:, :, :64]},
+        # mixed scale dtypes
+        {pre + "experts.down_proj.scale":
+            arrays[pre + "experts.down_proj.scale"].astype(np.float32)},
+        # a shared expert with only one projection
+        {pre + "shared_expert.gate_proj.qweight": np.zeros((128, 128), np.int8),
+         pre + "shared_expert.gate_proj.scale": np.zeros((128, 4), np.float16)},
+    ]
+    q = str(tmp_path / "bad_layer.safetensors")
+    for change in cases:
+        t = dict(arrays)
+        t.update(change)
+        ck.write_safetensors(q, t)
+        with qgmoe.LayerFile(q) as f:
+            with pytest.raises(qgmoe.QgmoeError):
+                f.layer_desc(pre, 2)
+    # and the unchanged set is accepted
+    ck.write_safetensors(q, arrays)
+    with qgmoe.LayerFile(q) as f:
+        assert f.layer_desc(pre, 2).n_experts == 4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [8, 4])
+def test_layer_from_file_matches_layer_from_arrays(tmp_path, bits):
+    """qgmoe_create from the mapped file and from the same arrays gives
+    bit-identical forwards (the desc differs only in where the bytes live)."""
+    from moe_cases import make_gpu_moe
+    m = _layer(bits, 128, seed=11)
+    path = _save(tmp_path, m)
+    a = make_gpu_moe(m, O.ROUTER_TOPK)
+    b = qgmoe.MoeMLP.from_file(path, "model.layers.0.mlp.", top_k=2)
+    x = O.randn(11, 9, (24, 128))
+    assert np.array_equal(a.forward_batch(x), b.forward_batch(x))
