@@ -129,6 +129,23 @@ def f16_bits(a: np.ndarray) -> np.ndarray:
     return h
 
 
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns, round to nearest even (NaN stays a
+    quiet NaN).  The reference reads bf16 weights as the high half of a
+    float32 (bf16f32, model/model.go:113-115); HF checkpoints store them so."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    r = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    nan = np.isnan(np.asarray(a, np.float32))
+    out = (r & 0xFFFF).astype(np.uint16)
+    out[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return out
+
+
+def bf16_widen(h: np.ndarray) -> np.ndarray:
+    """bf16f32 (model/model.go:113-115): the bits as the high half of a float32."""
+    return (np.ascontiguousarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
 def softmax(v: np.ndarray) -> np.ndarray:
     v = np.array(v, np.float32, copy=True)
     lib().qgo_softmax(_p(v, _f32p), v.size)
@@ -157,6 +174,12 @@ class MoeWeights:
     """Weights of one moeMLP in the reference layout (model/moe.go:10-25).
 
     bits 32: gate_up [E,2I,H], down [E,H,I], sh_gate/sh_up [Is,H], sh_down [H,Is].
+    bits 16: raw bf16 experts (gateUpRaw / downRaw, model/moe.go:14-15, 64-81):
+             q holds the bf16 bit patterns and the float32 fields their exact
+             widening; bf16matvec (model/moe.go:102-113) and the raw linear
+             (matvecRange, model/model.go:167-176) are the serial float32 dot of
+             matmulVec (model/tensors.go:77-89) over those widened values, so
+             the oracle runs the bits-32 arithmetic on them.
     bits 8/4: the same tensors as quantLinear codes + f32 scale arrays; the
     scale arrays here are what the dequantiser multiplies by (already
     rounded to fp16 when the fp16-scale format is modelled).
@@ -196,6 +219,14 @@ def make_moe(H, E, k, I, Is, bits, seed, std=0.02, scale_f16=True) -> MoeWeights
         if Is > 0:
             m.sh_gate, m.sh_up, m.sh_down = sh_gate, sh_up, sh_down
         return m
+    if bits == 16:
+        mats = {"gate_up": gate_up, "down": down}
+        if Is > 0:
+            mats.update(sh_gate=sh_gate, sh_up=sh_up, sh_down=sh_down)
+        for name, w in mats.items():
+            m.q[name] = bf16_bits(w)
+            setattr(m, name, bf16_widen(m.q[name]))
+        return m
     mats = {"gate_up": gate_up.reshape(E * 2 * I, H), "down": down.reshape(E * H, I)}
     if Is > 0:
         mats.update(sh_gate=sh_gate, sh_up=sh_up, sh_down=sh_down)
@@ -208,7 +239,7 @@ def make_moe(H, E, k, I, Is, bits, seed, std=0.02, scale_f16=True) -> MoeWeights
 
 
 def _lin(m: MoeWeights, name: str) -> _Lin:
-    if m.bits == 32:
+    if m.bits in (32, 16):
         return _Lin(_p(getattr(m, name), _f32p), C.cast(None, _u8p), C.cast(None, _f32p))
     if name not in m.q:
         return _Lin(C.cast(None, _f32p), C.cast(None, _u8p), C.cast(None, _f32p))
@@ -218,11 +249,11 @@ def _lin(m: MoeWeights, name: str) -> _Lin:
 def _struct(m: MoeWeights, mode: int) -> _Moe:
     st = _Moe()
     st.n_embed, st.n_experts, st.top_k, st.n_moe_mlp = m.H, m.E, m.k, m.I
-    st.n_shared_mlp, st.bits, st.router_mode = m.Is, m.bits, mode
+    st.n_shared_mlp, st.bits, st.router_mode = m.Is, 32 if m.bits == 16 else m.bits, mode
     st.router = _p(m.router, _f32p)
     st.shared_gate = _p(m.shared_gate, _f32p)
     for name in ("gate_up", "down", "sh_gate", "sh_up", "sh_down"):
-        if m.bits == 32 and getattr(m, name) is None:
+        if m.bits in (32, 16) and getattr(m, name) is None:
             setattr(st, name, _Lin(C.cast(None, _f32p), C.cast(None, _u8p), C.cast(None, _f32p)))
         else:
             setattr(st, name, _lin(m, name))

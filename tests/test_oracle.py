@@ -76,7 +76,10 @@ def np_moe_token(m, x, mode):
     out = np.zeros(H, np.float32)
 
     def lin(name, row0, rows, in_dim, v):
-        if m.bits == 32:
+        if m.bits == 16:  # bf16matvec: the bf16 bits widened (<< 16), then the f32 dot
+            h = m.q[name].reshape(-1, in_dim)[row0:row0 + rows]
+            W = (h.astype(np.uint32) << 16).view(np.float32)
+        elif m.bits == 32:
             W = getattr(m, name).reshape(-1, in_dim)[row0:row0 + rows]
         else:
             q = m.q[name][row0:row0 + rows]
@@ -249,7 +252,7 @@ def test_randn_counter_based_and_moments():
 # --------------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("bits", [32, 8, 4])
+@pytest.mark.parametrize("bits", [32, 16, 8, 4])
 @pytest.mark.parametrize("mode", [O.ROUTER_TOPK, O.ROUTER_PREFIX])
 @pytest.mark.parametrize("Is", [0, 64])
 def test_oracle_matches_numpy_restatement(bits, mode, Is):
@@ -276,3 +279,23 @@ def test_token_parallel_equals_serial():
     x = O.randn(2, 100, (13, 64))
     out, *_ = O.moe_forward(m, x)
     assert np.array_equal(O.moe_forward_mt(m, x, 4), out)
+
+
+def test_bf16_rounding_known_answers():
+    """float32 -> bf16 (round to nearest even on the dropped 16 bits) and the
+    reference's widening bf16f32 (model/model.go:113-115)."""
+    vals = np.array([1.0, 1.00390625, 1.01171875, 1.0078125, -2.5, 3.0e38, 1e-40, 0.0, -0.0,
+                     np.inf, -np.inf], np.float32)
+    bits = O.bf16_bits(vals)
+    # 1 + 2^-8 is a tie -> even (1.0); 1 + 3*2^-8 ties up to 1 + 2^-6; 1 + 2^-7 exact
+    assert bits.tolist()[:5] == [0x3F80, 0x3F80, 0x3F82, 0x3F81, 0xC020]
+    assert bits[5] == 0x7F62  # 3e38 rounds to 0x7F62 (3.0e38 ~ 0x7F61B1E6)
+    assert bits[7] == 0x0000 and bits[8] == 0x8000 and bits[9] == 0x7F80 and bits[10] == 0xFF80
+    w = O.bf16_widen(bits)
+    assert w[0] == 1.0 and w[2] == np.float32(1.015625) and w[4] == -2.5
+    nan = O.bf16_bits(np.array([np.nan], np.float32))
+    assert np.isnan(O.bf16_widen(nan)[0])
+    # widening is exact: every bf16 value survives a round trip
+    h = np.arange(0, 1 << 16, 97, dtype=np.uint32).astype(np.uint16)
+    finite = np.isfinite(O.bf16_widen(h))
+    assert np.array_equal(O.bf16_bits(O.bf16_widen(h))[finite], h[finite])
