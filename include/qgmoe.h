@@ -57,7 +57,9 @@ typedef struct qgmoe qgmoe_t;
 
 /* Weights of one moeMLP (model/moe.go:10-25).  Layouts are the reference's:
  * rows are (out, in), row-major.  bits selects the expert + shared-expert
- * weight format: 32 = float32 (gateUpW/downW), 8 or 4 = quantLinear codes
+ * weight format: 32 = float32 (gateUpW/downW), 16 = raw bf16 (gateUpRaw /
+ * downRaw, model/moe.go:14-15, 102-113: the *_q pointers hold the bf16 bit
+ * patterns, 2 bytes per element, no scales; CUDA-core path), 8 or 4 = quantLinear codes
  * (int8 [O, I] two's-complement bytes, or int4 packed [O, I/2] with element
  * 2c in the high nibble of byte c and element 2c+1 in the low nibble, each
  * stored as code + 8, model/moe.go:190-217) plus group-32 scales [O, I/32].  The router (gate) and sharedGate stay float32.

@@ -104,7 +104,10 @@ static int build_set(Allocs &al, int bits, int K, int rows_per_group, int groups
     for (int i = 0; i < nparts; i++) total_rows += parts[i].rows;
     if (total_rows != (int64_t)rows_per_group * groups)
         return set_error(QGMOE_ERR_INVALID_ARG, "internal: row count mismatch");
-    const size_t row_bytes = bits == 32 ? (size_t)K * 4 : (bits == 8 ? (size_t)K : (size_t)K / 2);
+    const size_t row_bytes = bits == 32   ? (size_t)K * 4
+                             : bits == 16 ? (size_t)K * 2
+                             : bits == 8  ? (size_t)K
+                                          : (size_t)K / 2;
     const cudaMemcpyKind kind = src_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     uint8_t *w = nullptr;
     int rc = al.alloc(reinterpret_cast<void **>(&w), row_bytes * total_rows);
@@ -121,6 +124,7 @@ static int build_set(Allocs &al, int bits, int K, int rows_per_group, int groups
         return QGMOE_OK;
     }
     ws->q = w;
+    if (bits == 16) return QGMOE_OK;  // raw bf16 rows: no scales
     __half *sc = nullptr;
     rc = al.alloc(reinterpret_cast<void **>(&sc), sizeof(__half) * total_rows * (K / QG_GROUP));
     if (rc) return rc;
@@ -592,8 +596,8 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
                          "bad shape H=%d E=%d k=%d I=%d Is=%d (H, I, Is multiples of 32; "
                          "1<=k<=min(E,32); E<=1024)",
                          H, E, k, I, Is);
-    if (bits != 32 && bits != 8 && bits != 4)
-        return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 8 or 4 (got %d)", bits);
+    if (bits != 32 && bits != 16 && bits != 8 && bits != 4)
+        return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 16 (bf16), 8 or 4 (got %d)", bits);
     if (d->router_mode != QGMOE_ROUTER_TOPK && d->router_mode != QGMOE_ROUTER_PREFIX)
         return set_error(QGMOE_ERR_INVALID_ARG, "bad router_mode %d", d->router_mode);
     if (d->scale_dtype != QGMOE_SCALE_F16 && d->scale_dtype != QGMOE_SCALE_F32)
@@ -601,7 +605,7 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
     if (!d->router || (Is > 0 && !d->shared_gate))
         return set_error(QGMOE_ERR_INVALID_ARG, "router / shared_gate pointer missing");
     const int W = d->ep_world > 1 ? d->ep_world : 1;
-    if (W > 1 && (E % W || d->ep_rank < 0 || d->ep_rank >= W || Is > 0 || bits == 32 ||
+    if (W > 1 && (E % W || d->ep_rank < 0 || d->ep_rank >= W || Is > 0 || bits > 8 ||
                   H % 128 || I % 128))
         return set_error(QGMOE_ERR_INVALID_ARG,
                          "expert parallelism needs E %% ep_world == 0, 0 <= ep_rank < ep_world, "

@@ -29,7 +29,7 @@ constexpr int GEMV_NT = 4;     // tokens staged per pass
 // Elements carried by one 16-byte weight chunk.
 template <int BITS>
 struct Chunk {
-    static constexpr int V = BITS == 32 ? 4 : (BITS == 8 ? 16 : 32);
+    static constexpr int V = BITS == 32 ? 4 : BITS == 16 ? 8 : (BITS == 8 ? 16 : 32);
 };
 
 // int8 x4 -> float x4 exactly: bias to unsigned, splice under 2^23, subtract.
@@ -63,6 +63,14 @@ __device__ __forceinline__ void decode_chunk(uint4 raw, float *v) {
         v[1] = __uint_as_float(raw.y);
         v[2] = __uint_as_float(raw.z);
         v[3] = __uint_as_float(raw.w);
+    } else if constexpr (BITS == 16) {
+        // bf16f32 (model/model.go:113-115): the bits as the high half of a float32
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            v[2 * i] = __uint_as_float(w4[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+        }
     } else if constexpr (BITS == 8) {
         i8x4(raw.x, v);
         i8x4(raw.y, v + 4);
@@ -105,7 +113,7 @@ __device__ __forceinline__ void rows_dot(const uint8_t *const (&row_bytes)[NR],
                 sc[r][u] = 1.f;
                 if (c < nchunks) {
                     raw[r][u] = __ldcs(reinterpret_cast<const uint4 *>(row_bytes[r]) + c);  // evict-first
-                    if constexpr (BITS != 32) sc[r][u] = __half2float(row_scales[r][(c * V) / QG_GROUP]);
+                    if constexpr (BITS <= 8) sc[r][u] = __half2float(row_scales[r][(c * V) / QG_GROUP]);
                 }
             }
         }
@@ -187,7 +195,10 @@ k_expert_gemv(ExpertArgs a) {
         const int out_rows = GATEUP ? ws.rows / 2 : ws.rows;
         const int nchunks = K / V;
         const int kpad = ((nchunks + 31) / 32) * 32 * V;
-        const size_t row_bytes = BITS == 32 ? (size_t)K * 4 : (BITS == 8 ? (size_t)K : (size_t)K / 2);
+        const size_t row_bytes = BITS == 32   ? (size_t)K * 4
+                                 : BITS == 16 ? (size_t)K * 2
+                                 : BITS == 8  ? (size_t)K
+                                              : (size_t)K / 2;
         const uint8_t *wbase = BITS == 32 ? reinterpret_cast<const uint8_t *>(ws.w32) : ws.q;
         wbase += (size_t)eidx * ws.rows * row_bytes;
         const __half *sbase = ws.s ? ws.s + (size_t)eidx * ws.rows * (K / QG_GROUP) : nullptr;
@@ -283,14 +294,16 @@ int launch_expert(bool gateup, const ExpertArgs &a, int max_items_groups, cudaSt
     const int bits = a.routed.bits;
     if (gateup) {
         if (bits == 32) return launch_t<32, true>(a, max_items, s);
+        if (bits == 16) return launch_t<16, true>(a, max_items, s);
         if (bits == 8) return launch_t<8, true>(a, max_items, s);
         if (bits == 4) return launch_t<4, true>(a, max_items, s);
     } else {
         if (bits == 32) return launch_t<32, false>(a, max_items, s);
+        if (bits == 16) return launch_t<16, false>(a, max_items, s);
         if (bits == 8) return launch_t<8, false>(a, max_items, s);
         if (bits == 4) return launch_t<4, false>(a, max_items, s);
     }
-    return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 8 or 4 (got %d)", bits);
+    return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 16, 8 or 4 (got %d)", bits);
 }
 
 // out[t, j] = sum_r w[t,r] * d[slot(t,r), j]  (+ sg[t] * d[T*k + t, j]),

@@ -195,3 +195,21 @@ def test_tensor_core_router_flags_activations_beyond_fp16():
         gpu.forward_batch(x)
     ok = gpu.forward_batch(x[:100])  # the CUDA-core router (T < 256) takes it; the error cleared
     assert np.all(np.isfinite(ok[np.arange(100) != 7]))
+
+
+@pytest.mark.parametrize("T", [1, 7, 40])
+@pytest.mark.parametrize("Is", [0, 128])
+def test_bf16_raw_experts(T, Is):
+    """Raw bf16 experts (gateUpRaw / downRaw, bf16matvec, model/moe.go:102-113)
+    on the CUDA-core path against the oracle's f32 arithmetic on the widened
+    weights."""
+    m = O.make_moe(H=256, E=8, k=2, I=128, Is=Is, bits=16, seed=90 + T)
+    x = O.randn(90, T, (T, 256))
+    g = qgmoe.MoeMLP(n_embed=256, n_experts=8, top_k=2, n_moe_mlp=128, n_shared_mlp=Is, bits=16,
+                     router=m.router, shared_gate=m.shared_gate, gate_up_q=m.q["gate_up"],
+                     down_q=m.q["down"], shared_gate_q=m.q.get("sh_gate"),
+                     shared_up_q=m.q.get("sh_up"), shared_down_q=m.q.get("sh_down"))
+    out, idx, w = g.forward_batch(x, return_routing=True)
+    ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
+    flipped = check_routing(idx, w, ridx, rw, probs)
+    check_outputs(out, ref, 32, skip_tokens=flipped)
