@@ -240,7 +240,7 @@ int qgmoe_route_static(const float *x, const float *router, int32_t T, int32_t H
  * device without an intermediate host copy.  Tensor names, with a caller
  * prefix such as "model.layers.3.mlp." (the reference's mlp.* names,
  * model/load.go:415-456):
- *   gate.weight                          F32 [E, H]           router
+ *   gate.weight                          F32 (or BF16) [E, H] router
  *   experts.gate_up_proj.qweight         I8/U8 [E, 2I, H]     int8 codes, or
  *                                        U8 [E, 2I, H/2]      int4 pairs
  *   experts.gate_up_proj.scale           F16/F32 [E, 2I, H/32]
@@ -249,8 +249,13 @@ int qgmoe_route_static(const float *x, const float *router, int32_t T, int32_t H
  *   three or none), [Is, H], [Is, H], [H, Is] as above
  *   shared_expert_gate.weight            F32 [1, H] or [H]    (with the shared expert)
  * int8 vs int4 follows from the code and scale shapes; every tensor must
- * have the same scale dtype.  Safetensors layout: u64 little-endian header
- * size, JSON header {name: {dtype, shape, data_offsets}}, data. */
+ * have the same scale dtype.  Raw (unquantised) layers, as the reference
+ * reads bf16 checkpoints: <base>.weight instead of .qweight / .scale, BF16
+ * (bits 16) or F32 (bits 32) [E, 2I, H] / [E, H, I] / [Is, H] ...; then a
+ * BF16 router or shared-expert gate is widened into a float32 copy the file
+ * handle owns.  One format per layer.  Safetensors layout: u64
+ * little-endian header size, JSON header {name: {dtype, shape,
+ * data_offsets}}, data. */
 typedef struct qgmoe_file qgmoe_file_t;
 #define QGMOE_DT_F32 0
 #define QGMOE_DT_F16 1

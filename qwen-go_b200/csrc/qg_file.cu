@@ -20,6 +20,7 @@
 #include <cstring>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "qg_common.cuh"
 
@@ -36,6 +37,9 @@ struct qgmoe_file {
     const uint8_t *data = nullptr;  // start of the tensor data
     uint64_t data_size = 0;
     std::unordered_map<std::string, Tensor> tensors;
+    // float32 copies of bf16 vectors the descriptor needs as float32 (router,
+    // shared-expert gate), owned by the handle
+    mutable std::unordered_map<std::string, std::vector<float>> widened;
 };
 
 namespace qg {
@@ -296,19 +300,38 @@ const qgmoe_file::Tensor *find(const qgmoe_file *f, const std::string &name) {
     return it == f->tensors.end() ? nullptr : &it->second;
 }
 
-// A quantised linear stack [G, O, K]: codes [.., O, K] (int8) or [.., O, K/2]
-// (int4) and scales [.., O, K/32] with the same leading dimensions.
-struct QuantPair {
-    const void *q = nullptr, *s = nullptr;
+// One linear stack [G, O, K] (G = experts, or absent for a single linear):
+// quantised <base>.qweight (I8/U8 [.., O, K] int8 or U8 [.., O, K/2] int4) +
+// <base>.scale (F16/F32 [.., O, K/32]), or raw <base>.weight (BF16 -> bits
+// 16, F32 -> bits 32; model/load.go:419-449 reads the stacked experts so).
+struct LinStack {
+    const void *w = nullptr, *s = nullptr;
     int bits = 0, sdt = -1;
     int64_t lead = 1, O = 0, K = 0;
 };
 
-int quant_pair(const qgmoe_file *f, const std::string &base, int want_rank, QuantPair &o) {
+int lin_stack(const qgmoe_file *f, const std::string &base, int want_rank, LinStack &o) {
     const auto *q = find(f, base + ".qweight");
+    if (!q) {
+        const auto *w = find(f, base + ".weight");
+        if (!w)
+            return set_error(QGMOE_ERR_INVALID_ARG, "%s.qweight / .weight not in the file",
+                             base.c_str());
+        if (w->rank != want_rank || (w->dtype != QGMOE_DT_BF16 && w->dtype != QGMOE_DT_F32))
+            return set_error(QGMOE_ERR_INVALID_ARG, "%s.weight: BF16 or F32 of rank %d expected",
+                             base.c_str(), want_rank);
+        o.lead = 1;
+        for (int i = 0; i < want_rank - 2; i++) o.lead *= w->shape[i];
+        o.O = w->shape[want_rank - 2];
+        o.K = w->shape[want_rank - 1];
+        o.bits = w->dtype == QGMOE_DT_BF16 ? 16 : 32;
+        o.w = f->data + w->begin;
+        o.s = nullptr;
+        o.sdt = -1;
+        return QGMOE_OK;
+    }
     const auto *s = find(f, base + ".scale");
-    if (!q || !s)
-        return set_error(QGMOE_ERR_INVALID_ARG, "%s.qweight / .scale not in the file", base.c_str());
+    if (!s) return set_error(QGMOE_ERR_INVALID_ARG, "%s.scale not in the file", base.c_str());
     if (q->rank != want_rank || s->rank != want_rank)
         return set_error(QGMOE_ERR_INVALID_ARG, "%s: expected rank %d", base.c_str(), want_rank);
     if (q->dtype != QGMOE_DT_I8 && q->dtype != QGMOE_DT_U8)
@@ -332,10 +355,27 @@ int quant_pair(const qgmoe_file *f, const std::string &base, int want_rank, Quan
                          "%s: codes of width %lld do not match scales for %lld inputs",
                          base.c_str(), (long long)qk, (long long)o.K);
     }
-    o.q = f->data + q->begin;
+    o.w = f->data + q->begin;
     o.s = f->data + s->begin;
     o.sdt = s->dtype == QGMOE_DT_F16 ? QGMOE_SCALE_F16 : QGMOE_SCALE_F32;
     return QGMOE_OK;
+}
+
+// A float32 vector the descriptor needs (router rows, shared-expert gate):
+// F32 in the mapping as is, BF16 widened once into a buffer the handle owns.
+const float *f32_view(const qgmoe_file *f, const std::string &name, const qgmoe_file::Tensor *t) {
+    if (t->dtype == QGMOE_DT_F32) return reinterpret_cast<const float *>(f->data + t->begin);
+    auto &v = f->widened[name];
+    if (v.empty()) {
+        const uint64_t n = (t->end - t->begin) / 2;
+        v.resize(n);
+        const uint8_t *b = f->data + t->begin;
+        for (uint64_t i = 0; i < n; i++) {
+            const uint32_t u = ((uint32_t)b[2 * i] | ((uint32_t)b[2 * i + 1] << 8)) << 16;
+            memcpy(&v[i], &u, 4);
+        }
+    }
+    return v.data();
 }
 
 }  // namespace
@@ -411,12 +451,13 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
     const std::string pre = prefix ? prefix : "";
     const auto *router = find(f, pre + "gate.weight");
     if (!router) return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight not in the file", pre.c_str());
-    if (router->dtype != QGMOE_DT_F32 || router->rank != 2)
-        return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight: F32 [E, H] expected", pre.c_str());
+    if ((router->dtype != QGMOE_DT_F32 && router->dtype != QGMOE_DT_BF16) || router->rank != 2)
+        return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight: F32 or BF16 [E, H] expected",
+                         pre.c_str());
     const int64_t E = router->shape[0], H = router->shape[1];
-    QuantPair gu, dn;
-    int rc = quant_pair(f, pre + "experts.gate_up_proj", 3, gu);
-    if (!rc) rc = quant_pair(f, pre + "experts.down_proj", 3, dn);
+    LinStack gu, dn;
+    int rc = lin_stack(f, pre + "experts.gate_up_proj", 3, gu);
+    if (!rc) rc = lin_stack(f, pre + "experts.down_proj", 3, dn);
     if (rc) return rc;
     const int64_t I = gu.O / 2;
     if (gu.lead != E || gu.O % 2 || gu.K != H || dn.lead != E || dn.O != H || dn.K != I)
@@ -426,17 +467,20 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
                          (long long)dn.lead, (long long)dn.O, (long long)dn.K, (long long)E,
                          (long long)H);
     if (gu.bits != dn.bits || gu.sdt != dn.sdt)
-        return set_error(QGMOE_ERR_INVALID_ARG, "expert stacks differ in bits or scale dtype");
-    memset(d, 0, sizeof(*d));
+        return set_error(QGMOE_ERR_INVALID_ARG, "expert stacks differ in format or scale dtype");
     const bool has_shared = find(f, pre + "shared_expert.gate_proj.qweight") ||
                             find(f, pre + "shared_expert.up_proj.qweight") ||
-                            find(f, pre + "shared_expert.down_proj.qweight");
+                            find(f, pre + "shared_expert.down_proj.qweight") ||
+                            find(f, pre + "shared_expert.gate_proj.weight") ||
+                            find(f, pre + "shared_expert.up_proj.weight") ||
+                            find(f, pre + "shared_expert.down_proj.weight");
+    LinStack sg, su, sd;
     int64_t Is = 0;
+    const float *gate_vec = nullptr;
     if (has_shared) {
-        QuantPair sg, su, sd;
-        rc = quant_pair(f, pre + "shared_expert.gate_proj", 2, sg);
-        if (!rc) rc = quant_pair(f, pre + "shared_expert.up_proj", 2, su);
-        if (!rc) rc = quant_pair(f, pre + "shared_expert.down_proj", 2, sd);
+        rc = lin_stack(f, pre + "shared_expert.gate_proj", 2, sg);
+        if (!rc) rc = lin_stack(f, pre + "shared_expert.up_proj", 2, su);
+        if (!rc) rc = lin_stack(f, pre + "shared_expert.down_proj", 2, sd);
         if (rc) return rc;
         Is = sg.O;
         if (sg.K != H || su.O != Is || su.K != H || sd.O != H || sd.K != Is)
@@ -445,23 +489,19 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
         if (sg.bits != gu.bits || su.bits != gu.bits || sd.bits != gu.bits ||
             sg.sdt != gu.sdt || su.sdt != gu.sdt || sd.sdt != gu.sdt)
             return set_error(QGMOE_ERR_INVALID_ARG,
-                             "shared expert differs from the experts in bits or scale dtype");
-        const auto *gate = find(f, pre + "shared_expert_gate.weight");
-        if (!gate || gate->dtype != QGMOE_DT_F32 ||
+                             "shared expert differs from the experts in format or scale dtype");
+        const std::string gname = pre + "shared_expert_gate.weight";
+        const auto *gate = find(f, gname);
+        if (!gate || (gate->dtype != QGMOE_DT_F32 && gate->dtype != QGMOE_DT_BF16) ||
             (gate->rank == 1 ? gate->shape[0] != H
                              : (gate->rank != 2 || gate->shape[0] != 1 || gate->shape[1] != H)))
-            return set_error(QGMOE_ERR_INVALID_ARG, "%sshared_expert_gate.weight: F32 [1, H] expected",
-                             pre.c_str());
-        d->shared_gate = reinterpret_cast<const float *>(f->data + gate->begin);
-        d->shared_gate_q = static_cast<const uint8_t *>(sg.q);
-        d->shared_gate_scale = sg.s;
-        d->shared_up_q = static_cast<const uint8_t *>(su.q);
-        d->shared_up_scale = su.s;
-        d->shared_down_q = static_cast<const uint8_t *>(sd.q);
-        d->shared_down_scale = sd.s;
+            return set_error(QGMOE_ERR_INVALID_ARG,
+                             "%s: F32 or BF16 [1, H] expected", gname.c_str());
+        gate_vec = f32_view(f, gname, gate);
     }
     if (E > INT32_MAX || H > INT32_MAX || I > INT32_MAX || Is > INT32_MAX)
         return set_error(QGMOE_ERR_INVALID_ARG, "dimensions beyond int32");
+    memset(d, 0, sizeof(*d));
     d->n_embed = (int32_t)H;
     d->n_experts = (int32_t)E;
     d->top_k = top_k;
@@ -469,14 +509,26 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
     d->n_shared_mlp = (int32_t)Is;
     d->bits = gu.bits;
     d->router_mode = router_mode;
-    d->scale_dtype = gu.sdt;
+    d->scale_dtype = gu.sdt >= 0 ? gu.sdt : QGMOE_SCALE_F16;
     d->weights_on_device = 0;
     d->device = device;
-    d->router = reinterpret_cast<const float *>(f->data + router->begin);
-    d->gate_up_q = static_cast<const uint8_t *>(gu.q);
-    d->gate_up_scale = gu.s;
-    d->down_q = static_cast<const uint8_t *>(dn.q);
-    d->down_scale = dn.s;
+    d->router = f32_view(f, pre + "gate.weight", router);
+    d->shared_gate = gate_vec;
+    auto put = [&](const LinStack &l, const float **w32, const uint8_t **q, const void **sc) {
+        if (l.bits == 32) {
+            *w32 = static_cast<const float *>(l.w);
+        } else {
+            *q = static_cast<const uint8_t *>(l.w);  // codes, or bf16 bit patterns (bits 16)
+            *sc = l.s;
+        }
+    };
+    put(gu, &d->gate_up, &d->gate_up_q, &d->gate_up_scale);
+    put(dn, &d->down, &d->down_q, &d->down_scale);
+    if (has_shared) {
+        put(sg, &d->shared_gate_proj, &d->shared_gate_q, &d->shared_gate_scale);
+        put(su, &d->shared_up_proj, &d->shared_up_q, &d->shared_up_scale);
+        put(sd, &d->shared_down_proj, &d->shared_down_q, &d->shared_down_scale);
+    }
     return QGMOE_OK;
 }
 

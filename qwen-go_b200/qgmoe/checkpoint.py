@@ -15,6 +15,11 @@ and fp16 (or f32) group scales under the same mlp.* names:
     <prefix>shared_expert.{gate,up,down}_proj.qweight/.scale   (optional)
     <prefix>shared_expert_gate.weight        F32 [1, H]        (with the shared expert)
 
+save_layer_raw writes a layer with raw stacked experts instead, as the
+reference reads them from bf16 checkpoints (<prefix>experts.gate_up_proj.weight
+BF16 [E, 2I, H], .down_proj.weight BF16 [E, H, I], shared_expert.*.weight);
+qgmoe_file_layer_desc takes either form (bits 16 for BF16, 32 for F32).
+
 Tensor data starts on 64-byte boundaries (the header is space-padded), so
 the mapped tensors are aligned for any element type.
 """
@@ -31,25 +36,31 @@ _DTYPES = {np.dtype(np.float32): "F32", np.dtype(np.float16): "F16", np.dtype(np
 _ALIGN = 64
 
 
-def write_safetensors(path: str, tensors: dict, metadata: dict | None = None) -> None:
+def write_safetensors(path: str, tensors: dict, metadata: dict | None = None,
+                      bf16: set | None = None) -> None:
     """tensors: name -> numpy array (float32/float16/int8/uint8/int32), in
-    the order given; fp16 scales may also come as uint16 bit patterns."""
+    the order given; uint16 arrays are fp16 bit patterns, or bf16 bit
+    patterns for the names in `bf16`."""
     header = {}
     if metadata:
         header["__metadata__"] = {str(k): str(v) for k, v in metadata.items()}
     blobs, off = [], 0
     for name, a in tensors.items():
         a = np.ascontiguousarray(a)
-        if a.dtype == np.uint16:  # fp16 bit patterns
-            a = a.view(np.float16)
-        if a.dtype not in _DTYPES:
+        dt = None
+        if a.dtype == np.uint16:
+            if bf16 and name in bf16:
+                dt = "BF16"
+            else:  # fp16 bit patterns
+                a = a.view(np.float16)
+        if dt is None and a.dtype not in _DTYPES:
             raise TypeError(f"{name}: unsupported dtype {a.dtype}")
         pad = (-off) % _ALIGN
         if pad:
             blobs.append(b"\0" * pad)
             off += pad
         raw = a.tobytes()
-        header[name] = {"dtype": _DTYPES[a.dtype], "shape": list(a.shape),
+        header[name] = {"dtype": dt or _DTYPES[a.dtype], "shape": list(a.shape),
                         "data_offsets": [off, off + len(raw)]}
         blobs.append(raw)
         off += len(raw)
@@ -122,3 +133,45 @@ def save_layer(path: str, prefix: str, *, router, gate_up_q, gate_up_scale, down
             man["quantized"] = list(dict.fromkeys(old.get("quantized", []) + names))
         with open(quant_json, "w") as f:
             json.dump(man, f, indent=1)
+
+
+def save_layer_raw(path: str, prefix: str, *, router, gate_up, down, shared_gate=None,
+                   shared_gate_proj=None, shared_up_proj=None, shared_down_proj=None,
+                   bf16: bool = True, append: dict | None = None,
+                   append_bf16: set | None = None):
+    """One MoE layer with raw (unquantised) stacked experts, as the reference's
+    loader reads them (model/load.go:419-449): <prefix>experts.gate_up_proj.weight
+    [E, 2I, H] and .down_proj.weight [E, H, I] in BF16 (uint16 bit patterns,
+    e.g. from qg_oracle.bf16_bits) or F32, the shared expert's .weight
+    tensors likewise, the router and shared-expert gate in F32 (or BF16 bits
+    when given as uint16).  `append` adds other tensors to the file, those
+    named in `append_bf16` being bf16 bit patterns."""
+    t = dict(append or {})
+    names16 = set(append_bf16 or ())
+
+    def put(name, a):
+        a = np.asarray(a)
+        if bf16 or a.dtype == np.uint16:
+            if a.dtype != np.uint16:
+                raise TypeError(f"{name}: bf16 bit patterns (uint16) expected")
+            names16.add(name)
+        elif a.dtype != np.float32:
+            raise TypeError(f"{name}: float32 expected")
+        t[name] = a
+
+    r = np.asarray(router)
+    t[prefix + "gate.weight"] = r
+    if r.dtype == np.uint16:
+        names16.add(prefix + "gate.weight")
+    E, H = r.shape
+    put(prefix + "experts.gate_up_proj.weight", np.asarray(gate_up).reshape(E, -1, H))
+    put(prefix + "experts.down_proj.weight", np.asarray(down).reshape(E, H, -1))
+    if shared_gate_proj is not None:
+        put(prefix + "shared_expert.gate_proj.weight", shared_gate_proj)
+        put(prefix + "shared_expert.up_proj.weight", shared_up_proj)
+        put(prefix + "shared_expert.down_proj.weight", shared_down_proj)
+        g = np.asarray(shared_gate).reshape(1, H)
+        t[prefix + "shared_expert_gate.weight"] = g
+        if g.dtype == np.uint16:
+            names16.add(prefix + "shared_expert_gate.weight")
+    write_safetensors(path, t, {"format": "pt"}, bf16=names16)

@@ -208,3 +208,91 @@ def test_layer_from_file_matches_layer_from_arrays(tmp_path, bits):
     b = qgmoe.MoeMLP.from_file(path, "model.layers.0.mlp.", top_k=2)
     x = O.randn(11, 9, (24, 128))
     assert np.array_equal(a.forward_batch(x), b.forward_batch(x))
+
+
+@pytest.mark.parametrize("raw", ["bf16", "f32"])
+@pytest.mark.parametrize("Is", [0, 128])
+def test_raw_layers_bf16_and_f32(tmp_path, raw, Is):
+    """Raw stacked experts as the reference reads them (experts.*.weight in
+    BF16 or F32): bits 16 / 32 descriptors pointing into the mapping; a BF16
+    router / shared gate is widened once into a buffer the handle owns."""
+    m = O.make_moe(H=128, E=4, k=2, I=64, Is=Is, bits=16 if raw == "bf16" else 32, seed=6)
+    pre = "model.layers.5.mlp."
+    path = str(tmp_path / "raw.safetensors")
+    if raw == "bf16":
+        router = O.bf16_bits(m.router)  # the router in bf16 too, as in bf16 checkpoints
+        args = dict(router=router, gate_up=m.q["gate_up"], down=m.q["down"])
+        if Is:
+            args.update(shared_gate=O.bf16_bits(m.shared_gate), shared_gate_proj=m.q["sh_gate"],
+                        shared_up_proj=m.q["sh_up"], shared_down_proj=m.q["sh_down"])
+        ck.save_layer_raw(path, pre, bf16=True, **args)
+    else:
+        args = dict(router=m.router, gate_up=m.gate_up, down=m.down)
+        if Is:
+            args.update(shared_gate=m.shared_gate, shared_gate_proj=m.sh_gate,
+                        shared_up_proj=m.sh_up, shared_down_proj=m.sh_down)
+        ck.save_layer_raw(path, pre, bf16=False, **args)
+    hdr = ck.read_header(path)
+    assert hdr[pre + "experts.gate_up_proj.weight"]["dtype"] == ("BF16" if raw == "bf16" else "F32")
+    assert hdr[pre + "experts.gate_up_proj.weight"]["shape"] == [4, 128, 128]
+    with qgmoe.LayerFile(path) as f:
+        d = f.layer_desc(pre, 2)
+        assert (d.n_embed, d.n_experts, d.n_moe_mlp, d.n_shared_mlp) == (128, 4, 64, Is)
+        if raw == "bf16":
+            assert d.bits == 16 and not d.gate_up and not d.down
+            assert _bytes(d.gate_up_q, m.q["gate_up"]) and _bytes(d.down_q, m.q["down"])
+            assert not d.gate_up_scale and not d.down_scale
+            assert _bytes(d.router, O.bf16_widen(O.bf16_bits(m.router)))
+            if Is:
+                assert _bytes(d.shared_gate_q, m.q["sh_gate"])
+                assert _bytes(d.shared_down_q, m.q["sh_down"])
+                assert _bytes(d.shared_gate, O.bf16_widen(O.bf16_bits(m.shared_gate)))
+        else:
+            assert d.bits == 32 and not d.gate_up_q
+            assert _bytes(d.gate_up, m.gate_up) and _bytes(d.down, m.down)
+            assert _bytes(d.router, m.router)
+            if Is:
+                assert _bytes(d.shared_up_proj, m.sh_up) and _bytes(d.shared_gate, m.shared_gate)
+        # the descriptor is stable across calls (the widened copies are reused)
+        d2 = f.layer_desc(pre, 2)
+        assert d2.router == d.router and d2.gate_up_q == d.gate_up_q
+
+
+def test_raw_and_quantised_stacks_do_not_mix(tmp_path):
+    m8 = _layer(8, 0)
+    p = _save(tmp_path, m8)
+    hdr = ck.read_header(p)
+    with open(p, "rb") as fh:
+        n = struct.unpack("<Q", fh.read(8))[0]
+        data = fh.read()[n:]
+    arrays = {}
+    for name, t in hdr.items():
+        if name != "__metadata__":
+            dt = {"F32": np.float32, "F16": np.float16, "I8": np.int8, "U8": np.uint8}[t["dtype"]]
+            b0, b1 = t["data_offsets"]
+            arrays[name] = np.frombuffer(data[b0:b1], dt).reshape(t["shape"])
+    pre = "model.layers.0.mlp."
+    # down as raw bf16 next to int8 gate_up codes
+    del arrays[pre + "experts.down_proj.qweight"], arrays[pre + "experts.down_proj.scale"]
+    arrays[pre + "experts.down_proj.weight"] = np.zeros((4, 128, 64), np.uint16)
+    q = str(tmp_path / "mixed.safetensors")
+    ck.write_safetensors(q, arrays, bf16={pre + "experts.down_proj.weight"})
+    with qgmoe.LayerFile(q) as f:
+        with pytest.raises(qgmoe.QgmoeError):
+            f.layer_desc(pre, 2)
+
+
+@pytest.mark.gpu
+def test_bf16_layer_from_file_matches_layer_from_arrays(tmp_path):
+    m = O.make_moe(H=128, E=4, k=2, I=64, Is=128, bits=16, seed=12)
+    path = str(tmp_path / "raw.safetensors")
+    ck.save_layer_raw(path, "mlp.", router=m.router, gate_up=m.q["gate_up"], down=m.q["down"],
+                      shared_gate=m.shared_gate, shared_gate_proj=m.q["sh_gate"],
+                      shared_up_proj=m.q["sh_up"], shared_down_proj=m.q["sh_down"])
+    a = qgmoe.MoeMLP(n_embed=128, n_experts=4, top_k=2, n_moe_mlp=64, n_shared_mlp=128, bits=16,
+                     router=m.router, shared_gate=m.shared_gate, gate_up_q=m.q["gate_up"],
+                     down_q=m.q["down"], shared_gate_q=m.q["sh_gate"], shared_up_q=m.q["sh_up"],
+                     shared_down_q=m.q["sh_down"])
+    b = qgmoe.MoeMLP.from_file(path, "mlp.", top_k=2)
+    x = O.randn(12, 9, (16, 128))
+    assert np.array_equal(a.forward_batch(x), b.forward_batch(x))
