@@ -135,3 +135,114 @@ def test_balanced_placement_is_a_permutation_and_evens_the_load():
     lb = max(load.sum() / W, load.max() + np.sort(load)[:G - 1].sum())
     assert per_rank.max() <= 1.01 * lb
     assert rr_rank.max() > 1.2 * per_rank.max()
+
+
+# --------------------------------------------------------------------------
+# The peer-memory exchange's index arithmetic (qwen-go_b200/csrc/qg_peer.cu),
+# restated: where k_px_send stores each row in its owner's grouped buffer,
+# and the (source, send position) k_px_tables maps each received row back to.
+# --------------------------------------------------------------------------
+
+
+def _px_send_positions(cnt, me):
+    """k_px_send: position at owner d of source `me`'s rows for d's local
+    expert g -- the rows of d's experts before g (all sources), then those of
+    the sources before `me` in d's order d, d+1, ..., d-1 (mod W)."""
+    W, _, G = cnt.shape
+    pos = np.zeros((W, G), np.int64)
+    for d in range(W):
+        for g in range(G):
+            p = int(cnt[:, d, :g].sum())
+            s = d
+            while s != me:
+                p += int(cnt[s, d, g])
+                s = (s + 1) % W
+            pos[d, g] = p
+    return pos
+
+
+def _px_out_map(cnt, me):
+    """k_px_tables at owner `me`: for each grouped row, (source, position of
+    the row in that source's send order)."""
+    W, _, G = cnt.shape
+    gbase = np.concatenate([[0], np.cumsum(cnt[:, me, :].sum(axis=0))])
+    seg = np.zeros((G, W), np.int64)
+    dst0 = np.zeros((G, W), np.int64)
+    for g in range(G):
+        for j in range(W):
+            s = (me + j) % W
+            r = int(gbase[g])
+            s2 = me
+            while s2 != s:
+                r += int(cnt[s2, me, g])
+                s2 = (s2 + 1) % W
+            seg[g, j] = r
+            dst0[g, j] = int(cnt[s, :me, :].sum()) + int(cnt[s, me, :g].sum())
+    out = []
+    for r in range(int(gbase[-1])):
+        g = int(np.searchsorted(gbase, r, side="right") - 1)
+        j = W - 1
+        while j > 0 and seg[g, j] > r:
+            j -= 1
+        s = (me + j) % W
+        out.append((s, int(dst0[g, j] + r - seg[g, j])))
+    return out
+
+
+@pytest.mark.parametrize("W_", [2, 3, 4, 8])
+def test_peer_exchange_positions_are_a_bijection(W_):
+    """Every source row lands in exactly one slot of its owner's grouped
+    buffer, the rows of one local expert are contiguous, and the owner's map
+    sends each output back to the source position it came from -- for random
+    (and some empty) count matrices at 2-8 ranks."""
+    rng = np.random.default_rng(W_)
+    G = 5
+    for trial in range(6):
+        cnt = rng.integers(0, 7, size=(W_, W_, G))
+        if trial == 1:
+            cnt[:, :, 2] = 0          # an expert nobody routes to
+        if trial == 2:
+            cnt[1 % W_] = 0           # a source with no tokens
+        for d in range(W_):
+            owner_rows = {}
+            for me in range(W_):
+                pos = _px_send_positions(cnt, me)
+                # source me's send order: keys (d, g) d-major, rows in order
+                p = 0
+                for dd in range(W_):
+                    for g in range(G):
+                        for jj in range(int(cnt[me, dd, g])):
+                            if dd == d:
+                                r = int(pos[d, g]) + jj
+                                assert r not in owner_rows
+                                owner_rows[r] = (me, p, g)
+                            p += 1
+            R = int(cnt[:, d, :].sum())
+            assert sorted(owner_rows) == list(range(R))
+            gbase = np.concatenate([[0], np.cumsum(cnt[:, d, :].sum(axis=0))])
+            for r, (_, _, g) in owner_rows.items():
+                assert gbase[g] <= r < gbase[g + 1]
+            back = _px_out_map(cnt, d)
+            for r in range(R):
+                assert back[r] == owner_rows[r][:2], (W_, trial, d, r)
+
+
+@pytest.mark.parametrize("W_", [2, 3, 8])
+@pytest.mark.parametrize("nw", [8, 13, 64, 4736])
+def test_peer_send_warps_cover_every_row_once(W_, nw):
+    """k_px_send's warp split: warp wg sends to rank (me + wg % W) % W the
+    rows wg / W, wg / W + nwd, ... of that destination, nwd the number of
+    warps with that slot; together the warps cover each row exactly once."""
+    rng = np.random.default_rng(nw + W_)
+    if nw < W_:
+        return  # the launcher gives at least one warp per destination
+    rows = rng.integers(0, 50, size=W_)
+    for me in range(W_):
+        seen = [np.zeros(n, np.int64) for n in rows]
+        for wg in range(nw):
+            j = wg % W_
+            d = (me + j) % W_
+            wi, nwd = wg // W_, (nw - j + W_ - 1) // W_
+            for p in range(wi, int(rows[d]), nwd):
+                seen[d][p] += 1
+        assert all(np.all(s == 1) for s in seen)
