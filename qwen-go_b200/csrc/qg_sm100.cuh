@@ -166,7 +166,8 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // One 64-wide k block as four K=16 MMAs in a single asm block: A in TMEM at
-// columns a, a+8, a+16, a+24; B at descriptor b advanced by 32 bytes (2 in
+// columns a, a+8, a+16, a+24 (each an M x 16 slice: row i in TMEM lane i,
+// its 16 K elements packed two per 32-bit column); B at descriptor b advanced by 32 bytes (2 in
 // the descriptor's 16-byte address units) per step.  The first MMA
 // accumulates only if `accumulate`; the other three always do.  Few
 // instructions per MMA: the issuing thread shares its scheduler with busy
