@@ -75,3 +75,37 @@ def test_device_ok_is_false_without_gpu():
     if torch.cuda.is_available():
         pytest.skip("GPU present")
     assert qgmoe.lib().qgmoe_device_ok(0) == 0
+
+
+def test_plain_c_host_uses_the_abi(tmp_path):
+    """include/qgmoe.h compiles as C99 (what cgo sees) and a C host can map a
+    layer file and build its descriptor through the library; create() then
+    answers without a GPU (no sm_100 device) or with one."""
+    import shutil
+    import subprocess
+
+    import numpy as np
+    import qg_oracle as O
+    from qgmoe import checkpoint as ck
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    build()
+    exe = str(tmp_path / "abi_host")
+    src = os.path.join(REPO, "tests", "c", "abi_host.c")
+    libdir = os.path.dirname(LIB)
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-pedantic", "-I",
+                    os.path.join(REPO, "include"), src, "-o", exe, "-L", libdir, "-lqgmoe",
+                    "-Wl,-rpath," + libdir], check=True)
+    m = O.make_moe(H=128, E=4, k=2, I=64, Is=0, bits=4, seed=3)
+    path = str(tmp_path / "l.safetensors")
+    ck.save_layer(path, "model.layers.7.mlp.", router=m.router, gate_up_q=m.q["gate_up"],
+                  gate_up_scale=m.s16["gate_up"], down_q=m.q["down"],
+                  down_scale=m.s16["down"], bits=4)
+    out = subprocess.run([exe, path, "model.layers.7.mlp.", "2"], capture_output=True, text=True,
+                         check=True).stdout
+    assert "router rc=0 dtype=0 rank=2 shape=4,128 bytes=2048" in out
+    assert "desc rc=0 H=128 E=4 k=2 I=64 Is=0 bits=4 scale=0" in out
+    rc = int(out.split("create rc=")[1].split()[0])
+    assert rc in (0, -7), out  # OK on a B200, QGMOE_ERR_NO_DEVICE without one
