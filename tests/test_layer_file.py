@@ -296,3 +296,40 @@ def test_bf16_layer_from_file_matches_layer_from_arrays(tmp_path):
     b = qgmoe.MoeMLP.from_file(path, "mlp.", top_k=2)
     x = O.randn(12, 9, (16, 128))
     assert np.array_equal(a.forward_batch(x), b.forward_batch(x))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("Is", [0, 128])
+def test_quantize_layer_tool(tmp_path, bits, Is):
+    """qgmoe.quantize_layer: raw bf16 layer in, quantised layer out, codes and
+    scales exactly those of quantizeInt8/Int4 on the widened weights (the
+    quantiser is the oracle's here; the library's GPU quantiser is bit-checked
+    against it in tests/test_gpu_quant.py)."""
+    from qgmoe.quantize_layer import quantize_layer
+    m = O.make_moe(H=128, E=4, k=2, I=64, Is=Is, bits=16, seed=21)
+    pre = "model.layers.2.mlp."
+    src, dst = str(tmp_path / "raw.safetensors"), str(tmp_path / "q.safetensors")
+    args = dict(router=m.router, gate_up=m.q["gate_up"], down=m.q["down"])
+    if Is:
+        args.update(shared_gate=m.shared_gate, shared_gate_proj=m.q["sh_gate"],
+                    shared_up_proj=m.q["sh_up"], shared_down_proj=m.q["sh_down"])
+    ck.save_layer_raw(src, pre, **args)
+
+    def oracle_quantize(w, b):
+        q, s = O.quantize(np.ascontiguousarray(w, np.float32), b)
+        return q, O.f16_bits(s)
+
+    qj = str(tmp_path / "quant.json")
+    quantize_layer(src, dst, pre, bits, quant_json=qj, quantize=oracle_quantize)
+    with qgmoe.LayerFile(dst) as f:
+        d = f.layer_desc(pre, 2)
+        assert d.bits == bits and d.n_shared_mlp == Is and d.scale_dtype == qgmoe.SCALE_F16
+        q_gu, s_gu = oracle_quantize(O.bf16_widen(m.q["gate_up"]).reshape(-1, 128), bits)
+        assert _bytes(d.gate_up_q, q_gu) and _bytes(d.gate_up_scale, s_gu)
+        q_dn, s_dn = oracle_quantize(O.bf16_widen(m.q["down"]).reshape(4 * 128, -1), bits)
+        assert _bytes(d.down_q, q_dn) and _bytes(d.down_scale, s_dn)
+        assert _bytes(d.router, m.router)
+        if Is:
+            q_sd, s_sd = oracle_quantize(O.bf16_widen(m.q["sh_down"]), bits)
+            assert _bytes(d.shared_down_q, q_sd) and _bytes(d.shared_down_scale, s_sd)
+    assert json.load(open(qj))["bits"] == bits
