@@ -213,3 +213,21 @@ def test_bf16_raw_experts(T, Is):
     ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
     flipped = check_routing(idx, w, ridx, rw, probs)
     check_outputs(out, ref, 32, skip_tokens=flipped)
+
+
+def test_committed_golden_vectors():
+    """The library against tests/golden/moe_small.npz (oracle outputs committed
+    with tests/golden/make_golden.py): 16 small layers, bits 32/16/8/4, both
+    router modes, with and without the shared expert."""
+    import importlib.util
+    import os
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    g = np.load(os.path.join(here, "moe_small.npz"))
+    for i, (bits, mode, Is) in enumerate(mg.CASES):
+        m, x = mg.case_arrays(i, bits, mode, Is)
+        out, idx, w = make_gpu_moe(m, mode).forward_batch(x, return_routing=True)
+        flipped = check_routing(idx, w, g[f"c{i}_idx"], g[f"c{i}_w"], g[f"c{i}_probs"])
+        check_outputs(out, g[f"c{i}_out"], 32 if bits == 16 else bits, skip_tokens=flipped)

@@ -299,3 +299,22 @@ def test_bf16_rounding_known_answers():
     h = np.arange(0, 1 << 16, 97, dtype=np.uint32).astype(np.uint16)
     finite = np.isfinite(O.bf16_widen(h))
     assert np.array_equal(O.bf16_bits(O.bf16_widen(h))[finite], h[finite])
+
+
+def test_oracle_reproduces_committed_golden_vectors():
+    """tests/golden/moe_small.npz (written by tests/golden/make_golden.py):
+    16 small layers (bits 32/16/8/4, both router modes, with and without the
+    shared expert) must come out bit for bit as committed."""
+    import importlib.util
+    import os
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    spec = importlib.util.spec_from_file_location("make_golden", os.path.join(here, "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    g = np.load(os.path.join(here, "moe_small.npz"))
+    assert [tuple(c) for c in g["cases"]] == [tuple(c) for c in mg.CASES]
+    for i, (bits, mode, Is) in enumerate(mg.CASES):
+        m, x = mg.case_arrays(i, bits, mode, Is)
+        y, idx, w, _, _ = O.moe_forward(m, x, mode)
+        assert np.array_equal(y, g[f"c{i}_out"]), i
+        assert np.array_equal(idx, g[f"c{i}_idx"]) and np.array_equal(w, g[f"c{i}_w"]), i
