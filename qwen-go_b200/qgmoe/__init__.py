@@ -10,9 +10,11 @@ module exposes the same objects over the C ABI in include/qgmoe.h:
     MoeMLP.forward_batch(x)             x [T, H]   -> out [T, H]   (batched)
     MoeMLP.forward_device(x, out, ...)  torch CUDA tensors, async on a stream
     QuantLinear(bits, q, scale).forward(x) / .dequantize()
+    QuantLinear.set_path(PATH_TENSOR)   prefill-sized projections on the tensor cores
     quantize_int8(w) / quantize_int4(w) -> (codes, scales)  on the GPU
-    MoeMLP.from_file(path, prefix, top_k)  a quantised layer from a safetensors
-                                        file (qgmoe.checkpoint writes them)
+    MoeMLP.from_file(path, prefix, top_k)  a layer from a safetensors file
+    LayerFile(path).tensor(name) / .layer_desc(prefix, top_k)   the mapped file
+    qgmoe.checkpoint.save_layer / save_layer_raw, python -m qgmoe.quantize_layer
 
 Every call goes to the CUDA library; there is no CPU fallback.  A failing
 status raises QgmoeError with the library's message.
@@ -169,6 +171,8 @@ class MoeMLP:
                shared_down_proj [H,Is] float32;
       bits 8/4: the same tensors as quantLinear codes (uint8) with group-32
                scales (fp16 bits as uint16, or float32 with scale_dtype=F32).
+    bits 16: raw bf16 experts (gateUpRaw / downRaw) as uint16 bit patterns in
+               the *_q arguments, no scales.
     Arrays may be numpy (host) or torch CUDA tensors (device); create()
     copies them.
     """
