@@ -458,6 +458,17 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def dtype_label(cfg, layer):
+    """The arithmetic the timed expert products run in: the tensor path
+    multiplies fp16 activations by fp16 dequantised weights into f32
+    accumulators (f32 in, f32 out); the router and the CUDA-core path are
+    f32 throughout."""
+    if cfg["bits"] in (8, 4):
+        return (f"fp16 tensor-core operands (activations, int{cfg['bits']} weights dequantised to "
+                f"fp16), f32 accumulate, f32 I/O; f32 router")
+    return "f32"
+
+
 def config_json(cfg, world):
     wb = weight_bytes(cfg)
     return {"workload": cfg["desc"], "H": cfg["H"], "E": cfg["E"], "top_k": cfg["k"],
@@ -602,8 +613,7 @@ def run_ours(args, cfg):
             "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 activations, int%d weights" % cfg["bits"]
-            if cfg["bits"] != 32 else "f32", "data": "synthetic", "config": cfgj,
+            "vs_baseline": None, "dtype": dtype_label(cfg, layer), "data": "synthetic", "config": cfgj,
             "stage_ms": stages, "forward_ms_device": forward_ms,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": layer.last_launch_count() * args.steps,
@@ -743,7 +753,7 @@ def run_ep(args, cfg, world, rank, local):
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 activations, int%d weights" % cfg["bits"], "data": "synthetic",
+            "dtype": dtype_label(cfg, None), "data": "synthetic",
             "config": cfgj, "stage_ms_rank0": stages, "stage_ms_min_max_over_ranks": stage_range,
             "roofline": roof, "cpu_baseline": None,
             "e2e": e2e, "gpu_launches": (layer.last_launch_count() if peer else 4 + 3 + 1)

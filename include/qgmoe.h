@@ -56,13 +56,27 @@ extern "C" {
 typedef struct qgmoe qgmoe_t;
 
 /* Weights of one moeMLP (model/moe.go:10-25).  Layouts are the reference's:
- * rows are (out, in), row-major.  bits selects the expert + shared-expert
- * weight format: 32 = float32 (gateUpW/downW), 16 = raw bf16 (gateUpRaw /
- * downRaw, model/moe.go:14-15, 102-113: the *_q pointers hold the bf16 bit
- * patterns, 2 bytes per element, no scales; CUDA-core path), 8 or 4 = quantLinear codes
- * (int8 [O, I] two's-complement bytes, or int4 packed [O, I/2] with element
- * 2c in the high nibble of byte c and element 2c+1 in the low nibble, each
- * stored as code + 8, model/moe.go:190-217) plus group-32 scales [O, I/32].  The router (gate) and sharedGate stay float32.
+ * rows are (out, in), row-major.  A weight group's format is one of
+ *   32  float32 rows (gateUpW / downW, linear.w);
+ *   16  raw bf16 rows (gateUpRaw / downRaw, linear.raw; model/moe.go:14-15,
+ *       102-113, model/model.go:167-176): the *_q pointers hold the bf16 bit
+ *       patterns, 2 bytes per element, no scales;
+ *   8/4 quantLinear codes (int8 [O, I] two's-complement bytes, or int4
+ *       packed [O, I/2] with element 2c in the high nibble of byte c and
+ *       element 2c+1 in the low nibble, each stored as code + 8,
+ *       model/moe.go:190-217) plus group-32 scales [O, I/32] (scale_dtype).
+ * bits is the routed experts' format; shared_bits the shared expert's (0 =
+ * same as bits) and router_bits the router's (0 or 32 = float32 `router`).
+ * The reference mixes them: a quantised router (routerQuant, model/moe.go:16,
+ * installed by model/load.go:651-652) and quantised shared-expert linears
+ * beside bf16 or f32 routed experts -- what cmd/qwen-quant writes for an MoE
+ * model, which quantises only the shared-expert projections
+ * (cmd/qwen-quant/main.go:61-65).  The router is turned into float32 rows at
+ * create time exactly as the reference's dequantize / bf16f32 do
+ * (model/moe.go:134-157, model/model.go:113-115; f32 scales used as given,
+ * the product rounded to nearest), so routing stays bit-exact.  Expert and
+ * shared-expert scales are stored as fp16 on the device (f32 scales rounded
+ * to nearest even).  sharedGate stays float32.
  * All pointers are either host pointers (weights_on_device = 0) or device
  * pointers on `device` (1); create() copies them, the caller keeps
  * ownership of its buffers. */
@@ -72,20 +86,21 @@ typedef struct qgmoe_desc {
     int32_t top_k;        /* k   moeMLP.topK (1..32, <= E) */
     int32_t n_moe_mlp;    /* I   moeMLP.nMoeMlp */
     int32_t n_shared_mlp; /* Is  shared expert width, 0 = none */
-    int32_t bits;         /* 32, 8 or 4 */
+    int32_t bits;         /* routed experts: 32, 16, 8 or 4 */
     int32_t router_mode;  /* QGMOE_ROUTER_* */
     int32_t scale_dtype;  /* QGMOE_SCALE_* for the *_scale arrays */
     int32_t weights_on_device;
     int32_t device;       /* CUDA ordinal that owns the handle */
-    const float *router;        /* [E, H]   mlp.gate.weight */
+    const float *router;        /* [E, H]   mlp.gate.weight (router_bits 0 / 32) */
     const float *shared_gate;   /* [H]      mlp.shared_expert_gate.weight (Is > 0) */
-    /* bits == 32 */
+    /* format 32 */
     const float *gate_up;       /* [E, 2I, H] mlp.experts.gate_up_proj (gate rows 0..I-1) */
     const float *down;          /* [E, H, I]  mlp.experts.down_proj */
     const float *shared_gate_proj; /* [Is, H] */
     const float *shared_up_proj;   /* [Is, H] */
     const float *shared_down_proj; /* [H, Is] */
-    /* bits == 8 / 4: codes and scales, same tensors quantised row-wise */
+    /* formats 16 / 8 / 4: bf16 bits, or codes and scales of the same
+     * tensors quantised row-wise */
     const uint8_t *gate_up_q;
     const void *gate_up_scale;
     const uint8_t *down_q;
@@ -107,6 +122,12 @@ typedef struct qgmoe_desc {
      * every rank (e.g. balanced by measured expert load).  NULL = round-robin:
      * expert e on rank e % W, local index e / W. */
     const int32_t *ep_slot;
+    /* Per-group formats (see above).  router_q: bf16 bits [E, H] (16) or
+     * codes (8 / 4) of mlp.gate, router_scale its group-32 scales. */
+    int32_t router_bits;
+    const void *router_q;
+    const void *router_scale;
+    int32_t shared_bits;
 } qgmoe_desc;
 
 /* Uploads the weights (device copies owned by the handle). */
@@ -217,20 +238,27 @@ const char *qgmoe_stage_name(const qgmoe_t *h, int32_t i);
  * device allocation itself, a stream-capture region in which allocation is
  * not permitted, or a serving loop whose memory budget is fixed at start-up
  * -- this runs the router step (logits, softmax, top-k and renormalised
- * weights, the same kernels qgmoe_forward uses) with all of its scratch in
- * one static device array of QGMOE_ROUTE_STATIC_SCRATCH bytes, which every
- * GPU that loads this library holds until the process exits.  x [T, H] f32,
- * router [E, H] f32 and the outputs sel_idx / sel_w [T, k] are DEVICE
- * pointers on the calling thread's current device; the work is enqueued on
+ * weights: the kernels and the exact routing of qgmoe_forward's router) with
+ * all of its scratch in one static device array of
+ * QGMOE_ROUTE_STATIC_SCRATCH bytes, which every GPU that loads this library
+ * holds until the process exits.  x [T, H] f32, router [E, H] f32 and the
+ * outputs sel_idx / sel_w [T, k] are DEVICE pointers on the calling thread's
+ * current device (x and router 16-byte aligned); the work is enqueued on
  * `stream` (a cudaStream_t, NULL = legacy default stream) and the call
- * returns.  A size whose scratch would not fit the array is rejected with
- * QGMOE_ERR_INVALID_ARG.  The first call on a device resolves the array's
- * device address; make that first call before any stream capture.  All
- * calls on a device share the array: calls that overlap on the GPU race, so
- * order them on one stream. */
+ * returns.  flags (optional, a DEVICE int32) receives the call's device
+ * error word once the work has run: 0, or 1 (an expert id out of range) / 2
+ * (a dispatch slot out of range), which only a corrupted call can raise;
+ * NaN or infinite activations are not errors -- they route as the reference
+ * does (experts 0..k-1 with NaN weights).  A size whose scratch would not
+ * fit the array is rejected with QGMOE_ERR_INVALID_ARG.  The first call on a
+ * device loads the library's device code there; make that first call before
+ * any stream capture.  All calls on a device share the array and it keeps
+ * the previous call's contents (the counters are cleared by each call):
+ * calls that overlap on the GPU race, so order them on one stream. */
 #define QGMOE_ROUTE_STATIC_SCRATCH (8 << 20)
 int qgmoe_route_static(const float *x, const float *router, int32_t T, int32_t H, int32_t E,
-                       int32_t k, int32_t mode, int32_t *sel_idx, float *sel_w, void *stream);
+                       int32_t k, int32_t mode, int32_t *sel_idx, float *sel_w, int32_t *flags,
+                       void *stream);
 
 /* ---- on-disk quantised MoE layers --------------------------------------
  * The reference's quantised checkpoint convention (quant.json + safetensors

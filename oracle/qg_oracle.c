@@ -262,14 +262,17 @@ typedef struct {
 
 typedef struct {
     int n_embed, n_experts, top_k, n_moe_mlp, n_shared_mlp;
-    int bits;         /* 32, 8, 4: experts and shared expert */
+    int bits;         /* 32, 8, 4: routed experts */
     int router_mode;  /* QGO_ROUTER_TOPK / QGO_ROUTER_PREFIX */
-    const float *router;       /* [E, H] f32 (moeMLP.gate) */
+    const float *router;       /* [E, H] f32 (moeMLP.gate), router_bits 32 */
     const float *shared_gate;  /* [H] (moeMLP.sharedGate), used when n_shared_mlp > 0 */
     qgo_lin gate_up;           /* stacked [E, 2I, H] */
     qgo_lin down;              /* stacked [E, H, I] */
     qgo_lin sh_gate, sh_up;    /* [Is, H] */
     qgo_lin sh_down;           /* [H, Is] */
+    int shared_bits;           /* 32, 8, 4: the shared expert's format */
+    int router_bits;           /* 32: router rows; 8 / 4: routerQuant (moe.go:16) */
+    qgo_lin router_q;          /* router_bits 8 / 4: codes + scales */
 } qgo_moe;
 
 /* proj(x, 1, ...) on one row block of a stacked tensor (model.go:196-205;
@@ -323,7 +326,14 @@ static void qg_moe_token(const qgo_moe *m, const float *x, float *out, int32_t *
     const int H = m->n_embed, E = m->n_experts, K = m->top_k, I = m->n_moe_mlp;
     const int Is = m->n_shared_mlp;
     float *logits = (float *)malloc(sizeof(float) * E);
-    qgo_matmul_vec(x, m->router, H, E, logits); /* proj(x,1,&m.gate,...) moe.go:42 */
+    float *rscratch = m->router_bits == 32 ? NULL : (float *)malloc(sizeof(float) * (size_t)E * H);
+    /* proj(x, 1, &m.gate, m.routerQuant, E), moe.go:42 and model.go:196-205:
+     * the router rows, or quantLinear.forward = dequantize, then matmulVec */
+    if (m->router_bits == 32)
+        qgo_matmul_vec(x, m->router, H, E, logits);
+    else
+        qg_linear_forward(&m->router_q, m->router_bits, 0, E, H, x, logits, rscratch);
+    free(rscratch);
     if (probs_out) {
         memcpy(probs_out, logits, sizeof(float) * E);
         qgo_softmax(probs_out, E);
@@ -358,11 +368,11 @@ static void qg_moe_token(const qgo_moe *m, const float *x, float *out, int32_t *
         float *g = (float *)malloc(sizeof(float) * Is);
         float *u = (float *)malloc(sizeof(float) * Is);
         float *s = (float *)malloc(sizeof(float) * H);
-        qg_linear_forward(&m->sh_gate, m->bits, 0, Is, H, x, g, scratch);
-        qg_linear_forward(&m->sh_up, m->bits, 0, Is, H, x, u, scratch);
+        qg_linear_forward(&m->sh_gate, m->shared_bits, 0, Is, H, x, g, scratch);
+        qg_linear_forward(&m->sh_up, m->shared_bits, 0, Is, H, x, u, scratch);
         qg_silu(g, Is);
         for (int i = 0; i < Is; i++) g[i] *= u[i];
-        qg_linear_forward(&m->sh_down, m->bits, 0, H, Is, g, s, scratch);
+        qg_linear_forward(&m->sh_down, m->shared_bits, 0, H, Is, g, s, scratch);
         /* sigmoid(shared_gate . x), moe.go:87-97 */
         float gd = 0;
         for (int i = 0; i < H; i++) gd += x[i] * m->shared_gate[i];
@@ -396,24 +406,31 @@ void qgo_moe_forward(const qgo_moe *m, const float *x, int T, float *out, int32_
 }
 
 /* Token-parallel variant (NOT the reference's behaviour, which is serial per
- * token): T independent tokens split over n_threads pthreads.  Used only as
- * the labelled all-cores CPU baseline.                                     */
+ * token): T independent tokens split over n_threads pthreads.  Each token's
+ * arithmetic is qg_moe_token's, so the results equal qgo_moe_forward's bit
+ * for bit.  Used as the labelled all-cores CPU baseline and by the tests to
+ * check hundreds of full-size tokens; idx/w/sg/probs may be NULL.          */
 typedef struct {
     const qgo_moe *m;
     const float *x;
     float *out;
+    int32_t *idx;
+    float *w, *sg, *probs;
     int t0, t1;
 } qg_job;
 
 static void *qg_worker(void *arg) {
     qg_job *j = (qg_job *)arg;
-    const int H = j->m->n_embed;
+    const int H = j->m->n_embed, K = j->m->top_k, E = j->m->n_experts;
     for (int t = j->t0; t < j->t1; t++)
-        qg_moe_token(j->m, j->x + (size_t)t * H, j->out + (size_t)t * H, NULL, NULL, NULL, NULL);
+        qg_moe_token(j->m, j->x + (size_t)t * H, j->out + (size_t)t * H,
+                     j->idx ? j->idx + (size_t)t * K : NULL, j->w ? j->w + (size_t)t * K : NULL,
+                     j->sg ? j->sg + t : NULL, j->probs ? j->probs + (size_t)t * E : NULL);
     return NULL;
 }
 
-int qgo_moe_forward_mt(const qgo_moe *m, const float *x, int T, float *out, int n_threads) {
+int qgo_moe_forward_mt(const qgo_moe *m, const float *x, int T, float *out, int32_t *idx,
+                       float *w, float *sg, float *probs, int n_threads) {
     if (n_threads < 1) n_threads = 1;
     if (n_threads > T) n_threads = T > 0 ? T : 1;
     pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * n_threads);
@@ -423,7 +440,7 @@ int qgo_moe_forward_mt(const qgo_moe *m, const float *x, int T, float *out, int 
     for (int i = 0; i < n_threads; i++) {
         int t0 = i * chunk, t1 = t0 + chunk > T ? T : t0 + chunk;
         if (t0 >= t1) break;
-        jobs[i] = (qg_job){m, x, out, t0, t1};
+        jobs[i] = (qg_job){m, x, out, idx, w, sg, probs, t0, t1};
         if (pthread_create(&th[i], NULL, qg_worker, &jobs[i]) != 0) {
             qg_worker(&jobs[i]);
             th[i] = 0;

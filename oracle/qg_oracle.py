@@ -41,6 +41,7 @@ class _Moe(C.Structure):
         ("router_mode", C.c_int),
         ("router", _f32p), ("shared_gate", _f32p),
         ("gate_up", _Lin), ("down", _Lin), ("sh_gate", _Lin), ("sh_up", _Lin), ("sh_down", _Lin),
+        ("shared_bits", C.c_int), ("router_bits", C.c_int), ("router_q", _Lin),
     ]
 
 
@@ -69,7 +70,8 @@ def lib():
         L.qgo_route_token.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, _i32p, _f32p]
         L.qgo_moe_forward.argtypes = [C.POINTER(_Moe), _f32p, C.c_int, _f32p, _i32p, _f32p,
                                       _f32p, _f32p]
-        L.qgo_moe_forward_mt.argtypes = [C.POINTER(_Moe), _f32p, C.c_int, _f32p, C.c_int]
+        L.qgo_moe_forward_mt.argtypes = [C.POINTER(_Moe), _f32p, C.c_int, _f32p, _i32p, _f32p,
+                                         _f32p, _f32p, C.c_int]
         L.qgo_moe_forward_mt.restype = C.c_int
         L.qgo_f16_encode.argtypes = [_f32p, C.c_int64, _u16p]
         L.qgo_f16_decode.argtypes = [_u16p, C.c_int64, _f32p]
@@ -181,8 +183,14 @@ class MoeWeights:
              matmulVec (model/tensors.go:77-89) over those widened values, so
              the oracle runs the bits-32 arithmetic on them.
     bits 8/4: the same tensors as quantLinear codes + f32 scale arrays; the
-    scale arrays here are what the dequantiser multiplies by (already
-    rounded to fp16 when the fp16-scale format is modelled).
+    scale arrays here are what the dequantiser multiplies by (rounded to
+    fp16: the library stores expert and shared-expert scales as fp16).
+    shared_bits (0 = bits): the shared expert's own format.  router_bits:
+    32 = float32 rows in `router`; 16 = bf16 bits in q["router"] (router
+    holds their widening); 8 / 4 = routerQuant (model/moe.go:16) codes in
+    q["router"] with scales s["router"] as dequantised (router holds the
+    dequantised rows), s16 / s32 the fp16 bits / raw f32 scales handed to
+    the library.
     """
     H: int
     E: int
@@ -200,63 +208,90 @@ class MoeWeights:
     q: dict = field(default_factory=dict)   # name -> codes
     s: dict = field(default_factory=dict)   # name -> f32 scales (as dequantised)
     s16: dict = field(default_factory=dict)  # name -> fp16 bits of the scales
+    s32: dict = field(default_factory=dict)  # name -> raw f32 scales (router, f32 format)
+    shared_bits: int = 0
+    router_bits: int = 32
 
 
-def make_moe(H, E, k, I, Is, bits, seed, std=0.02, scale_f16=True) -> MoeWeights:
+def make_moe(H, E, k, I, Is, bits, seed, std=0.02, shared_bits=0, router_bits=32,
+             router_scale_f32=False) -> MoeWeights:
     """Synthetic layer: draws router, gate_up, down, shared_gate, shared
-    gate/up/down from streams 0..6 of `seed` (N(0, std)), then quantises."""
+    gate/up/down from streams 0..6 of `seed` (N(0, std)), then puts each
+    group in its format: the routed experts in `bits`, the shared expert in
+    `shared_bits` (0 = bits), the router in `router_bits` (32 = f32 rows;
+    with router_scale_f32 a quantised router keeps its f32 scales, as
+    cmd/qwen-quant writes them)."""
     m = MoeWeights(H=H, E=E, k=k, I=I, Is=Is, bits=bits,
-                   router=randn(seed, 0, (E, H), std))
+                   router=randn(seed, 0, (E, H), std), shared_bits=shared_bits,
+                   router_bits=router_bits)
     gate_up = randn(seed, 1, (E, 2 * I, H), std)
     down = randn(seed, 2, (E, H, I), std)
+    mats = {"gate_up": (gate_up, bits), "down": (down, bits)}
     if Is > 0:
         m.shared_gate = randn(seed, 3, (H,), std)
-        sh_gate = randn(seed, 4, (Is, H), std)
-        sh_up = randn(seed, 5, (Is, H), std)
-        sh_down = randn(seed, 6, (H, Is), std)
-    if bits == 32:
-        m.gate_up, m.down = gate_up, down
-        if Is > 0:
-            m.sh_gate, m.sh_up, m.sh_down = sh_gate, sh_up, sh_down
-        return m
-    if bits == 16:
-        mats = {"gate_up": gate_up, "down": down}
-        if Is > 0:
-            mats.update(sh_gate=sh_gate, sh_up=sh_up, sh_down=sh_down)
-        for name, w in mats.items():
+        sb = shared_bits or bits
+        mats.update(sh_gate=(randn(seed, 4, (Is, H), std), sb),
+                    sh_up=(randn(seed, 5, (Is, H), std), sb),
+                    sh_down=(randn(seed, 6, (H, Is), std), sb))
+    for name, (w, b) in mats.items():
+        if b == 32:
+            setattr(m, name, w)
+        elif b == 16:
             m.q[name] = bf16_bits(w)
             setattr(m, name, bf16_widen(m.q[name]))
-        return m
-    mats = {"gate_up": gate_up.reshape(E * 2 * I, H), "down": down.reshape(E * H, I)}
-    if Is > 0:
-        mats.update(sh_gate=sh_gate, sh_up=sh_up, sh_down=sh_down)
-    for name, w in mats.items():
-        q, s = quantize(w, bits)
-        m.q[name] = q
-        m.s16[name] = f16_bits(s)
-        m.s[name] = f16_round(s) if scale_f16 else s
+        else:
+            q, s = quantize(w.reshape(-1, w.shape[-1]), b)
+            m.q[name] = q
+            m.s16[name] = f16_bits(s)
+            m.s[name] = f16_round(s)
+    if router_bits == 16:
+        m.q["router"] = bf16_bits(m.router)
+        m.router = bf16_widen(m.q["router"])
+    elif router_bits in (8, 4):
+        q, s = quantize(m.router, router_bits)
+        m.q["router"] = q
+        m.s16["router"] = f16_bits(s)
+        m.s32["router"] = s
+        m.s["router"] = s if router_scale_f32 else f16_round(s)
+        m.router = dequantize(router_bits, q, m.s["router"], H)
     return m
 
 
-def _lin(m: MoeWeights, name: str) -> _Lin:
-    if m.bits in (32, 16):
-        return _Lin(_p(getattr(m, name), _f32p), C.cast(None, _u8p), C.cast(None, _f32p))
+def _none_lin() -> _Lin:
+    return _Lin(C.cast(None, _f32p), C.cast(None, _u8p), C.cast(None, _f32p))
+
+
+def _lin(m: MoeWeights, name: str, bits: int) -> _Lin:
+    if bits in (32, 16):
+        w = getattr(m, name)
+        return _none_lin() if w is None else _Lin(_p(w, _f32p), C.cast(None, _u8p),
+                                                  C.cast(None, _f32p))
     if name not in m.q:
-        return _Lin(C.cast(None, _f32p), C.cast(None, _u8p), C.cast(None, _f32p))
+        return _none_lin()
     return _Lin(C.cast(None, _f32p), _p(m.q[name], _u8p), _p(m.s[name], _f32p))
 
 
 def _struct(m: MoeWeights, mode: int) -> _Moe:
+    """bf16 groups run as float32 on their exact widening (bf16matvec and the
+    raw linear are matmulVec over bf16f32 values)."""
     st = _Moe()
+    sb = m.shared_bits or m.bits
     st.n_embed, st.n_experts, st.top_k, st.n_moe_mlp = m.H, m.E, m.k, m.I
-    st.n_shared_mlp, st.bits, st.router_mode = m.Is, 32 if m.bits == 16 else m.bits, mode
+    st.n_shared_mlp, st.router_mode = m.Is, mode
+    st.bits = 32 if m.bits == 16 else m.bits
+    st.shared_bits = 32 if sb == 16 else sb
     st.router = _p(m.router, _f32p)
     st.shared_gate = _p(m.shared_gate, _f32p)
-    for name in ("gate_up", "down", "sh_gate", "sh_up", "sh_down"):
-        if m.bits in (32, 16) and getattr(m, name) is None:
-            setattr(st, name, _Lin(C.cast(None, _f32p), C.cast(None, _u8p), C.cast(None, _f32p)))
-        else:
-            setattr(st, name, _lin(m, name))
+    for name in ("gate_up", "down"):
+        setattr(st, name, _lin(m, name, m.bits))
+    for name in ("sh_gate", "sh_up", "sh_down"):
+        setattr(st, name, _lin(m, name, sb))
+    if m.router_bits in (8, 4):
+        st.router_bits = m.router_bits
+        st.router_q = _lin(m, "router", m.router_bits)
+    else:
+        st.router_bits = 32
+        st.router_q = _none_lin()
     return st
 
 
@@ -276,9 +311,21 @@ def moe_forward(m: MoeWeights, x: np.ndarray, mode: int = ROUTER_TOPK, want_prob
     return out, idx, w, sg, probs
 
 
-def moe_forward_mt(m: MoeWeights, x: np.ndarray, threads: int, mode: int = ROUTER_TOPK):
+def moe_forward_mt(m: MoeWeights, x: np.ndarray, threads: int, mode: int = ROUTER_TOPK,
+                   want_routing: bool = False):
+    """moe_forward over tokens split across `threads` host threads (the same
+    per-token arithmetic, bit-identical results).  Returns out, or (out, idx,
+    w, shared gate, probs) with want_routing."""
     x = np.ascontiguousarray(x, np.float32)
-    out = np.zeros((x.shape[0], m.H), np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, m.H), np.float32)
+    idx = w = sg = probs = None
+    if want_routing:
+        idx = np.zeros((T, m.k), np.int32)
+        w = np.zeros((T, m.k), np.float32)
+        sg = np.zeros(T, np.float32)
+        probs = np.zeros((T, m.E), np.float32)
     st = _struct(m, mode)
-    lib().qgo_moe_forward_mt(C.byref(st), _p(x, _f32p), x.shape[0], _p(out, _f32p), threads)
-    return out
+    lib().qgo_moe_forward_mt(C.byref(st), _p(x, _f32p), T, _p(out, _f32p), _p(idx, _i32p),
+                             _p(w, _f32p), _p(sg, _f32p), _p(probs, _f32p), threads)
+    return (out, idx, w, sg, probs) if want_routing else out

@@ -55,6 +55,9 @@ struct Allocs {
     }
 };
 
+// The kernels read and write activation rows with 16-byte vector accesses.
+static bool misaligned(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; }
+
 static int check_device(int device) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0)
@@ -158,6 +161,7 @@ using namespace qg;
 struct qgmoe {
     int device = 0;
     int H = 0, E = 0, k = 0, I = 0, Is = 0, bits = 0, mode = 0, has_shared = 0;
+    int shared_bits = 0;  // the shared expert's format (may differ from the routed experts')
     cudaStream_t stream = nullptr;
     Allocs weights;
     Allocs work;
@@ -198,7 +202,8 @@ struct qgmoe {
     CUtensorMap tmap_px_recv[4]{}, tmap_px_h[4]{};
     // tensor-core path (qg_umma.cu): UMMA-tiled weight copies, fp16
     // activation buffers and their TMA descriptors
-    bool tensor_ok = false;
+    bool tensor_ok = false;  // routed experts on the tensor cores
+    bool shared_tc = false;  // the shared expert too (else its CUDA-core GEMV)
     int path_mode = QGMOE_PATH_AUTO;
     // CUDA graphs of whole forwards, keyed by (T, x, out, stream): captured on
     // the second identical call, replayed after that (launch latency dominates
@@ -213,17 +218,11 @@ struct qgmoe {
         graph_seen.clear();
     }
     uint8_t *gu_pq = nullptr, *dn_pq = nullptr, *sgu_pq = nullptr, *sdn_pq = nullptr;
-    // router logits on the tensor cores (qg_router_tc.cu): split router rows
-    // at create time, split activations per call (workspace)
     // copy streams of the pipelined host-pointer forward (qgmoe_forward)
     static constexpr int kMaxChunks = 8;
     cudaStream_t h2d = nullptr, d2h = nullptr;
     cudaEvent_t ev_in[kMaxChunks] = {}, ev_out[kMaxChunks] = {};
-    bool rtc_ok = false;
-    RouterTC rtc{};
-    const RouterTC *rtc_for(int T) const {
-        return rtc_ok && T >= RTC_MIN_T && T <= rtc.cap ? &rtc : nullptr;
-    }
+    __half *xh16 = nullptr;  // fp16(x) [cap_T, H], written by the router (tensor path)
     __half *xp16 = nullptr, *h16 = nullptr, *d16 = nullptr;
     // boxes of 256 / 64 / 16 / 128 token rows (the tile sizes)
     CUtensorMap tmap_x[4]{}, tmap_h[4]{}, tmap_hs[4]{};
@@ -285,17 +284,14 @@ static int ensure_capacity(qgmoe *m, int T) {
     {
         const int Ep = m->E + m->has_shared;
         QG_A(st.logits, sizeof(float) * (size_t)cap * Ep);
-        QG_A(st.hist, sizeof(int32_t) * (size_t)((cap + 31) / 32) * m->E);
+        QG_A(st.hist, sizeof(int32_t) * (size_t)((cap + QG_TOPK_TOK - 1) / QG_TOPK_TOK) * m->E);
         QG_A(st.expert_off, sizeof(int32_t) * m->E);
     }
     if (m->tensor_ok) {
+        QG_A(m->xh16, sizeof(__half) * (size_t)cap * m->H);
         QG_A(m->xp16, sizeof(__half) * slots * m->H);
         QG_A(m->h16, sizeof(__half) * slots * m->hmax);
         QG_A(m->d16, sizeof(__half) * slots * m->H);
-    }
-    if (m->rtc_ok && cap >= RTC_MIN_T) {
-        QG_A(m->rtc.xh, sizeof(__half) * (size_t)cap * m->H);
-        QG_A(m->rtc.xl, sizeof(__half) * (size_t)cap * m->H);
     }
     QG_A(m->h, sizeof(float) * slots * m->hmax);
     QG_A(m->d, sizeof(float) * slots * m->H);
@@ -319,54 +315,17 @@ static int ensure_capacity(qgmoe *m, int T) {
                 return rc;
         }
     }
-    m->rtc.cap = 0;
-    if (m->rtc_ok && cap >= RTC_MIN_T) {
-        if ((rc = encode_act_map(&m->rtc.map_xh, m->rtc.xh, cap, m->H, m->H, 256)) ||
-            (rc = encode_act_map(&m->rtc.map_xl, m->rtc.xl, cap, m->H, m->H, 256)))
-            return rc;
-        m->rtc.cap = cap;
-    }
     m->cap_T = cap;
     return QGMOE_OK;
 }
 
-// Tensor-core router: the router rows (and the shared-gate row) split into
-// fp16 heads and tails once.  Rows beyond fp16 range keep the CUDA-core
-// router for this handle.
-static int build_router_tc(qgmoe *m) {
-    if (m->H % 64) return QGMOE_OK;
-    const int Ep = m->E + m->has_shared;
-    const int rows_pad = (Ep + 127) / 128 * 128;
-    Allocs &al = m->weights;
-    __half *wh = nullptr, *wl = nullptr;
-    int rc;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&wh), sizeof(__half) * (size_t)rows_pad * m->H)) ||
-        (rc = al.alloc(reinterpret_cast<void **>(&wl), sizeof(__half) * (size_t)rows_pad * m->H)))
-        return rc;
-    int *flag = nullptr;
-    if ((rc = al.alloc(reinterpret_cast<void **>(&flag), sizeof(int)))) return rc;
-    QG_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), m->stream));
-    if ((rc = launch_split_rows(m->router, m->shared_gate, m->E, Ep, m->H, rows_pad, wh, wl, flag,
-                                m->stream)))
-        return rc;
-    int h_flag = 0;
-    QG_CUDA(cudaMemcpyAsync(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
-    QG_CUDA(cudaStreamSynchronize(m->stream));
-    if (h_flag) return QGMOE_OK;  // router weights beyond fp16 range
-    if ((rc = encode_act_map(&m->rtc.map_wh, wh, rows_pad, m->H, m->H, 128)) ||
-        (rc = encode_act_map(&m->rtc.map_wl, wl, rows_pad, m->H, m->H, 128)))
-        return rc;
-    m->rtc.rows_pad = rows_pad;
-    m->rtc_ok = true;
-    return QGMOE_OK;
-}
-
-// Tensor-core path: int8/int4 weights, H, I (and the shared width) multiples
-// of 128 (128-row weight tiles of 64 gate + 64 up rows, 64-wide K blocks).
+// Tensor-core path: int8/int4 routed experts with H and I multiples of 128
+// (128-row weight tiles of 64 gate + 64 up rows, 64-wide K blocks); the
+// shared expert joins them when it is int8/int4 with a width that is a
+// multiple of 128, else it runs on the CUDA-core GEMV beside them.
 static int build_tensor_weights(qgmoe *m) {
     const int E = m->G, H = m->H, I = m->I, Is = m->Is, bits = m->bits;
-    if (!((bits == 8 || bits == 4) && H % 128 == 0 && I % 128 == 0 && Is % 128 == 0))
-        return QGMOE_OK;
+    if (!((bits == 8 || bits == 4) && H % 128 == 0 && I % 128 == 0)) return QGMOE_OK;
     Allocs &al = m->weights;
     int rc;
     // gate_up tiles: 64 gate rows + the matching 64 up rows; down: 128 rows
@@ -377,15 +336,18 @@ static int build_tensor_weights(qgmoe *m) {
                             m->stream)) ||
         (rc = launch_repack(m->dn.q, m->dn.s, bits, E, H, I, H / 128, 0, 0, m->dn_pq, m->stream)))
         return rc;
-    if (m->has_shared) {  // the shared expert as one more (single-expert) weight set
-        if ((rc = al.alloc(reinterpret_cast<void **>(&m->sgu_pq), packed_bytes(bits, 1, 2 * Is, H))) ||
-            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_pq), packed_bytes(bits, 1, H, Is))))
+    const int sb = m->shared_bits;
+    if (m->has_shared && (sb == 8 || sb == 4) && Is % 128 == 0) {
+        // the shared expert as one more (single-expert) weight set
+        if ((rc = al.alloc(reinterpret_cast<void **>(&m->sgu_pq), packed_bytes(sb, 1, 2 * Is, H))) ||
+            (rc = al.alloc(reinterpret_cast<void **>(&m->sdn_pq), packed_bytes(sb, 1, H, Is))))
             return rc;
-        if ((rc = launch_repack(m->sgu.q, m->sgu.s, bits, 1, 2 * Is, H, Is / 64, 1, Is, m->sgu_pq,
+        if ((rc = launch_repack(m->sgu.q, m->sgu.s, sb, 1, 2 * Is, H, Is / 64, 1, Is, m->sgu_pq,
                                 m->stream)) ||
-            (rc = launch_repack(m->sdn.q, m->sdn.s, bits, 1, H, Is, H / 128, 0, 0, m->sdn_pq,
+            (rc = launch_repack(m->sdn.q, m->sdn.s, sb, 1, H, Is, H / 128, 0, 0, m->sdn_pq,
                                 m->stream)))
             return rc;
+        m->shared_tc = true;
     }
     QG_CUDA(cudaStreamSynchronize(m->stream));
     m->tensor_ok = true;
@@ -417,6 +379,28 @@ static int tile_tokens_for(const qgmoe *m, int T) {
 // Index of the activation tensor maps whose box height is nt token rows.
 static int tile_map_index(int nt) { return nt == 256 ? 0 : nt == 64 ? 1 : nt == 16 ? 2 : 3; }
 
+// The shared expert alone on the CUDA-core GEMV, as the single group of
+// st.shared_act (slots T*k .. T*k+T-1 of token 0..T-1): gate_up + SwiGLU from
+// x into h, or down from h into d (f32 rows).
+static int launch_shared_gemv(qgmoe *m, bool gateup, const float *x, cudaStream_t s) {
+    ExpertArgs a{};
+    a.routed = gateup ? m->sgu : m->sdn;
+    a.shared = a.routed;
+    a.n_experts = 0;
+    a.has_shared = 1;
+    a.act_group = m->st.shared_act;
+    a.act_begin = m->st.shared_act + 1;
+    a.act_n = m->st.shared_act + 2;
+    a.n_act = m->st.shared_act + 3;
+    a.slot_token = m->st.slot_token;
+    a.err = m->err_dev;
+    a.in = gateup ? x : m->h;
+    a.in_stride = gateup ? m->H : m->hmax;
+    a.out = gateup ? m->h : m->d;
+    a.out_stride = gateup ? m->hmax : m->H;
+    return launch_expert(gateup, a, 1, s);
+}
+
 static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
     const int nt = tile_tokens_for(m, T);
     const int ti = tile_map_index(nt);
@@ -424,14 +408,13 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, m->xp16, m->err_dev, s, m->rtc_for(T));
+                          m->has_shared, m->st, m->xh16, m->xp16, m->err_dev, s);
     if (rc) return rc;
     m->mark(1, "route", s);
     const int pairs = T * m->k;
     const int tiles = (pairs + nt - 1) / nt + (pairs < m->E ? pairs : m->E);
-    // logits (+ the x split on the tensor-core router), top-k, scatter (fused
-    // into top-k for <= 32 tokens), gather
-    int launches = (m->rtc_for(T) ? 2 : 1) + 1 + (T > 32 ? 1 : 0) + 1;
+    // logits, top-k, scatter (fused into top-k for <= 32 tokens), gather
+    int launches = 1 + 1 + (T > 32 ? 1 : 0) + 1;
     UmmaLaunch l{};
     l.act_group = m->st.act_group;
     l.act_begin = m->st.act_begin;
@@ -450,7 +433,10 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     if ((rc = launch_umma(m->bits, true, &m->tmap_x[ti], l, s))) return rc;
     // shared expert gate_up (one group: slots T*k .. T*k+T-1)
     UmmaLaunch sl = l;
-    if (m->has_shared) {
+    if (m->has_shared && !m->shared_tc) {
+        if ((rc = launch_shared_gemv(m, true, x, s))) return rc;
+        launches++;
+    } else if (m->has_shared) {
         sl.act_group = m->st.shared_act;
         sl.act_begin = m->st.shared_act + 1;
         sl.act_n = m->st.shared_act + 2;
@@ -459,7 +445,7 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
         sl.wq = m->sgu_pq;
         sl.RT = m->Is / 64;
         sl.grid = ((T + nt - 1) / nt) * sl.RT;
-        if ((rc = launch_umma(m->bits, true, &m->tmap_x[ti], sl, s))) return rc;
+        if ((rc = launch_umma(m->shared_bits, true, &m->tmap_x[ti], sl, s))) return rc;
         launches++;
     }
     m->mark(2, "gate_up", s);
@@ -471,20 +457,27 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     l.out_stride = m->H;
     l.grid = tiles * l.RT;
     if ((rc = launch_umma(m->bits, false, &m->tmap_h[ti], l, s))) return rc;
-    if (m->has_shared) {
+    if (m->has_shared && !m->shared_tc) {
+        if ((rc = launch_shared_gemv(m, false, x, s))) return rc;
+        launches++;
+    } else if (m->has_shared) {
         sl.wq = m->sdn_pq;
         sl.RT = m->H / 128;
         sl.KB = m->Is / 64;
         sl.out = m->d16;
         sl.out_stride = m->H;
         sl.grid = ((T + nt - 1) / nt) * sl.RT;
-        if ((rc = launch_umma(m->bits, false, &m->tmap_hs[ti], sl, s))) return rc;
+        if ((rc = launch_umma(m->shared_bits, false, &m->tmap_hs[ti], sl, s))) return rc;
         launches++;
     }
     m->mark(3, "down", s);
-    if ((rc = launch_combine_f16(m->d16, m->H, T, m->k, m->st.pair_slot, m->st.topk_w,
-                                 m->st.shared_w, m->has_shared, out, s)))
-        return rc;
+    if (m->has_shared && !m->shared_tc)
+        rc = launch_combine_mixed(m->d16, m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w,
+                                  m->st.shared_w, out, s);
+    else
+        rc = launch_combine_f16(m->d16, m->H, T, m->k, m->st.pair_slot, m->st.topk_w,
+                                m->st.shared_w, m->has_shared, out, s);
+    if (rc) return rc;
     m->mark(4, "combine", s);
     m->last_launches = launches + 3;  // + gate_up, down, combine
     return QGMOE_OK;
@@ -513,19 +506,22 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, m->shared_gate,
-                          m->has_shared, m->st, nullptr, m->err_dev, s, m->rtc_for(T));
+                          m->has_shared, m->st, nullptr, nullptr, m->err_dev, s);
     if (rc) return rc;
     m->mark(1, "route", s);
+    // one launch per stage for routed + shared experts of one format; with
+    // different formats the shared expert gets launches of its own
+    const bool split = m->has_shared && m->shared_bits != m->bits;
     ExpertArgs a{};
     a.n_experts = m->E;
-    a.has_shared = m->has_shared;
+    a.has_shared = split ? 0 : m->has_shared;
     a.act_group = m->st.act_group;
     a.act_begin = m->st.act_begin;
     a.act_n = m->st.act_n;
-    a.n_act = m->st.n_act;
+    a.n_act = split ? m->st.n_act_routed : m->st.n_act;
     a.slot_token = m->st.slot_token;
     a.err = m->err_dev;
-    int groups = (T * m->k < m->E ? T * m->k : m->E) + m->has_shared;
+    int groups = (T * m->k < m->E ? T * m->k : m->E) + a.has_shared;
     // gate_up + SwiGLU: x -> h
     a.routed = m->gu;
     a.shared = m->sgu;
@@ -534,6 +530,7 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     a.out = m->h;
     a.out_stride = m->hmax;
     if ((rc = launch_expert(true, a, groups, s))) return rc;
+    if (split && (rc = launch_shared_gemv(m, true, x, s))) return rc;
     m->mark(2, "gate_up", s);
     // down: h -> d
     a.routed = m->dn;
@@ -543,12 +540,15 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     a.out = m->d;
     a.out_stride = m->H;
     if ((rc = launch_expert(false, a, groups, s))) return rc;
+    if (split && (rc = launch_shared_gemv(m, false, x, s))) return rc;
     m->mark(3, "down", s);
     if ((rc = launch_combine(m->d, m->H, T, m->k, m->st.pair_slot, m->st.topk_w, m->st.shared_w,
                              m->has_shared, out, s)))
         return rc;
     m->mark(4, "combine", s);
-    m->last_launches = 6;  // logits, top-k, scatter, gate_up, down, combine
+    // logits, top-k, scatter (fused into top-k for <= 32 tokens), gate_up,
+    // down (each + the shared expert's when split), combine
+    m->last_launches = 2 + (T > 32 ? 1 : 0) + 3 + (split ? 2 : 0);
     return QGMOE_OK;
 }
 
@@ -596,13 +596,19 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
                          "bad shape H=%d E=%d k=%d I=%d Is=%d (H, I, Is multiples of 32; "
                          "1<=k<=min(E,32); E<=1024)",
                          H, E, k, I, Is);
-    if (bits != 32 && bits != 16 && bits != 8 && bits != 4)
-        return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 16 (bf16), 8 or 4 (got %d)", bits);
+    auto fmt_ok = [](int b) { return b == 32 || b == 16 || b == 8 || b == 4; };
+    const int sbits = d->shared_bits ? d->shared_bits : bits;
+    const int rbits = d->router_bits ? d->router_bits : 32;
+    if (!fmt_ok(bits) || !fmt_ok(sbits) || !fmt_ok(rbits))
+        return set_error(QGMOE_ERR_INVALID_ARG,
+                         "formats must be 32, 16 (bf16), 8 or 4 (bits %d, shared_bits %d, "
+                         "router_bits %d)", bits, d->shared_bits, d->router_bits);
     if (d->router_mode != QGMOE_ROUTER_TOPK && d->router_mode != QGMOE_ROUTER_PREFIX)
         return set_error(QGMOE_ERR_INVALID_ARG, "bad router_mode %d", d->router_mode);
     if (d->scale_dtype != QGMOE_SCALE_F16 && d->scale_dtype != QGMOE_SCALE_F32)
         return set_error(QGMOE_ERR_INVALID_ARG, "bad scale_dtype %d", d->scale_dtype);
-    if (!d->router || (Is > 0 && !d->shared_gate))
+    if ((rbits == 32 ? !d->router : (!d->router_q || (rbits != 16 && !d->router_scale))) ||
+        (Is > 0 && !d->shared_gate))
         return set_error(QGMOE_ERR_INVALID_ARG, "router / shared_gate pointer missing");
     const int W = d->ep_world > 1 ? d->ep_world : 1;
     if (W > 1 && (E % W || d->ep_rank < 0 || d->ep_rank >= W || Is > 0 || bits > 8 ||
@@ -621,6 +627,7 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
     m->I = I;
     m->Is = Is;
     m->bits = bits;
+    m->shared_bits = sbits;
     m->mode = d->router_mode;
     m->has_shared = Is > 0;
     m->hmax = I > Is ? I : Is;
@@ -636,9 +643,32 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
     }
     cudaStream_t s = m->stream;
     do {
-        if ((rc = upload(m->weights, d->router, sizeof(float) * E * H, dev,
-                         reinterpret_cast<void **>(&m->router), s)))
-            break;
+        if (rbits == 32) {
+            if ((rc = upload(m->weights, d->router, sizeof(float) * E * H, dev,
+                             reinterpret_cast<void **>(&m->router), s)))
+                break;
+        } else {
+            // bf16 bits or codes + scales, turned into the float32 rows the
+            // reference multiplies by
+            Allocs tmp;
+            void *rq = nullptr, *rs = nullptr;
+            const size_t qb = rbits == 16 ? (size_t)E * H * 2
+                              : rbits == 8 ? (size_t)E * H : (size_t)E * H / 2;
+            const size_t sb = rbits == 16 ? 0
+                              : (size_t)E * (H / QG_GROUP) *
+                                    (d->scale_dtype == QGMOE_SCALE_F32 ? 4 : 2);
+            if (!(rc = upload(tmp, d->router_q, qb, dev, &rq, s)) &&
+                !(rc = upload(tmp, d->router_scale, sb, dev, &rs, s)) &&
+                !(rc = m->weights.alloc(reinterpret_cast<void **>(&m->router),
+                                        sizeof(float) * E * H)))
+                rc = launch_router_rows(rbits, E, H, static_cast<const uint8_t *>(rq), rs,
+                                        d->scale_dtype == QGMOE_SCALE_F32, m->router, s);
+            const cudaError_t se = cudaStreamSynchronize(s);
+            tmp.free_all();
+            if (!rc && se != cudaSuccess)
+                rc = set_error(QGMOE_ERR_CUDA, "router upload: %s", cudaGetErrorString(se));
+            if (rc) break;
+        }
         if (m->has_shared &&
             (rc = upload(m->weights, d->shared_gate, sizeof(float) * H, dev,
                          reinterpret_cast<void **>(&m->shared_gate), s)))
@@ -653,12 +683,12 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
         if (m->has_shared) {
             Part psg[2] = {{d->shared_gate_proj, d->shared_gate_q, d->shared_gate_scale, Is},
                            {d->shared_up_proj, d->shared_up_q, d->shared_up_scale, Is}};
-            if ((rc = build_set(m->weights, bits, H, 2 * Is, 1, psg, 2, d->scale_dtype, dev,
+            if ((rc = build_set(m->weights, sbits, H, 2 * Is, 1, psg, 2, d->scale_dtype, dev,
                                 &m->sgu, s)))
                 break;
             Part psd{d->shared_down_proj, d->shared_down_q, d->shared_down_scale, H};
-            if ((rc = build_set(m->weights, bits, Is, H, 1, &psd, 1, d->scale_dtype, dev, &m->sdn,
-                                s)))
+            if ((rc = build_set(m->weights, sbits, Is, H, 1, &psd, 1, d->scale_dtype, dev,
+                                &m->sdn, s)))
                 break;
         }
         e = cudaStreamSynchronize(s);
@@ -688,7 +718,6 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
             }
             m->st.ep_slot = slot_dev;
         }
-        if ((rc = build_router_tc(m))) break;
         if ((rc = build_tensor_weights(m))) break;
         if (W > 1 && !m->tensor_ok) {
             rc = set_error(QGMOE_ERR_UNSUPPORTED, "expert parallelism needs the tensor-core path");
@@ -739,6 +768,8 @@ int qgmoe_forward_device(qgmoe_t *m, const float *x, int32_t T, float *out, int3
     if (T < 0) return set_error(QGMOE_ERR_INVALID_ARG, "T < 0");
     if (T == 0) return QGMOE_OK;
     if (!x || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null x/out");
+    if (misaligned(x) || misaligned(out))
+        return set_error(QGMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
     QG_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
     int rc = ensure_capacity(m, T);
@@ -852,8 +883,8 @@ int qgmoe_set_path(qgmoe_t *m, int32_t mode) {
         return set_error(QGMOE_ERR_INVALID_ARG, "bad path mode %d", mode);
     if (mode == QGMOE_PATH_TENSOR && !m->tensor_ok)
         return set_error(QGMOE_ERR_UNSUPPORTED,
-                         "tensor-core path needs int8/int4 experts, no shared expert, "
-                         "H and I multiples of 128");
+                         "tensor-core path needs int8/int4 routed experts with H and I "
+                         "multiples of 128");
     m->path_mode = mode;
     m->drop_graphs();
     return QGMOE_OK;
@@ -926,6 +957,8 @@ int qgmoe_ep_dispatch(qgmoe_t *m, const float *x, int32_t T, void *send_rows, vo
     if (m->ep_world < 2) return set_error(QGMOE_ERR_UNSUPPORTED, "handle is not expert-parallel");
     if (T < 0 || (T > 0 && (!x || !send_rows)))
         return set_error(QGMOE_ERR_INVALID_ARG, "bad dispatch arguments");
+    if (misaligned(x) || misaligned(send_rows))
+        return set_error(QGMOE_ERR_INVALID_ARG, "x and send_rows must be 16-byte aligned");
     QG_CUDA(cudaSetDevice(m->device));
     m->last_T = T;
     if (T == 0) return QGMOE_OK;
@@ -933,7 +966,7 @@ int qgmoe_ep_dispatch(qgmoe_t *m, const float *x, int32_t T, void *send_rows, vo
     int rc = ensure_capacity(m, T);
     if (rc) return rc;
     return launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
-                        static_cast<__half *>(send_rows), m->err_dev, s, m->rtc_for(T));
+                        m->xh16, static_cast<__half *>(send_rows), m->err_dev, s);
 }
 
 int qgmoe_ep_send_counts(qgmoe_t *m, int32_t *counts, void *stream) {
@@ -968,6 +1001,8 @@ int qgmoe_ep_experts(qgmoe_t *m, const void *recv_rows, int32_t R, const int32_t
     if (total != R) return set_error(QGMOE_ERR_INVALID_ARG, "counts sum %lld != R=%d", (long long)total, R);
     if (R == 0) return QGMOE_OK;
     if (!recv_rows || !out_rows) return set_error(QGMOE_ERR_INVALID_ARG, "null rows");
+    if (misaligned(recv_rows) || misaligned(out_rows))
+        return set_error(QGMOE_ERR_INVALID_ARG, "recv_rows and out_rows must be 16-byte aligned");
     QG_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
     int rc = ep_capacity(m, R);
@@ -1048,6 +1083,8 @@ int qgmoe_ep_combine(qgmoe_t *m, const void *back_rows, int32_t T, float *out, i
     if (T != m->last_T) return set_error(QGMOE_ERR_INVALID_ARG, "T differs from the dispatch");
     if (T == 0) return QGMOE_OK;
     if (!back_rows || !out) return set_error(QGMOE_ERR_INVALID_ARG, "null rows/out");
+    if (misaligned(back_rows) || misaligned(out))
+        return set_error(QGMOE_ERR_INVALID_ARG, "back_rows and out must be 16-byte aligned");
     QG_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
     int rc = launch_combine_f16(static_cast<const __half *>(back_rows), m->H, T, m->k,
@@ -1162,6 +1199,8 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     if (T < 0 || T > m->px_cap)
         return set_error(QGMOE_ERR_INVALID_ARG, "T=%d outside [0, %d]", T, m->px_cap);
     if (T > 0 && (!x || !out)) return set_error(QGMOE_ERR_INVALID_ARG, "null x/out");
+    if (misaligned(x) || misaligned(out))
+        return set_error(QGMOE_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
     QG_CUDA(cudaSetDevice(m->device));
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
     int rc = 0;
@@ -1172,8 +1211,8 @@ int qgmoe_ep_px_forward(qgmoe_t *m, const float *x, int32_t T, float *out, void 
     m->begin_timed();
     m->mark(0, nullptr, s);
     if (T > 0) {
-        if ((rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0, m->st,
-                               nullptr, m->err_dev, s, m->rtc_for(T))))
+        if ((rc = launch_route(x, T, m->H, m->E, m->k, m->mode, m->router, nullptr, 0,
+                               m->st, nullptr, nullptr, m->err_dev, s)))
             return rc;
     } else {
         QG_CUDA(cudaMemsetAsync(m->st.expert_off, 0, sizeof(int32_t) * m->E, s));

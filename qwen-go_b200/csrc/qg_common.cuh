@@ -14,6 +14,10 @@
 
 namespace qg {
 
+// Tokens per top-k / scatter CTA of the router (one warp per token): the
+// router's per-CTA expert histograms have ceil(T / QG_TOPK_TOK) rows.
+constexpr int QG_TOPK_TOK = 32;
+
 // Records a failure detail for qgmoe_last_error() and returns `code`.
 int set_error(int code, const char *fmt, ...);
 
@@ -74,7 +78,7 @@ enum : int {
     QG_FLAG_BAD_SLOT = 2,     // dispatch slot out of range
     QG_FLAG_BAD_GROUP = 4,    // expert kernel saw an active group out of range
     QG_FLAG_TIMEOUT = 8,      // a bounded mbarrier wait in the tensor-core kernel ran out
-    QG_FLAG_RANGE = 16,       // an activation beyond fp16 range reached the tensor-core router
+    QG_FLAG_RANGE = 16,       // a finite activation beyond fp16 range reached the tensor-core path
 };
 
 // One stacked weight family (e.g. all experts' gate_up) in device memory.
@@ -185,37 +189,24 @@ struct ExpertArgs {
 };
 
 // Launch helpers implemented in the .cu files.
-// Router + dispatch: logits, top-k, scatter; with xp set, a 4th launch writes
-// every slot's fp16 activation row for the tensor-core path.
-// Router logits on the tensor cores (qg_router_tc.cu), for batches of at
-// least RTC_MIN_T tokens: the router rows split once into fp16 hi + lo
-// parts, x split per call, logits = xh.Wh + xh.Wl + xl.Wh accumulated in f32.
-constexpr int RTC_MIN_T = 256;
-struct RouterTC {
-    CUtensorMap map_wh, map_wl;  // [rows_pad, H] fp16, boxes of 64 x 128
-    CUtensorMap map_xh, map_xl;  // [cap, H] fp16, boxes of 64 x 256
-    __half *xh, *xl;             // [cap, H]
-    int rows_pad;                // router rows (+ shared-gate row) padded to 128
-    int cap;                     // tokens xh / xl hold
-};
-int launch_split_rows(const float *router, const float *shared_gate, int E, int Ep, int H,
-                      int rows_pad, __half *wh, __half *wl, int *err, cudaStream_t s);
-int launch_logits_tc(const RouterTC &tc, const float *x, int T, int H, int Ep, float *logits,
-                     int *err, cudaStream_t s);
-int launch_gather_h16(const __half *xh, const int32_t *slot_token, int nslots, int H, __half *xp,
-                      cudaStream_t s);
-
-// The router (logits, top-k, dispatch; fp16 gathered rows when xp is set).
-// With tc (and T >= RTC_MIN_T) the logits run on the tensor cores.
+// The router: logits in the reference's serial order, exact softmax, top-k
+// and weights, dispatch.  x, router and shared_gate are float32 device
+// arrays.  With xp set (the tensor path), xh [T, H] receives fp16(x) (a
+// finite value beyond fp16 range raises QG_FLAG_RANGE) and xp [slots, H] the
+// fp16 row of every slot.
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
-                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
-                 cudaStream_t s, const RouterTC *tc = nullptr);
-int route_splits(int T, int H, int Ep, int sms);
+                 const float *shared_gate, int has_shared, RouteState st, __half *xh, __half *xp,
+                 int *err, cudaStream_t s);
+
 int launch_expert(bool gateup, const ExpertArgs &a, int max_items, cudaStream_t s);
 // d rows are f32 (CUDA-core path) or fp16 (tensor-core path).
 int launch_combine_f16(const __half *d, int H, int T, int k, const int32_t *pair_slot,
                        const float *topk_w, const float *shared_w, int has_shared, float *out,
                        cudaStream_t s);
+// Routed rows fp16 (tensor path), shared-expert rows f32 (its CUDA-core GEMV).
+int launch_combine_mixed(const __half *d, const float *ds, int H, int T, int k,
+                         const int32_t *pair_slot, const float *topk_w, const float *shared_w,
+                         float *out, cudaStream_t s);
 int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
                    const float *topk_w, const float *shared_w, int has_shared, float *out,
                    cudaStream_t s);
@@ -223,6 +214,10 @@ int launch_quantize(int bits, int O, int I, const float *w, uint8_t *q, float *s
                     __half *s16, cudaStream_t s);
 int launch_dequantize(int bits, int O, int I, const uint8_t *q, const __half *scale,
                       const float *w32, float *w, cudaStream_t s);
+// The router as float32 rows from bf16 bits (16) or codes + scales (8 / 4;
+// scale_f32: float scales, else fp16), as the reference forms them.
+int launch_router_rows(int bits, int E, int H, const uint8_t *q, const void *scale, int scale_f32,
+                       float *w, cudaStream_t s);
 int launch_f32_to_f16(const float *in, __half *out, int64_t n, cudaStream_t s);
 int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, float stdv,
                  float *out, cudaStream_t s);
@@ -232,8 +227,6 @@ int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_
                   int RT, int interleave, int up_offset, uint8_t *qo, cudaStream_t s);
 // Bytes of the packed tensor-core copy of a weight set (codes + scales).
 size_t packed_bytes(int bits, int E, int rows_per_e, int K);
-int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
-                      cudaStream_t s);
 int launch_umma(int bits, bool swiglu, const void *tmap, const UmmaLaunch &l, cudaStream_t s);
 // QuantLinear on the tensor cores: x [T, K] f32 -> fp16 rows xp (a finite
 // value beyond fp16 range raises QG_FLAG_RANGE) and the one-group work

@@ -283,6 +283,9 @@ int parse_header(qgmoe_file *f, const char *h, size_t n) {
                     return set_error(QGMOE_ERR_INVALID_ARG, "tensor %s: shape overflows", name.c_str());
                 numel *= (uint64_t)t.shape[i];
             }
+            if (numel > UINT64_MAX / (uint64_t)eb)
+                return set_error(QGMOE_ERR_INVALID_ARG, "tensor %s: byte size overflows",
+                                 name.c_str());
             if (numel * (uint64_t)eb != t.end - t.begin)
                 return set_error(QGMOE_ERR_INVALID_ARG, "tensor %s: %llu bytes for its shape, %llu stored",
                                  name.c_str(), (unsigned long long)(numel * eb),
@@ -449,14 +452,28 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
                           int32_t router_mode, int32_t device, qgmoe_desc *d) {
     if (!f || !d) return set_error(QGMOE_ERR_INVALID_ARG, "null file/desc");
     const std::string pre = prefix ? prefix : "";
+    // router: float rows (gate.weight, F32 or BF16) or a quantised linear
+    // (gate.qweight / gate.scale: routerQuant, model/load.go:651-652)
+    LinStack rq;
     const auto *router = find(f, pre + "gate.weight");
-    if (!router) return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight not in the file", pre.c_str());
-    if ((router->dtype != QGMOE_DT_F32 && router->dtype != QGMOE_DT_BF16) || router->rank != 2)
-        return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight: F32 or BF16 [E, H] expected",
-                         pre.c_str());
-    const int64_t E = router->shape[0], H = router->shape[1];
+    const bool router_quant = find(f, pre + "gate.qweight") != nullptr;
+    int64_t E = 0, H = 0;
+    int rc = 0;
+    if (router_quant) {
+        if ((rc = lin_stack(f, pre + "gate", 2, rq))) return rc;
+        E = rq.O;
+        H = rq.K;
+    } else {
+        if (!router)
+            return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight not in the file", pre.c_str());
+        if ((router->dtype != QGMOE_DT_F32 && router->dtype != QGMOE_DT_BF16) || router->rank != 2)
+            return set_error(QGMOE_ERR_INVALID_ARG, "%sgate.weight: F32 or BF16 [E, H] expected",
+                             pre.c_str());
+        E = router->shape[0];
+        H = router->shape[1];
+    }
     LinStack gu, dn;
-    int rc = lin_stack(f, pre + "experts.gate_up_proj", 3, gu);
+    rc = lin_stack(f, pre + "experts.gate_up_proj", 3, gu);
     if (!rc) rc = lin_stack(f, pre + "experts.down_proj", 3, dn);
     if (rc) return rc;
     const int64_t I = gu.O / 2;
@@ -486,10 +503,9 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
         if (sg.K != H || su.O != Is || su.K != H || sd.O != H || sd.K != Is)
             return set_error(QGMOE_ERR_INVALID_ARG, "shared expert shapes do not fit H=%lld",
                              (long long)H);
-        if (sg.bits != gu.bits || su.bits != gu.bits || sd.bits != gu.bits ||
-            sg.sdt != gu.sdt || su.sdt != gu.sdt || sd.sdt != gu.sdt)
+        if (su.bits != sg.bits || sd.bits != sg.bits || su.sdt != sg.sdt || sd.sdt != sg.sdt)
             return set_error(QGMOE_ERR_INVALID_ARG,
-                             "shared expert differs from the experts in format or scale dtype");
+                             "shared expert projections differ in format or scale dtype");
         const std::string gname = pre + "shared_expert_gate.weight";
         const auto *gate = find(f, gname);
         if (!gate || (gate->dtype != QGMOE_DT_F32 && gate->dtype != QGMOE_DT_BF16) ||
@@ -498,6 +514,15 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
             return set_error(QGMOE_ERR_INVALID_ARG,
                              "%s: F32 or BF16 [1, H] expected", gname.c_str());
         gate_vec = f32_view(f, gname, gate);
+    }
+    // one scale dtype for every quantised group of the layer
+    int sdt = -1;
+    for (int g : {gu.sdt, has_shared ? sg.sdt : -1, router_quant ? rq.sdt : -1}) {
+        if (g < 0) continue;
+        if (sdt >= 0 && g != sdt)
+            return set_error(QGMOE_ERR_INVALID_ARG,
+                             "the layer's quantised groups mix F16 and F32 scales");
+        sdt = g;
     }
     if (E > INT32_MAX || H > INT32_MAX || I > INT32_MAX || Is > INT32_MAX)
         return set_error(QGMOE_ERR_INVALID_ARG, "dimensions beyond int32");
@@ -508,11 +533,18 @@ int qgmoe_file_layer_desc(const qgmoe_file_t *f, const char *prefix, int32_t top
     d->n_moe_mlp = (int32_t)I;
     d->n_shared_mlp = (int32_t)Is;
     d->bits = gu.bits;
+    d->shared_bits = has_shared ? sg.bits : 0;
     d->router_mode = router_mode;
-    d->scale_dtype = gu.sdt >= 0 ? gu.sdt : QGMOE_SCALE_F16;
+    d->scale_dtype = sdt >= 0 ? sdt : QGMOE_SCALE_F16;
     d->weights_on_device = 0;
     d->device = device;
-    d->router = f32_view(f, pre + "gate.weight", router);
+    if (router_quant) {
+        d->router_bits = rq.bits;
+        d->router_q = rq.w;
+        d->router_scale = rq.s;
+    } else {
+        d->router = f32_view(f, pre + "gate.weight", router);
+    }
     d->shared_gate = gate_vec;
     auto put = [&](const LinStack &l, const float **w32, const uint8_t **q, const void **sc) {
         if (l.bits == 32) {

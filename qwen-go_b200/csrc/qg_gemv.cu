@@ -306,10 +306,11 @@ int launch_expert(bool gateup, const ExpertArgs &a, int max_items_groups, cudaSt
     return set_error(QGMOE_ERR_INVALID_ARG, "bits must be 32, 16, 8 or 4 (got %d)", bits);
 }
 
-// out[t, j] = sum_r w[t,r] * d[slot(t,r), j]  (+ sg[t] * d[T*k + t, j]),
+// out[t, j] = sum_r w[t,r] * d[slot(t,r), j]  (+ sg[t] * ds[T*k + t, j]),
 // accumulated from zero in rank order with separately rounded products, as
-// `out[j] += w * d[j]` in model/moe.go:82-85 and :94-96.  d rows are f32
-// (CUDA-core path) or fp16 (tensor-core path).
+// `out[j] += w * d[j]` in model/moe.go:82-85 and :94-96.  Routed rows d and
+// shared-expert rows ds are f32 (CUDA-core path) or fp16 (tensor-core path);
+// they differ when the shared expert's format keeps it off the tensor cores.
 __device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 __device__ __forceinline__ float4 load4(const __half *p) {
     const uint2 u = *reinterpret_cast<const uint2 *>(p);
@@ -318,8 +319,8 @@ __device__ __forceinline__ float4 load4(const __half *p) {
     return make_float4(a.x, a.y, b.x, b.y);
 }
 
-template <typename D>
-__global__ void k_combine(const D *__restrict__ d, int H, int T, int k,
+template <typename D, typename DS>
+__global__ void k_combine(const D *__restrict__ d, const DS *__restrict__ ds, int H, int T, int k,
                           const int32_t *__restrict__ pair_slot,
                           const float *__restrict__ topk_w, const float *__restrict__ shared_w,
                           int has_shared, float *__restrict__ out) {
@@ -339,7 +340,7 @@ __global__ void k_combine(const D *__restrict__ d, int H, int T, int k,
     }
     if (has_shared) {
         const float w = shared_w[t];
-        const float4 v = load4(d + (size_t)(T * k + t) * H + 4 * j4);
+        const float4 v = load4(ds + (size_t)(T * k + t) * H + 4 * j4);
         acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
         acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
         acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
@@ -348,14 +349,14 @@ __global__ void k_combine(const D *__restrict__ d, int H, int T, int k,
     reinterpret_cast<float4 *>(out + (size_t)t * H)[j4] = acc;
 }
 
-template <typename D>
-static int launch_combine_t(const D *d, int H, int T, int k, const int32_t *pair_slot,
-                            const float *topk_w, const float *shared_w, int has_shared, float *out,
-                            cudaStream_t s) {
+template <typename D, typename DS>
+static int launch_combine_t(const D *d, const DS *ds, int H, int T, int k,
+                            const int32_t *pair_slot, const float *topk_w, const float *shared_w,
+                            int has_shared, float *out, cudaStream_t s) {
     const int threads = 128;
     dim3 grid((H / 4 + threads - 1) / threads, T);
-    QG_CUDA(launch_pdl(k_combine<D>, grid, dim3(threads), 0, s, 1, d, H, T, k, pair_slot, topk_w,
-                       shared_w, has_shared, out));
+    QG_CUDA(launch_pdl(k_combine<D, DS>, grid, dim3(threads), 0, s, 1, d, ds, H, T, k, pair_slot,
+                       topk_w, shared_w, has_shared, out));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }
@@ -363,13 +364,19 @@ static int launch_combine_t(const D *d, int H, int T, int k, const int32_t *pair
 int launch_combine(const float *d, int H, int T, int k, const int32_t *pair_slot,
                    const float *topk_w, const float *shared_w, int has_shared, float *out,
                    cudaStream_t s) {
-    return launch_combine_t(d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
+    return launch_combine_t(d, d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
 }
 
 int launch_combine_f16(const __half *d, int H, int T, int k, const int32_t *pair_slot,
                        const float *topk_w, const float *shared_w, int has_shared, float *out,
                        cudaStream_t s) {
-    return launch_combine_t(d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
+    return launch_combine_t(d, d, H, T, k, pair_slot, topk_w, shared_w, has_shared, out, s);
+}
+
+int launch_combine_mixed(const __half *d, const float *ds, int H, int T, int k,
+                         const int32_t *pair_slot, const float *topk_w, const float *shared_w,
+                         float *out, cudaStream_t s) {
+    return launch_combine_t(d, ds, H, T, k, pair_slot, topk_w, shared_w, 1, out, s);
 }
 
 }  // namespace qg

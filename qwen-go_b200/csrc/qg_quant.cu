@@ -117,6 +117,50 @@ int launch_dequantize(int bits, int O, int I, const uint8_t *q, const __half *s,
     return QGMOE_OK;
 }
 
+// Router rows as float32 [E, H] from a bf16 (bits 16) or quantLinear (8 / 4)
+// mlp.gate, exactly the values the reference multiplies by: bf16f32
+// (model/model.go:113-115), or dequantize (model/moe.go:134-157):
+// float32(code) * scale rounded to nearest, with fp16 scales widened (exact)
+// and f32 scales used as given -- cmd/qwen-quant writes f32 scales and the
+// loader keeps them (model/load.go:553-563).
+__global__ void k_router_rows(int bits, int E, int H, const uint8_t *__restrict__ q,
+                              const void *__restrict__ scale, int scale_f32,
+                              float *__restrict__ w) {
+    const int64_t n = (int64_t)E * H;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        if (bits == 16) {
+            const uint32_t u = reinterpret_cast<const uint16_t *>(q)[i];
+            w[i] = __uint_as_float(u << 16);
+            continue;
+        }
+        const int64_t o = i / H;
+        const int c = (int)(i - o * H);
+        const int64_t si = o * (H / QG_GROUP) + c / QG_GROUP;
+        const float sc = scale_f32 ? reinterpret_cast<const float *>(scale)[si]
+                                   : __half2float(reinterpret_cast<const __half *>(scale)[si]);
+        float v;
+        if (bits == 8) {
+            v = (float)(int8_t)q[i];
+        } else {
+            const uint8_t b = q[o * (H / 2) + c / 2];
+            v = (float)((c % 2 == 0) ? (b >> 4) : (b & 0xF)) - 8.f;
+        }
+        w[i] = __fmul_rn(v, sc);
+    }
+}
+
+int launch_router_rows(int bits, int E, int H, const uint8_t *q, const void *scale, int scale_f32,
+                       float *w, cudaStream_t s) {
+    const int64_t n = (int64_t)E * H;
+    if (n == 0) return QGMOE_OK;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 65535LL * 16) blocks = 65535LL * 16;
+    k_router_rows<<<(unsigned)blocks, 256, 0, s>>>(bits, E, H, q, scale, scale_f32, w);
+    QG_CUDA(cudaGetLastError());
+    return QGMOE_OK;
+}
+
 __global__ void k_f32_to_f16(const float *__restrict__ in, __half *__restrict__ out, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x)

@@ -1,50 +1,53 @@
 // Router + dispatch (kernels K1 and K2).
 //
 // Launches: k_logits, k_topk, k_scatter (fused into k_topk for <= 32 tokens)
-// (+ k_gather_f16 for the tensor path).
-// 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...), model/moe.go:42)
-//    as a split-K tiled f32 GEMM on CUDA cores: a CTA owns 64 tokens x 128
-//    router rows (32 x 32 for 9-64 tokens, 8 x 32 for up to 8) x one K
-//    slice.  The shared-expert gate vector rides along as
-//    router row E (model/moe.go:87-93).  Split-K keeps decode-sized batches
-//    (T = 1..64) spread over the SMs while the 1 MiB router matrix is read
-//    about once; the K slices of one tile form a thread-block cluster and add
-//    their partial tiles through distributed shared memory in rank order
-//    (deterministic), so only final logits reach global memory.
-// 2. k_topk: one warp per token reads its logits, then softmax (model/tensors.go:106-121: max-subtract, exp in float64 rounded
-//    to float32, divide by the sum), top-k (model/moe.go:44-52, TOPK or the
-//    literal PREFIX bound), w = p / (wSum + 1e-9) (model/moe.go:53-63) and
-//    sigmoid of the shared gate.  Each CTA writes its expert histogram; the
-//    last CTA (atomic ticket) scans the totals into expert offsets, the list
-//    of active experts and the tensor-core tile prefix, and re-zeroes the
-//    counters and the ticket so the next call (or a graph replay) starts clean.
+// (+ k_gather_h16 for the tensor path).
+// 1. k_logits: logits = x . router^T (proj(x,1,&m.gate,...),
+//    model/moe.go:42) in the reference's own order: each logit is a serial
+//    float32 sum in index order of separately rounded products (matmulVec,
+//    model/tensors.go:77-89; Go on amd64 does not contract a*b+c into FMA),
+//    so every logit equals the reference's bit for bit.  A serial sum cannot
+//    be split along K, so the parallelism is over (token, row) pairs: each
+//    thread carries TPT x RPT independent chains (register tiling, the
+//    chains hide the add latency), token and router tiles are staged in
+//    shared memory K-major, and __fmul_rn / __fadd_rn keep the compiler from
+//    fusing.  The shared-expert gate vector rides along as router row E
+//    (model/moe.go:87-93).  For the tensor path the CTAs of the first row
+//    tile also write fp16(x) (a finite value beyond fp16 range raises
+//    QG_FLAG_RANGE).
+// 2. k_topk: one warp per token: softmax exactly as model/tensors.go:106-121
+//    (max by `x > mx`, exp in float64 rounded to float32, float32 sum in
+//    index order, divide), so the probabilities are the reference's bit for
+//    bit; then top-k (model/moe.go:44-52: TOPK = the insertion sort over all
+//    experts, i.e. probability descending with ties to the lower index;
+//    PREFIX = its literal bound over experts 0..k-1), w = p / (wSum + 1e-9)
+//    (model/moe.go:53-63) and the sigmoid of the shared gate.  NaN behaves
+//    as in the reference: `x > mx` and `p[j] > p[j-1]` are false on NaN, so
+//    a NaN or infinite activation makes every probability of its token NaN
+//    and its selection experts 0..k-1.  Each CTA writes its expert
+//    histogram; the last CTA (atomic ticket) scans the totals into expert
+//    offsets, the list of active experts and the tensor-core tile prefix,
+//    and re-zeroes the counters and the ticket so the next call (or a graph
+//    replay) starts clean.
 // 3. k_scatter: each CTA ranks its own (token, rank) pairs per expert in pair
 //    order (warp match + per-warp counts) and adds the histograms of the CTAs
 //    before it, so slots are expert-sorted and deterministic without a serial
 //    pass.  With one token chunk (<= 32 tokens) the single top-k CTA does this
-//    itself once the offsets are known, one launch fewer.  For the tensor-core path k_gather_f16 then writes each slot's fp16
-//    activation row.
+//    itself once the offsets are known, one launch fewer.  For the tensor-core
+//    path k_gather_h16 then copies each slot's fp16 activation row.
 #include "qg_common.cuh"
-#include "qg_sm100.cuh"
 
 namespace qg {
-using sm100::cluster_ctarank;
-using sm100::cluster_sync;
-using sm100::ld_cluster_f32;
-using sm100::mapa_shared;
-using sm100::smem_u32;
 
-constexpr int LG_KC = 32;    // K chunk staged in shared memory
-constexpr int LG_MAX_SPLIT = 16; // K slices per tile = cluster size (16: non-portable opt-in)
-constexpr int LG_SMALL_T = 8;    // up to this many tokens: 8 x 32 tiles,
-constexpr int LG_MID_T = 64;     // up to this many: 32 x 32, else 64 x 128
-constexpr int TK_TOK = 32;   // tokens per top-k / scatter CTA
-constexpr int RT_THREADS = 1024;  // top-k and scatter CTAs: one warp per token
+constexpr int LG_KC = 32;                // K chunk staged in shared memory
+constexpr int TK_TOK = QG_TOPK_TOK;      // tokens per top-k / scatter CTA
+constexpr int RT_THREADS = 1024;         // top-k and scatter CTAs: one warp per token
 constexpr int RT_WARPS = RT_THREADS / 32;
+constexpr unsigned FULL = 0xffffffffu;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
     return v;
 }
 
@@ -57,179 +60,199 @@ __device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
     }
 }
 
-// logits tile tier: 0 = 64 x 128, 1 = 8 x 32, 2 = 32 x 32
-static int lg_tier(int T) { return T <= LG_SMALL_T ? 1 : T <= LG_MID_T ? 2 : 0; }
-
-int route_splits(int T, int H, int Ep, int sms) {
-    static const int tts[3] = {64, 8, 32}, rrs[3] = {128, 32, 32};
-    const int TT = tts[lg_tier(T)], RR = rrs[lg_tier(T)];
-    const int tiles = ((T + TT - 1) / TT) * ((Ep + RR - 1) / RR);
-    int s = 1;  // a power of two: the cluster size
-    while (s < LG_MAX_SPLIT && 2 * s * tiles <= sms && 2 * s * LG_KC <= H) s *= 2;
-    return s;
-}
-
 // ---- 1. logits ------------------------------------------------------------------
-// CTA tile: TT tokens x RR router rows x one K slice (TT x RR = 64 x 128 for
-// prefill batches, 8 x 32 or 32 x 32 for decode batches, so that a handful
-// of tokens still spreads over many CTAs).  Warp w owns tokens w*TT/8 ..., lane l owns
-// rows l*RR/32 ...: per K step the warp's x values and the lane's router
-// values come from shared memory and feed (TT/8) x (RR/32) FMAs.  The next K
-// chunk is fetched into registers while the current one is consumed.  With
-// KS > 1 the KS slices of a tile are one cluster: each CTA parks its partial
-// tile in its shared memory, and CTA c then sums elements
-// [c*TT*RR/KS, (c+1)*TT*RR/KS) of the tile over the ranks 0..KS-1 in order.
-template <int TT, int RR>
-struct LgTile {
-    static constexpr int TPW = TT / 8;   // tokens per warp
-    static constexpr int RPL = RR / 32;  // rows per lane
-    static constexpr int STAGE_FLOATS = LG_KC * (TT + 4) + LG_KC * (RR + 4);
-    static constexpr int SMEM =
-        4 * (STAGE_FLOATS > TT * RR ? STAGE_FLOATS : TT * RR);
+// CTA tile: TT = TPT*TTH tokens x RR = RPT*RTH router rows; thread (ty, tx)
+// owns tokens ty*TPT.. and rows tx*RPT...  Per 32-wide K chunk the tiles are
+// fetched into registers (the next chunk while the current one is consumed),
+// then stored K-major into shared memory so that a thread reads its TPT
+// activations and RPT router values of step kk with one vector load each.
+// For every kk in order: chain(t, r) = fl(chain + fl(x[t][kk] * w[r][kk])).
+template <int TPT, int RPT, int TTH, int RTH>
+struct LgCfg {
+    static constexpr int THREADS = TTH * RTH, TT = TPT * TTH, RR = RPT * RTH;
+    static constexpr int XV = TT * LG_KC / 4, WV = RR * LG_KC / 4;  // float4 per chunk
+    static constexpr int XPT = (XV + THREADS - 1) / THREADS, WPT = (WV + THREADS - 1) / THREADS;
 };
 
-template <int TT, int RR, int KS>
-__global__ void __launch_bounds__(256)
-k_logits(const float *__restrict__ x, int T, int H, int E, int Ep, const float *__restrict__ router,
-         const float *__restrict__ shared_gate, float *__restrict__ logits) {
-    using Tl = LgTile<TT, RR>;
-    constexpr int TPW = Tl::TPW, RPL = Tl::RPL;
-    constexpr int XV = TT * LG_KC / 4;   // float4 loads of x per K chunk
-    constexpr int WV = RR * LG_KC / 4;   // float4 loads of router rows per K chunk
-    constexpr int XPT = (XV + 255) / 256, WPT = WV / 256;
-    static_assert(WV % 256 == 0, "router chunk must split evenly over the CTA");
-    pdl_enter();
-    extern __shared__ __align__(16) float lg_smem[];
-    float (*xs)[TT + 4] = reinterpret_cast<float (*)[TT + 4]>(lg_smem);
-    float (*ws)[RR + 4] = reinterpret_cast<float (*)[RR + 4]>(lg_smem + LG_KC * (TT + 4));
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t0 = blockIdx.x * TT, r0 = blockIdx.y * RR, s = blockIdx.z;
-    const int kc = ((H / LG_KC + KS - 1) / KS) * LG_KC;
-    const int k0 = s * kc, k1 = min(H, k0 + kc);
-    float acc[TPW][RPL] = {};
-    // loaders: float4 i of a chunk covers item i / 8 (token or row), column (i % 8) * 4
-    const float *xrow[XPT];
-    int xi[XPT];
+template <int N>
+__device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
+    if constexpr (N == 4) {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+    } else if constexpr (N == 2) {
+        const float2 a = *reinterpret_cast<const float2 *>(p);
+        v[0] = a.x, v[1] = a.y;
+    } else {
 #pragma unroll
-    for (int j = 0; j < XPT; j++) {
-        xi[j] = tid + 256 * j;
-        const int t = t0 + xi[j] / 8;
-        xrow[j] = (xi[j] < XV && t < T) ? x + (size_t)t * H : nullptr;
+        for (int i = 0; i < N; i++) v[i] = p[i];
     }
-    const float *wrow[WPT];
+}
+
+template <int TPT, int RPT, int TTH, int RTH>
+__global__ void __launch_bounds__(TTH *RTH)
+k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
+         const float *__restrict__ router, const float *__restrict__ shared_gate,
+         float *__restrict__ logits, __half *__restrict__ xh, int *err) {
+    using C = LgCfg<TPT, RPT, TTH, RTH>;
+    constexpr int TT = C::TT, RR = C::RR, NTH = C::THREADS;
+    __shared__ __align__(16) float xs[LG_KC][TT + 4];
+    __shared__ __align__(16) float ws[LG_KC][RR + 4];
+    pdl_enter();
+    const int tid = threadIdx.x, tx = tid % RTH, ty = tid / RTH;
+    const int t0 = blockIdx.x * TT, r0 = blockIdx.y * RR;
+    const bool write_h = xh && blockIdx.y == 0;
+    // loaders: float4 i of a chunk covers item i / 8 (token or row), column (i % 8) * 4
+    const float *xrow[C::XPT];
+    const float *wrow[C::WPT];
 #pragma unroll
-    for (int j = 0; j < WPT; j++) {
-        const int r = r0 + (tid + 256 * j) / 8;
-        wrow[j] = r < Ep ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
+    for (int j = 0; j < C::XPT; j++) {
+        const int i = tid + NTH * j, t = t0 + i / 8;
+        xrow[j] = (i < C::XV && t < T) ? x + (size_t)t * H : nullptr;
+    }
+#pragma unroll
+    for (int j = 0; j < C::WPT; j++) {
+        const int i = tid + NTH * j, r = r0 + i / 8;
+        wrow[j] = (i < C::WV && r < Ep) ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
     }
     const int c4 = (tid % 8) * 4;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 xn[XPT], wn[WPT];
+    float4 xn[C::XPT], wn[C::WPT];
     auto fetch = [&](int kb) {
 #pragma unroll
-        for (int j = 0; j < XPT; j++)
-            xn[j] = xrow[j] ? *reinterpret_cast<const float4 *>(xrow[j] + kb + c4) : zero;
+        for (int j = 0; j < C::XPT; j++)
+            xn[j] = xrow[j] ? __ldg(reinterpret_cast<const float4 *>(xrow[j] + kb + c4)) : zero;
 #pragma unroll
-        for (int j = 0; j < WPT; j++)
+        for (int j = 0; j < C::WPT; j++)
             wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + c4)) : zero;
     };
-    if (k0 < k1) fetch(k0);
-    for (int kb = k0; kb < k1; kb += LG_KC) {
+    float acc[TPT][RPT];
 #pragma unroll
-        for (int j = 0; j < XPT; j++)
-            if (xi[j] < XV) {
-                const int t = xi[j] / 8;
+    for (int i = 0; i < TPT; i++)
+#pragma unroll
+        for (int j = 0; j < RPT; j++) acc[i][j] = 0.f;
+    bool range = false;
+    fetch(0);
+    for (int kb = 0; kb < H; kb += LG_KC) {
+#pragma unroll
+        for (int j = 0; j < C::XPT; j++) {
+            const int i = tid + NTH * j;
+            if (i < C::XV) {
+                const int t = i / 8;
                 xs[c4][t] = xn[j].x;
                 xs[c4 + 1][t] = xn[j].y;
                 xs[c4 + 2][t] = xn[j].z;
                 xs[c4 + 3][t] = xn[j].w;
+                if (write_h && xrow[j]) {
+                    const __half2 a = __floats2half2_rn(xn[j].x, xn[j].y);
+                    const __half2 b = __floats2half2_rn(xn[j].z, xn[j].w);
+                    const float2 af = __half22float2(a), bf = __half22float2(b);
+                    range |= (isfinite(xn[j].x) && isinf(af.x)) ||
+                             (isfinite(xn[j].y) && isinf(af.y)) ||
+                             (isfinite(xn[j].z) && isinf(bf.x)) ||
+                             (isfinite(xn[j].w) && isinf(bf.y));
+                    uint2 u;
+                    u.x = *reinterpret_cast<const uint32_t *>(&a);
+                    u.y = *reinterpret_cast<const uint32_t *>(&b);
+                    *reinterpret_cast<uint2 *>(xh + (size_t)(t0 + t) * H + kb + c4) = u;
+                }
             }
+        }
 #pragma unroll
-        for (int j = 0; j < WPT; j++) {
-            const int row = (tid + 256 * j) / 8;
-            ws[c4][row] = wn[j].x;
-            ws[c4 + 1][row] = wn[j].y;
-            ws[c4 + 2][row] = wn[j].z;
-            ws[c4 + 3][row] = wn[j].w;
+        for (int j = 0; j < C::WPT; j++) {
+            const int i = tid + NTH * j;
+            if (i < C::WV) {
+                const int row = i / 8;
+                ws[c4][row] = wn[j].x;
+                ws[c4 + 1][row] = wn[j].y;
+                ws[c4 + 2][row] = wn[j].z;
+                ws[c4 + 3][row] = wn[j].w;
+            }
         }
         __syncthreads();
-        if (kb + LG_KC < k1) fetch(kb + LG_KC);
-#pragma unroll 4
+        if (kb + LG_KC < H) fetch(kb + LG_KC);
+#pragma unroll 8
         for (int kk = 0; kk < LG_KC; kk++) {
-            float av[TPW], bv[RPL];
-            if constexpr (TPW % 4 == 0) {
+            float av[TPT], bv[RPT];
+            lds_vec<TPT>(&xs[kk][ty * TPT], av);
+            lds_vec<RPT>(&ws[kk][tx * RPT], bv);
 #pragma unroll
-                for (int i = 0; i < TPW; i += 4) {
-                    const float4 v = *reinterpret_cast<const float4 *>(&xs[kk][TPW * warp + i]);
-                    av[i] = v.x, av[i + 1] = v.y, av[i + 2] = v.z, av[i + 3] = v.w;
-                }
-            } else {
+            for (int i = 0; i < TPT; i++)
 #pragma unroll
-                for (int i = 0; i < TPW; i++) av[i] = xs[kk][TPW * warp + i];
-            }
-            if constexpr (RPL % 4 == 0) {
-#pragma unroll
-                for (int j = 0; j < RPL; j += 4) {
-                    const float4 v = *reinterpret_cast<const float4 *>(&ws[kk][RPL * lane + j]);
-                    bv[j] = v.x, bv[j + 1] = v.y, bv[j + 2] = v.z, bv[j + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < RPL; j++) bv[j] = ws[kk][RPL * lane + j];
-            }
-#pragma unroll
-            for (int i = 0; i < TPW; i++)
-#pragma unroll
-                for (int j = 0; j < RPL; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < RPT; j++)
+                    acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
         }
         __syncthreads();
     }
-    if constexpr (KS == 1) {
+    if (range) atomicOr(err, QG_FLAG_RANGE);
 #pragma unroll
-        for (int i = 0; i < TPW; i++) {
-            const int t = t0 + TPW * warp + i;
-            if (t >= T) continue;
+    for (int i = 0; i < TPT; i++) {
+        const int t = t0 + ty * TPT + i;
+        if (t >= T) continue;
 #pragma unroll
-            for (int j = 0; j < RPL; j++) {
-                const int r = r0 + RPL * lane + j;
-                if (r < Ep) logits[(size_t)t * Ep + r] = acc[i][j];
-            }
+        for (int j = 0; j < RPT; j++) {
+            const int r = r0 + tx * RPT + j;
+            if (r < Ep) logits[(size_t)t * Ep + r] = acc[i][j];
         }
-    } else {
-        // partial tile [TT tokens][RR rows] over the staging buffers (the K
-        // loop ended with a barrier)
-        float *red = lg_smem;
-#pragma unroll
-        for (int i = 0; i < TPW; i++)
-#pragma unroll
-            for (int j = 0; j < RPL; j++) red[(TPW * warp + i) * RR + RPL * lane + j] = acc[i][j];
-        cluster_sync();
-        constexpr int EPC = TT * RR / KS;  // tile elements reduced by this CTA
-        const int c = (int)cluster_ctarank();
-        for (int idx = c * EPC + tid; idx < (c + 1) * EPC; idx += 256) {
-            const uint32_t off = smem_u32(red + idx);
-            float v[KS];
-#pragma unroll
-            for (int q = 0; q < KS; q++) v[q] = ld_cluster_f32(mapa_shared(off, q));
-            float sum = v[0];
-#pragma unroll
-            for (int q = 1; q < KS; q++) sum += v[q];
-            const int t = t0 + idx / RR, row = r0 + idx % RR;
-            if (t < T && row < Ep) logits[(size_t)t * Ep + row] = sum;
-        }
-        cluster_sync();  // no CTA leaves while others still read its tile
     }
 }
 
+// Tile shapes by batch size: the chains are long (H steps each), so small
+// batches want many threads over the router rows and large batches enough
+// chains per thread to keep the FP32 pipes busy.
+template <int TPT, int RPT, int TTH, int RTH>
+static int launch_logits_t(const float *x, int T, int H, int E, int Ep, const float *router,
+                           const float *shared_gate, float *logits, __half *xh, int *err,
+                           cudaStream_t s) {
+    using C = LgCfg<TPT, RPT, TTH, RTH>;
+    QG_CUDA(launch_pdl(k_logits<TPT, RPT, TTH, RTH>,
+                       dim3((T + C::TT - 1) / C::TT, (Ep + C::RR - 1) / C::RR), dim3(C::THREADS),
+                       0, s, 1, x, T, H, E, Ep, router, shared_gate, logits, xh, err));
+    return QGMOE_OK;
+}
+
+static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
+                         const float *shared_gate, float *logits, __half *xh, int *err,
+                         cudaStream_t s) {
+    if (T <= 8)  // 8 tokens x 128 rows, 4 chains per thread
+        return launch_logits_t<1, 4, 8, 32>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
+    if (T <= 128)  // 16 tokens x 64 rows, 8 chains per thread
+        return launch_logits_t<2, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
+    // 32 tokens x 64 rows, 16 chains per thread
+    return launch_logits_t<4, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
+}
+
 // ---- 2. softmax + top-k + histograms --------------------------------------------
-// A warp holds one token's probabilities in registers: lane l owns experts
-// l, l+32, ..., l+32*(NJ-1) (NJ = ceil(E/32) rounded up to a power of two).
+// float32(exp(float64(v - mx))), the softmax numerator (model/tensors.go:116).
+__device__ __forceinline__ float sm_num(float v, float mx) {
+    return (float)exp((double)__fsub_rn(v, mx));
+}
+
+// Warp-wide best (larger value, then lower expert index) over the lane's
+// values v[j] (expert lane + 32 j) whose bit is set in `usable`.
+template <int NJ>
+__device__ __forceinline__ void warp_best(const float (&v)[NJ], unsigned usable, int lane,
+                                          float &bv, int &bi) {
+    bv = -INFINITY;
+    bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+        if ((usable >> j) & 1u) better(bv, bi, v[j], lane + 32 * j);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(FULL, bv, o);
+        const int i2 = __shfl_xor_sync(FULL, bi, o);
+        better(bv, bi, v2, i2);
+    }
+}
+
 __device__ __forceinline__ void scatter_chunk(int c, int T, int E, int k, int has_shared,
                                               const RouteState &st, int *err, int *sm,
                                               int *partial);
 
-// FUSED (T <= TK_TOK, one CTA): the scatter of the single token chunk
-// follows in the same CTA once the expert offsets are known.
+// One warp per token: lane l owns experts l, l+32, ..., l+32*(NJ-1) (NJ =
+// ceil(E/32) rounded up to a power of two).  FUSED (T <= TK_TOK, one CTA):
+// the scatter of the single token chunk follows in the same CTA once the
+// expert offsets are known.
 template <int NJ, bool FUSED>
 __global__ void __launch_bounds__(RT_THREADS)
 k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
@@ -245,70 +268,69 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
     for (int i = 0; i < TK_TOK / RT_WARPS; i++) {
         const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / RT_WARPS) + i;
         if (t >= T) break;
+        unsigned valid = 0;
         float v[NJ];
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int e = lane + 32 * j;
+            if (e < E) valid |= 1u << j;
             v[j] = e < E ? logits[(size_t)t * Ep + e] : -INFINITY;
         }
-        float mx = v[0];
-#pragma unroll
-        for (int j = 1; j < NJ; j++) mx = fmaxf(mx, v[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float sum = 0.f;
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            if (lane + 32 * j < E) {
-                v[j] = (float)exp((double)(v[j] - mx));
-                sum += v[j];
-            } else {
-                v[j] = -1.f;  // never selected
-            }
-        }
-        sum = warp_sum(sum);
+        // mx = v[0]; for x in v[1:]: if x > mx { mx = x }: fmaxf skips NaN
+        // as `x > mx` does, and a NaN in v[0] stays
+        const float v0 = __shfl_sync(FULL, v[0], 0);
+        float m = -INFINITY;
 #pragma unroll
         for (int j = 0; j < NJ; j++)
-            if (lane + 32 * j < E) v[j] = v[j] / sum;
+            if ((valid >> j) & 1u) m = fmaxf(m, v[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
+        const float mx = isnan(v0) ? v0 : m;
+        float p[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; j++) p[j] = ((valid >> j) & 1u) ? sm_num(v[j], mx) : 0.f;
+        // float32 sum in index order (every lane forms the same sum)
+        float sum = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; j++)
+#pragma unroll
+            for (int l = 0; l < 32; l++) {
+                const float u = __shfl_sync(FULL, p[j], l);
+                if (l + 32 * j < E) sum = __fadd_rn(sum, u);
+            }
+#pragma unroll
+        for (int j = 0; j < NJ; j++) p[j] = ((valid >> j) & 1u) ? __fdiv_rn(p[j], sum) : -1.f;
         int *sel = s_idx[warp];
         float selp = 0.f;  // lane r < k: probability of the rank-r expert
-        if (mode == QGMOE_ROUTER_TOPK) {
-            unsigned used = 0;
-#pragma unroll
-            for (int j = 0; j < NJ; j++)
-                if (lane + 32 * j >= E) used |= 1u << j;  // padding lanes never win
+        if (isnan(sum)) {
+            // every probability NaN: no comparison succeeds, the order stays 0..k-1
+            const float pr = __shfl_sync(FULL, p[0], lane < k ? lane : 0);
+            if (lane < k) {
+                sel[lane] = lane;
+                selp = pr;
+            }
+        } else if (mode == QGMOE_ROUTER_TOPK) {
+            unsigned usable = valid;
             for (int r = 0; r < k; r++) {
-                float bv = -2.f;
-                int bi = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < NJ; j++)
-                    if (!((used >> j) & 1u)) better(bv, bi, v[j], lane + 32 * j);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-                    better(bv, bi, v2, i2);
-                }
-                if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+                float bv;
+                int bi;
+                warp_best(p, usable, lane, bv, bi);
+                if ((bi & 31) == lane) usable &= ~(1u << (bi >> 5));
                 if (lane == r) selp = bv;
                 if (lane == 0) sel[r] = bi;
             }
         } else {
             // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1
-            // (k <= 32, so expert q < k is v[0] of lane q).
-            const float pq = v[0];
+            // (k <= 32, so expert q < k is p[0] of lane q): insertion sort
+            const float pq = p[0];
             float pk[QG_MAX_TOPK];
-            int ik[QG_MAX_TOPK];
-            for (int q = 0; q < k; q++) {
-                pk[q] = __shfl_sync(0xffffffffu, pq, q);
-                ik[q] = q;
-            }
+#pragma unroll
+            for (int q = 0; q < QG_MAX_TOPK; q++) pk[q] = __shfl_sync(FULL, pq, q);
             if (lane == 0) {
+                int ik[QG_MAX_TOPK];
+                for (int q = 0; q < k; q++) ik[q] = q;
                 for (int a2 = 1; a2 < k && a2 < E; a2++)
-                    for (int b2 = a2; b2 > 0 && pk[b2] > pk[b2 - 1]; b2--) {
-                        const float tp = pk[b2];
-                        pk[b2] = pk[b2 - 1];
-                        pk[b2 - 1] = tp;
+                    for (int b2 = a2; b2 > 0 && pk[ik[b2]] > pk[ik[b2 - 1]]; b2--) {
                         const int ti = ik[b2];
                         ik[b2] = ik[b2 - 1];
                         ik[b2 - 1] = ti;
@@ -316,15 +338,14 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
                 for (int q = 0; q < k; q++) sel[q] = ik[q];
             }
             __syncwarp();
-            // probability of rank `lane`: the owner of expert sel[lane] is lane sel[lane]
             const int myexp = lane < k ? sel[lane] : 0;
-            const float got = __shfl_sync(0xffffffffu, pq, myexp);
+            const float got = __shfl_sync(FULL, pq, myexp);
             if (lane < k) selp = got;
         }
         __syncwarp();
         // wSum over ranks in rank order, then w = p / (wSum + 1e-9)
         float wsum = 0.f;
-        for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, selp, r));
+        for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, __shfl_sync(FULL, selp, r));
         const float den = __fadd_rn(wsum, 1e-9f);
         if (lane < k) {
             const int e = sel[lane];
@@ -336,8 +357,9 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
                 atomicOr(err, QG_FLAG_BAD_EXPERT);
         }
         if (has_shared && lane == 0) {
+            // sigmoid1 (model/tensors.go:97) of the shared-gate logit
             const float g = logits[(size_t)t * Ep + E];
-            st.shared_w[t] = 1.f / (1.f + (float)exp(-(double)g));
+            st.shared_w[t] = __fdiv_rn(1.f, __fadd_rn(1.f, (float)exp(-(double)g)));
         }
         __syncwarp();
     }
@@ -523,49 +545,41 @@ k_scatter(int T, int E, int k, int has_shared, RouteState st, int *err) {
     scatter_chunk(blockIdx.x, T, E, k, has_shared, st, err, sm, partial);
 }
 
-// CUDA-core logits: the split-K tiled f32 GEMM above.
-static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
-                         const float *shared_gate, float *logits, int dev, cudaStream_t s) {
-    const int ks = route_splits(T, H, Ep, num_sms(dev));
-    const int tier = lg_tier(T);
-    using LgKern = void (*)(const float *, int, int, int, int, const float *, const float *, float *);
-    static const LgKern kerns[3][5] = {
-        {k_logits<64, 128, 1>, k_logits<64, 128, 2>, k_logits<64, 128, 4>, k_logits<64, 128, 8>,
-         k_logits<64, 128, 16>},
-        {k_logits<8, 32, 1>, k_logits<8, 32, 2>, k_logits<8, 32, 4>, k_logits<8, 32, 8>,
-         k_logits<8, 32, 16>},
-        {k_logits<32, 32, 1>, k_logits<32, 32, 2>, k_logits<32, 32, 4>, k_logits<32, 32, 8>,
-         k_logits<32, 32, 16>}};
-    static const int tts[3] = {64, 8, 32}, rrs[3] = {128, 32, 32};
-    static const int smems[3] = {LgTile<64, 128>::SMEM, LgTile<8, 32>::SMEM, LgTile<32, 32>::SMEM};
-    const int ki = ks == 1 ? 0 : ks == 2 ? 1 : ks == 4 ? 2 : ks == 8 ? 3 : 4;
-    const LgKern kern = kerns[tier][ki];
-    static bool wide[64] = {false};  // 16-CTA clusters need the non-portable opt-in
-    if (dev < 64 && !wide[dev]) {
-        for (int i = 0; i < 3; i++)
-            QG_CUDA(cudaFuncSetAttribute(kerns[i][4], cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        wide[dev] = true;
+
+// xp[s, :] = xh[slot_token[s], :] (fp16 rows, 16-byte copies).
+__global__ void k_gather_h16(const __half *__restrict__ xh, const int32_t *__restrict__ slot_token,
+                             int nslots, int H, __half *__restrict__ xp) {
+    pdl_enter();
+    const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nw = (gridDim.x * blockDim.x) >> 5;
+    for (int s = wg; s < nslots; s += nw) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xh + (size_t)slot_token[s] * H);
+        uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)s * H);
+        for (int c = lane; c < H / 8; c += 32) dst[c] = src[c];
     }
-    const int TT = tts[tier], RR = rrs[tier];
-    QG_CUDA(launch_pdl(kern, dim3((T + TT - 1) / TT, (Ep + RR - 1) / RR, ks), dim3(256),
-                       smems[tier], s, ks, x, T, H, E, Ep, router, shared_gate, logits));
+}
+
+static int launch_gather_h16(const __half *xh, const int32_t *slot_token, int nslots, int H,
+                             __half *xp, int dev, cudaStream_t s) {
+    if (nslots <= 0) return QGMOE_OK;
+    int blocks = (nslots + 7) / 8;
+    const int cap = num_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    QG_CUDA(launch_pdl(k_gather_h16, dim3(blocks), dim3(256), 0, s, 1, xh, slot_token, nslots, H,
+                       xp));
     return QGMOE_OK;
 }
 
 int launch_route(const float *x, int T, int H, int E, int k, int mode, const float *router,
-                 const float *shared_gate, int has_shared, RouteState st, __half *xp, int *err,
-                 cudaStream_t s, const RouterTC *tc) {
+                 const float *shared_gate, int has_shared, RouteState st, __half *xh, __half *xp,
+                 int *err, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int Ep = E + (has_shared ? 1 : 0);
-    const bool on_tc = tc && T >= RTC_MIN_T && T <= tc->cap && Ep <= tc->rows_pad;
-    if (on_tc) {
-        int rc = launch_logits_tc(*tc, x, T, H, Ep, st.logits, err, s);
-        if (rc) return rc;
-    } else {
-        int rc = launch_logits(x, T, H, E, Ep, router, shared_gate, st.logits, dev, s);
-        if (rc) return rc;
-    }
+    int rc = launch_logits(x, T, H, E, Ep, router, shared_gate, st.logits, xp ? xh : nullptr, err,
+                           s);
+    if (rc) return rc;
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;
     const size_t sm3 = sizeof(int) * (size_t)(RT_WARPS + 1) * E;
@@ -599,9 +613,7 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     }
     if (xp) {
         const int nslots = T * k + (has_shared ? T : 0);
-        // after the tensor-core logits the fp16 rows exist already (xh = fp16(x))
-        return on_tc ? launch_gather_h16(tc->xh, st.slot_token, nslots, H, xp, s)
-                     : launch_gather_f16(x, st.slot_token, nslots, H, xp, s);
+        return launch_gather_h16(xh, st.slot_token, nslots, H, xp, dev, s);
     }
     return QGMOE_OK;
 }

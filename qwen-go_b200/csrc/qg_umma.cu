@@ -867,26 +867,6 @@ k_umma_ts(const __grid_constant__ CUtensorMap tmap_b, const UmmaArgs a) {
     }
 }
 
-// ---- activation gather: xp[s, :] = fp16(x[slot_token[s], :]) -------------
-__global__ void k_gather_f16(const float *__restrict__ x, const int32_t *__restrict__ slot_token,
-                             int nslots, int H, __half *__restrict__ xp) {
-    pdl_enter();
-    const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    const int nw = (gridDim.x * blockDim.x) >> 5;
-    for (int s = wg; s < nslots; s += nw) {
-        const float *src = x + (size_t)slot_token[s] * H;
-        __half *dst = xp + (size_t)s * H;
-        for (int k = lane * 8; k < H; k += 256) {
-            const float4 v0 = *reinterpret_cast<const float4 *>(src + k);
-            const float4 v1 = *reinterpret_cast<const float4 *>(src + k + 4);
-            __half2 h[4] = {__floats2half2_rn(v0.x, v0.y), __floats2half2_rn(v0.z, v0.w),
-                            __floats2half2_rn(v1.x, v1.y), __floats2half2_rn(v1.z, v1.w)};
-            *reinterpret_cast<uint4 *>(dst + k) = *reinterpret_cast<uint4 *>(h);
-        }
-    }
-}
-
 // ---- QuantLinear on the tensor cores: fp16 rows + one-group tables ----------
 __global__ void k_ql_prep(const float *__restrict__ x, int64_t n4, __half *__restrict__ xp, int T,
                           int nt, int32_t *__restrict__ tab, int *err) {
@@ -1078,20 +1058,6 @@ int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_
     if (n == 0) return QGMOE_OK;
     k_repack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, sc, bits, E, rows_per_e, K, RT,
                                                           interleave, up_offset, qo);
-    QG_CUDA(cudaGetLastError());
-    return QGMOE_OK;
-}
-
-int launch_gather_f16(const float *x, const int32_t *slot_token, int nslots, int H, __half *xp,
-                      cudaStream_t s) {
-    if (nslots <= 0) return QGMOE_OK;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int blocks = (nslots + 7) / 8;
-    const int cap = num_sms(dev) * 8;
-    if (blocks > cap) blocks = cap;
-    QG_CUDA(launch_pdl(k_gather_f16, dim3(blocks), dim3(256), 0, s, 1, x, slot_token, nslots, H,
-                       xp));
     QG_CUDA(cudaGetLastError());
     return QGMOE_OK;
 }

@@ -61,6 +61,8 @@ class _Desc(C.Structure):
         ("shared_down_q", _vp), ("shared_down_scale", _vp),
         ("ep_world", C.c_int32), ("ep_rank", C.c_int32),
         ("ep_slot", _vp),
+        ("router_bits", C.c_int32), ("router_q", _vp), ("router_scale", _vp),
+        ("shared_bits", C.c_int32),
     ]
 
 
@@ -102,7 +104,7 @@ SIGNATURES = {
     "qg_randn_device": ([C.c_uint64, C.c_uint64, C.c_uint64, C.c_int64, C.c_float, _vp, _vp],
                         C.c_int),
     "qgmoe_route_static": ([_vp, _vp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
-                            _vp, _vp, _vp], C.c_int),
+                            _vp, _vp, _vp, _vp], C.c_int),
     "qgmoe_strerror": ([C.c_int], C.c_char_p),
     "qgmoe_last_error": ([], C.c_char_p),
     "qgmoe_device_ok": ([C.c_int32], C.c_int),
@@ -173,18 +175,24 @@ class MoeMLP:
                scales (fp16 bits as uint16, or float32 with scale_dtype=F32).
     bits 16: raw bf16 experts (gateUpRaw / downRaw) as uint16 bit patterns in
                the *_q arguments, no scales.
+    shared_bits (0 = bits) gives the shared expert its own format (the
+    shared_* arguments in that format); router_bits 16 / 8 / 4 takes the
+    router as bf16 bits or quantLinear codes in router_q (+ router_scale)
+    instead of float32 rows (routerQuant, model/moe.go:16).
     Arrays may be numpy (host) or torch CUDA tensors (device); create()
     copies them.
     """
 
     def __init__(self, *, n_embed, n_experts, top_k, n_moe_mlp, n_shared_mlp=0, bits=32,
                  router_mode=ROUTER_TOPK, scale_dtype=SCALE_F16, device=0, ep_world=1, ep_rank=0,
-                 ep_slot=None, router, shared_gate=None,
+                 ep_slot=None, router=None, shared_gate=None, router_bits=0, router_q=None,
+                 router_scale=None, shared_bits=0,
                  gate_up=None, down=None, shared_gate_proj=None, shared_up_proj=None,
                  shared_down_proj=None, gate_up_q=None, gate_up_scale=None, down_q=None,
                  down_scale=None, shared_gate_q=None, shared_gate_scale=None, shared_up_q=None,
                  shared_up_scale=None, shared_down_q=None, shared_down_scale=None):
-        arrays = dict(router=router, shared_gate=shared_gate, gate_up=gate_up, down=down,
+        arrays = dict(router=router, router_q=router_q, router_scale=router_scale,
+                      shared_gate=shared_gate, gate_up=gate_up, down=down,
                       shared_gate_proj=shared_gate_proj, shared_up_proj=shared_up_proj,
                       shared_down_proj=shared_down_proj, gate_up_q=gate_up_q,
                       gate_up_scale=gate_up_scale, down_q=down_q, down_scale=down_scale,
@@ -201,6 +209,7 @@ class MoeMLP:
             scale_dtype
         d.weights_on_device, d.device = int(on_dev), device
         d.ep_world, d.ep_rank = ep_world, ep_rank
+        d.router_bits, d.shared_bits = router_bits, shared_bits
         slot = None
         if ep_slot is not None:
             slot = np.ascontiguousarray(ep_slot, np.int32)

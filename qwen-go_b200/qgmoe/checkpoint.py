@@ -19,6 +19,11 @@ save_layer_raw writes a layer with raw stacked experts instead, as the
 reference reads them from bf16 checkpoints (<prefix>experts.gate_up_proj.weight
 BF16 [E, 2I, H], .down_proj.weight BF16 [E, H, I], shared_expert.*.weight);
 qgmoe_file_layer_desc takes either form (bits 16 for BF16, 32 for F32).
+save_layer_groups writes each group (router, routed experts, shared expert)
+in its own format, as the reference's checkpoints mix them: cmd/qwen-quant
+quantises an MoE model's shared-expert projections and leaves the router and
+the stacked experts raw (cmd/qwen-quant/main.go:61-65), and a quantised
+router (mlp.gate.qweight / .scale) loads as routerQuant (model/load.go:651).
 
 Tensor data starts on 64-byte boundaries (the header is space-padded), so
 the mapped tensors are aligned for any element type.
@@ -175,3 +180,70 @@ def save_layer_raw(path: str, prefix: str, *, router, gate_up, down, shared_gate
         if g.dtype == np.uint16:
             names16.add(prefix + "shared_expert_gate.weight")
     write_safetensors(path, t, {"format": "pt"}, bf16=names16)
+
+
+def save_layer_groups(path: str, prefix: str, *, router, experts, shared=None, shared_gate=None,
+                      append: dict | None = None, quant_json: str | None = None):
+    """One MoE layer, each group in its own format.  A weight is given as a
+    float32 array (F32 <name>.weight), a uint16 array of bf16 bit patterns
+    (BF16 <name>.weight) or a (codes, scales) pair of a quantised linear
+    (<name>.qweight I8 [.., K] for int8 or U8 [.., K/2] for int4, <name>.scale
+    F32, F16 or fp16 bits as uint16, [.., K/32]).
+      router      [E, H]
+      experts     (gate_up [E, 2I, H], down [E, H, I])
+      shared      (gate_proj [Is, H], up_proj [Is, H], down_proj [H, Is]) or None
+      shared_gate [H] float32 (with the shared expert)
+    With quant_json, also writes the reference's manifest of the quantised
+    tensors (one bit width per manifest, as the reference's)."""
+    t = dict(append or {})
+    names16, quantised, widths = set(), [], set()
+
+    def put(base, w, lead):
+        if isinstance(w, tuple):
+            q, s = (np.asarray(a) for a in w)
+            s = s.reshape(lead + (-1,))
+            K = s.shape[-1] * 32
+            q = q.reshape(lead + (-1,))
+            bits = 8 if q.shape[-1] == K else 4
+            if bits == 4 and 2 * q.shape[-1] != K:
+                raise ValueError(f"{base}: codes of width {q.shape[-1]} do not fit {K} inputs")
+            t[prefix + base + ".qweight"] = q.view(np.int8) if bits == 8 else q.view(np.uint8)
+            if s.dtype not in (np.float32, np.float16, np.uint16):
+                raise TypeError(f"{base}: scales must be float32, float16 or fp16 bits")
+            t[prefix + base + ".scale"] = s
+            quantised.append(prefix + base + ".weight")
+            widths.add(bits)
+            return
+        a = np.asarray(w)
+        if a.dtype == np.uint16:
+            names16.add(prefix + base + ".weight")
+        elif a.dtype != np.float32:
+            raise TypeError(f"{base}: float32, bf16 bits (uint16) or (codes, scales) expected")
+        t[prefix + base + ".weight"] = a.reshape(lead + (-1,))
+
+    def rows_cols(w):  # (rows, inputs) of a weight in any of the three forms
+        if isinstance(w, tuple):
+            s = np.asarray(w[1])
+            K = s.shape[-1] * 32
+            return s.size // s.shape[-1], K
+        a = np.asarray(w)
+        return a.size // a.shape[-1], a.shape[-1]
+
+    E, H = rows_cols(router)
+    gu, dn = experts
+    put("gate", router, (E,))
+    put("experts.gate_up_proj", gu, (E, rows_cols(gu)[0] // E))
+    put("experts.down_proj", dn, (E, H))
+    if shared is not None:
+        sg, su, sd = shared
+        Is = rows_cols(sg)[0]
+        put("shared_expert.gate_proj", sg, (Is,))
+        put("shared_expert.up_proj", su, (Is,))
+        put("shared_expert.down_proj", sd, (H,))
+        t[prefix + "shared_expert_gate.weight"] = np.asarray(shared_gate, np.float32).reshape(1, H)
+    write_safetensors(path, t, {"format": "pt"}, bf16=names16)
+    if quant_json and quantised:
+        if len(widths) != 1:
+            raise ValueError("quant.json holds one bit width; the layer mixes int8 and int4")
+        with open(quant_json, "w") as f:
+            json.dump({"bits": widths.pop(), "quantized": quantised}, f, indent=1)

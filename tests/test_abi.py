@@ -34,6 +34,25 @@ def test_exports_every_declared_symbol():
     assert set(names) == set(qgmoe.SIGNATURES), set(names) ^ set(qgmoe.SIGNATURES)
 
 
+def test_descriptor_layout_matches_the_c_struct(tmp_path):
+    """The ctypes mirror of qgmoe_desc (qgmoe/__init__.py) has the C struct's
+    size and field offsets, compiled from include/qgmoe.h with gcc."""
+    import subprocess
+    fields = [f for f, _ in qgmoe._Desc._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"qgmoe.h\"\n"
+                   "int main(void) {\n  printf(\"%zu\\n\", sizeof(qgmoe_desc));\n" +
+                   "".join(f'  printf("%zu\\n", offsetof(qgmoe_desc, {f}));\n' for f in fields) +
+                   "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(REPO, "include"), str(src), "-o",
+                    str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert got[0] == C.sizeof(qgmoe._Desc)
+    assert got[1:] == [getattr(qgmoe._Desc, f).offset for f in fields]
+
+
 def test_status_strings():
     assert qgmoe.status_text(0) == "ok"
     assert "invalid" in qgmoe.status_text(-1)

@@ -134,11 +134,14 @@ def test_malformed_files_are_rejected(tmp_path):
             f.write(content)
         with pytest.raises(qgmoe.QgmoeError):
             qgmoe.LayerFile(p)
-    # data beyond the file, byte count not matching the shape, missing keys
+    # data beyond the file, byte count not matching the shape, missing keys,
+    # a byte count that overflows
     for hdr, data in (({"a": {"dtype": "F32", "shape": [4], "data_offsets": [0, 16]}}, b"\0" * 8),
                       ({"a": {"dtype": "F32", "shape": [3], "data_offsets": [0, 16]}}, b"\0" * 16),
                       ({"a": {"dtype": "F32", "shape": [4]}}, b"\0" * 16),
-                      ({"a": {"dtype": "F32", "shape": [-4], "data_offsets": [0, 16]}}, b"\0" * 16)):
+                      ({"a": {"dtype": "F32", "shape": [-4], "data_offsets": [0, 16]}}, b"\0" * 16),
+                      # 2^62 float32s: the byte count wraps to 0 in 64 bits
+                      ({"a": {"dtype": "F32", "shape": [1 << 62], "data_offsets": [0, 0]}}, b"")):
         _write_raw(p, hdr, data)
         with pytest.raises(qgmoe.QgmoeError):
             qgmoe.LayerFile(p)
@@ -333,3 +336,47 @@ def test_quantize_layer_tool(tmp_path, bits, Is):
             q_sd, s_sd = oracle_quantize(O.bf16_widen(m.q["sh_down"]), bits)
             assert _bytes(d.shared_down_q, q_sd) and _bytes(d.shared_down_scale, s_sd)
     assert json.load(open(qj))["bits"] == bits
+
+
+@pytest.mark.parametrize("sdt", ["f16", "f32"])
+def test_mixed_layer_desc(tmp_path, sdt):
+    """A layer whose groups have their own formats (bf16 routed experts, an
+    int8 shared expert, an int8 router) gives a descriptor with each group's
+    format and pointers into the mapping at the written bytes, and the
+    reference's quant.json lists the quantised linears; a layer whose
+    quantised groups mix F16 and F32 scales is rejected."""
+    m = O.make_moe(H=128, E=4, k=2, I=64, Is=64, bits=16, seed=31, shared_bits=8, router_bits=8)
+    sc = (lambda s16, s32: s16) if sdt == "f16" else (lambda s16, s32: s32)
+    s32 = {k: m.s[k] for k in ("sh_gate", "sh_up", "sh_down")}
+    s32["router"] = m.s32["router"]
+    p = str(tmp_path / "mixed.safetensors")
+    qj = str(tmp_path / "quant.json")
+    ck.save_layer_groups(
+        p, "L.", router=(m.q["router"], sc(m.s16["router"], s32["router"])),
+        experts=(m.q["gate_up"], m.q["down"]),
+        shared=tuple((m.q[k], sc(m.s16[k], s32[k])) for k in ("sh_gate", "sh_up", "sh_down")),
+        shared_gate=m.shared_gate, quant_json=qj)
+    with qgmoe.LayerFile(p) as f:
+        d = f.layer_desc("L.", top_k=2)
+        assert (d.n_embed, d.n_experts, d.n_moe_mlp, d.n_shared_mlp) == (128, 4, 64, 64)
+        assert (d.bits, d.shared_bits, d.router_bits) == (16, 8, 8)
+        assert d.scale_dtype == (qgmoe.SCALE_F16 if sdt == "f16" else qgmoe.SCALE_F32)
+        assert not d.router
+        _, _, rq, nb = f.tensor("L.gate.qweight")
+        assert d.router_q == rq and nb == m.q["router"].nbytes
+        assert bytes(C.string_at(d.router_q, nb)) == m.q["router"].tobytes()
+        assert bytes(C.string_at(d.gate_up_q, m.q["gate_up"].nbytes)) == m.q["gate_up"].tobytes()
+        assert bytes(C.string_at(d.shared_up_q, m.q["sh_up"].nbytes)) == m.q["sh_up"].tobytes()
+    with open(qj) as fh:
+        man = json.load(fh)
+    assert man == {"bits": 8, "quantized": ["L.gate.weight"] + [
+        f"L.shared_expert.{n}_proj.weight" for n in ("gate", "up", "down")]}
+    # mixed scale dtypes across groups
+    bad = str(tmp_path / "bad.safetensors")
+    ck.save_layer_groups(
+        bad, "L.", router=(m.q["router"], m.s16["router"]), experts=(m.q["gate_up"], m.q["down"]),
+        shared=tuple((m.q[k], s32[k]) for k in ("sh_gate", "sh_up", "sh_down")),
+        shared_gate=m.shared_gate)
+    with qgmoe.LayerFile(bad) as f:
+        with pytest.raises(qgmoe.QgmoeError):
+            f.layer_desc("L.", top_k=2)
