@@ -277,11 +277,14 @@ def oracle_layer_cpu(cfg, threads):
 
     host = {"router": gen(0, (E, H))}
     x = gen(100, (cfg["T"], H), 1.0)
+    info = {}
     if cfg["zipf"]:
         x += MU
         host["router"] -= host["router"].mean(axis=1, keepdims=True)
-        c, _ = calibrate_zipf(host["router"], x[:1024], k)
+        c, hist = calibrate_zipf(host["router"], x[:1024], k)
         host["router"] += zipf_bias_rows(E, H, c)[:, None]
+        info["zipf_c"] = c
+        info["calibration_expert_load_top8"] = sorted(hist.tolist(), reverse=True)[:8]
     mats = {"gate_up": (1, (E * 2 * I, H)), "down": (2, (E * H, I))}
     if Is:
         host["shared_gate"] = gen(3, (H,))
@@ -294,7 +297,7 @@ def oracle_layer_cpu(cfg, threads):
             q, s = O.quantize(w, bits)
             host[name + "_q"] = q
             host[name + "_s"] = O.f16_round(s)
-    return oracle_weights(cfg, host), x
+    return oracle_weights(cfg, host), x, info
 
 
 # --------------------------------------------------------------------------
@@ -304,8 +307,8 @@ def oracle_layer_cpu(cfg, threads):
 
 class ClockSampler:
     """Samples SM clock and clock-event (throttle) reasons of one GPU during
-    the timed region: NVML polled every ~10 ms from a thread (so even a
-    region of a few ms gets samples), nvidia-smi -lms 50 as a fallback."""
+    the timed regions: NVML polled every ~2 ms from a thread, so even a
+    region of a few ms gets several samples."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
@@ -341,7 +344,7 @@ class ClockSampler:
                                              int(get_r(h))))
                     except Exception:
                         pass
-                    time.sleep(0.01)
+                    time.sleep(0.002)
             self.t = threading.Thread(target=run, daemon=True)
             self.t.start()
         except Exception:
@@ -363,7 +366,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(s for s, _ in self.samples),
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
-                "samples": len(self.samples), "source": "nvml, 10 ms poll"}
+                "samples": len(self.samples), "source": "nvml, 2 ms poll"}
 
 
 # --------------------------------------------------------------------------
@@ -425,7 +428,7 @@ def run_reference(args, cfg):
         return
     import qg_oracle as O
     threads = os.cpu_count() or 1
-    m, x = oracle_layer_cpu(cfg, threads)
+    m, x, info = oracle_layer_cpu(cfg, threads)
     # size one step to a bounded token sample (a few seconds on all cores)
     t0 = time.perf_counter()
     O.moe_forward_mt(m, x[:threads], threads)
@@ -447,7 +450,7 @@ def run_reference(args, cfg):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_json(cfg, world),
+        "data": "synthetic", "config": dict(config_json(cfg, world), **info),
         "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{n} of {cfg['T']} tokens per step, token-parallel over "
                                    f"{threads} threads (the Go reference runs the MoE serially "
@@ -480,6 +483,113 @@ def config_json(cfg, world):
             "batch": "T tokens per GPU (weak scaling over GPUs)"}
 
 
+def stage_bytes(cfg, stage, distinct, T):
+    """Algorithmic HBM bytes of one decode stage: the weights of the experts
+    the batch routed to (gate_up = 2/3 of an expert, down = 1/3), the shared
+    expert's share, and the stage's activations (f32 in and out)."""
+    H, E, I, Is = cfg["H"], cfg["E"], cfg["I"], cfg["Is"]
+    bpw = {32: 4.0, 16: 2.0, 8: 1.0 + 2 / 32, 4: 0.5 + 2 / 32}[cfg["bits"]]
+    if stage == "route":
+        return (E + (1 if Is else 0)) * H * 4 + T * H * 4
+    if stage == "gate_up":
+        return (distinct * 2 * I * H + 2 * Is * H) * bpw + T * H * 4
+    if stage == "down":
+        return (distinct * I * H + Is * H) * bpw + T * H * 4
+    return T * H * 4 * (cfg["k"] + 1)  # combine: k rows in, one out
+
+
+def time_forwards(layer, x, out, sel, steps, flush, stream, dev):
+    """K forwards bracketed one by one by CUDA events on the launching stream
+    (an L2 flush, when given, runs before each event pair); then the same K
+    forwards with per-stage events (graphs off).  Returns (total ms, stage ms
+    per forward, forwards timed)."""
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        if flush is not None:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+        evs[i][0].record(stream)
+        layer.forward_device(x, out, sel_idx=sel, stream=stream)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    layer.sync(stream)
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+    layer.set_timing(True)
+    for _ in range(steps):
+        if flush is not None:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+        layer.forward_device(x, out, sel_idx=sel, stream=stream)
+    stage_ms, nf = layer.read_timing()
+    layer.set_timing(False)
+    layer.sync(stream)
+    return total_ms, {k: v / max(nf, 1) for k, v in stage_ms.items()}, nf
+
+
+def measure_decode(name, T, steps, dev, peaks):
+    """One decode configuration: tokens/s of the layer forward (graph replay,
+    L2 flushed before every forward when the layer fits in L2), the stage
+    times, and the dominant stage's algorithmic HBM bytes against the
+    measured copy bandwidth."""
+    import torch
+    cfg = dict(CONFIGS[name])
+    cfg["T"] = T
+    layer, x, _host, _info = build_gpu_layer(cfg, dev, keep_host=False)
+    out = torch.empty_like(x)
+    sel = torch.empty((T, cfg["k"]), dtype=torch.int32, device=x.device)
+    fits_l2 = cfg["E"] * weight_bytes(cfg) + 3 * cfg["Is"] * cfg["H"] * 2 <= L2_BYTES
+    flush = (torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=x.device)
+             if fits_l2 else None)
+    stream = torch.cuda.Stream(dev)
+    for _ in range(5):
+        layer.forward_device(x, out, sel_idx=sel, stream=stream)
+    layer.sync(stream)
+    distinct = int((np.bincount(sel.cpu().numpy().ravel(), minlength=cfg["E"]) > 0).sum())
+    total_ms, stages, _ = time_forwards(layer, x, out, sel, steps, flush, stream, dev)
+    dom = max(("gate_up", "down", "route"), key=lambda s: stages.get(s, 0.0))
+    by = stage_bytes(cfg, dom, distinct, T)
+    gbs = by / (stages[dom] / 1e3) / 1e9
+    res = {"config": name, "tokens": T, "tokens_per_s": T * steps / (total_ms / 1e3),
+           "forward_us": 1e3 * total_ms / steps, "distinct_experts": distinct,
+           "stage_us": {k: round(1e3 * v, 2) for k, v in stages.items()},
+           "dominant": dom, "dominant_bytes": int(by), "dominant_gbs": gbs,
+           "hbm_frac": gbs / peaks["hbm_gbs"], "l2": "flushed" if flush is not None else
+           "weights > L2", "launches": layer.last_launch_count()}
+    layer.close()
+    del x, out, sel, flush
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_stack(dev):
+    """Config 4's MoE layers: 48 int8 layers of the Qwen3-MoE shape (H=2048,
+    E=128, top-8, I=768, ~31 GB of weights, so nothing stays in L2), a
+    512-token prefill and 256 single-token decode steps layer after layer
+    through qgmoe_forward from the plain-C host tests/c/stack_host.c (the
+    call a cgo shim makes, the residual kept on the host as decodeLayers
+    does).  Attention, embeddings and sampling are outside the rebuilt path.
+    Reports the host's JSON line (MoE tokens/s = tokens / time inside
+    qgmoe_forward; loop tokens/s includes the host's norm and residual)."""
+    import torch
+    from qgmoe.build import build_host
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    exe = build_host("stack_host")
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=os.environ.get("CUDA_VISIBLE_DEVICES", str(dev)))
+    r = subprocess.run([exe, "bench", "48", "2048", "128", "8", "768", "8", "512", "256", "4"],
+                       capture_output=True, text=True, timeout=900, env=env)
+    if r.returncode != 0:
+        return {"error": (r.stderr or r.stdout).strip()[-300:]}
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    res["workload"] = ("c4: 48 int8 MoE layers (H=2048, E=128, top-8, I=768), 512-token "
+                       "prefill + 256 decode steps through qgmoe_forward from a C host; "
+                       "synthetic N(0,1) activations, seed 4")
+    return res
+
+
 def run_ours(args, cfg):
     import torch
     import qgmoe
@@ -489,6 +599,7 @@ def run_ours(args, cfg):
     torch.cuda.set_device(dev)
     if world > 1:
         return run_ep(args, cfg, world, rank, local)
+    peaks, peak_src = load_peaks()
     layer, x, host, info = build_gpu_layer(cfg, dev)
     layer.set_path({"auto": qgmoe.PATH_AUTO, "cuda_core": qgmoe.PATH_CUDA_CORE,
                     "tensor": qgmoe.PATH_TENSOR}[args.path])
@@ -502,55 +613,53 @@ def run_ours(args, cfg):
     # A dedicated stream: the library's NULL-stream argument means "the
     # handle's own stream", so torch's default stream must not be passed.
     stream = torch.cuda.Stream(dev)
-
-    def step():
-        with torch.cuda.stream(stream):
-            if flush is not None:
-                flush.zero_()
-            layer.forward_device(x, out, sel_idx=sel, stream=stream)
-
     torch.cuda.synchronize(dev)
     for _ in range(max(args.warmup, 3)):
-        step()
+        if flush is not None:
+            with torch.cuda.stream(stream):
+                flush.zero_()
+        layer.forward_device(x, out, sel_idx=sel, stream=stream)
     layer.sync(stream)
     hist = np.bincount(sel.cpu().numpy().ravel(), minlength=cfg["E"])
     distinct = int((hist > 0).sum())
 
-    # ---- timed region (device events, max over ranks) ----
+    # ---- timed regions (device events on the launching stream) ----
     # Repeated identical forwards replay a CUDA graph inside the library.
     # Each forward is bracketed by its own event pair, so the L2 flush that
-    # precedes it (small layers) stays outside the timed sum.
+    # precedes it (small layers) stays outside the timed sum; the second pass
+    # records an event between consecutive stages (graphs off).
     barrier(world)
-    torch.cuda.synchronize(dev)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
     with ClockSampler(dev) as clk:
-        for i in range(args.steps):
-            with torch.cuda.stream(stream):
-                if flush is not None:
+        total_ms, stages, nf = time_forwards(layer, x, out, sel, args.steps, flush, stream, dev)
+        total_ms = max_over_ranks(total_ms, world)
+        ms_per_step = total_ms / args.steps
+        forward_ms = sum(stages.values())
+        value = T * world * args.steps / (total_ms / 1e3)
+
+        # ---- end to end through the public host API (pinned buffers) ----
+        xh = x.cpu().pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        L = qgmoe.lib()
+        for _ in range(2):
+            rc = L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
+            assert rc == 0, qgmoe.last_error()
+        e2e_steps = max(1, min(args.steps, 20))
+        barrier(world)
+        e2e_s = 0.0
+        for _ in range(e2e_steps):
+            if flush is not None:
+                with torch.cuda.stream(stream):
                     flush.zero_()
-            evs[i][0].record(stream)
-            layer.forward_device(x, out, sel_idx=sel, stream=stream)
-            evs[i][1].record(stream)
-        torch.cuda.synchronize(dev)
-    layer.sync(stream)
-    total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs), world)
-    ms_per_step = total_ms / args.steps
-    # ---- second timed region: the same K steps with a CUDA event between
-    # consecutive launches (graphs off), for the per-kernel durations ----
-    layer.set_timing(True)
-    torch.cuda.synchronize(dev)
-    for _ in range(args.steps):
-        step()
-    stage_ms, nf = layer.read_timing()
-    layer.set_timing(False)
-    layer.sync(stream)
-    forward_ms = sum(stage_ms.values()) / max(nf, 1)
-    value = T * world * args.steps / (total_ms / 1e3)
+                stream.synchronize()
+            t0 = time.perf_counter()
+            L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
+            e2e_s += time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s, world)
+    e2e = {"value": T * world * e2e_steps / e2e_s, "unit": "tokens/s",
+           "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
+           "api": "qgmoe_forward (host pointers, blocking)"}
 
     # ---- roofline of the dominant kernel ----
-    peaks, peak_src = load_peaks()
-    stages = {kname: v / max(nf, 1) for kname, v in stage_ms.items()}
     dom = max(stages, key=stages.get)
     dom_ms = stages[dom]
     prefill = cfg["T"] >= 512
@@ -565,8 +674,7 @@ def run_ours(args, cfg):
                 "peak_source": f"{peak_src} bf16 dense (MEASURED_PEAKS.json bf16_tflops)",
                 "algorithmic_per_launch": f"{flops / 1e9:.1f} GFLOP", "traffic": traffic}
     else:
-        frac_w = (2 / 3) if dom == "gate_up" else (1 / 3)
-        bytes_ = distinct * weight_bytes(cfg) * frac_w + T * H * 4 * 2
+        bytes_ = stage_bytes(cfg, dom, distinct, T)
         achieved = bytes_ / (dom_ms / 1e3) / 1e9
         peak = peaks["hbm_gbs"]
         roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -575,33 +683,24 @@ def run_ours(args, cfg):
     if traffic is not None:
         roof["traffic_unit"] = "DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)"
         roof["traffic_source"] = traffic_src
-
-    # ---- end to end through the public host API (pinned buffers) ----
-    xh = x.cpu().pin_memory()
-    oh = torch.empty_like(xh).pin_memory()
-    L = qgmoe.lib()
-    for _ in range(2):
-        rc = L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
-        assert rc == 0, qgmoe.last_error()
-    e2e_steps = max(1, min(args.steps, 20))
-    barrier(world)
-    e2e_s = 0.0
-    for _ in range(e2e_steps):
-        if flush is not None:
-            with torch.cuda.stream(stream):
-                flush.zero_()
-            stream.synchronize()
-        t0 = time.perf_counter()
-        L.qgmoe_forward(layer.h, xh.data_ptr(), T, oh.data_ptr(), None, None)
-        e2e_s += time.perf_counter() - t0
-    e2e_s = max_over_ranks(e2e_s, world)
-    e2e = {"value": T * world * e2e_steps / e2e_s, "unit": "tokens/s",
-           "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
-           "api": "qgmoe_forward (host pointers, blocking)"}
+    launches = layer.last_launch_count()
+    layer.close()
+    del layer, out, sel, flush
+    torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_ours(cfg, host, x.cpu().numpy())
+    del x
+
+    # ---- the decode configurations (1 GPU, replicas only) ----
+    decode = None
+    if args.config == "c3" and not args.no_decode:
+        decode = [measure_decode(name, t, max(args.steps, 50), dev, peaks)
+                  for name, ts in (("c1", (1, 8, 32)), ("c2", (1, 16, 64))) for t in ts]
+    stack = None
+    if args.config == "c3" and not args.no_stack:
+        stack = run_stack(dev)
 
     if rank == 0:
         cfgj = config_json(cfg, world)
@@ -613,14 +712,17 @@ def run_ours(args, cfg):
             "metric": "MoE-layer tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": dtype_label(cfg, layer), "data": "synthetic", "config": cfgj,
-            "stage_ms": stages, "forward_ms_device": forward_ms,
+            "vs_baseline": None, "dtype": dtype_label(cfg, None), "data": "synthetic",
+            "config": cfgj, "stage_ms": stages, "forward_ms_device": forward_ms,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": layer.last_launch_count() * args.steps,
+            "gpu_launches": launches * args.steps,
             "clocks": clk.summary(),
         }
+        if decode is not None:
+            line["decode"] = decode
+        if stack is not None:
+            line["c4_stack"] = stack
         print(json.dumps(line), flush=True)
-    layer.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -777,6 +879,10 @@ def main():
     ap.add_argument("--path", default="auto", choices=["auto", "cuda_core", "tensor"],
                     help="expert-product path (qgmoe_set_path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="config 3: skip the decode configurations in the line")
+    ap.add_argument("--no-stack", action="store_true",
+                    help="config 3: skip the 48-layer config-4 stack in the line")
     ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "round-robin"],
                     help="N > 1: expert placement over the ranks")
     ap.add_argument("--ep-nccl", action="store_true",

@@ -36,6 +36,7 @@
 //    itself once the offsets are known, one launch fewer.  For the tensor-core
 //    path k_gather_h16 then copies each slot's fp16 activation row.
 #include "qg_common.cuh"
+#include "qg_sm100.cuh"
 
 namespace qg {
 
@@ -73,6 +74,21 @@ struct LgCfg {
     static constexpr int XV = TT * LG_KC / 4, WV = RR * LG_KC / 4;  // float4 per chunk
     static constexpr int XPT = (XV + THREADS - 1) / THREADS, WPT = (WV + THREADS - 1) / THREADS;
 };
+
+// Two float32 additions per instruction (sm_100 packed f32x2), each rounded
+// to nearest exactly as a scalar __fadd_rn.  The products stay scalar
+// __fmul_rn: a packed multiply feeding a packed add is contracted into a
+// packed FMA by the compiler even with explicit .rn (measured on B200: 3658
+// of 4096 serial sums differed from separately rounded ones), while a
+// scalar product feeding the packed add is not (0 of 4096).
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
 
 template <int N>
 __device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
@@ -125,11 +141,12 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
         for (int j = 0; j < C::WPT; j++)
             wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + c4)) : zero;
     };
-    float acc[TPT][RPT];
+    static_assert(RPT % 2 == 0, "rows per thread are paired for the packed adds");
+    float2 acc[TPT][RPT / 2];
 #pragma unroll
     for (int i = 0; i < TPT; i++)
 #pragma unroll
-        for (int j = 0; j < RPT; j++) acc[i][j] = 0.f;
+        for (int j = 0; j < RPT / 2; j++) acc[i][j] = make_float2(0.f, 0.f);
     bool range = false;
     fetch(0);
     for (int kb = 0; kb < H; kb += LG_KC) {
@@ -178,8 +195,9 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
 #pragma unroll
             for (int i = 0; i < TPT; i++)
 #pragma unroll
-                for (int j = 0; j < RPT; j++)
-                    acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+                for (int j = 0; j < RPT / 2; j++)
+                    acc[i][j] = add2_rn(acc[i][j], make_float2(__fmul_rn(av[i], bv[2 * j]),
+                                                               __fmul_rn(av[i], bv[2 * j + 1])));
         }
         __syncthreads();
     }
@@ -191,14 +209,138 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
 #pragma unroll
         for (int j = 0; j < RPT; j++) {
             const int r = r0 + tx * RPT + j;
-            if (r < Ep) logits[(size_t)t * Ep + r] = acc[i][j];
+            if (r < Ep) logits[(size_t)t * Ep + r] = (j & 1) ? acc[i][j / 2].y : acc[i][j / 2].x;
         }
     }
 }
 
+// ---- 1b. logits of decode-sized batches ----------------------------------------------
+// A serial chain is H dependent adds long, so at a few tokens the tiled
+// kernel above spends its time waiting for each 32-wide K chunk.  Here a CTA
+// owns LR_RR router rows and TT tokens and holds their WHOLE rows in shared
+// memory: one thread issues 1-D bulk copies of every row in LR_SEG K
+// segments (one mbarrier each) -- the router rows before waiting for the
+// previous kernel, since they do not depend on it -- and each thread runs one
+// chain (row tid % LR_RR, token tid / LR_RR) segment by segment as the
+// segments land.  Rows are padded by 4 floats so the 8 rows (and 4 tokens)
+// a warp reads at one k fall in distinct banks.
+constexpr int LR_RR = 8, LR_SEG = 4;
+constexpr long long LR_WAIT_CYCLES = 2000000000LL;  // ~1 s: a lost copy cannot hang the GPU
+constexpr size_t LR_SMEM_MAX = 220 * 1024;           // of the 227 KB a CTA may opt into
+
+__host__ __device__ constexpr size_t lr_smem_bytes(int TT, int H) {
+    return sizeof(float) * (size_t)(LR_RR + TT) * (H + 4) + sizeof(uint64_t) * 2 * LR_SEG;
+}
+
+template <int TT>
+__global__ void __launch_bounds__(LR_RR *TT)
+k_logits_rows(const float *__restrict__ x, int T, int H, int E, int Ep,
+              const float *__restrict__ router, const float *__restrict__ shared_gate,
+              float *__restrict__ logits, __half *__restrict__ xh, int *err) {
+    extern __shared__ __align__(16) float lr_smem[];
+    const int HP = H + 4, L = H / LR_SEG;
+    float *ws = lr_smem;                                          // [LR_RR][HP]
+    float *xs = ws + LR_RR * HP;                                  // [TT][HP]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(xs + TT * HP);   // w segments, x segments
+    const int tid = threadIdx.x;
+    const int r0 = blockIdx.x * LR_RR, t0 = blockIdx.y * TT;
+    const int nr = min(LR_RR, Ep - r0), nt = min(TT, T - t0);
+    if (tid == 0) {
+        for (int i = 0; i < 2 * LR_SEG; i++) sm100::mbar_init(&bar[i], 1);
+        sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0)  // router rows (weights): before the wait for the previous kernel
+        for (int s = 0; s < LR_SEG; s++) {
+            sm100::mbar_arrive_expect_tx(&bar[s], (uint32_t)(nr * L * 4));
+            for (int r = 0; r < nr; r++) {
+                const float *src = (r0 + r < E ? router + (size_t)(r0 + r) * H : shared_gate);
+                sm100::bulk_load(ws + r * HP + s * L, src + s * L, L * 4, &bar[s]);
+            }
+        }
+    pdl_launch_dependents();
+    pdl_wait();
+    if (tid == 0)
+        for (int s = 0; s < LR_SEG; s++) {
+            sm100::mbar_arrive_expect_tx(&bar[LR_SEG + s], (uint32_t)(nt * L * 4));
+            for (int t = 0; t < nt; t++)
+                sm100::bulk_load(xs + t * HP + s * L, x + (size_t)(t0 + t) * H + s * L, L * 4,
+                                 &bar[LR_SEG + s]);
+        }
+    const int r = tid % LR_RR, t = tid / LR_RR;
+    float acc = 0.f;
+    bool ok = true;
+    for (int s = 0; s < LR_SEG && ok; s++) {
+        ok = sm100::mbar_wait(&bar[s], 0, 0, LR_WAIT_CYCLES) &&
+             sm100::mbar_wait(&bar[LR_SEG + s], 0, 0, LR_WAIT_CYCLES);
+        if (!ok) break;
+        const float4 *wp = reinterpret_cast<const float4 *>(ws + r * HP + s * L);
+        const float4 *xp = reinterpret_cast<const float4 *>(xs + t * HP + s * L);
+        // the add chain is the critical path: the next step's operands are
+        // loaded and its products formed while the current adds retire
+        const int n4 = L / 4;
+        float4 a = xp[0], b = wp[0];
+#pragma unroll 4
+        for (int c = 0; c < n4; c++) {
+            const int cn = c + 1 < n4 ? c + 1 : c;
+            const float4 an = xp[cn], bn = wp[cn];
+            const float p0 = __fmul_rn(a.x, b.x), p1 = __fmul_rn(a.y, b.y);
+            const float p2 = __fmul_rn(a.z, b.z), p3 = __fmul_rn(a.w, b.w);
+            acc = __fadd_rn(acc, p0);
+            acc = __fadd_rn(acc, p1);
+            acc = __fadd_rn(acc, p2);
+            acc = __fadd_rn(acc, p3);
+            a = an;
+            b = bn;
+        }
+    }
+    if (!ok) {
+        atomicOr(err, QG_FLAG_TIMEOUT);
+        // this CTA's copies must land before its shared memory goes away
+        if (tid == 0)
+            for (int i = 0; i < 2 * LR_SEG; i++) sm100::mbar_wait(&bar[i], 0, 0, LR_WAIT_CYCLES);
+        return;
+    }
+    if (r < nr && t < nt) logits[(size_t)(t0 + t) * Ep + r0 + r] = acc;
+    if (xh && blockIdx.x == 0) {  // fp16 rows of this token tile for the tensor path
+        bool range = false;
+        const int q4 = H / 4;
+        for (int i = tid; i < nt * q4; i += LR_RR * TT) {
+            const int tt = i / q4, c = i - tt * q4;
+            const float4 v = *reinterpret_cast<const float4 *>(xs + tt * HP + 4 * c);
+            const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+            const float2 af = __half22float2(a), bf = __half22float2(b);
+            range |= (isfinite(v.x) && isinf(af.x)) || (isfinite(v.y) && isinf(af.y)) ||
+                     (isfinite(v.z) && isinf(bf.x)) || (isfinite(v.w) && isinf(bf.y));
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t *>(&a);
+            u.y = *reinterpret_cast<const uint32_t *>(&b);
+            *reinterpret_cast<uint2 *>(xh + (size_t)(t0 + tt) * H + 4 * c) = u;
+        }
+        if (range) atomicOr(err, QG_FLAG_RANGE);
+    }
+}
+
+template <int TT>
+static int launch_logits_rows(const float *x, int T, int H, int E, int Ep, const float *router,
+                              const float *shared_gate, float *logits, __half *xh, int *err,
+                              int dev, cudaStream_t s) {
+    static bool attr[64] = {false};
+    const size_t smem = lr_smem_bytes(TT, H);
+    if (dev < 64 && !attr[dev]) {
+        QG_CUDA(cudaFuncSetAttribute(k_logits_rows<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)LR_SMEM_MAX));
+        attr[dev] = true;
+    }
+    QG_CUDA(launch_pdl(k_logits_rows<TT>, dim3((Ep + LR_RR - 1) / LR_RR, (T + TT - 1) / TT),
+                       dim3(LR_RR * TT), smem, s, 1, x, T, H, E, Ep, router, shared_gate, logits,
+                       xh, err));
+    return QGMOE_OK;
+}
+
 // Tile shapes by batch size: the chains are long (H steps each), so small
-// batches want many threads over the router rows and large batches enough
-// chains per thread to keep the FP32 pipes busy.
+// batches hold whole rows in shared memory (k_logits_rows) and large batches
+// keep enough chains per thread to keep the FP32 pipes busy.
 template <int TPT, int RPT, int TTH, int RTH>
 static int launch_logits_t(const float *x, int T, int H, int E, int Ep, const float *router,
                            const float *shared_gate, float *logits, __half *xh, int *err,
@@ -211,13 +353,13 @@ static int launch_logits_t(const float *x, int T, int H, int E, int Ep, const fl
 }
 
 static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
-                         const float *shared_gate, float *logits, __half *xh, int *err,
+                         const float *shared_gate, float *logits, __half *xh, int *err, int dev,
                          cudaStream_t s) {
-    if (T <= 8)  // 8 tokens x 128 rows, 4 chains per thread
-        return launch_logits_t<1, 4, 8, 32>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
-    if (T <= 128)  // 16 tokens x 64 rows, 8 chains per thread
-        return launch_logits_t<2, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
-    // 32 tokens x 64 rows, 16 chains per thread
+    if (T <= 8 && lr_smem_bytes(8, H) <= LR_SMEM_MAX)
+        return launch_logits_rows<8>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
+    if (T <= 64 && lr_smem_bytes(16, H) <= LR_SMEM_MAX)
+        return launch_logits_rows<16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
+    // 32 tokens x 64 rows, 16 chains per thread (8 f32x2 pairs)
     return launch_logits_t<4, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
 }
 
@@ -578,7 +720,7 @@ int launch_route(const float *x, int T, int H, int E, int k, int mode, const flo
     cudaGetDevice(&dev);
     const int Ep = E + (has_shared ? 1 : 0);
     int rc = launch_logits(x, T, H, E, Ep, router, shared_gate, st.logits, xp ? xh : nullptr, err,
-                           s);
+                           dev, s);
     if (rc) return rc;
     const int nc = (T + TK_TOK - 1) / TK_TOK;
     const size_t sm2 = sizeof(int) * (size_t)E;

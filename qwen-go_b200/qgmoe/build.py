@@ -87,5 +87,29 @@ def build(force: bool = False, verbose_ptxas: bool = False, extra: list[str] | N
     return LIB
 
 
+HOSTS_SRC = os.path.join(REPO, "tests", "c")
+HOSTS_BUILD = os.path.join(HOSTS_SRC, "_build")
+
+
+def build_host(name: str) -> str:
+    """Compiles the plain-C host tests/c/<name>.c (a C99 program using only
+    include/qgmoe.h and the CUDA runtime's C API) against the in-tree
+    library; returns the executable's path.  Incremental by mtime."""
+    src = os.path.join(HOSTS_SRC, name + ".c")
+    exe = os.path.join(HOSTS_BUILD, name)
+    lib = build()
+    if _stale(exe, [src, lib, os.path.join(REPO, "include", "qgmoe.h")]):
+        os.makedirs(HOSTS_BUILD, exist_ok=True)
+        cuda = os.path.dirname(os.path.dirname(nvcc()))
+        cmd = ["gcc", "-std=c99", "-O2", "-Wall", "-Wextra", "-pedantic", "-D_POSIX_C_SOURCE=200809L",
+               "-I", os.path.join(REPO, "include"), "-I", os.path.join(cuda, "include"), src,
+               "-o", exe, "-L", LIB_DIR, "-lqgmoe", "-L", os.path.join(cuda, "lib64"), "-lcudart",
+               "-lm", "-Wl,-rpath," + LIB_DIR + ":" + os.path.join(cuda, "lib64")]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"gcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    return exe
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv))
