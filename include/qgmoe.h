@@ -204,12 +204,15 @@ int qgmoe_sync(qgmoe_t *h, void *stream);
 /* Number of kernel launches the last forward enqueued (instrumentation). */
 int qgmoe_last_launch_count(const qgmoe_t *h);
 
-/* Expert-product path.  AUTO picks the tcgen05 tensor-core grouped GEMMs
- * whenever the layer allows them (int8/int4 experts; H, I and the shared
- * width multiples of 128), except for the smallest batches of a layer with
- * a shared expert (T*k < 16), and the CUDA-core streaming GEMV otherwise.
- * CUDA_CORE / TENSOR force one path (TENSOR returns QGMOE_ERR_UNSUPPORTED
- * when the layer does not allow it). */
+/* Expert-product path.  AUTO runs decode-sized batches (up to 8 tokens,
+ * routed and shared experts in one format, the batch's rows within the
+ * kernels' shared memory) on the four-kernel decode path (router logits;
+ * routing; gate_up; down + combine), larger ones on the tcgen05 tensor-core
+ * grouped GEMMs whenever the layer allows them (int8/int4 routed experts; H
+ * and I multiples of 128), except for the smallest batches of a layer with
+ * a shared expert (T*k < 16), and on the CUDA-core streaming GEMV otherwise.
+ * CUDA_CORE / TENSOR force one of the general paths (TENSOR returns
+ * QGMOE_ERR_UNSUPPORTED when the layer does not allow it). */
 /* CUDA graphs (default on): the second forward with the same T, x, out and
  * stream is captured into a graph and later identical calls replay it, which
  * removes the per-launch host cost of decode-sized calls.  Disabled while

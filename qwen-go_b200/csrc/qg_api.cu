@@ -175,6 +175,7 @@ struct qgmoe {
     float *d = nullptr;  // [slots, H]
     float *x_dev = nullptr, *out_dev = nullptr;
     int *err_dev = nullptr;
+    DecRoute *dec_route = nullptr;  // the decode path's routing of its batch
     int hmax = 0;
     int last_launches = 0;
     // expert parallelism: this rank owns experts e with e % ep_world == ep_rank
@@ -298,6 +299,7 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(m->x_dev, sizeof(float) * (size_t)cap * m->H);
     QG_A(m->out_dev, sizeof(float) * (size_t)cap * m->H);
     QG_A(m->err_dev, sizeof(int));
+    QG_A(m->dec_route, sizeof(DecRoute));
 #undef QG_A
     QG_CUDA(cudaMemsetAsync(st.counts, 0, sizeof(int32_t) * m->E, m->stream));
     QG_CUDA(cudaMemsetAsync(st.done_ctr, 0, sizeof(int32_t), m->stream));
@@ -483,6 +485,63 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     return QGMOE_OK;
 }
 
+// The decode path (qg_decode.cu): a batch of up to FD_MAX_T tokens in four
+// kernels -- serial-order router logits; routing of the batch; gate_up +
+// SwiGLU; down + rank-order combine -- instead of the seven of the general
+// paths.  AUTO takes it whenever the batch fits: routed and shared experts
+// in one format, the token and router rows within the logits kernel's
+// shared memory, and the batch's h rows within the down kernel's.
+static bool use_decode(const qgmoe *m, int T) {
+    if (m->path_mode != QGMOE_PATH_AUTO || m->ep_world > 1 || T > FD_MAX_T) return false;
+    if (m->has_shared && m->shared_bits != m->bits) return false;
+    if (!router_rows_fit(T, m->H)) return false;
+    return dec_smem_gateup(m->bits, T, m->H) <= (size_t)FD_SMEM_MAX &&
+           dec_smem_down(m->bits, T, m->k, m->I, m->has_shared ? m->Is : 0) <=
+               (size_t)FD_SMEM_MAX;
+}
+
+static int enqueue_forward_decode(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    m->begin_timed();
+    m->mark(0, nullptr, s);
+    const int Ep = m->E + m->has_shared;
+    int rc = launch_router_logits(x, T, m->H, m->E, Ep, m->router, m->shared_gate, m->st.logits,
+                                  m->err_dev, s);
+    if (rc) return rc;
+    m->mark(1, "logits", s);
+    DecodeArgs a{};
+    a.x = x;
+    a.T = T;
+    a.H = m->H;
+    a.E = m->E;
+    a.Ep = Ep;
+    a.k = m->k;
+    a.mode = m->mode;
+    a.has_shared = m->has_shared;
+    a.I = m->I;
+    a.Is = m->Is;
+    a.logits = m->st.logits;
+    a.gu = m->gu;
+    a.dn = m->dn;
+    a.sgu = m->sgu;
+    a.sdn = m->sdn;
+    a.h = m->h;
+    a.hmax = m->hmax;
+    a.out = out;
+    a.topk_idx = m->st.topk_idx;
+    a.topk_w = m->st.topk_w;
+    a.shared_w = m->st.shared_w;
+    a.route = m->dec_route;
+    a.err = m->err_dev;
+    if ((rc = launch_decode(m->bits, a, 0, s))) return rc;
+    m->mark(2, "route", s);
+    if ((rc = launch_decode(m->bits, a, 1, s))) return rc;
+    m->mark(3, "gate_up", s);
+    if ((rc = launch_decode(m->bits, a, 2, s))) return rc;
+    m->mark(4, "down", s);  // down products and the rank-order combine
+    m->last_launches = 4;
+    return QGMOE_OK;
+}
+
 static int read_flag(qgmoe *m, cudaStream_t s) {
     int flag = 0;
     QG_CUDA(cudaMemcpyAsync(&flag, m->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -502,6 +561,7 @@ static int enqueue_forward(qgmoe *m, const float *x, int T, float *out, cudaStre
     if (m->ep_world > 1)
         return set_error(QGMOE_ERR_UNSUPPORTED,
                          "expert-parallel handle: use qgmoe_ep_dispatch / _experts / _combine");
+    if (use_decode(m, T)) return enqueue_forward_decode(m, x, T, out, s);
     if (use_tensor(m, T)) return enqueue_forward_tensor(m, x, T, out, s);
     m->begin_timed();
     m->mark(0, nullptr, s);

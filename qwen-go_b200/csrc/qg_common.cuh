@@ -188,6 +188,48 @@ struct ExpertArgs {
     int *err;
 };
 
+// The decode forward (qg_decode.cu) for batches of up to FD_MAX_T tokens:
+// router logits; routing (one small CTA); gate_up + SwiGLU; down + combine.
+constexpr int FD_MAX_T = 8;
+constexpr int FD_SMEM_MAX = 200 * 1024;  // dynamic shared memory of one decode CTA
+// The batch's routing as the decode kernels read it (device memory).
+struct DecRoute {
+    int sel[FD_MAX_T][QG_MAX_TOPK];               // experts in rank order
+    float w[FD_MAX_T][QG_MAX_TOPK];               // their renormalised weights
+    float sg[FD_MAX_T];                           // shared-expert gate
+    int nd;                                       // distinct selected experts
+    int dexp[FD_MAX_T * QG_MAX_TOPK];             // their ids
+    unsigned dmask[FD_MAX_T * QG_MAX_TOPK];       // the tokens that chose each
+    signed char drank[FD_MAX_T * QG_MAX_TOPK][FD_MAX_T];  // its rank in token t's list
+    int np;                                       // (token, rank) pairs, by expert
+    int pexp[FD_MAX_T * QG_MAX_TOPK];             // expert of pair p
+    int prow[FD_MAX_T * QG_MAX_TOPK];             // its h row: t * k + rank
+};
+struct DecodeArgs {
+    const float *x;                 // [T, H]
+    int T, H, E, Ep, k, mode, has_shared, I, Is;
+    const float *logits;            // [T, Ep], the router's serial-order logits
+    WeightSet gu, dn, sgu, sdn;     // routed and shared expert weights (one format)
+    float *h;                       // [T*k + T, hmax]: pair (t, r) at row t*k + r,
+    int hmax;                       //   shared-expert token t at row T*k + t
+    float *out;                     // [T, H]
+    int32_t *topk_idx;              // [T, k] routing outputs
+    float *topk_w, *shared_w;
+    DecRoute *route;                // written by the routing kernel
+    int *err;
+};
+// Dynamic shared memory the expert kernels of the decode path need.
+size_t dec_smem_gateup(int bits, int T, int H);
+size_t dec_smem_down(int bits, int T, int k, int I, int Is);
+// Stage 0: routing; 1: gate_up + SwiGLU; 2: down + combine.
+int launch_decode(int bits, const DecodeArgs &a, int stage, cudaStream_t s);
+// Router logits only, [T, Ep] in the reference's serial order.  For the
+// decode path: router_rows_fit says whether a decode batch's token and
+// router rows fit the shared memory of the logits kernel.
+int launch_router_logits(const float *x, int T, int H, int E, int Ep, const float *router,
+                         const float *shared_gate, float *logits, int *err, cudaStream_t s);
+bool router_rows_fit(int T, int H);
+
 // Launch helpers implemented in the .cu files.
 // The router: logits in the reference's serial order, exact softmax, top-k
 // and weights, dispatch.  x, router and shared_gate are float32 device

@@ -17,6 +17,7 @@
 // rows with 128-bit loads (16 B per lane), FMAs them against the NT staged
 // rows and reduces with warp shuffles.
 #include "qg_common.cuh"
+#include "qg_gemv.cuh"
 
 namespace qg {
 
@@ -25,71 +26,6 @@ constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 constexpr int GEMV_ROWS = 8;   // output rows per work item (1 per warp)
 constexpr int GEMV_UNR = 4;    // 16-byte chunks per lane loaded ahead
 constexpr int GEMV_NT = 4;     // tokens staged per pass
-
-// Elements carried by one 16-byte weight chunk.
-template <int BITS>
-struct Chunk {
-    static constexpr int V = BITS == 32 ? 4 : BITS == 16 ? 8 : (BITS == 8 ? 16 : 32);
-};
-
-// int8 x4 -> float x4 exactly: bias to unsigned, splice under 2^23, subtract.
-__device__ __forceinline__ void i8x4(uint32_t w, float *f) {
-    const uint32_t u = w ^ 0x80808080u;
-    f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - 8388736.f;
-    f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - 8388736.f;
-    f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - 8388736.f;
-    f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - 8388736.f;
-}
-
-// 4 packed bytes = 8 int4 codes -> float x8 (code - 8), element order
-// hi(b0), lo(b0), hi(b1), lo(b1), ...
-__device__ __forceinline__ void i4x8(uint32_t w, float *f) {
-    const uint32_t hi = (w >> 4) & 0x0F0F0F0Fu;
-    const uint32_t lo = w & 0x0F0F0F0Fu;
-    f[0] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540)) - 8388616.f;
-    f[1] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540)) - 8388616.f;
-    f[2] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7541)) - 8388616.f;
-    f[3] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7541)) - 8388616.f;
-    f[4] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7542)) - 8388616.f;
-    f[5] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7542)) - 8388616.f;
-    f[6] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7543)) - 8388616.f;
-    f[7] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7543)) - 8388616.f;
-}
-
-template <int BITS>
-__device__ __forceinline__ void decode_chunk(uint4 raw, float *v) {
-    if constexpr (BITS == 32) {
-        v[0] = __uint_as_float(raw.x);
-        v[1] = __uint_as_float(raw.y);
-        v[2] = __uint_as_float(raw.z);
-        v[3] = __uint_as_float(raw.w);
-    } else if constexpr (BITS == 16) {
-        // bf16f32 (model/model.go:113-115): the bits as the high half of a float32
-        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            v[2 * i] = __uint_as_float(w4[i] << 16);
-            v[2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
-        }
-    } else if constexpr (BITS == 8) {
-        i8x4(raw.x, v);
-        i8x4(raw.y, v + 4);
-        i8x4(raw.z, v + 8);
-        i8x4(raw.w, v + 12);
-    } else {
-        i4x8(raw.x, v);
-        i4x8(raw.y, v + 8);
-        i4x8(raw.z, v + 16);
-        i4x8(raw.w, v + 24);
-    }
-}
-
-// Position (in floats) of element (chunk c, offset j) of a staged row, so
-// that lane (c % 32) reading float4 j/4 of iteration c/32 is conflict-free.
-template <int V>
-__device__ __forceinline__ int stage_pos(int c, int j) {
-    return (((c >> 5) * (V / 4) + (j >> 2)) * 32 + (c & 31)) * 4 + (j & 3);
-}
 
 // Dot products of NR weight rows (gate and up for GATEUP) against the staged
 // rows: acc[r][t] += row_r . x_t.  Each lane takes chunks lane, lane+32, ...;
@@ -151,11 +87,6 @@ __device__ __forceinline__ float warp_allsum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
-}
-
-__device__ __forceinline__ float silu_ref(float g) {
-    // g / (1 + float32(exp(-float64(g))))   (model/tensors.go:93)
-    return __fdiv_rn(g, __fadd_rn(1.f, (float)exp(-(double)g)));
 }
 
 template <int BITS, bool GATEUP>

@@ -36,6 +36,7 @@
 //    itself once the offsets are known, one launch fewer.  For the tensor-core
 //    path k_gather_h16 then copies each slot's fp16 activation row.
 #include "qg_common.cuh"
+#include "qg_router.cuh"
 #include "qg_sm100.cuh"
 
 namespace qg {
@@ -44,22 +45,6 @@ constexpr int LG_KC = 32;                // K chunk staged in shared memory
 constexpr int TK_TOK = QG_TOPK_TOK;      // tokens per top-k / scatter CTA
 constexpr int RT_THREADS = 1024;         // top-k and scatter CTAs: one warp per token
 constexpr int RT_WARPS = RT_THREADS / 32;
-constexpr unsigned FULL = 0xffffffffu;
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-    return v;
-}
-
-// Larger prob, then lower index: the order a stable descending insertion
-// sort produces.
-__device__ __forceinline__ void better(float &v, int &i, float v2, int i2) {
-    if (v2 > v || (v2 == v && i2 < i)) {
-        v = v2;
-        i = i2;
-    }
-}
 
 // ---- 1. logits ------------------------------------------------------------------
 // CTA tile: TT = TPT*TTH tokens x RR = RPT*RTH router rows; thread (ty, tx)
@@ -117,29 +102,33 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
     const int tid = threadIdx.x, tx = tid % RTH, ty = tid / RTH;
     const int t0 = blockIdx.x * TT, r0 = blockIdx.y * RR;
     const bool write_h = xh && blockIdx.y == 0;
-    // loaders: float4 i of a chunk covers item i / 8 (token or row), column (i % 8) * 4
+    // loaders: float4 i of a chunk covers item i % TT (token) or i % RR (row)
+    // and columns 4 (i / TT) .. + 3, so a warp stores one K column of 32
+    // consecutive tokens or rows: conflict-free transposed stores
     const float *xrow[C::XPT];
     const float *wrow[C::WPT];
+    int xc[C::XPT], wc[C::WPT];
 #pragma unroll
     for (int j = 0; j < C::XPT; j++) {
-        const int i = tid + NTH * j, t = t0 + i / 8;
+        const int i = tid + NTH * j, t = t0 + i % TT;
+        xc[j] = (i / TT) * 4;
         xrow[j] = (i < C::XV && t < T) ? x + (size_t)t * H : nullptr;
     }
 #pragma unroll
     for (int j = 0; j < C::WPT; j++) {
-        const int i = tid + NTH * j, r = r0 + i / 8;
+        const int i = tid + NTH * j, r = r0 + i % RR;
+        wc[j] = (i / RR) * 4;
         wrow[j] = (i < C::WV && r < Ep) ? (r < E ? router + (size_t)r * H : shared_gate) : nullptr;
     }
-    const int c4 = (tid % 8) * 4;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     float4 xn[C::XPT], wn[C::WPT];
     auto fetch = [&](int kb) {
 #pragma unroll
         for (int j = 0; j < C::XPT; j++)
-            xn[j] = xrow[j] ? __ldg(reinterpret_cast<const float4 *>(xrow[j] + kb + c4)) : zero;
+            xn[j] = xrow[j] ? __ldg(reinterpret_cast<const float4 *>(xrow[j] + kb + xc[j])) : zero;
 #pragma unroll
         for (int j = 0; j < C::WPT; j++)
-            wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + c4)) : zero;
+            wn[j] = wrow[j] ? __ldg(reinterpret_cast<const float4 *>(wrow[j] + kb + wc[j])) : zero;
     };
     static_assert(RPT % 2 == 0, "rows per thread are paired for the packed adds");
     float2 acc[TPT][RPT / 2];
@@ -154,7 +143,7 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
         for (int j = 0; j < C::XPT; j++) {
             const int i = tid + NTH * j;
             if (i < C::XV) {
-                const int t = i / 8;
+                const int t = i % TT, c4 = xc[j];
                 xs[c4][t] = xn[j].x;
                 xs[c4 + 1][t] = xn[j].y;
                 xs[c4 + 2][t] = xn[j].z;
@@ -178,7 +167,7 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
         for (int j = 0; j < C::WPT; j++) {
             const int i = tid + NTH * j;
             if (i < C::WV) {
-                const int row = i / 8;
+                const int row = i % RR, c4 = wc[j];
                 ws[c4][row] = wn[j].x;
                 ws[c4 + 1][row] = wn[j].y;
                 ws[c4 + 2][row] = wn[j].z;
@@ -187,17 +176,29 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
         }
         __syncthreads();
         if (kb + LG_KC < H) fetch(kb + LG_KC);
-#pragma unroll 8
+        // the operands of step kk + 2 are loaded while step kk's chains advance
+        float a0[TPT], b0[RPT], a1[TPT], b1[RPT];
+        lds_vec<TPT>(&xs[0][ty * TPT], a0);
+        lds_vec<RPT>(&ws[0][tx * RPT], b0);
+        lds_vec<TPT>(&xs[1][ty * TPT], a1);
+        lds_vec<RPT>(&ws[1][tx * RPT], b1);
+#pragma unroll
         for (int kk = 0; kk < LG_KC; kk++) {
-            float av[TPT], bv[RPT];
-            lds_vec<TPT>(&xs[kk][ty * TPT], av);
-            lds_vec<RPT>(&ws[kk][tx * RPT], bv);
+            float a2[TPT], b2[RPT];
+            if (kk + 2 < LG_KC) {
+                lds_vec<TPT>(&xs[kk + 2][ty * TPT], a2);
+                lds_vec<RPT>(&ws[kk + 2][tx * RPT], b2);
+            }
 #pragma unroll
             for (int i = 0; i < TPT; i++)
 #pragma unroll
                 for (int j = 0; j < RPT / 2; j++)
-                    acc[i][j] = add2_rn(acc[i][j], make_float2(__fmul_rn(av[i], bv[2 * j]),
-                                                               __fmul_rn(av[i], bv[2 * j + 1])));
+                    acc[i][j] = add2_rn(acc[i][j], make_float2(__fmul_rn(a0[i], b0[2 * j]),
+                                                               __fmul_rn(a0[i], b0[2 * j + 1])));
+#pragma unroll
+            for (int i = 0; i < TPT; i++) a0[i] = a1[i], a1[i] = a2[i];
+#pragma unroll
+            for (int j = 0; j < RPT; j++) b0[j] = b1[j], b1[j] = b2[j];
         }
         __syncthreads();
     }
@@ -224,7 +225,7 @@ k_logits(const float *__restrict__ x, int T, int H, int E, int Ep,
 // chain (row tid % LR_RR, token tid / LR_RR) segment by segment as the
 // segments land.  Rows are padded by 4 floats so the 8 rows (and 4 tokens)
 // a warp reads at one k fall in distinct banks.
-constexpr int LR_RR = 8, LR_SEG = 4;
+constexpr int LR_RR = 8, LR_SEG = 4, LR_B4 = 8;
 constexpr long long LR_WAIT_CYCLES = 2000000000LL;  // ~1 s: a lost copy cannot hang the GPU
 constexpr size_t LR_SMEM_MAX = 220 * 1024;           // of the 227 KB a CTA may opt into
 
@@ -276,22 +277,39 @@ k_logits_rows(const float *__restrict__ x, int T, int H, int E, int Ep,
         if (!ok) break;
         const float4 *wp = reinterpret_cast<const float4 *>(ws + r * HP + s * L);
         const float4 *xp = reinterpret_cast<const float4 *>(xs + t * HP + s * L);
-        // the add chain is the critical path: the next step's operands are
-        // loaded and its products formed while the current adds retire
-        const int n4 = L / 4;
-        float4 a = xp[0], b = wp[0];
-#pragma unroll 4
-        for (int c = 0; c < n4; c++) {
-            const int cn = c + 1 < n4 ? c + 1 : c;
-            const float4 an = xp[cn], bn = wp[cn];
-            const float p0 = __fmul_rn(a.x, b.x), p1 = __fmul_rn(a.y, b.y);
-            const float p2 = __fmul_rn(a.z, b.z), p3 = __fmul_rn(a.w, b.w);
-            acc = __fadd_rn(acc, p0);
-            acc = __fadd_rn(acc, p1);
-            acc = __fadd_rn(acc, p2);
-            acc = __fadd_rn(acc, p3);
-            a = an;
-            b = bn;
+        // the add chain is the critical path (5 cycles per dependent add on
+        // B200): operands come in register blocks of LR_B4 float4 each; a
+        // block's products are formed first (independent of the chain), the
+        // next block's shared-memory loads are issued, then the block's
+        // dependent adds run from registers
+        const int L4 = L / 4, nfull = L4 / LR_B4;  // float4 per segment, full blocks
+        if (nfull > 0) {
+            float4 ca[LR_B4], cb[LR_B4];
+#pragma unroll
+            for (int j = 0; j < LR_B4; j++) ca[j] = xp[j], cb[j] = wp[j];
+            for (int blk = 0; blk < nfull; blk++) {
+                float p[4 * LR_B4];
+#pragma unroll
+                for (int j = 0; j < LR_B4; j++) {
+                    p[4 * j] = __fmul_rn(ca[j].x, cb[j].x);
+                    p[4 * j + 1] = __fmul_rn(ca[j].y, cb[j].y);
+                    p[4 * j + 2] = __fmul_rn(ca[j].z, cb[j].z);
+                    p[4 * j + 3] = __fmul_rn(ca[j].w, cb[j].w);
+                }
+                const int nxt = blk + 1 < nfull ? blk + 1 : blk;
+#pragma unroll
+                for (int j = 0; j < LR_B4; j++)
+                    ca[j] = xp[nxt * LR_B4 + j], cb[j] = wp[nxt * LR_B4 + j];
+#pragma unroll
+                for (int j = 0; j < 4 * LR_B4; j++) acc = __fadd_rn(acc, p[j]);
+            }
+        }
+        for (int c = nfull * LR_B4; c < L4; c++) {  // the segment's remainder
+            const float4 a = xp[c], b = wp[c];
+            acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+            acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+            acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+            acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
         }
     }
     if (!ok) {
@@ -363,30 +381,19 @@ static int launch_logits(const float *x, int T, int H, int E, int Ep, const floa
     return launch_logits_t<4, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
 }
 
+bool router_rows_fit(int T, int H) {
+    return T <= 8 ? lr_smem_bytes(8, H) <= LR_SMEM_MAX
+                  : T <= 64 && lr_smem_bytes(16, H) <= LR_SMEM_MAX;
+}
+
+int launch_router_logits(const float *x, int T, int H, int E, int Ep, const float *router,
+                         const float *shared_gate, float *logits, int *err, cudaStream_t s) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return launch_logits(x, T, H, E, Ep, router, shared_gate, logits, nullptr, err, dev, s);
+}
+
 // ---- 2. softmax + top-k + histograms --------------------------------------------
-// float32(exp(float64(v - mx))), the softmax numerator (model/tensors.go:116).
-__device__ __forceinline__ float sm_num(float v, float mx) {
-    return (float)exp((double)__fsub_rn(v, mx));
-}
-
-// Warp-wide best (larger value, then lower expert index) over the lane's
-// values v[j] (expert lane + 32 j) whose bit is set in `usable`.
-template <int NJ>
-__device__ __forceinline__ void warp_best(const float (&v)[NJ], unsigned usable, int lane,
-                                          float &bv, int &bi) {
-    bv = -INFINITY;
-    bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < NJ; j++)
-        if ((usable >> j) & 1u) better(bv, bi, v[j], lane + 32 * j);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float v2 = __shfl_xor_sync(FULL, bv, o);
-        const int i2 = __shfl_xor_sync(FULL, bi, o);
-        better(bv, bi, v2, i2);
-    }
-}
-
 __device__ __forceinline__ void scatter_chunk(int c, int T, int E, int k, int has_shared,
                                               const RouteState &st, int *err, int *sm,
                                               int *partial);
@@ -410,89 +417,12 @@ k_topk(const float *__restrict__ logits, int T, int E, int Ep, int k, int mode,
     for (int i = 0; i < TK_TOK / RT_WARPS; i++) {
         const int t = blockIdx.x * TK_TOK + warp * (TK_TOK / RT_WARPS) + i;
         if (t >= T) break;
-        unsigned valid = 0;
-        float v[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; j++) {
-            const int e = lane + 32 * j;
-            if (e < E) valid |= 1u << j;
-            v[j] = e < E ? logits[(size_t)t * Ep + e] : -INFINITY;
-        }
-        // mx = v[0]; for x in v[1:]: if x > mx { mx = x }: fmaxf skips NaN
-        // as `x > mx` does, and a NaN in v[0] stays
-        const float v0 = __shfl_sync(FULL, v[0], 0);
-        float m = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < NJ; j++)
-            if ((valid >> j) & 1u) m = fmaxf(m, v[j]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, o));
-        const float mx = isnan(v0) ? v0 : m;
-        float p[NJ];
-#pragma unroll
-        for (int j = 0; j < NJ; j++) p[j] = ((valid >> j) & 1u) ? sm_num(v[j], mx) : 0.f;
-        // float32 sum in index order (every lane forms the same sum)
-        float sum = 0.f;
-#pragma unroll
-        for (int j = 0; j < NJ; j++)
-#pragma unroll
-            for (int l = 0; l < 32; l++) {
-                const float u = __shfl_sync(FULL, p[j], l);
-                if (l + 32 * j < E) sum = __fadd_rn(sum, u);
-            }
-#pragma unroll
-        for (int j = 0; j < NJ; j++) p[j] = ((valid >> j) & 1u) ? __fdiv_rn(p[j], sum) : -1.f;
         int *sel = s_idx[warp];
-        float selp = 0.f;  // lane r < k: probability of the rank-r expert
-        if (isnan(sum)) {
-            // every probability NaN: no comparison succeeds, the order stays 0..k-1
-            const float pr = __shfl_sync(FULL, p[0], lane < k ? lane : 0);
-            if (lane < k) {
-                sel[lane] = lane;
-                selp = pr;
-            }
-        } else if (mode == QGMOE_ROUTER_TOPK) {
-            unsigned usable = valid;
-            for (int r = 0; r < k; r++) {
-                float bv;
-                int bi;
-                warp_best(p, usable, lane, bv, bi);
-                if ((bi & 31) == lane) usable &= ~(1u << (bi >> 5));
-                if (lane == r) selp = bv;
-                if (lane == 0) sel[r] = bi;
-            }
-        } else {
-            // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1
-            // (k <= 32, so expert q < k is p[0] of lane q): insertion sort
-            const float pq = p[0];
-            float pk[QG_MAX_TOPK];
-#pragma unroll
-            for (int q = 0; q < QG_MAX_TOPK; q++) pk[q] = __shfl_sync(FULL, pq, q);
-            if (lane == 0) {
-                int ik[QG_MAX_TOPK];
-                for (int q = 0; q < k; q++) ik[q] = q;
-                for (int a2 = 1; a2 < k && a2 < E; a2++)
-                    for (int b2 = a2; b2 > 0 && pk[ik[b2]] > pk[ik[b2 - 1]]; b2--) {
-                        const int ti = ik[b2];
-                        ik[b2] = ik[b2 - 1];
-                        ik[b2 - 1] = ti;
-                    }
-                for (int q = 0; q < k; q++) sel[q] = ik[q];
-            }
-            __syncwarp();
-            const int myexp = lane < k ? sel[lane] : 0;
-            const float got = __shfl_sync(FULL, pq, myexp);
-            if (lane < k) selp = got;
-        }
-        __syncwarp();
-        // wSum over ranks in rank order, then w = p / (wSum + 1e-9)
-        float wsum = 0.f;
-        for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, __shfl_sync(FULL, selp, r));
-        const float den = __fadd_rn(wsum, 1e-9f);
+        const float wr = route_token<NJ>(logits + (size_t)t * Ep, E, k, mode, lane, sel);
         if (lane < k) {
             const int e = sel[lane];
             st.topk_idx[(size_t)t * k + lane] = e;
-            st.topk_w[(size_t)t * k + lane] = __fdiv_rn(selp, den);
+            st.topk_w[(size_t)t * k + lane] = wr;
             if (e >= 0 && e < E)
                 atomicAdd(&hist_s[dispatch_key(e, E, st.ep_world, st.ep_slot)], 1);
             else
