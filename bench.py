@@ -495,6 +495,9 @@ def stage_bytes(cfg, stage, distinct, T):
         return (distinct * 2 * I * H + 2 * Is * H) * bpw + T * H * 4
     if stage == "down":
         return (distinct * I * H + Is * H) * bpw + T * H * 4
+    if stage == "decode":  # the one-launch decode kernel: router, experts, x in, out
+        return ((E + (1 if Is else 0)) * H * 4 + (distinct * 3 * I * H + 3 * Is * H) * bpw
+                + 2 * T * H * 4)
     return T * H * 4 * (cfg["k"] + 1)  # combine: k rows in, one out
 
 
@@ -549,7 +552,7 @@ def measure_decode(name, T, steps, dev, peaks):
     layer.sync(stream)
     distinct = int((np.bincount(sel.cpu().numpy().ravel(), minlength=cfg["E"]) > 0).sum())
     total_ms, stages, _ = time_forwards(layer, x, out, sel, steps, flush, stream, dev)
-    dom = max(("gate_up", "down", "route"), key=lambda s: stages.get(s, 0.0))
+    dom = max(("decode", "gate_up", "down", "route"), key=lambda s: stages.get(s, 0.0))
     by = stage_bytes(cfg, dom, distinct, T)
     gbs = by / (stages[dom] / 1e3) / 1e9
     res = {"config": name, "tokens": T, "tokens_per_s": T * steps / (total_ms / 1e3),

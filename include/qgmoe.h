@@ -205,14 +205,16 @@ int qgmoe_sync(qgmoe_t *h, void *stream);
 int qgmoe_last_launch_count(const qgmoe_t *h);
 
 /* Expert-product path.  AUTO runs decode-sized batches (up to 8 tokens,
- * routed and shared experts in one format, the batch's rows within the
- * kernels' shared memory) on the four-kernel decode path (router logits;
- * routing; gate_up; down + combine), larger ones on the tcgen05 tensor-core
- * grouped GEMMs whenever the layer allows them (int8/int4 routed experts; H
- * and I multiples of 128), except for the smallest batches of a layer with
- * a shared expert (T*k < 16), and on the CUDA-core streaming GEMV otherwise.
- * CUDA_CORE / TENSOR force one of the general paths (TENSOR returns
- * QGMOE_ERR_UNSUPPORTED when the layer does not allow it). */
+ * routed and shared experts in one format, at most 256 experts, the batch
+ * within the kernel's shared memory) on the decode kernel: one persistent
+ * launch over every SM (it expects the device to itself; a grid barrier
+ * that waits about a second raises QGMOE_ERR_DEVICE_FLAG, flag 8).  Larger
+ * batches run on the tcgen05 tensor-core grouped GEMMs whenever the layer
+ * allows them (int8/int4 routed experts; H and I multiples of 128), except
+ * for the smallest batches of a layer with a shared expert (T*k < 16), and
+ * on the CUDA-core streaming GEMV otherwise.  CUDA_CORE / TENSOR force one
+ * of the general paths (TENSOR returns QGMOE_ERR_UNSUPPORTED when the layer
+ * does not allow it). */
 /* CUDA graphs (default on): the second forward with the same T, x, out and
  * stream is captured into a graph and later identical calls replay it, which
  * removes the per-launch host cost of decode-sized calls.  Disabled while
@@ -223,6 +225,13 @@ int qgmoe_set_graphs(qgmoe_t *h, int32_t enable);
 #define QGMOE_PATH_CUDA_CORE 1
 #define QGMOE_PATH_TENSOR 2
 int qgmoe_set_path(qgmoe_t *h, int32_t mode);
+
+/* Decode kernel speculation (default on): while the router logits are
+ * summed in the reference's serial order, the experts of an approximate
+ * top-k are streamed already; experts the exact routing picks that the
+ * approximation missed are computed afterwards.  Results are identical
+ * either way; enable = 0 computes every expert after the exact routing. */
+int qgmoe_set_decode_speculation(qgmoe_t *h, int32_t enable);
 
 /* Per-stage device timing (instrumentation for benchmarks): when enabled,
  * every forward records CUDA events on its stream between consecutive

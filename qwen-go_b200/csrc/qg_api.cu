@@ -175,7 +175,15 @@ struct qgmoe {
     float *d = nullptr;  // [slots, H]
     float *x_dev = nullptr, *out_dev = nullptr;
     int *err_dev = nullptr;
-    DecRoute *dec_route = nullptr;  // the decode path's routing of its batch
+    // decode kernel (qg_decode.cu): its routing, speculative logits, h and
+    // down rows, and its grid-barrier counter and flags (zeroed once, never
+    // reset while the workspace lives)
+    DecRoute *dec_route = nullptr;
+    float *dec_approx = nullptr, *dec_d = nullptr;
+    unsigned char *dec_h = nullptr;
+    unsigned long long *dec_bar = nullptr, *dec_flags = nullptr;
+    int dec_hrow = 0;
+    int dec_speculate = 1;
     int hmax = 0;
     int last_launches = 0;
     // expert parallelism: this rank owns experts e with e % ep_world == ep_rank
@@ -299,7 +307,19 @@ static int ensure_capacity(qgmoe *m, int T) {
     QG_A(m->x_dev, sizeof(float) * (size_t)cap * m->H);
     QG_A(m->out_dev, sizeof(float) * (size_t)cap * m->H);
     QG_A(m->err_dev, sizeof(int));
-    QG_A(m->dec_route, sizeof(DecRoute));
+    {
+        m->dec_hrow = decode_hrow_bytes(m->bits, m->I, m->Is);
+        const size_t dslots = (size_t)dec_slots(m->k);
+        const int nflags = num_sms(m->device) + FD_MAX_T;
+        QG_A(m->dec_route, sizeof(DecRoute));
+        QG_A(m->dec_approx, sizeof(float) * FD_MAX_T * (m->E + m->has_shared));
+        QG_A(m->dec_h, dslots * m->dec_hrow);
+        QG_A(m->dec_d, sizeof(float) * dslots * m->H);
+        QG_A(m->dec_bar, sizeof(unsigned long long));
+        QG_A(m->dec_flags, sizeof(unsigned long long) * nflags);
+        QG_CUDA(cudaMemsetAsync(m->dec_bar, 0, sizeof(unsigned long long), m->stream));
+        QG_CUDA(cudaMemsetAsync(m->dec_flags, 0, sizeof(unsigned long long) * nflags, m->stream));
+    }
 #undef QG_A
     QG_CUDA(cudaMemsetAsync(st.counts, 0, sizeof(int32_t) * m->E, m->stream));
     QG_CUDA(cudaMemsetAsync(st.done_ctr, 0, sizeof(int32_t), m->stream));
@@ -485,60 +505,70 @@ static int enqueue_forward_tensor(qgmoe *m, const float *x, int T, float *out, c
     return QGMOE_OK;
 }
 
-// The decode path (qg_decode.cu): a batch of up to FD_MAX_T tokens in four
-// kernels -- serial-order router logits; routing of the batch; gate_up +
-// SwiGLU; down + rank-order combine -- instead of the seven of the general
-// paths.  AUTO takes it whenever the batch fits: routed and shared experts
-// in one format, the token and router rows within the logits kernel's
-// shared memory, and the batch's h rows within the down kernel's.
-static bool use_decode(const qgmoe *m, int T) {
+// The decode path (qg_decode.cu): a batch of up to FD_MAX_T tokens in one
+// persistent kernel instead of the seven launches of the general paths.
+// AUTO takes it whenever the batch fits: routed and shared experts in one
+// format, at most FD_MAX_E experts, row lengths whose bulk copies stay
+// 16-byte aligned, and the kernel's shared-memory plan.
+static bool decode_args(const qgmoe *m, const float *x, int T, float *out, DecodeArgs &a) {
     if (m->path_mode != QGMOE_PATH_AUTO || m->ep_world > 1 || T > FD_MAX_T) return false;
     if (m->has_shared && m->shared_bits != m->bits) return false;
-    if (!router_rows_fit(T, m->H)) return false;
-    return dec_smem_gateup(m->bits, T, m->H) <= (size_t)FD_SMEM_MAX &&
-           dec_smem_down(m->bits, T, m->k, m->I, m->has_shared ? m->Is : 0) <=
-               (size_t)FD_SMEM_MAX;
-}
-
-static int enqueue_forward_decode(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
-    m->begin_timed();
-    m->mark(0, nullptr, s);
-    const int Ep = m->E + m->has_shared;
-    int rc = launch_router_logits(x, T, m->H, m->E, Ep, m->router, m->shared_gate, m->st.logits,
-                                  m->err_dev, s);
-    if (rc) return rc;
-    m->mark(1, "logits", s);
-    DecodeArgs a{};
+    a = DecodeArgs{};
     a.x = x;
     a.T = T;
     a.H = m->H;
     a.E = m->E;
-    a.Ep = Ep;
+    a.Ep = m->E + m->has_shared;
     a.k = m->k;
     a.mode = m->mode;
     a.has_shared = m->has_shared;
     a.I = m->I;
     a.Is = m->Is;
-    a.logits = m->st.logits;
+    a.router = m->router;
+    a.shared_gate = m->shared_gate;
     a.gu = m->gu;
     a.dn = m->dn;
     a.sgu = m->sgu;
     a.sdn = m->sdn;
-    a.h = m->h;
-    a.hmax = m->hmax;
+    a.gu_pq = m->gu_pq;
+    a.dn_pq = m->dn_pq;
+    a.sgu_pq = m->sgu_pq;
+    a.sdn_pq = m->sdn_pq;
+    for (const WeightSet *w : {&a.gu, &a.dn, &a.sgu, &a.sdn})
+        if (misaligned(w->w32) || misaligned(w->q) || misaligned(w->s)) return false;
+    if (misaligned(a.router) || misaligned(a.shared_gate)) return false;
     a.out = out;
+    a.speculate = m->dec_speculate;
+    return decode_plan(a, m->bits, num_sms(m->device));
+}
+
+static bool use_decode(const qgmoe *m, int T) {
+    DecodeArgs a;
+    return decode_args(m, nullptr, T, nullptr, a);
+}
+
+static int enqueue_forward_decode(qgmoe *m, const float *x, int T, float *out, cudaStream_t s) {
+    DecodeArgs a;
+    if (!decode_args(m, x, T, out, a) || a.hrow > m->dec_hrow)
+        return set_error(QGMOE_ERR_UNSUPPORTED, "decode path chosen for a batch it cannot take");
+    a.approx = m->dec_approx;
+    a.logits = m->st.logits;
+    a.hbuf = m->dec_h;
+    a.hrow = m->dec_hrow;
+    a.dbuf = m->dec_d;
     a.topk_idx = m->st.topk_idx;
     a.topk_w = m->st.topk_w;
     a.shared_w = m->st.shared_w;
     a.route = m->dec_route;
+    a.bar = m->dec_bar;
+    a.flags = m->dec_flags;
     a.err = m->err_dev;
-    if ((rc = launch_decode(m->bits, a, 0, s))) return rc;
-    m->mark(2, "route", s);
-    if ((rc = launch_decode(m->bits, a, 1, s))) return rc;
-    m->mark(3, "gate_up", s);
-    if ((rc = launch_decode(m->bits, a, 2, s))) return rc;
-    m->mark(4, "down", s);  // down products and the rank-order combine
-    m->last_launches = 4;
+    m->begin_timed();
+    m->mark(0, nullptr, s);
+    int rc = launch_decode(m->bits, a, s);
+    if (rc) return rc;
+    m->mark(1, "decode", s);
+    m->last_launches = 1;
     return QGMOE_OK;
 }
 
@@ -946,6 +976,15 @@ int qgmoe_set_path(qgmoe_t *m, int32_t mode) {
                          "tensor-core path needs int8/int4 routed experts with H and I "
                          "multiples of 128");
     m->path_mode = mode;
+    m->drop_graphs();
+    return QGMOE_OK;
+}
+
+int qgmoe_set_decode_speculation(qgmoe_t *m, int32_t enable) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    QG_CUDA(cudaSetDevice(m->device));
+    cudaStreamSynchronize(m->stream);
+    m->dec_speculate = enable != 0;
     m->drop_graphs();
     return QGMOE_OK;
 }

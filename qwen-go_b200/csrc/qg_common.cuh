@@ -188,47 +188,59 @@ struct ExpertArgs {
     int *err;
 };
 
-// The decode forward (qg_decode.cu) for batches of up to FD_MAX_T tokens:
-// router logits; routing (one small CTA); gate_up + SwiGLU; down + combine.
+// The decode forward (qg_decode.cu): batches of up to FD_MAX_T tokens in one
+// persistent kernel, one CTA per SM.
 constexpr int FD_MAX_T = 8;
-constexpr int FD_SMEM_MAX = 200 * 1024;  // dynamic shared memory of one decode CTA
-// The batch's routing as the decode kernels read it (device memory).
+constexpr int FD_MAX_E = 256;  // experts the decode kernel routes (ceil(E/32) <= 8)
+// The batch's exact routing, published by the kernel's routing warps.
 struct DecRoute {
-    int sel[FD_MAX_T][QG_MAX_TOPK];               // experts in rank order
-    float w[FD_MAX_T][QG_MAX_TOPK];               // their renormalised weights
-    float sg[FD_MAX_T];                           // shared-expert gate
-    int nd;                                       // distinct selected experts
-    int dexp[FD_MAX_T * QG_MAX_TOPK];             // their ids
-    unsigned dmask[FD_MAX_T * QG_MAX_TOPK];       // the tokens that chose each
-    signed char drank[FD_MAX_T * QG_MAX_TOPK][FD_MAX_T];  // its rank in token t's list
-    int np;                                       // (token, rank) pairs, by expert
-    int pexp[FD_MAX_T * QG_MAX_TOPK];             // expert of pair p
-    int prow[FD_MAX_T * QG_MAX_TOPK];             // its h row: t * k + rank
+    int sel[FD_MAX_T][QG_MAX_TOPK];  // experts in rank order
+    float w[FD_MAX_T][QG_MAX_TOPK];  // their renormalised weights
+    float sg[FD_MAX_T];              // shared-expert gate
 };
 struct DecodeArgs {
-    const float *x;                 // [T, H]
+    const float *x;                   // [T, H]
     int T, H, E, Ep, k, mode, has_shared, I, Is;
-    const float *logits;            // [T, Ep], the router's serial-order logits
-    WeightSet gu, dn, sgu, sdn;     // routed and shared expert weights (one format)
-    float *h;                       // [T*k + T, hmax]: pair (t, r) at row t*k + r,
-    int hmax;                       //   shared-expert token t at row T*k + t
-    float *out;                     // [T, H]
-    int32_t *topk_idx;              // [T, k] routing outputs
+    const float *router;              // [E, H] float32 router rows
+    const float *shared_gate;         // [H] or null
+    WeightSet gu, dn, sgu, sdn;       // routed and shared expert weights (one format)
+    // int8/int4: the tensor path's packed 128-row x 64-code tiles of the same
+    // weights (qg_umma.cu k_repack), streamed instead of the row-major codes
+    const uint8_t *gu_pq, *dn_pq, *sgu_pq, *sdn_pq;
+    int kbi_gu, kbi_dn, kbi_sdn;      // 64-code k blocks per streamed item
+    float *approx;                    // [T, Ep] approximate logits (speculation)
+    float *logits;                    // [T, Ep] logits in the reference's serial order
+    unsigned char *hbuf;              // h rows, [dec_slots(k), hrow bytes]
+    int hrow;
+    float *dbuf;                      // down rows, [dec_slots(k), H]
+    float *out;                       // [T, H]
+    int32_t *topk_idx;                // [T, k] routing outputs
     float *topk_w, *shared_w;
-    DecRoute *route;                // written by the routing kernel
+    DecRoute *route;
+    unsigned long long *bar;          // grid barrier arrivals (never reset)
+    unsigned long long *flags;        // [gridDim.x] logits-done, then [FD_MAX_T] routed
     int *err;
+    int speculate;                    // stream the approximate top-k's experts early
+    // shared-memory plan (bytes from the start of dynamic shared memory)
+    int nrc;                          // router rows per CTA
+    int xstride;                      // float32 token rows (floats)
+    int x16tok, h16tok;               // fp16 operand rows per token (bytes, tensor-core path)
+    int ns;                           // weight ring stages
+    int hsstride;                     // staged float32 h rows (floats, CUDA-core path)
+    int hwin;                         // down-phase tasks whose h rows are staged at once
+    int stage_bytes;                  // one weight ring stage
+    int off_xs, off_x16, off_hs, off_ring, off_xch, off_tok, off_lrow;
+    int smem;                         // total dynamic bytes
 };
-// Dynamic shared memory the expert kernels of the decode path need.
-size_t dec_smem_gateup(int bits, int T, int H);
-size_t dec_smem_down(int bits, int T, int k, int I, int Is);
-// Stage 0: routing; 1: gate_up + SwiGLU; 2: down + combine.
-int launch_decode(int bits, const DecodeArgs &a, int stage, cudaStream_t s);
-// Router logits only, [T, Ep] in the reference's serial order.  For the
-// decode path: router_rows_fit says whether a decode batch's token and
-// router rows fit the shared memory of the logits kernel.
-int launch_router_logits(const float *x, int T, int H, int E, int Ep, const float *router,
-                         const float *shared_gate, float *logits, int *err, cudaStream_t s);
-bool router_rows_fit(int T, int H);
+// h / d rows of the decode buffers: pairs of the speculative phase, the
+// shared expert's tokens, pairs computed after exact routing.
+inline int dec_slots(int k) { return 2 * FD_MAX_T * k + FD_MAX_T; }
+// Fills a's shared-memory plan for T tokens on a device with `sms` SMs;
+// false when the batch does not fit the decode kernel.
+bool decode_plan(DecodeArgs &a, int bits, int sms);
+// Bytes of one h row of the decode buffers for a layer's widest expert.
+int decode_hrow_bytes(int bits, int I, int Is);
+int launch_decode(int bits, const DecodeArgs &a, cudaStream_t s);
 
 // Launch helpers implemented in the .cu files.
 // The router: logits in the reference's serial order, exact softmax, top-k

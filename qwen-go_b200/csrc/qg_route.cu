@@ -381,18 +381,6 @@ static int launch_logits(const float *x, int T, int H, int E, int Ep, const floa
     return launch_logits_t<4, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
 }
 
-bool router_rows_fit(int T, int H) {
-    return T <= 8 ? lr_smem_bytes(8, H) <= LR_SMEM_MAX
-                  : T <= 64 && lr_smem_bytes(16, H) <= LR_SMEM_MAX;
-}
-
-int launch_router_logits(const float *x, int T, int H, int E, int Ep, const float *router,
-                         const float *shared_gate, float *logits, int *err, cudaStream_t s) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    return launch_logits(x, T, H, E, Ep, router, shared_gate, logits, nullptr, err, dev, s);
-}
-
 // ---- 2. softmax + top-k + histograms --------------------------------------------
 __device__ __forceinline__ void scatter_chunk(int c, int T, int E, int k, int has_shared,
                                               const RouteState &st, int *err, int *sm,

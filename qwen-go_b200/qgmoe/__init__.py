@@ -82,6 +82,7 @@ SIGNATURES = {
     "qgmoe_ep_px_forward": ([_vp, _vp, C.c_int32, _vp, _vp], C.c_int),
     "qgmoe_last_launch_count": ([_vp], C.c_int),
     "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
+    "qgmoe_set_decode_speculation": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_graphs": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_timing": ([_vp, C.c_int32], C.c_int),
     "qgmoe_read_timing": ([_vp, C.POINTER(C.c_float), C.c_int32, C.POINTER(C.c_int32)], C.c_int),
@@ -289,6 +290,12 @@ class MoeMLP:
     def set_path(self, mode: int):
         """PATH_AUTO, PATH_CUDA_CORE or PATH_TENSOR (see include/qgmoe.h)."""
         _check(lib().qgmoe_set_path(self.h, mode), "qgmoe_set_path")
+
+    def set_decode_speculation(self, enable: bool = True):
+        """Stream the approximate top-k's experts while the exact router
+        logits are summed (default on); results are the same either way."""
+        _check(lib().qgmoe_set_decode_speculation(self.h, int(enable)),
+               "qgmoe_set_decode_speculation")
 
     def set_graphs(self, enable: bool = True):
         """CUDA-graph replay of repeated identical forwards (default on)."""

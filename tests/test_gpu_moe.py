@@ -131,7 +131,8 @@ def test_device_entry_point_matches_host_entry_point():
     gpu.forward_device(xd, out, sel_idx=idx, stream=s)
     gpu.sync(s)
     assert np.array_equal(out.cpu().numpy(), ref)
-    assert gpu.last_launch_count() >= 3  # the decode path: logits, gate_up, down
+    # int8 rows of 128 are below the decode kernel's 256-wide alignment: general path
+    assert gpu.last_launch_count() >= 3
 
 
 def test_workspace_growth_keeps_results():
