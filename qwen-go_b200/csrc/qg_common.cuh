@@ -194,9 +194,11 @@ constexpr int FD_MAX_T = 8;
 constexpr int FD_MAX_E = 256;  // experts the decode kernel routes (ceil(E/32) <= 8)
 // The batch's exact routing, published by the kernel's routing warps.
 struct DecRoute {
-    int sel[FD_MAX_T][QG_MAX_TOPK];  // experts in rank order
-    float w[FD_MAX_T][QG_MAX_TOPK];  // their renormalised weights
-    float sg[FD_MAX_T];              // shared-expert gate
+    int sel[FD_MAX_T][QG_MAX_TOPK];   // experts in rank order
+    float w[FD_MAX_T][QG_MAX_TOPK];   // their renormalised weights
+    float sg[FD_MAX_T];               // shared-expert gate
+    int slot[FD_MAX_T][QG_MAX_TOPK];  // the down row holding (token, rank)
+    int miss[FD_MAX_T];               // a selected expert was not a candidate
 };
 struct DecodeArgs {
     const float *x;                   // [T, H]

@@ -79,9 +79,9 @@ struct FzShared {
     int slot[FD_MAX_T][QG_MAX_TOPK];       // d row of (token, exact rank)
     float part[FZ_WORKERS][2 * FD_MAX_T];  // approximate-logit partial sums
     int rsel[QG_MAX_TOPK];
-    long long inst;                        // last grid barrier's instance
-    long long epoch;                       // this launch's first barrier instance
-    int epoch_set;
+    unsigned long long base;               // barrier arrivals before this launch
+    int nbar;                              // grid barriers passed (thread 0)
+    int cand_ready;                        // S.cand is final
 };
 
 __device__ __forceinline__ void wsync() {
@@ -103,16 +103,16 @@ __device__ __forceinline__ void fence_proxy_async() {
 
 __device__ __forceinline__ void fz_timeout(const DecodeArgs &a) { atomicOr(a.err, QG_FLAG_TIMEOUT); }
 
-// All worker threads of every CTA.  The arrival counter only grows: this
-// barrier's instance is old / G, shared by its G arrivals because no CTA can
-// arrive at the next instance before this one is complete.
-__device__ long long fz_grid_sync(const DecodeArgs &a, FzShared &S) {
+// All worker threads of every CTA.  The arrival counter only grows, by G
+// per barrier: a launch's n-th barrier completes when it reaches base +
+// n G, where base (a multiple of G) is the count when the launch began.
+// Arrivals are fire-and-forget releases; thread 0 polls with acquires.
+__device__ void fz_grid_sync(const DecodeArgs &a, FzShared &S) {
     wsync();
     if (threadIdx.x == 0) {
         __threadfence();
-        const unsigned long long G = gridDim.x;
-        const unsigned long long old = atomicAdd(a.bar, 1ull);
-        const unsigned long long target = (old / G + 1) * G;
+        asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.bar) : "memory");
+        const unsigned long long target = S.base + (unsigned long long)(++S.nbar) * gridDim.x;
         if (ld_acq(a.bar) < target) {
             const long long t0 = clock64();
             while (ld_acq(a.bar) < target) {
@@ -120,14 +120,11 @@ __device__ long long fz_grid_sync(const DecodeArgs &a, FzShared &S) {
                     fz_timeout(a);
                     break;
                 }
-                __nanosleep(32);
             }
         }
         __threadfence();
-        S.inst = (long long)(old / G);
     }
     wsync();
-    return S.inst;
 }
 
 __device__ __forceinline__ bool fz_wait_flag(const DecodeArgs &a, const unsigned long long *f,
@@ -209,24 +206,6 @@ __device__ __forceinline__ void msync() {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
-// Codes 4q .. 4q+3 of one row's 16-code chunk -> fp16 pairs {4q, 4q+1},
-// {4q+2, 4q+3}, exact (code - 8, or the unbiased int8 code).
-template <int BITS>
-__device__ __forceinline__ void tc_pairs(const unsigned char *row, int q, uint32_t &p0,
-                                         uint32_t &p1) {
-    if constexpr (BITS == 4) {
-        const __half2 b1032 = u2h(0x64086408u), r16 = u2h(0x2C002C00u), m72 = u2h(0xD480D480u);
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(row + (q >> 1) * 4) >> ((q & 1) * 8);
-        p0 = h2u(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), b1032));
-        p1 = h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), r16, m72));
-    } else {
-        const __half2 b1152 = u2h(0x64806480u);
-        const uint32_t u = *reinterpret_cast<const uint32_t *>(row + q * 4);
-        p0 = h2u(__hsub2(u2h(__byte_perm(u, 0x64646464u, 0x4140)), b1152));
-        p1 = h2u(__hsub2(u2h(__byte_perm(u, 0x64646464u, 0x4342)), b1152));
-    }
-}
-
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
@@ -235,11 +214,48 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// One 64-code k block of tile rows r0 and r0 + 8 (the fragment's rows g and
-// g + 8, thread (g = lane / 4, q = lane % 4)) against B (this thread's token
-// row at xb, fp16, the block's 64 elements): per 32-wide group two MMAs whose
-// k slots 2q, 2q+1 / 2q+8, 2q+9 carry codes 4q, 4q+1 / 4q+2, 4q+3 of each
-// 16-code chunk, then acc += group scale * result.
+// Eight consecutive codes of one tile row -> four fp16 pairs {0,1} {2,3}
+// {4,5} {6,7}, exact (code - 8, or the unbiased int8 code).
+template <int BITS>
+__device__ __forceinline__ void tc_word(const unsigned char *p, uint32_t (&c)[4]) {
+    if constexpr (BITS == 4) {
+        const __half2 b1032 = u2h(0x64086408u), r16 = u2h(0x2C002C00u), m72 = u2h(0xD480D480u);
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(p), w8 = w >> 8;
+        c[0] = h2u(__hsub2(u2h((w & 0x000F000Fu) | 0x64006400u), b1032));
+        c[1] = h2u(__hfma2(u2h((w & 0x00F000F0u) | 0x64006400u), r16, m72));
+        c[2] = h2u(__hsub2(u2h((w8 & 0x000F000Fu) | 0x64006400u), b1032));
+        c[3] = h2u(__hfma2(u2h((w8 & 0x00F000F0u) | 0x64006400u), r16, m72));
+    } else {
+        const __half2 b1152 = u2h(0x64806480u);
+        const uint2 u = *reinterpret_cast<const uint2 *>(p);
+        c[0] = h2u(__hsub2(u2h(__byte_perm(u.x, 0x64646464u, 0x4140)), b1152));
+        c[1] = h2u(__hsub2(u2h(__byte_perm(u.x, 0x64646464u, 0x4342)), b1152));
+        c[2] = h2u(__hsub2(u2h(__byte_perm(u.y, 0x64646464u, 0x4140)), b1152));
+        c[3] = h2u(__hsub2(u2h(__byte_perm(u.y, 0x64646464u, 0x4342)), b1152));
+    }
+}
+
+// One 32-wide scale group (chunks 2 grp, 2 grp + 1) of tile rows r0 and
+// r0 + 8 against B (this thread's token row, fp16, at xb = the k block's 64
+// elements): thread (g, q) takes codes base .. base+7, base = 16 (q / 2) +
+// 8 (q % 2) of the group, as k slots 2q, 2q+1, 2q+8, 2q+9 of the group's two
+// MMAs (codes base+0..3, then base+4..7); B holds the same elements.
+template <int BITS>
+__device__ __forceinline__ void tc_group(const unsigned char *tile, const unsigned char *xb,
+                                         int grp, int r0, int q, float (&d)[4]) {
+    using P = PTile<BITS>;
+    const unsigned char *ra = tile + ((grp * 2 + (q >> 1)) * 128 + r0) * P::CB + (q & 1) * (P::CB / 2);
+    uint32_t ca[4], cb[4];
+    tc_word<BITS>(ra, ca);
+    tc_word<BITS>(ra + 8 * P::CB, cb);
+    const uint4 b = *reinterpret_cast<const uint4 *>(xb + (grp * 32 + (q >> 1) * 16 + (q & 1) * 8) * 2);
+    d[0] = d[1] = d[2] = d[3] = 0.f;
+    mma16816(d, ca[0], cb[0], ca[1], cb[1], b.x, b.y);
+    mma16816(d, ca[2], cb[2], ca[3], cb[3], b.z, b.w);
+}
+
+// One 64-code k block: its two groups, each scaled by the rows' group scale
+// in f32 into acc (C rows g / g + 8, columns 2q, 2q+1).
 template <int BITS>
 __device__ __forceinline__ void tc_kblock(const unsigned char *tile, const unsigned char *xb,
                                           int r0, int q, float (&acc)[4]) {
@@ -249,16 +265,8 @@ __device__ __forceinline__ void tc_kblock(const unsigned char *tile, const unsig
         __half22float2(u2h(*reinterpret_cast<const uint32_t *>(tile + P::CODE + (r0 + 8) * 4)));
 #pragma unroll
     for (int grp = 0; grp < 2; grp++) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const int c = grp * 2 + cc;
-            uint32_t a0, a1, a2, a3;
-            tc_pairs<BITS>(tile + (c * 128 + r0) * P::CB, q, a0, a2);
-            tc_pairs<BITS>(tile + (c * 128 + r0 + 8) * P::CB, q, a1, a3);
-            const uint2 bx = *reinterpret_cast<const uint2 *>(xb + (c * 16 + 4 * q) * 2);
-            mma16816(d, a0, a1, a2, a3, bx.x, bx.y);
-        }
+        float d[4];
+        tc_group<BITS>(tile, xb, grp, r0, q, d);
         const float sa = grp ? s0.y : s0.x, sb = grp ? s1.y : s1.x;
         acc[0] = fmaf(d[0], sa, acc[0]);
         acc[1] = fmaf(d[1], sa, acc[1]);
@@ -334,7 +342,7 @@ __device__ void fz_phase_tc(const DecodeArgs &a, FzShared &S, const FzList &L, b
     }
     if (warp >= FZ_MW) return;
     const int g = lane >> 2, qq = lane & 3, m = warp;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
     int hd = -1;  // task whose h rows are staged (down)
     for (int j = 0; j < nitems; j++) {
         const It x = item(j);
@@ -358,13 +366,20 @@ __device__ void fz_phase_tc(const DecodeArgs &a, FzShared &S, const FzList &L, b
         const unsigned char *st = smem + a.off_ring + s * a.stage_bytes;
         const unsigned char *xrow =
             GATEUP ? smem + a.off_x16 + g * a.x16tok : smem + a.off_hs + g * a.h16tok;
-        for (int kk = 0; kk < x.kbi; kk++)
-            tc_kblock<BITS>(st + kk * P::BYTES, xrow + (size_t)(x.it * x.kbi + kk) * 128,
-                            16 * m + g, qq, acc);
+        // even and odd k blocks into separate sums: two independent chains
+        const unsigned char *xk = xrow + (size_t)x.it * x.kbi * 128;
+        int kk = 0;
+        for (; kk + 1 < x.kbi; kk += 2) {
+            tc_kblock<BITS>(st + kk * P::BYTES, xk + kk * 128, 16 * m + g, qq, acc);
+            tc_kblock<BITS>(st + (kk + 1) * P::BYTES, xk + (kk + 1) * 128, 16 * m + g, qq, acc2);
+        }
+        if (kk < x.kbi) tc_kblock<BITS>(st + kk * P::BYTES, xk + kk * 128, 16 * m + g, qq, acc);
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(&S.empty[s]);
         if (x.it != x.ni - 1) continue;
         // the unit's rows are complete; C rows g / g + 8, columns (tokens) 2q, 2q+1
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[i] += acc2[i], acc2[i] = 0.f;
         if constexpr (GATEUP) {
             float4 *xch = reinterpret_cast<float4 *>(smem + a.off_xch) + (nx & 1) * 4 * 32;
             if (m >= 4) xch[(m - 4) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -664,20 +679,13 @@ __device__ void fz_chains(const DecodeArgs &a, FzShared &S, unsigned char *smem,
     if (act) a.logits[(size_t)t * a.Ep + b + q * G] = acc;
     __syncwarp();
     // publish "this CTA's logits are written" under this launch's epoch
-    volatile long long *ep = &S.epoch;
+    // (base / G: unique per launch, larger than any earlier launch's)
+    const unsigned long long want = S.base / G + 1;
     if (lane == 0) {
         __threadfence();
-        const long long t0 = clock64();
-        while (!*reinterpret_cast<volatile int *>(&S.epoch_set)) {
-            if (clock64() - t0 > FZ_WAIT) {
-                fz_timeout(a);
-                break;
-            }
-        }
-        st_rel(&a.flags[b], (unsigned long long)*ep + 1);
+        st_rel(&a.flags[b], want);
     }
     __syncwarp();
-    const unsigned long long want = (unsigned long long)*ep + 1;
     float *lrow = reinterpret_cast<float *>(smem + a.off_lrow);
     for (int tt = b; tt < T; tt += n_chain) {
         for (int i = lane; i < n_chain; i += 32) fz_wait_flag(a, &a.flags[i], want);
@@ -685,13 +693,39 @@ __device__ void fz_chains(const DecodeArgs &a, FzShared &S, unsigned char *smem,
         for (int e = lane; e < a.Ep; e += 32) lrow[e] = __ldcg(a.logits + (size_t)tt * a.Ep + e);
         __syncwarp();
         const float wr = fz_route(lrow, a.E, a.k, a.mode, lane, S.rsel);
+        // where each (token, rank) pair's down row will be: the speculative
+        // pair's if the expert was a candidate, else a row computed after
+        // routing (this CTA's candidates equal every CTA's)
+        if (lane == 0) {
+            const long long t0 = clock64();
+            while (!*reinterpret_cast<volatile int *>(&S.cand_ready)) {
+                if (clock64() - t0 > FZ_WAIT) {
+                    fz_timeout(a);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __syncwarp();
+        bool missed = false;
         if (lane < a.k) {
-            const int e = S.rsel[lane];
+            int e = S.rsel[lane];
+            if (e < 0 || e >= a.E) {
+                atomicOr(a.err, QG_FLAG_BAD_EXPERT);
+                e = 0;  // keeps every index in range; the flag reports the fault
+            }
+            int c = -1;
+            for (int i = 0; i < a.k; i++)
+                if (reinterpret_cast<volatile int *>(S.cand[tt])[i] == e) c = i;
+            missed = c < 0;
             a.route->sel[tt][lane] = e;
             a.route->w[tt][lane] = wr;
+            a.route->slot[tt][lane] = missed ? T * a.k + T + tt * a.k + lane : tt * a.k + c;
             a.topk_idx[(size_t)tt * a.k + lane] = e;
             a.topk_w[(size_t)tt * a.k + lane] = wr;
         }
+        const unsigned anymiss = __ballot_sync(FULL, missed);
+        if (lane == 0) a.route->miss[tt] = anymiss != 0u;
         if (a.has_shared && lane == 0) {
             // sigmoid1 (model/tensors.go:97) of the shared-gate logit
             const float g = lrow[a.E];
@@ -727,7 +761,8 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         sm100::mbar_init(&S.wbar, 1);
         sm100::mbar_init(&S.hbar, 1);
         sm100::fence_mbar_init();
-        S.epoch_set = 0;
+        S.nbar = 0;
+        S.cand_ready = 0;
     }
     __syncthreads();
     // router rows: static weights, fetched while the previous kernel ends
@@ -741,6 +776,13 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
     }
     pdl_launch_dependents();
     pdl_wait();
+    if (tid == 0) {
+        // earlier launches are complete, and this launch's first barrier
+        // cannot complete before this CTA arrives: the count lies in
+        // [base, base + G)
+        const unsigned long long v = ld_acq(a.bar);
+        S.base = v - v % (unsigned long long)G;
+    }
     bool range = false;
     for (int i = tid; i < T * H; i += FZ_THREADS) {
         const int t = i / H, kk = i - t * H;
@@ -796,12 +838,8 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
             a.approx[(size_t)t * a.Ep + b + q * G] = v;
         }
     }
-    const long long epoch = fz_grid_sync(a, S);
-    if (tid == 0) {
-        S.epoch = epoch;
-        __threadfence_block();
-        *reinterpret_cast<volatile int *>(&S.epoch_set) = 1;
-    }
+    fz_grid_sync(a, S);
+    const unsigned long long epoch = S.base / G;
 
     // ---- 2. candidates: approximate top-k per token, distinct experts ----
     if (warp < T) {
@@ -820,6 +858,10 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         if (lane < k && cand[lane] >= 0) atomicOr(&tok[cand[lane]], 1u << warp);
     }
     wsync();
+    if (tid == 0) {
+        __threadfence_block();
+        *reinterpret_cast<volatile int *>(&S.cand_ready) = 1;
+    }
     if (warp == 0) fz_compact(tok, a.E, S.A, 0);
     wsync();
     for (int i = tid; i < S.A.n * T; i += FZ_WT) {
@@ -851,7 +893,7 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
 
     // ---- 5. exact routing; pairs the candidates missed ----
     if (warp == 0) {
-        if (lane < T) fz_wait_flag(a, &a.flags[G + lane], (unsigned long long)epoch + 1);
+        if (lane < T) fz_wait_flag(a, &a.flags[G + lane], epoch + 1);
         __syncwarp();
     }
     wsync();
@@ -859,33 +901,23 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         const int t = i / k, r = i - t * k;
         S.sel[t][r] = __ldcg(&a.route->sel[t][r]);
         S.w[t][r] = __ldcg(&a.route->w[t][r]);
+        S.slot[t][r] = __ldcg(&a.route->slot[t][r]);
     }
     if (a.has_shared && tid < T) S.sg[tid] = __ldcg(&a.route->sg[tid]);
-    for (int e = tid; e < a.E; e += FZ_WT) tok[e] = 0u;
-    wsync();
+    bool anymiss = false;
+    for (int t = 0; t < T; t++) anymiss |= __ldcg(&a.route->miss[t]) != 0;
     const int base_b = T * k + T;
-    for (int i = tid; i < T * k; i += FZ_WT) {
-        const int t = i / k, r = i - t * k;
-        int e = S.sel[t][r];
-        if (e < 0 || e >= a.E) {
-            atomicOr(a.err, QG_FLAG_BAD_EXPERT);
-            e = 0;  // keeps every index in range; the flag reports the fault
-            S.sel[t][r] = 0;
+    if (anymiss) {
+        // rare: experts the approximate top-k missed, by expert
+        for (int e = tid; e < a.E; e += FZ_WT) tok[e] = 0u;
+        wsync();
+        for (int i = tid; i < T * k; i += FZ_WT) {
+            const int t = i / k, r = i - t * k;
+            if (S.slot[t][r] >= base_b) atomicOr(&tok[S.sel[t][r]], 1u << t);
         }
-        int rr = -1;
-        for (int c = 0; c < k; c++)
-            if (S.cand[t][c] == e) rr = c;
-        if (rr >= 0) {
-            S.slot[t][r] = t * k + rr;
-        } else {
-            S.slot[t][r] = base_b + t * k + r;
-            atomicOr(&tok[e], 1u << t);
-        }
-    }
-    wsync();
-    if (warp == 0) fz_compact(tok, a.E, S.B, base_b);
-    wsync();
-    if (S.B.n > 0) {
+        wsync();
+        if (warp == 0) fz_compact(tok, a.E, S.B, base_b);
+        wsync();
         for (int i = tid; i < S.B.n * T; i += FZ_WT) {
             const int d = i / T, t = i - d * T;
             if ((S.B.dmask[d] >> t) & 1u)
