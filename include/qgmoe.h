@@ -233,6 +233,15 @@ int qgmoe_set_path(qgmoe_t *h, int32_t mode);
  * either way; enable = 0 computes every expert after the exact routing. */
 int qgmoe_set_decode_speculation(qgmoe_t *h, int32_t enable);
 
+/* How long a device-side wait on another CTA or another rank (the decode
+ * kernel's grid barriers and routing flags, the expert-parallel exchange's
+ * peer flags) spins before it gives up, in microseconds of SM clock; 0
+ * restores the defaults (about 1 s, 2 s for peers).  A wait that gives up
+ * raises device flag 8: the next qgmoe_sync / blocking forward returns
+ * QGMOE_ERR_DEVICE_FLAG and the outputs of that call are not valid; the
+ * handle stays usable.  Waits on a CTA's own copies keep their defaults. */
+int qgmoe_set_wait_limit(qgmoe_t *h, int64_t microseconds);
+
 /* Per-stage device timing (instrumentation for benchmarks): when enabled,
  * every forward records CUDA events on its stream between consecutive
  * stages, without host syncs.  read_timing waits for those forwards, writes

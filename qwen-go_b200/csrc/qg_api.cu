@@ -184,6 +184,7 @@ struct qgmoe {
     unsigned long long *dec_bar = nullptr, *dec_flags = nullptr;
     int dec_hrow = 0;
     int dec_speculate = 1;
+    long long wait_cycles = 0;  // qgmoe_set_wait_limit; 0: the kernels' defaults (1-2 s)
     int hmax = 0;
     int last_launches = 0;
     // expert parallelism: this rank owns experts e with e % ep_world == ep_rank
@@ -317,6 +318,7 @@ static int ensure_capacity(qgmoe *m, int T) {
         QG_A(m->dec_d, sizeof(float) * dslots * m->H);
         QG_A(m->dec_bar, sizeof(unsigned long long));
         QG_A(m->dec_flags, sizeof(unsigned long long) * nflags);
+        QG_CUDA(cudaMemsetAsync(m->dec_route, 0, sizeof(DecRoute), m->stream));
         QG_CUDA(cudaMemsetAsync(m->dec_bar, 0, sizeof(unsigned long long), m->stream));
         QG_CUDA(cudaMemsetAsync(m->dec_flags, 0, sizeof(unsigned long long) * nflags, m->stream));
     }
@@ -563,6 +565,7 @@ static int enqueue_forward_decode(qgmoe *m, const float *x, int T, float *out, c
     a.bar = m->dec_bar;
     a.flags = m->dec_flags;
     a.err = m->err_dev;
+    a.wait = m->wait_cycles;
     m->begin_timed();
     m->mark(0, nullptr, s);
     int rc = launch_decode(m->bits, a, s);
@@ -578,6 +581,14 @@ static int read_flag(qgmoe *m, cudaStream_t s) {
     QG_CUDA(cudaStreamSynchronize(s));
     if (flag) {
         cudaMemsetAsync(m->err_dev, 0, sizeof(int), s);
+        if ((flag & QG_FLAG_TIMEOUT) && m->dec_bar) {
+            // a decode launch whose waits ran out may have left its CTAs'
+            // barrier arrivals out of step: start the count and the flags
+            // again (the launch is complete)
+            cudaMemsetAsync(m->dec_bar, 0, sizeof(unsigned long long), s);
+            cudaMemsetAsync(m->dec_flags, 0,
+                            sizeof(unsigned long long) * (num_sms(m->device) + FD_MAX_T), s);
+        }
         cudaStreamSynchronize(s);
         return set_error(QGMOE_ERR_DEVICE_FLAG,
                          "device flag 0x%x (1=expert id, 2=slot, 4=group, 8=wait timeout, "
@@ -985,6 +996,19 @@ int qgmoe_set_decode_speculation(qgmoe_t *m, int32_t enable) {
     QG_CUDA(cudaSetDevice(m->device));
     cudaStreamSynchronize(m->stream);
     m->dec_speculate = enable != 0;
+    m->drop_graphs();
+    return QGMOE_OK;
+}
+
+int qgmoe_set_wait_limit(qgmoe_t *m, int64_t microseconds) {
+    if (!m) return set_error(QGMOE_ERR_INVALID_ARG, "null handle");
+    if (microseconds < 0) return set_error(QGMOE_ERR_INVALID_ARG, "negative wait limit");
+    QG_CUDA(cudaSetDevice(m->device));
+    int khz = 0;
+    QG_CUDA(cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, m->device));
+    cudaStreamSynchronize(m->stream);
+    m->wait_cycles = microseconds ? microseconds * (long long)khz / 1000 : 0;
+    m->px.wait = m->wait_cycles;
     m->drop_graphs();
     return QGMOE_OK;
 }

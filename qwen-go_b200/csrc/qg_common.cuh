@@ -138,6 +138,7 @@ struct PxArgs {
     int W, me, G, H, k, T;
     int64_t recv_cap;       // rows of a region's recv buffer
     size_t off_epoch, off_ticket, off_inbox, off_recv, off_back;
+    long long wait;         // clock cycles a wait on a peer's flag may take (<= 0: default)
 };
 struct PxTables {  // this rank's grouped-row tables (device)
     int32_t *act_group, *act_begin, *act_n, *n_act, *tile_prefix, *out_map, *n_rows;
@@ -222,6 +223,7 @@ struct DecodeArgs {
     unsigned long long *bar;          // grid barrier arrivals (never reset)
     unsigned long long *flags;        // [gridDim.x] logits-done, then [FD_MAX_T] routed
     int *err;
+    long long wait;                   // cycles a wait on other CTAs may take (<= 0: default)
     int speculate;                    // stream the approximate top-k's experts early
     // shared-memory plan (bytes from the start of dynamic shared memory)
     int nrc;                          // router rows per CTA
@@ -236,7 +238,7 @@ struct DecodeArgs {
 };
 // h / d rows of the decode buffers: pairs of the speculative phase, the
 // shared expert's tokens, pairs computed after exact routing.
-inline int dec_slots(int k) { return 2 * FD_MAX_T * k + FD_MAX_T; }
+__host__ __device__ inline int dec_slots(int k) { return 2 * FD_MAX_T * k + FD_MAX_T; }
 // Fills a's shared-memory plan for T tokens on a device with `sms` SMs;
 // false when the batch does not fit the decode kernel.
 bool decode_plan(DecodeArgs &a, int bits, int sms);

@@ -114,9 +114,10 @@ __device__ void fz_grid_sync(const DecodeArgs &a, FzShared &S) {
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long target = S.base + (unsigned long long)(++S.nbar) * gridDim.x;
         if (ld_acq(a.bar) < target) {
+            const long long budget = a.wait > 0 ? a.wait : FZ_WAIT;
             const long long t0 = clock64();
             while (ld_acq(a.bar) < target) {
-                if (clock64() - t0 > FZ_WAIT) {
+                if (clock64() - t0 > budget) {
                     fz_timeout(a);
                     break;
                 }
@@ -130,9 +131,10 @@ __device__ void fz_grid_sync(const DecodeArgs &a, FzShared &S) {
 __device__ __forceinline__ bool fz_wait_flag(const DecodeArgs &a, const unsigned long long *f,
                                              unsigned long long v) {
     if (ld_acq(f) >= v) return true;
+    const long long budget = a.wait > 0 ? a.wait : FZ_WAIT;
     const long long t0 = clock64();
     while (ld_acq(f) < v) {
-        if (clock64() - t0 > FZ_WAIT) {
+        if (clock64() - t0 > budget) {
             fz_timeout(a);
             return false;
         }
@@ -897,11 +899,13 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         __syncwarp();
     }
     wsync();
+    // (values of a wait that ran out may be stale: indices stay in range)
     for (int i = tid; i < T * k; i += FZ_WT) {
         const int t = i / k, r = i - t * k;
-        S.sel[t][r] = __ldcg(&a.route->sel[t][r]);
+        const int e = __ldcg(&a.route->sel[t][r]), sl = __ldcg(&a.route->slot[t][r]);
+        S.sel[t][r] = e >= 0 && e < a.E ? e : 0;
         S.w[t][r] = __ldcg(&a.route->w[t][r]);
-        S.slot[t][r] = __ldcg(&a.route->slot[t][r]);
+        S.slot[t][r] = sl >= 0 && sl < dec_slots(k) ? sl : 0;
     }
     if (a.has_shared && tid < T) S.sg[tid] = __ldcg(&a.route->sg[tid]);
     bool anymiss = false;

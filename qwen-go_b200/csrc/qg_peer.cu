@@ -56,11 +56,12 @@ __device__ __forceinline__ void st_release_sys(uint64_t *p, uint64_t v) {
 }
 
 // Bounded wait until flags[0..W-1] >= epoch.
-__device__ bool px_wait_flags(const uint64_t *flags, int W, uint64_t epoch) {
+__device__ bool px_wait_flags(const uint64_t *flags, int W, uint64_t epoch, long long wait) {
+    const long long budget = wait > 0 ? wait : PX_WAIT_CYCLES;
     const long long t0 = clock64();
     for (int s = 0; s < W; s++)
         while (ld_acquire_sys(flags + s) < epoch) {
-            if (clock64() - t0 > PX_WAIT_CYCLES) return false;
+            if (clock64() - t0 > budget) return false;
             __nanosleep(64);
         }
     return true;
@@ -124,7 +125,7 @@ k_px_send(PxArgs a, const float *__restrict__ x, const int32_t *__restrict__ exp
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         s_epoch = px_epoch(a);
-        s_ok = px_wait_flags(px_flag(a, a.me, PX_CNT, 0), W, s_epoch);
+        s_ok = px_wait_flags(px_flag(a, a.me, PX_CNT, 0), W, s_epoch, a.wait);
         if (!s_ok) atomicOr(err, QG_FLAG_TIMEOUT);
     }
     __syncthreads();
@@ -197,7 +198,7 @@ k_px_tables(PxArgs a, int tile_tokens, PxTables t, int *err) {
     __shared__ int s_ok;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
-        s_ok = px_wait_flags(px_flag(a, a.me, PX_DATA, 0), W, px_epoch(a));
+        s_ok = px_wait_flags(px_flag(a, a.me, PX_DATA, 0), W, px_epoch(a), a.wait);
         if (!s_ok) atomicOr(err, QG_FLAG_TIMEOUT);
     }
     __syncthreads();
@@ -302,7 +303,7 @@ __global__ void k_px_signal(PxArgs a) {
 
 // Before the combine: every owner has returned my rows.
 __global__ void k_px_wait(PxArgs a, int *err) {
-    if (threadIdx.x == 0 && !px_wait_flags(px_flag(a, a.me, PX_BACK, 0), a.W, px_epoch(a)))
+    if (threadIdx.x == 0 && !px_wait_flags(px_flag(a, a.me, PX_BACK, 0), a.W, px_epoch(a), a.wait))
         atomicOr(err, QG_FLAG_TIMEOUT);
 }
 

@@ -36,6 +36,10 @@ PATH_AUTO = 0
 PATH_CUDA_CORE = 1
 PATH_TENSOR = 2
 
+# status codes (include/qgmoe.h)
+ERR_INVALID_ARG, ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_DEVICE_FLAG, ERR_UNSUPPORTED, ERR_NO_DEVICE = (
+    -1, -2, -3, -4, -5, -6, -7)
+
 _vp = C.c_void_p
 
 
@@ -83,6 +87,7 @@ SIGNATURES = {
     "qgmoe_last_launch_count": ([_vp], C.c_int),
     "qgmoe_set_path": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_decode_speculation": ([_vp, C.c_int32], C.c_int),
+    "qgmoe_set_wait_limit": ([_vp, C.c_int64], C.c_int),
     "qgmoe_set_graphs": ([_vp, C.c_int32], C.c_int),
     "qgmoe_set_timing": ([_vp, C.c_int32], C.c_int),
     "qgmoe_read_timing": ([_vp, C.POINTER(C.c_float), C.c_int32, C.POINTER(C.c_int32)], C.c_int),
@@ -296,6 +301,10 @@ class MoeMLP:
         logits are summed (default on); results are the same either way."""
         _check(lib().qgmoe_set_decode_speculation(self.h, int(enable)),
                "qgmoe_set_decode_speculation")
+
+    def set_wait_limit(self, microseconds: int = 0):
+        """Limit of the device waits on other CTAs / ranks (0: defaults)."""
+        _check(lib().qgmoe_set_wait_limit(self.h, int(microseconds)), "qgmoe_set_wait_limit")
 
     def set_graphs(self, enable: bool = True):
         """CUDA-graph replay of repeated identical forwards (default on)."""

@@ -10,6 +10,8 @@ fp16 operands (the prefill tensor path's arithmetic), f32/bf16 experts keep
 the CUDA-core arithmetic and equal that path bit for bit.  Outputs meet the
 oracle bar: within 1e-3, 2e-3 for int4.  Speculation on or off gives the
 same bits."""
+import re
+
 import numpy as np
 import pytest
 
@@ -119,3 +121,26 @@ def test_general_path_beyond_eight_tokens():
     ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
     assert not check_routing(idx, w, ridx, rw, probs)
     check_outputs(out, ref, c["bits"])
+
+
+def test_decode_kernel_wait_limit_runs_out_and_recovers():
+    """A wait that runs out: with a 1 us limit the kernel's grid barriers and
+    routing-flag waits give up, the call reports device flag 8 (timeout)
+    instead of hanging, and the next call with the default limit is correct
+    again (the barrier count and flags were restarted)."""
+    m = host_case(H=256, E=16, k=4, I=256, Is=0, bits=8, seed=440)
+    g = make_gpu_moe(m, O.ROUTER_TOPK)
+    g.set_graphs(False)
+    x = O.randn(440, 1, (2, 256))
+    good = g.forward_batch(x)
+    g.set_wait_limit(1)
+    with pytest.raises(qgmoe.QgmoeError) as ei:
+        for _ in range(3):  # a fast GPU might finish inside the limit once
+            g.forward_batch(x)
+    assert ei.value.status == qgmoe.ERR_DEVICE_FLAG
+    assert int(re.search(r"device flag 0x([0-9a-f]+)", str(ei.value)).group(1), 16) & 8
+    g.set_wait_limit(0)
+    for _ in range(2):
+        assert np.array_equal(g.forward_batch(x), good)
+    ref, *_ = O.moe_forward(m, x)
+    check_outputs(good, ref, 8)
