@@ -238,8 +238,8 @@ int qgmoe_set_decode_speculation(qgmoe_t *h, int32_t enable);
  * peer flags) spins before it gives up, in microseconds of SM clock; 0
  * restores the defaults (about 1 s, 2 s for peers).  A wait that gives up
  * raises device flag 8: the next qgmoe_sync / blocking forward returns
- * QGMOE_ERR_DEVICE_FLAG and the outputs of that call are not valid; the
- * handle stays usable.  Waits on a CTA's own copies keep their defaults. */
+ * QGMOE_ERR_TIMEOUT and the outputs of that call are not valid; the handle
+ * stays usable.  Waits on a CTA's own copies keep their defaults. */
 int qgmoe_set_wait_limit(qgmoe_t *h, int64_t microseconds);
 
 /* Per-stage device timing (instrumentation for benchmarks): when enabled,

@@ -590,9 +590,9 @@ static int read_flag(qgmoe *m, cudaStream_t s) {
                             sizeof(unsigned long long) * (num_sms(m->device) + FD_MAX_T), s);
         }
         cudaStreamSynchronize(s);
-        return set_error(QGMOE_ERR_DEVICE_FLAG,
+        return set_error((flag & QG_FLAG_TIMEOUT) ? QGMOE_ERR_TIMEOUT : QGMOE_ERR_DEVICE_FLAG,
                          "device flag 0x%x (1=expert id, 2=slot, 4=group, 8=wait timeout, "
-                         "16=activation beyond fp16 range in the tensor-core router)",
+                         "16=activation beyond fp16 range on the tensor cores)",
                          flag);
     }
     return QGMOE_OK;

@@ -125,8 +125,8 @@ def test_general_path_beyond_eight_tokens():
 
 def test_decode_kernel_wait_limit_runs_out_and_recovers():
     """A wait that runs out: with a 1 us limit the kernel's grid barriers and
-    routing-flag waits give up, the call reports device flag 8 (timeout)
-    instead of hanging, and the next call with the default limit is correct
+    routing-flag waits give up, the call reports QGMOE_ERR_TIMEOUT (device
+    flag 8) instead of hanging, and the next call with the default limit is correct
     again (the barrier count and flags were restarted)."""
     m = host_case(H=256, E=16, k=4, I=256, Is=0, bits=8, seed=440)
     g = make_gpu_moe(m, O.ROUTER_TOPK)
@@ -137,7 +137,7 @@ def test_decode_kernel_wait_limit_runs_out_and_recovers():
     with pytest.raises(qgmoe.QgmoeError) as ei:
         for _ in range(3):  # a fast GPU might finish inside the limit once
             g.forward_batch(x)
-    assert ei.value.status == qgmoe.ERR_DEVICE_FLAG
+    assert ei.value.status == qgmoe.ERR_TIMEOUT
     assert int(re.search(r"device flag 0x([0-9a-f]+)", str(ei.value)).group(1), 16) & 8
     g.set_wait_limit(0)
     for _ in range(2):

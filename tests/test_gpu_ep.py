@@ -68,6 +68,11 @@ def _rank_main(rank, port, result_dir, mode="nccl"):
                          down_scale=np.ascontiguousarray(m.s16["down"][dn_rows]))
     ep = ExpertParallelMoE(layer) if mode == "nccl" else PeerExpertParallelMoE(layer, 400)
     peer = mode != "nccl"
+    if mode == "peer_skip":
+        _skip_step(rank, layer, ep, x_all[lo:hi], result_dir)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     x = torch.from_numpy(x_all[lo:hi]).cuda()
     out = torch.empty_like(x)
     s = torch.cuda.Stream()
@@ -83,6 +88,44 @@ def _rank_main(rank, port, result_dir, mode="nccl"):
     np.save(os.path.join(result_dir, f"ep{rank}.npy"), out.cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
+
+
+def _skip_step(rank, layer, ep, xs, result_dir):
+    """Two good steps on both ranks, then rank 1 leaves out the third (it
+    launches nothing: between steps, no kernel in flight) while rank 0 runs
+    it with a 50 ms wait limit: rank 0's kernels give up on rank 1's flags
+    and its sync reports the timeout."""
+    import torch
+
+    import qgmoe
+    x = torch.from_numpy(xs).cuda()
+    out = torch.empty_like(x)
+    s = torch.cuda.Stream()
+    for _ in range(2):
+        ep.forward(x, out, s)
+        s.synchronize()
+    assert qgmoe.lib().qgmoe_sync(layer.h, None) == 0, qgmoe.last_error()
+    torch.distributed.barrier()
+    status = 0
+    if rank == 0:
+        layer.set_wait_limit(50000)
+        ep.forward(x, out, s)
+        s.synchronize()
+        status = qgmoe.lib().qgmoe_sync(layer.h, None)
+    with open(os.path.join(result_dir, f"skip{rank}.txt"), "w") as f:
+        f.write(str(status))
+
+
+def test_two_gpu_peer_exchange_times_out_when_a_rank_skips_a_step(tmp_path):
+    import torch
+    if torch.cuda.device_count() < W:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    import qgmoe
+    mp.spawn(_rank_main, args=(_free_port(), str(tmp_path), "peer_skip"), nprocs=W, join=True)
+    assert int((tmp_path / "skip0.txt").read_text()) == qgmoe.ERR_TIMEOUT
+    assert int((tmp_path / "skip1.txt").read_text()) == 0
 
 
 @pytest.mark.parametrize("mode", ["nccl", "peer", "peer_perm"])
