@@ -424,6 +424,32 @@ def cpu_baseline_ours(cfg, host, x_host, budget_s=12.0):
                       f"model/model.go:507-514)"}
 
 
+def oracle_expert_load(m, x, threads):
+    """Expert load of the whole batch as the oracle routes it (serial-order
+    f32 logits, then the reference's top-k): the same histogram the GPU
+    arm reports from its own routing, over every token, not the sample."""
+    import ctypes as C
+    from concurrent.futures import ThreadPoolExecutor
+
+    import qg_oracle as O
+    L, f32p = O.lib(), C.POINTER(C.c_float)
+    T, H = x.shape
+    E, k = m.router.shape[0], m.k
+    router = np.ascontiguousarray(m.router, np.float32)
+    idx = np.zeros((T, k), np.int32)
+
+    def part(i):
+        logits = np.zeros(E, np.float32)
+        for t in range(i, T, threads):
+            xt = np.ascontiguousarray(x[t], np.float32)
+            L.qgo_matmul_vec(xt.ctypes.data_as(f32p), router.ctypes.data_as(f32p), H, E,
+                             logits.ctypes.data_as(f32p))
+            idx[t] = O.route_token(logits, k, O.ROUTER_TOPK)[0]
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(part, range(threads)))
+    return np.bincount(idx.ravel(), minlength=E)
+
+
 def run_reference(args, cfg):
     world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
     if rank != 0:
@@ -431,6 +457,9 @@ def run_reference(args, cfg):
     import qg_oracle as O
     threads = os.cpu_count() or 1
     m, x, info = oracle_layer_cpu(cfg, threads)
+    hist = oracle_expert_load(m, x, threads)
+    info["expert_load_top8"] = sorted(hist.tolist(), reverse=True)[:8]
+    info["expert_load_min"] = int(hist.min())
     # size one step to a bounded token sample (a few seconds on all cores)
     t0 = time.perf_counter()
     O.moe_forward_mt(m, x[:threads], threads)
