@@ -744,10 +744,19 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
     }
     cudaStream_t s = m->stream;
     do {
+        // router rows and the shared-expert gate row in one [E + 1, H] array
+        // (row E = the gate), so the logits kernels stage them as one matrix
+        const size_t router_bytes = sizeof(float) * (size_t)(E + (m->has_shared ? 1 : 0)) * H;
         if (rbits == 32) {
-            if ((rc = upload(m->weights, d->router, sizeof(float) * E * H, dev,
-                             reinterpret_cast<void **>(&m->router), s)))
+            if ((rc = m->weights.alloc(reinterpret_cast<void **>(&m->router), router_bytes)))
                 break;
+            const cudaError_t ce = cudaMemcpyAsync(m->router, d->router, sizeof(float) * E * H,
+                                                   dev ? cudaMemcpyDeviceToDevice
+                                                       : cudaMemcpyHostToDevice, s);
+            if (ce != cudaSuccess) {
+                rc = set_error(QGMOE_ERR_CUDA, "router upload: %s", cudaGetErrorString(ce));
+                break;
+            }
         } else {
             // bf16 bits or codes + scales, turned into the float32 rows the
             // reference multiplies by
@@ -760,8 +769,7 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
                                     (d->scale_dtype == QGMOE_SCALE_F32 ? 4 : 2);
             if (!(rc = upload(tmp, d->router_q, qb, dev, &rq, s)) &&
                 !(rc = upload(tmp, d->router_scale, sb, dev, &rs, s)) &&
-                !(rc = m->weights.alloc(reinterpret_cast<void **>(&m->router),
-                                        sizeof(float) * E * H)))
+                !(rc = m->weights.alloc(reinterpret_cast<void **>(&m->router), router_bytes)))
                 rc = launch_router_rows(rbits, E, H, static_cast<const uint8_t *>(rq), rs,
                                         d->scale_dtype == QGMOE_SCALE_F32, m->router, s);
             const cudaError_t se = cudaStreamSynchronize(s);
@@ -770,10 +778,17 @@ int qgmoe_create(const qgmoe_desc *d, qgmoe_t **out) {
                 rc = set_error(QGMOE_ERR_CUDA, "router upload: %s", cudaGetErrorString(se));
             if (rc) break;
         }
-        if (m->has_shared &&
-            (rc = upload(m->weights, d->shared_gate, sizeof(float) * H, dev,
-                         reinterpret_cast<void **>(&m->shared_gate), s)))
-            break;
+        if (m->has_shared) {
+            m->shared_gate = m->router + (size_t)E * H;
+            const cudaError_t ce = cudaMemcpyAsync(m->shared_gate, d->shared_gate,
+                                                   sizeof(float) * H,
+                                                   dev ? cudaMemcpyDeviceToDevice
+                                                       : cudaMemcpyHostToDevice, s);
+            if (ce != cudaSuccess) {
+                rc = set_error(QGMOE_ERR_CUDA, "shared gate upload: %s", cudaGetErrorString(ce));
+                break;
+            }
+        }
         const int G = m->G;  // expert stacks passed in: the experts this rank owns
         Part pgu{d->gate_up, d->gate_up_q, d->gate_up_scale, G * 2 * I};
         if ((rc = build_set(m->weights, bits, H, 2 * I, G, &pgu, 1, d->scale_dtype, dev, &m->gu, s)))

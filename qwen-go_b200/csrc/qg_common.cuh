@@ -281,6 +281,7 @@ int launch_randn(uint64_t seed, uint64_t stream, uint64_t offset, int64_t n, flo
                  float *out, cudaStream_t s);
 int num_sms(int device);
 int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld, int box_rows);
+bool encode_f32_map(void *map_out, const float *ptr, int rows, int cols, int box_rows);
 int launch_repack(const uint8_t *q, const __half *sc, int bits, int E, int rows_per_e, int K,
                   int RT, int interleave, int up_offset, uint8_t *qo, cudaStream_t s);
 // Bytes of the packed tensor-core copy of a weight set (codes + scales).

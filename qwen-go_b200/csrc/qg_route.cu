@@ -339,6 +339,203 @@ k_logits_rows(const float *__restrict__ x, int T, int H, int E, int Ep,
     }
 }
 
+// ---- 1c. logits of prefill batches: TMA-fed, about one CTA per SM ------------------
+// The serial chains leave no K parallelism, so the limit is the FP32 pipe (a
+// separately rounded product and sum per step, 2048 steps per chain at
+// H = 2048) fed from shared memory.  k_logits runs 256 CTAs of 4 warps with a
+// 4 x 4 register tile: 108 SMs get two CTAs and 40 get one.  Here a CTA owns
+// TT = 4 TPT tokens x RR = 64 RPT router rows, and TPT is picked per batch so
+// the grid is about one CTA per SM (4096 tokens x 128 rows: 147 CTAs of 28
+// tokens).  Eight consumer warps, two per scheduler so one's dependent adds
+// hide behind the other's: warp w takes tokens (w % 4) TPT .. + TPT - 1 (the
+// same for all its lanes: broadcast loads) and lane l rows
+// l + 32 (RPT (w / 4) + j), j < RPT.  Router rows and token rows arrive in
+// 32-wide K chunks by TMA (128B swizzle) into an LT_S-stage ring that a
+// producer warp keeps full.  Every product and sum is rounded separately in
+// index order as in k_logits, so the logits are the reference's bit for bit.
+// In row tile 0 a converter warp also writes the fp16 activation rows of the
+// tensor path from the staged token chunks (kept off the consumer warps,
+// whose pace sets the ring's).
+constexpr int LT_G = 4;               // token groups per CTA
+constexpr int LT_W = 2 * LT_G;        // consumer warps: token group x row half
+constexpr int LT_S = 4;               // ring stages
+constexpr int LT_THREADS = (LT_W + 2) * 32;  // + producer warp + converter warp
+
+template <int TPT, int RPT>
+struct LtCfg {
+    static constexpr int TT = LT_G * TPT, RR = 64 * RPT;
+    static constexpr int W_BYTES = RR * 128;                        // multiple of 1024
+    static constexpr int X_BYTES = (TT * 128 + 1023) / 1024 * 1024;
+    static constexpr int STAGE = W_BYTES + X_BYTES;
+    static constexpr int TX = (RR + TT) * 128;                      // bytes per stage
+    static constexpr int SMEM = LT_S * STAGE + 1024 + 2 * LT_S * 8;
+};
+
+// Shared address of line r of a 1024-byte aligned tile written by TMA with
+// the 128B swizzle, pre-swizzled: 16-byte chunk c of the line is at
+// lt_line(tile, r) ^ (c << 4).
+__device__ __forceinline__ uint32_t lt_line(uint32_t tile, int r) {
+    return tile + r * 128 + ((r & 7) << 4);
+}
+
+__device__ __forceinline__ float lt_el(const float4 &v, int e) {
+    return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+}
+
+template <int TPT, int RPT>
+__global__ void __launch_bounds__(LT_THREADS, 1)
+k_logits_tma(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+             int T, int H, int Ep, float *__restrict__ logits, __half *__restrict__ xh,
+             int *err) {
+    using C = LtCfg<TPT, RPT>;
+    extern __shared__ __align__(1024) uint8_t lt_raw[];
+    // offset, not integer casts, so the compiler keeps shared-memory accesses
+    uint8_t *base = lt_raw + ((1024u - (sm100::smem_u32(lt_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = sm100::smem_u32(base);
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + LT_S * C::STAGE);
+    uint64_t *empty = full + LT_S;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * C::TT, r0 = blockIdx.y * C::RR, nk = H / 32;
+    const bool do_h = xh && blockIdx.y == 0;
+    if (tid == 0) {
+        for (int s = 0; s < LT_S; s++) {
+            sm100::mbar_init(&full[s], 1);
+            sm100::mbar_init(&empty[s], LT_W + (do_h ? 1 : 0));
+        }
+        sm100::fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_enter();
+    if (warp == LT_W + 1) {
+        // converter: lane = (token of a group of 4, 16-byte chunk); fp16 rows
+        // out as 8-byte stores
+        if (!do_h) return;
+        bool range = false;
+        const int sub = lane >> 3, q = lane & 7;
+        for (int c = 0; c < nk; c++) {
+            const int s = c % LT_S;
+            if (!sm100::mbar_wait(&full[s], (c / LT_S) & 1, 0, LR_WAIT_CYCLES)) {
+                atomicOr(err, QG_FLAG_TIMEOUT);
+                break;
+            }
+            const uint32_t X = sbase + s * C::STAGE + C::W_BYTES;
+#pragma unroll
+            for (int i = 0; i < TPT; i++) {
+                const int ti = 4 * i + sub, t = t0 + ti;
+                const float4 v = sm100::ld_shared_f4(lt_line(X, ti) ^ (q << 4));
+                const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+                const float2 af = __half22float2(a), bf = __half22float2(b);
+                range |= (isfinite(v.x) && isinf(af.x)) || (isfinite(v.y) && isinf(af.y)) ||
+                         (isfinite(v.z) && isinf(bf.x)) || (isfinite(v.w) && isinf(bf.y));
+                if (t < T) {
+                    uint2 u;
+                    u.x = *reinterpret_cast<const uint32_t *>(&a);
+                    u.y = *reinterpret_cast<const uint32_t *>(&b);
+                    *reinterpret_cast<uint2 *>(xh + (size_t)t * H + c * 32 + q * 4) = u;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&empty[s]);
+        }
+        if (range) atomicOr(err, QG_FLAG_RANGE);
+        return;
+    }
+    if (warp == LT_W) {
+        // producer: chunk c into stage c % LT_S once the consumers freed it
+        if (lane == 0) {
+            sm100::prefetch_tmap(&tm_x);
+            sm100::prefetch_tmap(&tm_w);
+            int last = -1;
+            for (int c = 0; c < nk; c++) {
+                const int s = c % LT_S;
+                if (c >= LT_S &&
+                    !sm100::mbar_wait(&empty[s], ((c / LT_S) + 1) & 1, 0, LR_WAIT_CYCLES)) {
+                    atomicOr(err, QG_FLAG_TIMEOUT);
+                    break;
+                }
+                uint8_t *st = base + s * C::STAGE;
+                sm100::mbar_arrive_expect_tx(&full[s], C::TX);
+                sm100::tma_load_2d(st, &tm_w, c * 32, r0, &full[s]);
+                sm100::tma_load_2d(st + C::W_BYTES, &tm_x, c * 32, t0, &full[s]);
+                last = c;
+            }
+            // the CTA's shared memory must outlive every copy issued into it
+            if (last >= 0)
+                sm100::mbar_wait(&full[last % LT_S], (last / LT_S) & 1, 0, LR_WAIT_CYCLES);
+        }
+        return;
+    }
+    const int g = warp % LT_G, half = warp / LT_G;
+    const int tq = g * TPT;                // first token of this warp in the tile
+    const int rq = 32 * RPT * half;        // first row block of this warp
+    constexpr int NP = RPT / 2;  // row pairs (packed adds), plus one single row if RPT is odd
+    float2 acc[TPT][NP > 0 ? NP : 1];
+    float acc1[TPT];
+#pragma unroll
+    for (int i = 0; i < TPT; i++) {
+#pragma unroll
+        for (int j = 0; j < NP; j++) acc[i][j] = make_float2(0.f, 0.f);
+        acc1[i] = 0.f;
+    }
+    for (int c = 0; c < nk; c++) {
+        const int s = c % LT_S;
+        if (!sm100::mbar_wait(&full[s], (c / LT_S) & 1, 0, LR_WAIT_CYCLES)) {
+            atomicOr(err, QG_FLAG_TIMEOUT);
+            break;
+        }
+        const uint32_t W = sbase + s * C::STAGE, X = W + C::W_BYTES;
+        // rows rq + lane + 32 j share the swizzle phase lane & 7
+        const uint32_t wl = lt_line(W, rq + lane);
+        // operands of 4 K steps; the next group's loads are issued before
+        // the current group's products
+        float4 xa[2][TPT], wa[2][RPT];
+        auto load = [&](int q4, float4 (&xd)[TPT], float4 (&wd)[RPT]) {
+#pragma unroll
+            for (int i = 0; i < TPT; i++) xd[i] = sm100::ld_shared_f4(lt_line(X, tq + i) ^ (q4 << 4));
+#pragma unroll
+            for (int j = 0; j < RPT; j++) wd[j] = sm100::ld_shared_f4((wl + j * 4096) ^ (q4 << 4));
+        };
+        load(0, xa[0], wa[0]);
+#pragma unroll
+        for (int q4 = 0; q4 < 8; q4++) {
+            if (q4 < 7) load(q4 + 1, xa[(q4 + 1) & 1], wa[(q4 + 1) & 1]);
+            const float4 (&xc)[TPT] = xa[q4 & 1];
+            const float4 (&wc)[RPT] = wa[q4 & 1];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+#pragma unroll
+                for (int i = 0; i < TPT; i++) {
+                    const float xv = lt_el(xc[i], e);
+#pragma unroll
+                    for (int j = 0; j < NP; j++)
+                        acc[i][j] = add2_rn(acc[i][j], make_float2(__fmul_rn(xv, lt_el(wc[2 * j], e)),
+                                                                   __fmul_rn(xv, lt_el(wc[2 * j + 1], e))));
+                    if constexpr (RPT % 2 == 1)
+                        acc1[i] = __fadd_rn(acc1[i], __fmul_rn(xv, lt_el(wc[RPT - 1], e)));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int i = 0; i < TPT; i++) {
+        const int t = t0 + tq + i;
+        if (t >= T) continue;
+        float *row = logits + (size_t)t * Ep;
+#pragma unroll
+        for (int j = 0; j < NP; j++) {
+            const int r = r0 + rq + lane + 64 * j;
+            if (r < Ep) row[r] = acc[i][j].x;
+            if (r + 32 < Ep) row[r + 32] = acc[i][j].y;
+        }
+        if constexpr (RPT % 2 == 1) {
+            const int r = r0 + rq + lane + 32 * (RPT - 1);
+            if (r < Ep) row[r] = acc1[i];
+        }
+    }
+}
+
 template <int TT>
 static int launch_logits_rows(const float *x, int T, int H, int E, int Ep, const float *router,
                               const float *shared_gate, float *logits, __half *xh, int *err,
@@ -370,6 +567,54 @@ static int launch_logits_t(const float *x, int T, int H, int E, int Ep, const fl
     return QGMOE_OK;
 }
 
+template <int TPT, int RPT>
+static int launch_logits_tma_t(const CUtensorMap &mx, const CUtensorMap &mw, int T, int H, int Ep,
+                               float *logits, __half *xh, int *err, int dev, cudaStream_t s) {
+    using C = LtCfg<TPT, RPT>;
+    static bool attr[64] = {false};
+    if (dev >= 64 || !attr[dev]) {
+        QG_CUDA(cudaFuncSetAttribute(k_logits_tma<TPT, RPT>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        if (dev < 64) attr[dev] = true;
+    }
+    QG_CUDA(launch_pdl(k_logits_tma<TPT, RPT>, dim3((T + C::TT - 1) / C::TT, (Ep + C::RR - 1) / C::RR),
+                       dim3(LT_THREADS), C::SMEM, s, 1, mx, mw, T, H, Ep, logits, xh, err));
+    return QGMOE_OK;
+}
+
+using LtLaunch = int (*)(const CUtensorMap &, const CUtensorMap &, int, int, int, float *, __half *,
+                         int *, int, cudaStream_t);
+template <int RPT>
+static LtLaunch lt_pick(int tpt) {
+    static const LtLaunch f[8] = {launch_logits_tma_t<1, RPT>, launch_logits_tma_t<2, RPT>,
+                                  launch_logits_tma_t<3, RPT>, launch_logits_tma_t<4, RPT>,
+                                  launch_logits_tma_t<5, RPT>, launch_logits_tma_t<6, RPT>,
+                                  launch_logits_tma_t<7, RPT>, launch_logits_tma_t<8, RPT>};
+    return f[tpt - 1];
+}
+
+// k_logits_tma when its layout applies (router rows and the shared gate row
+// contiguous, x and the router 16-byte aligned); returns 1 when it does not,
+// so the caller takes k_logits.  Router rows per CTA: 64 RPT (RPT = 1..4,
+// the smallest that holds Ep, row tiles of 256 beyond); tokens per CTA:
+// 4 TPT, the smallest TPT <= 8 that covers the batch in one wave.
+static int launch_logits_tma(const float *x, int T, int H, int E, int Ep, const float *router,
+                             const float *shared_gate, float *logits, __half *xh, int *err,
+                             int dev, cudaStream_t s) {
+    if (Ep > E && shared_gate != router + (size_t)E * H) return 1;
+    const int RPT = Ep <= 64 ? 1 : Ep <= 128 ? 2 : Ep <= 192 ? 3 : 4;
+    const int RT = (Ep + 64 * RPT - 1) / (64 * RPT);
+    const int per = LT_G * num_sms(dev);  // token groups of one wave
+    int tpt = (int)(((int64_t)T * RT + per - 1) / per);
+    tpt = tpt < 1 ? 1 : tpt > 8 ? 8 : tpt;
+    CUtensorMap mx, mw;
+    if (!encode_f32_map(&mx, x, T, H, LT_G * tpt) || !encode_f32_map(&mw, router, Ep, H, 64 * RPT))
+        return 1;
+    const LtLaunch f = RPT == 1 ? lt_pick<1>(tpt) : RPT == 2 ? lt_pick<2>(tpt)
+                     : RPT == 3 ? lt_pick<3>(tpt) : lt_pick<4>(tpt);
+    return f(mx, mw, T, H, Ep, logits, xh, err, dev, s);
+}
+
 static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
                          const float *shared_gate, float *logits, __half *xh, int *err, int dev,
                          cudaStream_t s) {
@@ -377,6 +622,8 @@ static int launch_logits(const float *x, int T, int H, int E, int Ep, const floa
         return launch_logits_rows<8>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
     if (T <= 64 && lr_smem_bytes(16, H) <= LR_SMEM_MAX)
         return launch_logits_rows<16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
+    const int rc = launch_logits_tma(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
+    if (rc != 1) return rc;
     // 32 tokens x 64 rows, 16 chains per thread (8 f32x2 pairs)
     return launch_logits_t<4, 4, 8, 16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, s);
 }

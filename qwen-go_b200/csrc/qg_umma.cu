@@ -1046,6 +1046,26 @@ int encode_act_map(void *map_out, const __half *ptr, int rows, int cols, int ld,
     return QGMOE_OK;
 }
 
+// 2-D float32 [rows, cols] row-major tensor (row pitch = cols), box 32 cols
+// (one 128-byte line) x box_rows rows, 128B swizzle, zero fill beyond the
+// edges.  Returns false (and leaves the error state alone) when the driver
+// entry point is missing or the layout does not suit TMA, so the caller can
+// take a path without tensor maps.
+bool encode_f32_map(void *map_out, const float *ptr, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || cols % 32 || rows <= 0 ||
+        box_rows <= 0 || box_rows > 256)
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(reinterpret_cast<CUtensorMap *>(map_out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+              const_cast<float *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 size_t packed_bytes(int bits, int E, int rows_per_e, int K) {
     // rows_per_e / 128 row tiles x K / 64 k blocks per expert
     const size_t tiles = (size_t)E * (rows_per_e / UM_M) * (K / UM_BK);

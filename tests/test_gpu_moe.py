@@ -172,6 +172,21 @@ def test_routing_exact_at_any_batch(bits, Is, T):
     assert not flipped
 
 
+@pytest.mark.parametrize("E,Is", [(16, 0), (60, 64), (100, 0), (128, 64), (200, 0), (300, 0)])
+@pytest.mark.parametrize("T", [300, 1200, 4000])
+def test_prefill_logits_tiles_route_exactly(E, Is, T):
+    """Batches above 64 tokens take the TMA-fed logits kernel, whose tile
+    (tokens per warp, router rows per lane) follows the batch size and the
+    number of router rows (E, plus the shared-expert gate row): 16 and 61
+    rows (one per lane and warp), 100 (two), 129 (three), 200 (four) and
+    300 (two row tiles of 256), each at three batch sizes.  Routing must
+    equal the oracle's bit for bit."""
+    m = host_case(H=256, E=E, k=4, I=64, Is=Is, bits=8, seed=70 + E + T)
+    x = O.randn(70, T, (T, 256))
+    _, flipped = run_both(m, x, O.ROUTER_TOPK)
+    assert not flipped
+
+
 def test_routing_near_ties_follow_the_serial_sum():
     """Router rows that differ in one low-order bit per element give logits
     a few ulps apart and many exact probability ties: the order must still be
