@@ -786,14 +786,32 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         S.base = v - v % (unsigned long long)G;
     }
     bool range = false;
-    for (int i = tid; i < T * H; i += FZ_THREADS) {
-        const int t = i / H, kk = i - t * H;
-        const float v = a.x[i];
-        xs[t * a.xstride + (TC ? kk : stage_pos<V>(kk / V, kk % V))] = v;
-        if constexpr (TC) {  // fp16 B rows; absent tokens' columns are never read back
-            const __half hv = __float2half_rn(v);
-            range |= isinf(__half2float(hv)) && isfinite(v);
-            reinterpret_cast<__half *>(fz_smem + a.off_x16 + t * a.x16tok)[kk] = hv;
+    if (TC && !(reinterpret_cast<uintptr_t>(a.x) & 15)) {
+        // 16-byte loads: one memory round trip per thread at decode sizes
+        const int h4 = H / 4;
+        for (int i = tid; i < T * h4; i += FZ_THREADS) {
+            const int t = i / h4, k4 = i - t * h4;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
+            *reinterpret_cast<float4 *>(xs + t * a.xstride + 4 * k4) = v;
+            const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+            const float2 lf = __half22float2(lo), hf = __half22float2(hi);
+            range |= (isinf(lf.x) && isfinite(v.x)) || (isinf(lf.y) && isfinite(v.y)) ||
+                     (isinf(hf.x) && isfinite(v.z)) || (isinf(hf.y) && isfinite(v.w));
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t *>(&lo);
+            u.y = *reinterpret_cast<const uint32_t *>(&hi);
+            *reinterpret_cast<uint2 *>(fz_smem + a.off_x16 + t * a.x16tok + 8 * k4) = u;
+        }
+    } else {
+        for (int i = tid; i < T * H; i += FZ_THREADS) {
+            const int t = i / H, kk = i - t * H;
+            const float v = a.x[i];
+            xs[t * a.xstride + (TC ? kk : stage_pos<V>(kk / V, kk % V))] = v;
+            if constexpr (TC) {  // fp16 B rows; absent tokens' columns are never read back
+                const __half hv = __float2half_rn(v);
+                range |= isinf(__half2float(hv)) && isfinite(v);
+                reinterpret_cast<__half *>(fz_smem + a.off_x16 + t * a.x16tok)[kk] = hv;
+            }
         }
     }
     if (range) atomicOr(a.err, QG_FLAG_RANGE);
