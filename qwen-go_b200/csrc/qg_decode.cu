@@ -106,11 +106,12 @@ __device__ __forceinline__ void fz_timeout(const DecodeArgs &a) { atomicOr(a.err
 // All worker threads of every CTA.  The arrival counter only grows, by G
 // per barrier: a launch's n-th barrier completes when it reaches base +
 // n G, where base (a multiple of G) is the count when the launch began.
-// Arrivals are fire-and-forget releases; thread 0 polls with acquires.
+// Arrivals are fire-and-forget releases; thread 0 polls with acquires.  The
+// CTA barrier orders the other workers' writes before thread 0's release
+// (release is cumulative) and after its acquire, so no separate fences.
 __device__ void fz_grid_sync(const DecodeArgs &a, FzShared &S) {
     wsync();
     if (threadIdx.x == 0) {
-        __threadfence();
         asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long target = S.base + (unsigned long long)(++S.nbar) * gridDim.x;
         if (ld_acq(a.bar) < target) {
@@ -123,7 +124,6 @@ __device__ void fz_grid_sync(const DecodeArgs &a, FzShared &S) {
                 }
             }
         }
-        __threadfence();
     }
     wsync();
 }
@@ -594,24 +594,34 @@ __device__ void fz_compact(const unsigned *tok, int E, FzList &L, int base) {
 }
 
 // Approximate top-k of token t (warp): larger logit first, then the lower
-// index; experts whose logits are NaN are never chosen (-1).
+// index; experts whose logits are NaN are never chosen (-1).  A candidate
+// set only has to be close -- the exact routing computes what it missed --
+// so each logit becomes one 32-bit key, its order-preserving bits with the
+// low byte replaced by 255 - expert (E <= 256), and each rank is one
+// warp-wide max reduction; logits within 2^-15 of each other order by index.
 template <int NJ>
 __device__ void fz_topk(const DecodeArgs &a, int t, int lane, int *cand) {
-    float v[NJ];
-    unsigned usable = 0;
+    unsigned key[NJ];
 #pragma unroll
     for (int j = 0; j < NJ; j++) {
         const int e = lane + 32 * j;
-        v[j] = e < a.E ? __ldcg(a.approx + (size_t)t * a.Ep + e) : -INFINITY;
-        if (e < a.E) usable |= 1u << j;
+        const float v = e < a.E ? __ldcg(a.approx + (size_t)t * a.Ep + e) : __int_as_float(0x7fffffff);
+        const unsigned u = __float_as_uint(v);
+        const unsigned mono = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        key[j] = (e < a.E && !isnan(v)) ? ((mono & ~0xFFu) | (unsigned)(255 - e)) : 0u;
     }
     for (int r = 0; r < a.k; r++) {
-        float bv;
-        int bi;
-        warp_best<NJ>(v, usable, lane, bv, bi);
-        const bool ok = bi >= 0 && bi < a.E;
-        if (ok && (bi & 31) == lane) usable &= ~(1u << (bi >> 5));
-        if (lane == 0) cand[r] = ok ? bi : -1;
+        unsigned best = 0u;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) best = max(best, key[j]);
+        best = __reduce_max_sync(FULL, best);
+        const int bi = best ? 255 - (int)(best & 0xFFu) : -1;
+        if (bi >= 0 && (bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if (j == (bi >> 5)) key[j] = 0u;
+        }
+        if (lane == 0) cand[r] = bi;
     }
     __syncwarp();
 }
