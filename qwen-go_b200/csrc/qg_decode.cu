@@ -70,7 +70,7 @@ struct FzList {
 
 struct FzShared {
     uint64_t full[FZ_NSMAX], empty[FZ_NSMAX];
-    uint64_t wbar, hbar;                   // router rows; staged h rows
+    uint64_t wbar, hbar, xbar;             // router rows; staged h rows; token rows
     FzList A, B;                           // speculative tasks; tasks after exact routing
     int cand[FD_MAX_T][QG_MAX_TOPK];       // approximate selection (-1: none)
     int sel[FD_MAX_T][QG_MAX_TOPK];        // exact selection
@@ -772,6 +772,7 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         }
         sm100::mbar_init(&S.wbar, 1);
         sm100::mbar_init(&S.hbar, 1);
+        sm100::mbar_init(&S.xbar, 1);
         sm100::fence_mbar_init();
         S.nbar = 0;
         S.cand_ready = 0;
@@ -797,12 +798,18 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
     }
     bool range = false;
     if (TC && !(reinterpret_cast<uintptr_t>(a.x) & 15)) {
-        // 16-byte loads: one memory round trip per thread at decode sizes
+        // token rows by bulk copies (one memory round trip), then fp16 rows
+        // converted from shared memory
+        if (tid == 0) {
+            sm100::mbar_arrive_expect_tx(&S.xbar, (uint32_t)(T * H * 4));
+            for (int t = 0; t < T; t++)
+                sm100::bulk_load(xs + t * a.xstride, a.x + (size_t)t * H, H * 4, &S.xbar);
+        }
+        if (!sm100::mbar_wait(&S.xbar, 0, 0, FZ_WAIT) && lane == 0) fz_timeout(a);
         const int h4 = H / 4;
         for (int i = tid; i < T * h4; i += FZ_THREADS) {
             const int t = i / h4, k4 = i - t * h4;
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(a.x) + i);
-            *reinterpret_cast<float4 *>(xs + t * a.xstride + 4 * k4) = v;
+            const float4 v = *reinterpret_cast<const float4 *>(xs + t * a.xstride + 4 * k4);
             const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
             const float2 lf = __half22float2(lo), hf = __half22float2(hi);
             range |= (isinf(lf.x) && isfinite(v.x)) || (isinf(lf.y) && isfinite(v.y)) ||
@@ -836,29 +843,38 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
     const bool spec_topk = a.speculate && a.mode == QGMOE_ROUTER_TOPK;
     if (spec_topk && nr > 0) {
         if (!sm100::mbar_wait(&S.wbar, 0, 0, FZ_WAIT) && lane == 0) fz_timeout(a);
-        const int nl = nr * T;  // (row, token) pairs
-        float acc[2 * FD_MAX_T];
+        const int nl = nr * T;  // (row, token) pairs, pair q T + t
+        float acc[2][FD_MAX_T];
 #pragma unroll
-        for (int i = 0; i < 2 * FD_MAX_T; i++) acc[i] = 0.f;
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+            for (int t = 0; t < FD_MAX_T; t++) acc[q][t] = 0.f;
         for (int p = tid; p < H / 4; p += FZ_WT) {
 #pragma unroll
-            for (int i = 0; i < 2 * FD_MAX_T; i++) {
-                if (i >= nl) break;
-                const int q = i / T, t = i - q * T;
+            for (int q = 0; q < 2; q++) {
+                if (q >= nr) break;
                 const float4 wv =
                     *reinterpret_cast<const float4 *>(fz_smem + ((size_t)q * (H + 4) + 4 * p) * 4);
-                const float4 xv = x4<BITS>(xs, a.xstride, t, p);
-                acc[i] = fmaf(wv.x, xv.x,
-                              fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[i]))));
+#pragma unroll
+                for (int t = 0; t < FD_MAX_T; t++) {
+                    if (t >= T) break;
+                    const float4 xv = x4<BITS>(xs, a.xstride, t, p);
+                    acc[q][t] = fmaf(wv.x, xv.x,
+                                     fmaf(wv.y, xv.y, fmaf(wv.z, xv.z, fmaf(wv.w, xv.w, acc[q][t]))));
+                }
             }
         }
 #pragma unroll
-        for (int i = 0; i < 2 * FD_MAX_T; i++) {
-            if (i >= nl) break;
-            float v = acc[i];
+        for (int q = 0; q < 2; q++) {
+            if (q >= nr) break;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-            if (lane == 0) S.part[warp][i] = v;
+            for (int t = 0; t < FD_MAX_T; t++) {
+                if (t >= T) break;
+                float v = acc[q][t];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+                if (lane == 0) S.part[warp][q * T + t] = v;
+            }
         }
         wsync();
         if (tid < nl) {
@@ -936,8 +952,13 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
         S.slot[t][r] = sl >= 0 && sl < dec_slots(k) ? sl : 0;
     }
     if (a.has_shared && tid < T) S.sg[tid] = __ldcg(&a.route->sg[tid]);
-    bool anymiss = false;
-    for (int t = 0; t < T; t++) anymiss |= __ldcg(&a.route->miss[t]) != 0;
+    // S.sel / S.w / S.slot / S.sg are read by other threads below (the
+    // missed pairs' list, the combine): every write lands first
+    wsync();
+    bool anymiss = false;  // the T loads in flight together
+#pragma unroll
+    for (int t = 0; t < FD_MAX_T; t++)
+        if (t < T) anymiss |= __ldcg(&a.route->miss[t]) != 0;
     const int base_b = T * k + T;
     if (anymiss) {
         // rare: experts the approximate top-k missed, by expert

@@ -144,3 +144,20 @@ def test_decode_kernel_wait_limit_runs_out_and_recovers():
         assert np.array_equal(g.forward_batch(x), good)
     ref, *_ = O.moe_forward(m, x)
     check_outputs(good, ref, 8)
+
+
+def test_decode_kernel_many_batches_at_config1():
+    """Twelve different 8-token batches on one handle at config 1 (shared
+    expert, E=16): every CTA's combine reads routing entries that other
+    threads of the CTA stage, so each batch's output must match the oracle
+    whatever the timing (a missing barrier there once let a combine read
+    the previous launch's slots)."""
+    c = CONFIGS["c1"]
+    m, dev = device_case(**c)
+    g = make_gpu_moe(m, O.ROUTER_TOPK, dev)
+    for i in range(12):
+        x = O.randn(c["seed"] + i, 200, (8, c["H"]))
+        out, idx, w = g.forward_batch(x, return_routing=True)
+        ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
+        assert not check_routing(idx, w, ridx, rw, probs)
+        check_outputs(out, ref, c["bits"])
