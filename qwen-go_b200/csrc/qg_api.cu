@@ -182,6 +182,7 @@ struct qgmoe {
     float *dec_approx = nullptr, *dec_d = nullptr;
     unsigned char *dec_h = nullptr;
     unsigned long long *dec_bar = nullptr, *dec_flags = nullptr;
+    unsigned *dec_tdone = nullptr;  // gate_up tiles done per decode task (two lists)
     int dec_hrow = 0;
     int dec_speculate = 1;
     long long wait_cycles = 0;  // qgmoe_set_wait_limit; 0: the kernels' defaults (1-2 s)
@@ -318,6 +319,7 @@ static int ensure_capacity(qgmoe *m, int T) {
         QG_A(m->dec_d, sizeof(float) * dslots * m->H);
         QG_A(m->dec_bar, sizeof(unsigned long long));
         QG_A(m->dec_flags, sizeof(unsigned long long) * nflags);
+        QG_A(m->dec_tdone, sizeof(unsigned) * 2 * (FD_MAX_T * QG_MAX_TOPK + 1));
         QG_CUDA(cudaMemsetAsync(m->dec_route, 0, sizeof(DecRoute), m->stream));
         QG_CUDA(cudaMemsetAsync(m->dec_bar, 0, sizeof(unsigned long long), m->stream));
         QG_CUDA(cudaMemsetAsync(m->dec_flags, 0, sizeof(unsigned long long) * nflags, m->stream));
@@ -562,6 +564,7 @@ static int enqueue_forward_decode(qgmoe *m, const float *x, int T, float *out, c
     a.topk_w = m->st.topk_w;
     a.shared_w = m->st.shared_w;
     a.route = m->dec_route;
+    a.tdone = m->dec_tdone;
     a.bar = m->dec_bar;
     a.flags = m->dec_flags;
     a.err = m->err_dev;

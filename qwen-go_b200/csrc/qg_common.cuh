@@ -211,6 +211,7 @@ struct DecodeArgs {
     // weights (qg_umma.cu k_repack), streamed instead of the row-major codes
     const uint8_t *gu_pq, *dn_pq, *sgu_pq, *sdn_pq;
     int kbi_gu, kbi_dn, kbi_sdn;      // 64-code k blocks per streamed item
+    unsigned *tdone;                  // [2][FD_MAX_T * QG_MAX_TOPK + 1] gate_up tiles done per task
     float *approx;                    // [T, Ep] approximate logits (speculation)
     float *logits;                    // [T, Ep] logits in the reference's serial order
     unsigned char *hbuf;              // h rows, [dec_slots(k), hrow bytes]

@@ -143,6 +143,23 @@ __device__ __forceinline__ bool fz_wait_flag(const DecodeArgs &a, const unsigned
     return true;
 }
 
+// Bounded wait until *p >= v (acquire).
+__device__ __forceinline__ bool fz_wait_u32(const DecodeArgs &a, const unsigned *p, unsigned v) {
+    auto ld = [&]() {
+        unsigned r;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+        return r;
+    };
+    if (ld() >= v) return true;
+    const long long budget = a.wait > 0 ? a.wait : FZ_WAIT;
+    const long long t0 = clock64();
+    while (ld() < v) {
+        if (clock64() - t0 > budget) return false;
+        __nanosleep(32);
+    }
+    return true;
+}
+
 // ---- CUDA-core products (f32 / bf16 experts) ---------------------------------------
 // NR weight rows in shared memory dotted with the staged rows of the tokens
 // in `mask` (token t at xs + t * xstride): per lane the chunks lane,
@@ -286,7 +303,8 @@ __device__ __forceinline__ void tc_kblock(const unsigned char *tile, const unsig
 // form h = silu(g) * u (fp16) for the tile's 64 rows.
 template <int BITS, bool GATEUP>
 __device__ void fz_phase_tc(const DecodeArgs &a, FzShared &S, const FzList &L, bool with_shared,
-                            unsigned char *smem, int &qi, int &qc, int &hph, int &nx) {
+                            unsigned char *smem, int &qi, int &qc, int &hph, int &nx,
+                            unsigned *tdone) {
     using P = PTile<BITS>;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = gridDim.x, b = blockIdx.x, T = a.T, k = a.k;
@@ -353,6 +371,9 @@ __device__ void fz_phase_tc(const DecodeArgs &a, FzShared &S, const FzList &L, b
             hd = x.d;
             const int K = x.shared ? a.Is : a.I;
             if (tid == 0) {
+                // every gate_up tile of the task has written its h rows
+                if (!fz_wait_u32(a, tdone + x.d, (unsigned)(x.shared ? a.Is / 64 : a.I / 64)))
+                    fz_timeout(a);
                 fence_proxy_async();
                 sm100::mbar_arrive_expect_tx(&S.hbar, (uint32_t)(__popc(x.mask) * K * 2));
                 for (int t = 0; t < T; t++)
@@ -404,6 +425,11 @@ __device__ void fz_phase_tc(const DecodeArgs &a, FzShared &S, const FzList &L, b
                     }
                 }
             }
+            // the tile's h rows are out: count it for its task (the down
+            // phase stages a task's h rows once all its tiles are counted)
+            msync();
+            if (tid == 0)
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(tdone + x.d) : "memory");
         } else {
 #pragma unroll
             for (int h = 0; h < 2; h++) {
@@ -833,6 +859,10 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
     }
     if (range) atomicOr(a.err, QG_FLAG_RANGE);
     for (int e = tid; e < a.E; e += FZ_THREADS) tok[e] = 0u;
+    // this launch's task counters start at zero; the first grid barrier
+    // orders the clearing before any tile is counted
+    if (b == 0)
+        for (int i = tid; i < 2 * (FZ_MAXD + 1); i += FZ_THREADS) a.tdone[i] = 0u;
     __syncthreads();
     if (warp == FZ_WORKERS) {
         if (nr > 0) fz_chains<BITS>(a, S, fz_smem, nr);
@@ -923,19 +953,21 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
 
     // ---- 3, 4. gate_up and down of the candidates and the shared expert ----
     int qi = 0, qc = 0, hph = 0, nx = 0;
-    auto phases = [&](const FzList &L, bool with_shared) {
-        if constexpr (TC)
-            fz_phase_tc<BITS, true>(a, S, L, with_shared, fz_smem, qi, qc, hph, nx);
-        else
+    // Tensor cores: no grid barrier between gate_up and down -- a down task
+    // waits only for its own gate_up tiles (counted in a.tdone, one counter
+    // set per list), so CTAs done with gate_up early start their down work.
+    auto phases = [&](const FzList &L, bool with_shared, unsigned *tdone) {
+        if constexpr (TC) {
+            fz_phase_tc<BITS, true>(a, S, L, with_shared, fz_smem, qi, qc, hph, nx, tdone);
+            fz_phase_tc<BITS, false>(a, S, L, with_shared, fz_smem, qi, qc, hph, nx, tdone);
+        } else {
             fz_phase<BITS, MT, true>(a, S, L, with_shared, fz_smem, qi, qc, hph);
-        fz_grid_sync(a, S);
-        if constexpr (TC)
-            fz_phase_tc<BITS, false>(a, S, L, with_shared, fz_smem, qi, qc, hph, nx);
-        else
+            fz_grid_sync(a, S);
             fz_phase<BITS, MT, false>(a, S, L, with_shared, fz_smem, qi, qc, hph);
+        }
         fz_grid_sync(a, S);
     };
-    phases(S.A, a.has_shared);
+    phases(S.A, a.has_shared, a.tdone);
 
     // ---- 5. exact routing; pairs the candidates missed ----
     if (warp == 0) {
@@ -981,7 +1013,7 @@ __global__ void __launch_bounds__(FZ_THREADS, 1) k_decode(const __grid_constant_
                     }
         }
         wsync();
-        phases(S.B, false);
+        phases(S.B, false, a.tdone + FZ_MAXD + 1);
     }
 
     // ---- 6. combine, output columns split over the CTAs ----
