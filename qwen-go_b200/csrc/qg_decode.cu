@@ -13,7 +13,9 @@
 //   2. every CTA: the approximate top-k of each token (the candidates) and
 //      the batch's distinct candidate experts;
 //   3. gate_up + SwiGLU of the candidates and the shared expert
-//      (model/moe.go:64-76, model/model.go:350-358) -> grid barrier;
+//      (model/moe.go:64-76, model/model.go:350-358) -> grid barrier (f32 /
+//      bf16 experts) or, on the tensor path, per-task counters: a down task
+//      starts once its own gate_up tiles are done;
 //   4. down rows of every (token, candidate) pair -> grid barrier;
 //   5. wait for the exact routing, which the chain warps publish once every
 //      chain has finished: the reference's softmax, top-k and weights
