@@ -618,7 +618,10 @@ static int launch_logits_tma(const float *x, int T, int H, int E, int Ep, const 
 static int launch_logits(const float *x, int T, int H, int E, int Ep, const float *router,
                          const float *shared_gate, float *logits, __half *xh, int *err, int dev,
                          cudaStream_t s) {
-    if (T <= 8 && lr_smem_bytes(8, H) <= LR_SMEM_MAX)
+    // up to 64 tokens: 8-token tiles, so the chains spread over more SMs
+    // (64 tokens x 128 rows: 128 CTAs) -- each chain's serial adds, not the
+    // copies, set the time
+    if (T <= 64 && lr_smem_bytes(8, H) <= LR_SMEM_MAX)
         return launch_logits_rows<8>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);
     if (T <= 64 && lr_smem_bytes(16, H) <= LR_SMEM_MAX)
         return launch_logits_rows<16>(x, T, H, E, Ep, router, shared_gate, logits, xh, err, dev, s);

@@ -103,14 +103,26 @@ __device__ __forceinline__ float route_token(const float *__restrict__ lrow, int
             selp = pr;
         }
     } else if (mode == QGMOE_ROUTER_TOPK) {
+        // rank r: the largest remaining probability, ties to the lower
+        // expert -- one warp max over the probabilities' bits (p >= 0, so
+        // the bits order like the values), then one warp min over the
+        // experts that hold it
         unsigned usable = valid;
         for (int r = 0; r < k; r++) {
-            float bv;
-            int bi;
-            warp_best(p, usable, lane, bv, bi);
-            if ((bi & 31) == lane) usable &= ~(1u << (bi >> 5));
-            if (lane == r) selp = bv;
-            if (lane == 0) sel[r] = bi;
+            unsigned lkey = 0u;
+            int lj = -1;
+#pragma unroll
+            for (int j = 0; j < NJ; j++)
+                if ((usable >> j) & 1u) {
+                    const unsigned key = __float_as_uint(p[j]) | 0x80000000u;
+                    if (lj < 0 || key > lkey) lkey = key, lj = j;  // equal: lower j kept
+                }
+            const unsigned top = __reduce_max_sync(FULL, lj >= 0 ? lkey : 0u);
+            const unsigned bi = __reduce_min_sync(
+                FULL, (lj >= 0 && lkey == top) ? (unsigned)(lane + 32 * lj) : 0xFFFFFFFFu);
+            if ((int)(bi & 31u) == lane) usable &= ~(1u << (bi >> 5));
+            if (lane == r) selp = __uint_as_float(top & 0x7FFFFFFFu);
+            if (lane == 0) sel[r] = (int)bi;
         }
     } else {
         // PREFIX: the literal moe.go:49 bound orders only experts 0..k-1
