@@ -87,6 +87,22 @@ def test_ties_pick_lowest_index():
     check_outputs(out, ref, 32)
 
 
+@pytest.mark.parametrize("E,T", [(16, 300), (128, 200), (200, 70)])
+def test_ties_pick_lowest_index_at_batch_sizes(E, T):
+    """Every probability equal (zero router) on the batched top-k kernels:
+    each rank's winner is the lowest remaining expert, as the reference's
+    insertion sort leaves them, so every token selects 0..k-1."""
+    m = host_case(H=64, E=E, k=6, I=32, Is=0, bits=8, seed=49 + E)
+    m.router[:] = 0
+    gpu = make_gpu_moe(m, O.ROUTER_TOPK)
+    x = O.randn(49, E, (T, 64))
+    out, idx, w = gpu.forward_batch(x, return_routing=True)
+    assert np.all(idx == np.arange(6))
+    ref, ridx, rw, _, probs = O.moe_forward(m, x, want_probs=True)
+    assert not check_routing(idx, w, ridx, rw, probs)
+    check_outputs(out, ref, 8)
+
+
 @pytest.mark.parametrize("E,k", [(1, 1), (8, 8), (8, 1), (64, 32)])
 def test_extreme_topk(E, k):
     m = host_case(H=64, E=E, k=k, I=32, Is=32, bits=8, seed=42 + E + k)
