@@ -63,7 +63,7 @@ def load_peaks():
 # profiles/ (same workload, same kernel build): (config, tokens, kernel) ->
 # (bytes, summary file).  Other workloads report null.
 NCU_TRAFFIC = {
-    ("c3", 4096, "gate_up"): (562.258944e6 + 52.420352e6, "profiles/full_c3_prefill_t4096.md"),
+    ("c3", 4096, "gate_up"): (568.004864e6 + 52.227584e6, "profiles/full_c3_prefill_t4096.md"),
     ("c2", 64, "gate_up"): (219.797248e6 + 5.550848e6, "profiles/full_c2_decode_t64.md"),
     ("c2", 1, "decode"): (22.441472e6, "profiles/full_k_decode_c2.md"),
     ("c2", 8, "decode"): (136.638976e6 + 4.069632e6, "profiles/full_k_decode_c2.md"),
